@@ -1,0 +1,365 @@
+#!/usr/bin/env python
+"""Benchmark: det images/s (config 3) and rec lines/s (config 4) on B200.
+
+One step = one pass of the hot path over one batch of synthetic input:
+  det: B x 3 x 960 x 960 ImageNet-normalised pixels through the DB detector
+       (PP-LCNet backbone, DBFPN, DB head) -> [B, 1, 960, 960] probabilities.
+  rec: 256 x 3 x 48 x 320 lines through the SVTR-style recogniser with the
+       CTC argmax exit -> [256, 40, 2] (value, index) pairs.
+`value` is whole-job det img/s with inputs resident in HBM (CUDA-graph
+replays timed with CUDA events on the replay stream, max over ranks).  `e2e`
+is the same metric through the public session API with host tensors
+(host->device input copy and device->host result read inside every step).
+Inputs (708 MB per det step) are larger than L2, so no L2 flush is needed.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU: torchrun, one process per GPU, each rank a full replica on its own
+shard of images (weak scaling, no data-path collective); rank 0 prints.
+`--impl reference` times the reference CPU path (the C++ restatement in
+oracle/, all host threads) on the same workload and prints its own line.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+DET_HW = 960
+REC_B = 256
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of one GPU during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        dist.barrier()
+
+
+def roofline(profile, hbm, tf):
+    """Dominant kernel family by device time; achieved = algorithmic bytes (or
+    flops) per launch / mean launch duration (CUDA events, this process)."""
+    fam = {}
+    for kern, node, by, fl, ms in profile:
+        f = fam.setdefault(kern, [0.0, 0.0, 0.0, 0])
+        f[0] += by
+        f[1] += fl
+        f[2] += ms
+        f[3] += 1
+    total_ms = sum(v[2] for v in fam.values())
+    kern, (by, fl, ms, n) = max(fam.items(), key=lambda kv: kv[1][2])
+    tensor = kern in ("head_gemm",)
+    if tensor:
+        ach = fl / (ms * 1e-3) / 1e12
+        peak, unit, bound = tf, "TFLOP/s", "tensor"
+    else:
+        ach = by / (ms * 1e-3) / 1e9
+        peak, unit, bound = hbm, "GB/s", "hbm"
+    shares = {k: round(v[2] / total_ms, 4) for k, v in sorted(fam.items(), key=lambda kv: -kv[1][2])}
+    return {"kernel": kern, "bound": bound, "achieved": round(ach, 1), "peak": peak, "unit": unit,
+            "frac": round(ach / peak, 4), "traffic": None, "launches_per_step": n,
+            "bytes_per_launch": by / n, "flops_per_launch": fl / n, "ms_per_launch": ms / n,
+            "share_of_step": round(ms / total_ms, 4), "family_shares": shares}
+
+
+def cpu_baseline_det(seconds_budget=20.0):
+    """The reference CPU path (oracle restatement, all host threads) on a
+    bounded sample: whole 960x960 images, one at a time."""
+    import numpy as np
+
+    import oracle
+    import qppocr_b200 as q
+    from qppocr_b200 import nets
+
+    g, w = nets.build_det()
+    g = q.optimize(g, w)
+    x = nets.det_input(1, DET_HW, DET_HW)
+    oracle.run_graph(g, w, {"x": x})  # warm
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        oracle.run_graph(g, w, {"x": x})
+        n += 1
+        if time.perf_counter() - t0 > seconds_budget or n >= 20:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 4), "unit": "img/s", "cores": oracle.threads(), "kind": "port",
+            "sample": f"{n} det images 3x{DET_HW}x{DET_HW}, one at a time, {dt:.1f} s"}
+
+
+def cpu_baseline_rec(seconds_budget=10.0):
+    import oracle
+    import qppocr_b200 as q
+    from qppocr_b200 import nets
+
+    g, w = nets.build_rec()
+    g = q.optimize(g, w)
+    x = nets.rec_input(16)
+    oracle.argmax_pairs(oracle.run_graph(g, w, {"x": x})[0])
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        oracle.argmax_pairs(oracle.run_graph(g, w, {"x": x})[0])
+        n += 16
+        if time.perf_counter() - t0 > seconds_budget:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "lines/s", "cores": oracle.threads(), "kind": "port",
+            "sample": f"{n} lines 3x48x320 in batches of 16, {dt:.1f} s"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    import oracle
+
+    oracle.build()
+    per_step = []
+    import numpy as np  # noqa: F401
+
+    from qppocr_b200 import graph as G
+    from qppocr_b200 import nets
+
+    g, w = nets.build_det()
+    g = G.optimize(g, w)
+    x = nets.det_input(1, DET_HW, DET_HW)
+    for _ in range(max(args.warmup, 1)):
+        oracle.run_graph(g, w, {"x": x})
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.run_graph(g, w, {"x": x})
+        per_step.append(time.perf_counter() - t0)
+    total = sum(per_step)
+    v = len(per_step) / total
+    line = {"metric": "det_img_per_s (DB det 3x960x960) + rec_lines_per_s", "value": round(v, 4),
+            "unit": "img/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1000 * total / len(per_step), 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "config 3: DB det, 3x960x960, 1 image per step (CPU sample)"},
+            "cpu_baseline": {"value": round(v, 4), "unit": "img/s", "cores": oracle.threads(),
+                             "kind": "port",
+                             "sample": f"{len(per_step)} det images, one per step, C++ restatement of "
+                                       "the reference CPU path"},
+            "e2e": {"value": round(v, 4), "unit": "img/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=64, help="det images per step per GPU")
+    ap.add_argument("--rec-batch", type=int, default=REC_B)
+    ap.add_argument("--math", default="tf32", choices=["tf32", "3xtf32"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-rec", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_init()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+
+    import numpy as np
+    import torch
+
+    import qppocr_b200 as q
+    from qppocr_b200 import nets
+
+    torch.cuda.set_device(local)
+    ctx = q.CudaContext.open(local)
+    hbm, tf, peak_src = peaks()
+
+    # ---------------------------------------------------------------- det
+    g, w = nets.build_det()
+    g = q.optimize(g, w)
+    B = args.batch
+    x = nets.det_input(B, DET_HW, DET_HW, seed=3 + rank)
+    det = ctx.create_session(g, w, role="det", math=args.math)
+    det.run({"x": x})                       # plan build + graph capture
+    for _ in range(args.warmup):
+        det.replay({"x": x}, 1)
+    clocks = Clocks(local) if rank == 0 else None
+    barrier(world)
+    if clocks:
+        clocks.start()
+    torch.cuda.synchronize()
+    ms = det.replay({"x": x}, args.steps)   # K back-to-back replays, CUDA events
+    torch.cuda.synchronize()
+    clk = clocks.stop() if clocks else None
+    barrier(world)
+    ms_max = max_over_ranks(ms, world)
+    value = world * B / (ms_max / 1000.0)
+
+    prof = det.profile({"x": x}, iters=2)
+    launches = len(prof)
+    rl = roofline(prof, hbm, tf)
+    rl["peak_source"] = peak_src
+
+    # e2e through the public API: host inputs, H2D + compute + D2H every step
+    for _ in range(2):
+        det.run({"x": x})
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        det.run({"x": x})
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    e2e_s = max_over_ranks(e2e_s, world)
+    e2e = {"value": round(world * B / e2e_s, 2), "unit": "img/s",
+           "h2d_bytes_per_step": int(x.nbytes), "d2h_bytes_per_step": int(B * DET_HW * DET_HW * 4),
+           "timing": "wall clock of K synchronous session.run calls, max over ranks"}
+
+    # ---------------------------------------------------------------- rec
+    rec = None
+    if not args.no_rec:
+        gr, wr = nets.build_rec()
+        gr = q.optimize(gr, wr)
+        xr = nets.rec_input(args.rec_batch, seed=4 + rank)
+        rs = ctx.create_session(gr, wr, role="rec", math=args.math)
+        rs.run({"x": xr})
+        for _ in range(args.warmup):
+            rs.replay({"x": xr}, 1)
+        barrier(world)
+        rms = max_over_ranks(rs.replay({"x": xr}, args.steps), world)
+        rprof = rs.profile({"x": xr}, iters=2)
+        for _ in range(2):
+            rs.run({"x": xr})
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            rs.run({"x": xr})
+        re2e = max_over_ranks((time.perf_counter() - t0) / args.steps, world)
+        rec = {"metric": "rec_lines_per_s", "value": round(world * args.rec_batch / (rms / 1000.0), 1),
+               "unit": "lines/s", "ms_per_step": round(rms, 3), "batch": args.rec_batch,
+               "roofline": roofline(rprof, hbm, tf),
+               "e2e": {"value": round(world * args.rec_batch / re2e, 1), "unit": "lines/s",
+                       "h2d_bytes_per_step": int(xr.nbytes),
+                       "d2h_bytes_per_step": int(args.rec_batch * 40 * 2 * 4)},
+               "gpu_launches": len(rprof) * args.steps}
+        rs.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_det()
+        if rec is not None:
+            rec["cpu_baseline"] = cpu_baseline_rec()
+
+    if rank == 0:
+        line = {
+            "metric": "det_img_per_s (DB det 3x960x960) + rec_lines_per_s",
+            "value": round(value, 2), "unit": "img/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"config 3: DB det (PP-LCNet x1.0 13-block, DBFPN 96, DB head), "
+                                   f"batch {B} x 3x{DET_HW}x{DET_HW} per GPU",
+                       "math": args.math, "global_batch": world * B,
+                       "parallelism": f"dp{world} (replicas, image shards)",
+                       "l2": "inputs 708 MB/step > 126 MB L2, no flush"},
+            "roofline": rl, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "gpu_launches": launches * args.steps, "rec": rec,
+        }
+        print(json.dumps(line), flush=True)
+    det.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

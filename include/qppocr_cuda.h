@@ -1,0 +1,234 @@
+/*
+ * qppocr_cuda.h — C ABI of libqppocr_cuda.so, the B200 (sm_100a) device
+ * backend for qppocr.
+ *
+ * It fills the reference's CUDA stub (crates/qppocr-gpu/src/cuda.rs:112-230,
+ * whose create_session returns "kernels not implemented") behind the
+ * backend-agnostic device seam of qppocr-core:
+ *   trait DeviceContext  (crates/qppocr-core/src/device.rs:83-101)
+ *   trait DeviceSession  (crates/qppocr-core/src/device.rs:125-176)
+ *   trait DeferredRun    (crates/qppocr-core/src/device.rs:105-108)
+ * A thin Rust FFI crate (qppocr-cuda) binds these symbols and implements the
+ * traits; the bindings are listed in INTEGRATION.md.
+ *
+ * Conventions: every function returns int status (QPC_OK == 0).  On failure,
+ * qpc_last_error() returns a thread-local message naming the node, op or CUDA
+ * call — the same "no silent fallback" discipline as Error::Graph /
+ * Error::Device (crates/qppocr-core/src/error.rs:15-18).  Plain pointers and
+ * sizes only; tensors are fp32 row-major (logical NCHW) on the host side.
+ * Sessions are safe to use from many threads at once (device.rs:120-125).
+ */
+#ifndef QPPOCR_CUDA_H
+#define QPPOCR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+#define QPC_OK 0
+#define QPC_ERR_INVALID 1 /* bad argument (null pointer, wrong count, ...) */
+#define QPC_ERR_GRAPH 2   /* Error::Graph: unsupported op / shape, missing tensor */
+#define QPC_ERR_DEVICE 3  /* Error::Device: no device, CUDA failure, kernel fault */
+#define QPC_ERR_TIMEOUT 4 /* qpc_complete deadline passed (run still in flight) */
+#define QPC_ERR_OOM 5     /* device or pinned-host allocation failed */
+
+/* Message of the last failing call on this thread ("" if none).
+ * Replaces the Error::Device / Error::Graph strings (error.rs:15-18). */
+const char* qpc_last_error(void);
+
+/* ------------------------------------------------------ device discovery */
+/* Number of CUDA devices (0 when the driver is absent is not an error).
+ * Replaces enumerate() (crates/qppocr-gpu/src/cuda.rs:63-110). */
+int qpc_device_count(int* count);
+
+/* Name, driver version (e.g. 12090) and compute capability of one device.
+ * Replaces CudaContext::open + DeviceContext::info (cuda.rs:121-212).
+ * Fails with QPC_ERR_DEVICE for an out-of-range index or a device that is
+ * not sm_100 (this library carries sm_100a code only). */
+int qpc_device_info(int device, char* name, int name_len, int* driver_version, int* cc_major,
+                    int* cc_minor);
+
+/* -------------------------------------------------- graph description
+ * Mirrors the reference's in-memory ONNX model (crates/qppocr-core/src/
+ * onnx/model.rs:13-127) as handed to DeviceContext::create_session: the graph
+ * has already been through the load-time passes (BN folded into Conv, Conv
+ * carries `act` (0/1 gelu/2 relu) + act_c1..3, bias in inputs[2], residual in
+ * inputs[3]; Add(Mul(f, g), r) collapsed to MulAddScale), see
+ * crates/qppocr-core/src/onnx/parse.rs:731-747. */
+enum qpc_attr_kind {
+  QPC_ATTR_FLOAT = 1,  /* Attribute.f      (field 2) */
+  QPC_ATTR_INT = 2,    /* Attribute.i      (field 3) */
+  QPC_ATTR_STRING = 3, /* Attribute.s      (field 4) */
+  QPC_ATTR_FLOATS = 4, /* Attribute.floats (field 7) */
+  QPC_ATTR_INTS = 5    /* Attribute.ints   (field 8) */
+};
+
+typedef struct {
+  const char* name;
+  int kind; /* qpc_attr_kind */
+  float f;
+  int64_t i;
+  const char* s;
+  const float* floats;
+  const int64_t* ints;
+  int n; /* length of floats / ints */
+} qpc_attr;
+
+typedef struct {
+  const char* op_type; /* "Conv", "MatMul", ... (Node.op_type) */
+  const char* name;
+  const char* const* inputs; /* "" = absent optional input */
+  int n_inputs;
+  const char* const* outputs;
+  int n_outputs;
+  const qpc_attr* attrs;
+  int n_attrs;
+} qpc_node;
+
+typedef struct {
+  const qpc_node* nodes; /* topological order (Graph.nodes) */
+  int n_nodes;
+  const char* const* inputs; /* Graph.inputs */
+  int n_inputs;
+  const char* const* outputs; /* Graph.outputs */
+  int n_outputs;
+} qpc_graph;
+
+enum qpc_dtype { QPC_F32 = 0, QPC_I64 = 1 }; /* tensor.rs:10-18 DType */
+
+/* A host tensor (tensor.rs:28-40): initializers and run inputs. */
+typedef struct {
+  const char* name;
+  const int64_t* shape;
+  int rank;
+  int dtype; /* qpc_dtype */
+  const void* data;
+} qpc_tensor;
+
+/* ---------------------------------------------------------------- session */
+/* ModelRole (device.rs:53-66). */
+enum qpc_role { QPC_ROLE_OTHER = 0, QPC_ROLE_DET = 1, QPC_ROLE_REC = 2, QPC_ROLE_CLS = 3 };
+
+/* Math of the tensor-core contractions (QPPOCR_CUDA_MATH). */
+enum qpc_math { QPC_MATH_TF32 = 0, QPC_MATH_3XTF32 = 1 };
+
+typedef struct {
+  int math;                  /* qpc_math; default TF32 */
+  int argmax_exit;           /* rec: emit [B,T,2] (val, idx bits) instead of [B,T,C]
+                                (DeviceSession::rec_argmax_pairs, device.rs:159-163);
+                                -1 = role default (on for REC) */
+  int64_t plan_budget_bytes; /* per-shape plan cache byte budget; 0 = default (8 GiB) */
+  int use_cuda_graph;        /* 1 = one captured CUDA graph per shape (default), 0 = stream launches */
+} qpc_session_options;
+
+typedef struct qpc_session qpc_session;
+
+/* DeviceContext::create_session (device.rs:88-101): weights are copied to the
+ * device once and owned by the session.  Unsupported ops fail here, naming the
+ * node (QPC_ERR_GRAPH).  opts may be NULL (defaults). */
+int qpc_session_create(int device, const qpc_graph* graph, const qpc_tensor* weights,
+                       int n_weights, int role, const qpc_session_options* opts,
+                       qpc_session** out);
+
+/* Capability queries of DeviceSession (device.rs:134-163). */
+typedef struct {
+  int prefers_host_parallelism; /* prefers_host_parallelism()  :134 (GPU: 0) */
+  int bucket_grain;             /* bucket_grain()              :139 (GPU: 64) */
+  int batch_grain;              /* batch_grain()               :148 */
+  int rec_chunk;                /* rec_chunk()                 :157 */
+  int argmax_pairs;             /* rec_argmax_pairs()          :163 */
+} qpc_caps;
+int qpc_session_caps(const qpc_session* s, qpc_caps* caps);
+
+/* A run in flight or completed (DeferredRun, device.rs:105-108). */
+typedef struct qpc_ticket qpc_ticket;
+
+/* DeviceSession::run_deferred (device.rs:164-176): stage the inputs, launch
+ * the shape's captured graph and return at once.  Two runs of the same shape
+ * may be in flight: the session keeps a separate plan instance per run
+ * (inputs/outputs never share buffers). */
+int qpc_run_async(qpc_session* s, const qpc_tensor* inputs, int n_inputs, qpc_ticket** ticket);
+
+/* DeferredRun::complete: wait (bounded by timeout_ms; <0 = no bound) for the
+ * run, check for device faults.  On QPC_ERR_TIMEOUT the ticket stays valid. */
+int qpc_complete(qpc_ticket* ticket, int timeout_ms);
+
+/* Outputs of a completed ticket in graph-output order (DeviceSession::run
+ * return value, device.rs:130).  *data stays valid until qpc_ticket_release. */
+int qpc_ticket_output_count(const qpc_ticket* ticket, int* count);
+int qpc_ticket_output(const qpc_ticket* ticket, int index, const float** data,
+                      const int64_t** shape, int* rank);
+int qpc_ticket_release(qpc_ticket* ticket);
+
+/* DeviceSession::run (device.rs:130): run_async + complete(no bound). */
+int qpc_run(qpc_session* s, const qpc_tensor* inputs, int n_inputs, qpc_ticket** ticket);
+
+/* Device time (ms, CUDA events on the run's stream) of a completed ticket. */
+int qpc_ticket_device_ms(const qpc_ticket* ticket, float* ms);
+
+int qpc_session_destroy(qpc_session* s);
+
+/* ------------------------------------------------------- diagnostics
+ * Per-step device timing and kernel-only replay, the counterpart of the
+ * reference's QPPOCR_GPU_PROF per-dispatch timestamps
+ * (crates/qppocr-gpu/src/vulkan/session.rs:828-835, 2073-2139). */
+
+/* Run the plan for these input shapes `iters` times with CUDA events between
+ * steps; *n_steps = number of steps (kernel launches). */
+int qpc_session_profile(qpc_session* s, const qpc_tensor* inputs, int n_inputs, int iters,
+                        int* n_steps);
+/* Step `idx` of the last profile: kernel family, graph node, algorithmic DRAM
+ * bytes and flops of one launch, mean device ms. */
+int qpc_session_profile_step(const qpc_session* s, int idx, const char** kernel,
+                             const char** node, double* bytes, double* flops, float* ms);
+/* Stage inputs once, then replay the shape's compute graph `iters` times back
+ * to back; *ms_per_replay = device ms per replay (no host copies inside). */
+int qpc_session_replay(qpc_session* s, const qpc_tensor* inputs, int n_inputs, int iters,
+                       float* ms_per_replay);
+
+/* ------------------------------------------------ operator entry points
+ * Device-pointer entry points for single operators (the qppocr-kernels
+ * functions the session composes), for callers that manage device memory
+ * themselves and for operator-level parity tests.  All pointers are device
+ * pointers, 16-byte aligned; `stream` is a cudaStream_t (NULL = legacy).
+ * Activations are NHWC fp32.  act: 0 none, 1 relu, 2 hardswish
+ * (x * HardSigmoid(x; alpha, beta)), 3 sigmoid, 4 gelu, 5 hardsigmoid,
+ * 6 swish; act_p = {alpha, beta, c1, c2, c3} (NULL = PP-OCR defaults
+ * 1/6, 1/2, sqrt2, 1, 0.5). */
+
+/* Depthwise conv, group == C.  Replaces conv2d_res_into's depthwise branch
+ * (crates/qppocr-kernels/src/conv.rs:461-505, plane kernel :45-71) and
+ * depthwise_nhwc_packed (conv.rs:912-1051).  w_tap_major: [kh*kw][c].
+ * pads: {ph, pw, peh, pew}; strides {sh, sw}; residual may be NULL. */
+int qpc_op_dwconv_nhwc(const float* x, int n, int h, int w, int c, const float* w_tap_major,
+                       int kh, int kw, const int* strides, const int* pads, const float* bias,
+                       int act, const float* act_p, const float* residual, float* y,
+                       void* stream);
+
+/* Pointwise conv / linear layer on tcgen05 tensor cores:
+ * y[M,N] = act(x[M,K] * w[N,K]^T + bias) + residual.  Replaces the 1x1 path
+ * of conv2d_res_into (conv.rs:264-460 -> sgemm_res, gemm.rs:53-66, 223-466),
+ * conv1x1_nhwc (conv.rs:856-901) and constant-B matmul (shape.rs:568-653).
+ * math: qpc_math.  w_lo: for QPC_MATH_3XTF32, w minus its tf32 truncation
+ * (see qpc_op_split_tf32); ignored for TF32. */
+int qpc_op_gemm(const float* x, int64_t m, int k, const float* w, const float* w_lo, int n,
+                const float* bias, int act, const float* act_p, const float* residual, float* y,
+                int math, void* stream);
+
+/* Split fp32 device values into tf32 hi (truncation) and lo = v - hi parts,
+ * the load-time weight preparation of the 3xTF32 mode. */
+int qpc_op_split_tf32(const float* v, int64_t count, float* hi, float* lo, void* stream);
+
+/* Device fault / timeout flag raised by kernels with bounded waits on the
+ * current device since the last call (0 = none); clears it. */
+int qpc_kernel_error(int device, unsigned int* flags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QPPOCR_CUDA_H */

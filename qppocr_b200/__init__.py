@@ -1,0 +1,466 @@
+"""qppocr_b200 — B200-native (sm_100a) device backend for qppocr.
+
+Python mirror of the reference's device seam over the C ABI of
+libqppocr_cuda.so (include/qppocr_cuda.h):
+
+  CudaContext.open(index)        crates/qppocr-gpu/src/cuda.rs:121-200 (CudaContext::open)
+  CudaContext.create_session()   crates/qppocr-core/src/device.rs:88-101 (DeviceContext::create_session)
+  CudaSession.run(inputs)        device.rs:130 (DeviceSession::run)
+  CudaSession.run_deferred()     device.rs:164-176 (-> DeferredRun)
+  DeferredRun.complete()         device.rs:105-108
+  caps: prefers_host_parallelism / bucket_grain / batch_grain / rec_chunk /
+        rec_argmax_pairs         device.rs:134-163
+
+Errors mirror Error::Graph / Error::Device (crates/qppocr-core/src/error.rs):
+GraphError for unsupported ops or shapes, DeviceError for CUDA failures.  There
+is no CPU fallback: if the CUDA library cannot be loaded, every entry point
+raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from .graph import Graph, Node, optimize  # noqa: F401
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libqppocr_cuda.so")
+
+QPC_OK, QPC_ERR_INVALID, QPC_ERR_GRAPH, QPC_ERR_DEVICE, QPC_ERR_TIMEOUT, QPC_ERR_OOM = range(6)
+ROLE = {"other": 0, "det": 1, "rec": 2, "cls": 3}
+MATH = {"tf32": 0, "3xtf32": 1}
+ACT = {None: 0, "none": 0, "relu": 1, "hswish": 2, "sigmoid": 3, "gelu": 4, "hsigmoid": 5, "swish": 6}
+
+
+class QppocrError(RuntimeError):
+    pass
+
+
+class GraphError(QppocrError):
+    """Error::Graph — unsupported op / shape, missing tensor."""
+
+
+class DeviceError(QppocrError):
+    """Error::Device — no device, CUDA failure, kernel fault or timeout."""
+
+
+class TimeoutError_(DeviceError):
+    pass
+
+
+# ------------------------------------------------------------------ C structs
+class QpcAttr(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("kind", ctypes.c_int), ("f", ctypes.c_float),
+                ("i", ctypes.c_int64), ("s", ctypes.c_char_p),
+                ("floats", ctypes.POINTER(ctypes.c_float)), ("ints", ctypes.POINTER(ctypes.c_int64)),
+                ("n", ctypes.c_int)]
+
+
+class QpcNode(ctypes.Structure):
+    _fields_ = [("op_type", ctypes.c_char_p), ("name", ctypes.c_char_p),
+                ("inputs", ctypes.POINTER(ctypes.c_char_p)), ("n_inputs", ctypes.c_int),
+                ("outputs", ctypes.POINTER(ctypes.c_char_p)), ("n_outputs", ctypes.c_int),
+                ("attrs", ctypes.POINTER(QpcAttr)), ("n_attrs", ctypes.c_int)]
+
+
+class QpcGraph(ctypes.Structure):
+    _fields_ = [("nodes", ctypes.POINTER(QpcNode)), ("n_nodes", ctypes.c_int),
+                ("inputs", ctypes.POINTER(ctypes.c_char_p)), ("n_inputs", ctypes.c_int),
+                ("outputs", ctypes.POINTER(ctypes.c_char_p)), ("n_outputs", ctypes.c_int)]
+
+
+class QpcTensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("shape", ctypes.POINTER(ctypes.c_int64)),
+                ("rank", ctypes.c_int), ("dtype", ctypes.c_int), ("data", ctypes.c_void_p)]
+
+
+class QpcOptions(ctypes.Structure):
+    _fields_ = [("math", ctypes.c_int), ("argmax_exit", ctypes.c_int),
+                ("plan_budget_bytes", ctypes.c_int64), ("use_cuda_graph", ctypes.c_int)]
+
+
+class QpcCaps(ctypes.Structure):
+    _fields_ = [("prefers_host_parallelism", ctypes.c_int), ("bucket_grain", ctypes.c_int),
+                ("batch_grain", ctypes.c_int), ("rec_chunk", ctypes.c_int),
+                ("argmax_pairs", ctypes.c_int)]
+
+
+# Every symbol include/qppocr_cuda.h declares (checked by the CPU test suite).
+EXPORTED = (
+    "qpc_last_error", "qpc_device_count", "qpc_device_info", "qpc_session_create",
+    "qpc_session_caps", "qpc_run_async", "qpc_complete", "qpc_ticket_output_count",
+    "qpc_ticket_output", "qpc_ticket_release", "qpc_run", "qpc_ticket_device_ms",
+    "qpc_session_destroy", "qpc_session_profile", "qpc_session_profile_step",
+    "qpc_session_replay", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_split_tf32",
+    "qpc_kernel_error",
+)
+
+_lib = None
+
+
+def lib():
+    """Load libqppocr_cuda.so (raises DeviceError if it is missing)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise DeviceError(f"{LIB_PATH} not built (run __graft_entry__.build())")
+    L = ctypes.CDLL(LIB_PATH)
+    L.qpc_last_error.restype = ctypes.c_char_p
+    P = ctypes.c_void_p
+    L.qpc_session_create.argtypes = [ctypes.c_int, ctypes.POINTER(QpcGraph), ctypes.POINTER(QpcTensor),
+                                     ctypes.c_int, ctypes.c_int, ctypes.POINTER(QpcOptions),
+                                     ctypes.POINTER(P)]
+    L.qpc_session_caps.argtypes = [P, ctypes.POINTER(QpcCaps)]
+    L.qpc_run_async.argtypes = [P, ctypes.POINTER(QpcTensor), ctypes.c_int, ctypes.POINTER(P)]
+    L.qpc_run.argtypes = [P, ctypes.POINTER(QpcTensor), ctypes.c_int, ctypes.POINTER(P)]
+    L.qpc_complete.argtypes = [P, ctypes.c_int]
+    L.qpc_ticket_output_count.argtypes = [P, ctypes.POINTER(ctypes.c_int)]
+    L.qpc_ticket_output.argtypes = [P, ctypes.c_int, ctypes.POINTER(ctypes.POINTER(ctypes.c_float)),
+                                    ctypes.POINTER(ctypes.POINTER(ctypes.c_int64)),
+                                    ctypes.POINTER(ctypes.c_int)]
+    L.qpc_ticket_release.argtypes = [P]
+    L.qpc_ticket_device_ms.argtypes = [P, ctypes.POINTER(ctypes.c_float)]
+    L.qpc_session_destroy.argtypes = [P]
+    L.qpc_session_profile.argtypes = [P, ctypes.POINTER(QpcTensor), ctypes.c_int, ctypes.c_int,
+                                      ctypes.POINTER(ctypes.c_int)]
+    L.qpc_session_profile_step.argtypes = [P, ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
+                                           ctypes.POINTER(ctypes.c_char_p),
+                                           ctypes.POINTER(ctypes.c_double),
+                                           ctypes.POINTER(ctypes.c_double),
+                                           ctypes.POINTER(ctypes.c_float)]
+    L.qpc_session_replay.argtypes = [P, ctypes.POINTER(QpcTensor), ctypes.c_int, ctypes.c_int,
+                                     ctypes.POINTER(ctypes.c_float)]
+    L.qpc_op_dwconv_nhwc.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P,
+                                     ctypes.c_int, ctypes.c_int, P, P, P, ctypes.c_int, P, P, P, P]
+    L.qpc_op_gemm.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P, ctypes.c_int, P,
+                              P, P, ctypes.c_int, P]
+    L.qpc_op_split_tf32.argtypes = [P, ctypes.c_int64, P, P, P]
+    L.qpc_kernel_error.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]
+    _lib = L
+    return L
+
+
+def _check(rc: int):
+    if rc == QPC_OK:
+        return
+    msg = lib().qpc_last_error().decode(errors="replace")
+    if rc == QPC_ERR_GRAPH:
+        raise GraphError(msg)
+    if rc == QPC_ERR_TIMEOUT:
+        raise TimeoutError_(msg)
+    if rc in (QPC_ERR_DEVICE, QPC_ERR_OOM):
+        raise DeviceError(msg)
+    raise QppocrError(f"status {rc}: {msg}")
+
+
+def device_count() -> int:
+    n = ctypes.c_int(0)
+    _check(lib().qpc_device_count(ctypes.byref(n)))
+    return n.value
+
+
+# ------------------------------------------------------------------ marshalling
+class _Keep:
+    """Holds ctypes buffers alive for the duration of a call."""
+
+    def __init__(self):
+        self.objs = []
+
+    def add(self, o):
+        self.objs.append(o)
+        return o
+
+
+def _cstrs(keep: _Keep, names: Sequence[str]):
+    arr = (ctypes.c_char_p * max(len(names), 1))(*[n.encode() for n in names])
+    return keep.add(arr)
+
+
+def _attr(keep: _Keep, name: str, v) -> QpcAttr:
+    a = QpcAttr()
+    a.name = keep.add(name.encode())
+    if isinstance(v, bool) or isinstance(v, (int, np.integer)):
+        a.kind, a.i = 2, int(v)
+    elif isinstance(v, (float, np.floating)):
+        a.kind, a.f = 1, float(v)
+    elif isinstance(v, str):
+        a.kind, a.s = 3, keep.add(v.encode())
+    elif isinstance(v, (list, tuple, np.ndarray)):
+        vals = list(v)
+        if all(isinstance(x, (int, np.integer)) for x in vals):
+            arr = keep.add((ctypes.c_int64 * max(len(vals), 1))(*[int(x) for x in vals]))
+            a.kind, a.ints, a.n = 5, arr, len(vals)
+        else:
+            arr = keep.add((ctypes.c_float * max(len(vals), 1))(*[float(x) for x in vals]))
+            a.kind, a.floats, a.n = 4, arr, len(vals)
+    else:
+        raise TypeError(f"attribute {name}: {type(v)}")
+    return a
+
+
+def _tensor(keep: _Keep, name: str, arr: np.ndarray) -> QpcTensor:
+    if arr.dtype == np.int64 or arr.dtype == np.int32:
+        arr = keep.add(np.ascontiguousarray(arr, np.int64))
+        dt = 1
+    else:
+        arr = keep.add(np.ascontiguousarray(arr, np.float32))
+        dt = 0
+    shp = keep.add((ctypes.c_int64 * max(arr.ndim, 1))(*arr.shape))
+    t = QpcTensor()
+    t.name = keep.add(name.encode())
+    t.shape = shp
+    t.rank = arr.ndim
+    t.dtype = dt
+    t.data = arr.ctypes.data
+    return t
+
+
+def _tensors(keep: _Keep, items: Dict[str, np.ndarray]):
+    arr = (QpcTensor * max(len(items), 1))()
+    for k, (n, a) in enumerate(items.items()):
+        arr[k] = _tensor(keep, n, a)
+    return keep.add(arr), len(items)
+
+
+def _graph(keep: _Keep, g: Graph) -> QpcGraph:
+    nodes = (QpcNode * max(len(g.nodes), 1))()
+    for k, n in enumerate(g.nodes):
+        qn = QpcNode()
+        qn.op_type = keep.add(n.op_type.encode())
+        qn.name = keep.add(n.name.encode())
+        qn.inputs = _cstrs(keep, n.inputs)
+        qn.n_inputs = len(n.inputs)
+        qn.outputs = _cstrs(keep, n.outputs)
+        qn.n_outputs = len(n.outputs)
+        attrs = (QpcAttr * max(len(n.attrs), 1))()
+        for j, (an, av) in enumerate(n.attrs.items()):
+            attrs[j] = _attr(keep, an, av)
+        qn.attrs = keep.add(attrs)
+        qn.n_attrs = len(n.attrs)
+        nodes[k] = qn
+    qg = QpcGraph()
+    qg.nodes = keep.add(nodes)
+    qg.n_nodes = len(g.nodes)
+    qg.inputs = _cstrs(keep, g.inputs)
+    qg.n_inputs = len(g.inputs)
+    qg.outputs = _cstrs(keep, g.outputs)
+    qg.n_outputs = len(g.outputs)
+    return qg
+
+
+# ------------------------------------------------------------------ device seam
+class DeferredRun:
+    """A submitted run (DeferredRun, device.rs:105-108)."""
+
+    def __init__(self, session: "CudaSession", ticket: ctypes.c_void_p):
+        self._s = session
+        self._t = ticket
+
+    def complete(self, timeout_ms: int = -1) -> List[np.ndarray]:
+        L = lib()
+        _check(L.qpc_complete(self._t, timeout_ms))
+        n = ctypes.c_int(0)
+        _check(L.qpc_ticket_output_count(self._t, ctypes.byref(n)))
+        outs = []
+        for k in range(n.value):
+            data = ctypes.POINTER(ctypes.c_float)()
+            shp = ctypes.POINTER(ctypes.c_int64)()
+            rank = ctypes.c_int(0)
+            _check(L.qpc_ticket_output(self._t, k, ctypes.byref(data), ctypes.byref(shp), ctypes.byref(rank)))
+            shape = tuple(shp[i] for i in range(rank.value))
+            cnt = int(np.prod(shape)) if shape else 1
+            outs.append(np.ctypeslib.as_array(data, shape=(cnt,)).reshape(shape).copy())
+        ms = ctypes.c_float(0)
+        _check(L.qpc_ticket_device_ms(self._t, ctypes.byref(ms)))
+        self.device_ms = ms.value
+        self.release()
+        return outs
+
+    def release(self):
+        if self._t:
+            lib().qpc_ticket_release(self._t)
+            self._t = None
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+class CudaSession:
+    """One model on one device (DeviceSession, device.rs:125-176)."""
+
+    def __init__(self, handle: ctypes.c_void_p, input_names: List[str]):
+        self._h = handle
+        self.input_names = input_names
+
+    def _inputs(self, keep, inputs):
+        if isinstance(inputs, dict):
+            items = inputs
+        else:
+            items = {n: a for n, a in inputs}
+        return _tensors(keep, items)
+
+    def run(self, inputs) -> List[np.ndarray]:
+        return self.run_deferred(inputs).complete()
+
+    def run_deferred(self, inputs) -> DeferredRun:
+        keep = _Keep()
+        arr, n = self._inputs(keep, inputs)
+        t = ctypes.c_void_p()
+        _check(lib().qpc_run_async(self._h, arr, n, ctypes.byref(t)))
+        return DeferredRun(self, t)
+
+    def caps(self) -> Dict[str, int]:
+        c = QpcCaps()
+        _check(lib().qpc_session_caps(self._h, ctypes.byref(c)))
+        return {k: getattr(c, k) for k, _ in QpcCaps._fields_}
+
+    def prefers_host_parallelism(self) -> bool:
+        return bool(self.caps()["prefers_host_parallelism"])
+
+    def bucket_grain(self) -> int:
+        return self.caps()["bucket_grain"]
+
+    def batch_grain(self) -> int:
+        return self.caps()["batch_grain"]
+
+    def rec_chunk(self) -> int:
+        return self.caps()["rec_chunk"]
+
+    def rec_argmax_pairs(self) -> bool:
+        return bool(self.caps()["argmax_pairs"])
+
+    def profile(self, inputs, iters: int = 3):
+        """Per-step device times: list of (kernel, node, bytes, flops, ms)."""
+        keep = _Keep()
+        arr, n = self._inputs(keep, inputs)
+        ns = ctypes.c_int(0)
+        _check(lib().qpc_session_profile(self._h, arr, n, iters, ctypes.byref(ns)))
+        out = []
+        for k in range(ns.value):
+            kern, node = ctypes.c_char_p(), ctypes.c_char_p()
+            by, fl = ctypes.c_double(), ctypes.c_double()
+            ms = ctypes.c_float()
+            _check(lib().qpc_session_profile_step(self._h, k, ctypes.byref(kern), ctypes.byref(node),
+                                                  ctypes.byref(by), ctypes.byref(fl), ctypes.byref(ms)))
+            out.append((kern.value.decode(), node.value.decode(), by.value, fl.value, ms.value))
+        return out
+
+    def replay(self, inputs, iters: int) -> float:
+        """Device ms per replay of the captured graph, inputs staged once."""
+        keep = _Keep()
+        arr, n = self._inputs(keep, inputs)
+        ms = ctypes.c_float(0)
+        _check(lib().qpc_session_replay(self._h, arr, n, iters, ctypes.byref(ms)))
+        return ms.value
+
+    def close(self):
+        if self._h:
+            lib().qpc_session_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class CudaContext:
+    """One CUDA device (CudaContext, crates/qppocr-gpu/src/cuda.rs:112-230)."""
+
+    def __init__(self, index: int, name: str, driver: int, cc: Tuple[int, int]):
+        self.index = index
+        self.name = name
+        self.driver = driver
+        self.cc = cc
+
+    @classmethod
+    def open(cls, index: Optional[int] = None) -> "CudaContext":
+        idx = 0 if index is None else int(index)
+        name = ctypes.create_string_buffer(256)
+        drv, ma, mi = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        _check(lib().qpc_device_info(idx, name, 256, ctypes.byref(drv), ctypes.byref(ma), ctypes.byref(mi)))
+        return cls(idx, name.value.decode(), drv.value, (ma.value, mi.value))
+
+    def info(self) -> Dict[str, str]:
+        v = self.driver
+        return {"kind": "cuda", "name": self.name, "api": f"cuda {v // 1000}.{v % 1000 // 10}"}
+
+    def create_session(self, graph: Graph, initializers: Dict[str, np.ndarray], role: str = "other",
+                       math: str = "tf32", argmax_exit: Optional[bool] = None,
+                       use_cuda_graph: bool = True, plan_budget_bytes: int = 0) -> CudaSession:
+        keep = _Keep()
+        qg = _graph(keep, graph)
+        wt, nw = _tensors(keep, initializers)
+        opts = QpcOptions()
+        opts.math = MATH[math]
+        opts.argmax_exit = -1 if argmax_exit is None else int(bool(argmax_exit))
+        opts.plan_budget_bytes = plan_budget_bytes
+        opts.use_cuda_graph = 1 if use_cuda_graph else 0
+        h = ctypes.c_void_p()
+        _check(lib().qpc_session_create(self.index, ctypes.byref(qg), wt, nw, ROLE[role], ctypes.byref(opts),
+                                        ctypes.byref(h)))
+        return CudaSession(h, list(graph.inputs))
+
+
+# ------------------------------------------------------------------ operator entry points
+def _dptr(t) -> int:
+    """Device pointer of a torch CUDA tensor (None -> 0)."""
+    if t is None:
+        return None
+    assert t.is_cuda and t.is_contiguous(), "device tensor expected"
+    return t.data_ptr()
+
+
+def op_dwconv_nhwc(x, w_tap_major, kh, kw, strides, pads, bias=None, act=None, act_p=None,
+                   residual=None, out=None, stream=None):
+    """Depthwise conv on torch CUDA tensors (NHWC)."""
+    import torch
+    n, h, w, c = x.shape
+    oh = (h + pads[0] + pads[2] - kh) // strides[0] + 1
+    ow = (w + pads[1] + pads[3] - kw) // strides[1] + 1
+    y = out if out is not None else torch.empty((n, oh, ow, c), dtype=torch.float32, device=x.device)
+    st = (ctypes.c_int * 2)(*strides)
+    pd = (ctypes.c_int * 4)(*pads)
+    ap = (ctypes.c_float * 5)(*act_p) if act_p is not None else None
+    _check(lib().qpc_op_dwconv_nhwc(_dptr(x), n, h, w, c, _dptr(w_tap_major), kh, kw,
+                                    ctypes.cast(st, ctypes.c_void_p), ctypes.cast(pd, ctypes.c_void_p),
+                                    _dptr(bias), ACT[act],
+                                    ctypes.cast(ap, ctypes.c_void_p) if ap is not None else None,
+                                    _dptr(residual), _dptr(y), stream))
+    return y
+
+
+def op_gemm(x, w, n=None, bias=None, act=None, act_p=None, residual=None, math="tf32", w_lo=None,
+            out=None, stream=None):
+    """y[M,N] = act(x[M,K] w[N,K]^T + bias) + residual on torch CUDA tensors."""
+    import torch
+    m, k = x.shape
+    nn = w.shape[0]
+    y = out if out is not None else torch.empty((m, nn), dtype=torch.float32, device=x.device)
+    ap = (ctypes.c_float * 5)(*act_p) if act_p is not None else None
+    _check(lib().qpc_op_gemm(_dptr(x), m, k, _dptr(w), _dptr(w_lo), nn, _dptr(bias), ACT[act],
+                             ctypes.cast(ap, ctypes.c_void_p) if ap is not None else None,
+                             _dptr(residual), _dptr(y), MATH[math], stream))
+    return y
+
+
+def op_split_tf32(v, stream=None):
+    import torch
+    hi = torch.empty_like(v)
+    lo = torch.empty_like(v)
+    _check(lib().qpc_op_split_tf32(_dptr(v), v.numel(), _dptr(hi), _dptr(lo), stream))
+    return hi, lo
+
+
+def kernel_error(device: int = 0) -> int:
+    f = ctypes.c_uint(0)
+    _check(lib().qpc_kernel_error(device, ctypes.byref(f)))
+    return f.value

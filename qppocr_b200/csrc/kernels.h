@@ -1,0 +1,76 @@
+// Launchers for the sm_100a kernels of the qppocr B200 backend.  All tensors
+// are fp32 device pointers; 4-D activations are NHWC.  Every launcher returns
+// a cudaError_t from the launch itself (asynchronous faults surface at the
+// next synchronisation).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace qpc {
+
+// Convolution geometry (ONNX Conv attributes after pad resolution;
+// qppocr-kernels conv.rs:124-143 ConvParams).
+struct ConvGeom {
+  int n, h, w, c;        // input NHWC
+  int oh, ow, m;         // output spatial and channels
+  int kh, kw, sh, sw;
+  int ph, pw;            // begin pads (end pads are implied by oh/ow)
+};
+
+// Depthwise conv (group == C, one filter per channel), NHWC in/out.
+// wt is tap-major [kh*kw][C].  out = act(sum_taps + bias) (+ residual).
+// Restates conv.rs:45-71 (fma from 0, ky outer / kx inner, bias after) with
+// the fused activation and residual of conv.rs:673-713.
+cudaError_t launch_dwconv_nhwc(const float* x, const float* wt, const float* bias,
+                               const float* residual, float* y, const ConvGeom& g,
+                               const ActParams& act, cudaStream_t st);
+
+// GEMM epilogue: out[r, col] = act(acc + bias[col]) + residual[r', col]
+// where r' = r, or, for a nearest-upsample residual (FPN top-down add fused
+// into the lateral 1x1 conv), the row of the coarser map that the nearest
+// resize of resize.rs:8-57 reads.
+struct GemmEpilogue {
+  const float* bias = nullptr;      // [N]
+  const float* residual = nullptr;  // [Mres, ldr]
+  float* out = nullptr;             // [M, ldo]
+  int ldo = 0, ldr = 0;
+  int col_off = 0;                  // column offset of this GEMM inside `out`
+  ActParams act{};
+  // nearest-upsample residual: output rows are pixels of an (n, oh, ow) map;
+  // the residual is an (n, rh, rw) map. rh == 0 disables the remap.
+  int oh = 0, ow = 0, rh = 0, rw = 0;
+};
+
+enum MathMode : int { MATH_TF32 = 0, MATH_3XTF32 = 1 };
+
+// Row-major GEMM on tcgen05 tensor cores: D[M,N] = A[M,K] * B[N,K]^T with the
+// fused epilogue.  A rows are NHWC pixels (or tokens); B is the weight matrix
+// in the ONNX Conv layout [Cout, Cin] (K-major).  For MATH_3XTF32, b_lo holds
+// B - tf32(B) (prepared at load time) and A is split on chip.
+// K % 4 == 0 (16-byte TMA row pitch); pointers 16-byte aligned.  `err` is the
+// device error word that a timed-out pipeline wait sets.
+cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const float* b,
+                           const float* b_lo, int N, const GemmEpilogue& epi, int math,
+                           unsigned int* err, cudaStream_t st);
+
+// kxk stride-1 dense conv as implicit GEMM on tcgen05: A tiles are 4-D TMA
+// boxes of the NHWC input shifted per tap (out-of-bounds rows/cols read as
+// the zero padding).  wk is tap-major [kh*kw][M][C] (and wk_lo its 3xTF32
+// residue).  Epilogue as launch_gemm_tc with out rows = output pixels.
+cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, const float* wk_lo,
+                           const GemmEpilogue& epi, int math, unsigned int* err,
+                           cudaStream_t st);
+
+// Direct (SIMT) dense conv for shapes the tensor-core path does not take
+// (C % 4 != 0 stems, strided kxk).  Input is NCHW when x_nchw != 0 (graph
+// input), NHWC otherwise.  w is the ONNX layout [M][C/group][kh][kw].
+// Accumulation order: ch -> ky -> kx ascending, fma from 0, bias after
+// (gemm.rs:75-128 implicit-GEMM k order).
+cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const float* bias,
+                               const float* residual, float* y, const ConvGeom& g, int group,
+                               const ActParams& act, cudaStream_t st);
+
+}  // namespace qpc

@@ -1,0 +1,594 @@
+// SIMT kernels for the operators around the tensor-core path.  Each restates
+// one qppocr-kernels CPU routine element by element (cited per kernel), so
+// that, given identical inputs, their outputs match the reference bit for bit
+// (reductions in f64 match to the final f32 rounding).
+#include "misc.h"
+
+namespace qpc {
+
+static int grid_for(int64_t threads, int block = 256) {
+  int64_t blocks = (threads + block - 1) / block;
+  const int64_t cap = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  return (int)(blocks < cap ? blocks : cap);
+}
+#define GRID_LOOP(i, total) \
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (total); i += (int64_t)gridDim.x * blockDim.x)
+
+// ------------------------------------------------------------ direct conv
+// Implicit-GEMM per-element semantics of conv.rs:553-637 / gemm.rs:75-128 and
+// 523-589: k order ch -> ky -> kx; acc from 0 then + bias, except M%4 tail rows
+// of a partial 32-wide output-column panel, which seed the chain with bias.
+// Each thread computes MB output channels of one output pixel.
+template <int MB>
+__global__ void __launch_bounds__(256) conv_direct_kernel(
+    const float* __restrict__ x, int x_nchw, const float* __restrict__ w,
+    const float* __restrict__ bias, const float* __restrict__ residual, float* __restrict__ y,
+    int N, int C, int H, int W, int M, int OH, int OW, int KH, int KW, int SH, int SW, int PH,
+    int PW, int group, ActParams act) {
+  const int cg = C / group, mg = M / group;
+  const int mblocks = (M + MB - 1) / MB;
+  const int64_t total = (int64_t)N * OH * OW * mblocks;
+  const int m4 = mg - (mg % 4);
+  const int full_cols = (OW / 32) * 32;
+  GRID_LOOP(t, total) {
+    const int mb = (int)(t % mblocks);
+    int64_t r = t / mblocks;
+    const int ox = (int)(r % OW);
+    r /= OW;
+    const int oy = (int)(r % OH);
+    const int n = (int)(r / OH);
+    const int m0 = mb * MB;
+    float acc[MB];
+#pragma unroll
+    for (int i = 0; i < MB; ++i) {
+      const int m = m0 + i;
+      float seed = 0.f;
+      if (m < M && bias) {
+        const int mo = m % mg;
+        if (mo >= m4 && ox >= full_cols) seed = __ldg(bias + m);
+      }
+      acc[i] = seed;
+    }
+    const int g = (m0 / mg);  // MB never straddles a group (MB divides mg or group == 1)
+    for (int ch = 0; ch < cg; ++ch) {
+      const int ci = g * cg + ch;
+      for (int ky = 0; ky < KH; ++ky) {
+        const int iy = oy * SH - PH + ky;
+        for (int kx = 0; kx < KW; ++kx) {
+          const int ix = ox * SW - PW + kx;
+          float v = 0.f;
+          if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+            v = x_nchw ? __ldg(x + (((int64_t)n * C + ci) * H + iy) * W + ix)
+                       : __ldg(x + (((int64_t)n * H + iy) * W + ix) * C + ci);
+          const int kidx = (ch * KH + ky) * KW + kx;
+#pragma unroll
+          for (int i = 0; i < MB; ++i)
+            if (m0 + i < M) acc[i] = __fmaf_rn(__ldg(w + (int64_t)(m0 + i) * cg * KH * KW + kidx), v, acc[i]);
+        }
+      }
+    }
+    const int64_t obase = (((int64_t)n * OH + oy) * OW + ox) * M;
+#pragma unroll
+    for (int i = 0; i < MB; ++i) {
+      const int m = m0 + i;
+      if (m >= M) break;
+      float o = acc[i];
+      if (bias) {
+        const int mo = m % mg;
+        if (!(mo >= m4 && ox >= full_cols)) o = __fadd_rn(o, __ldg(bias + m));
+      }
+      o = apply_act(o, act);
+      if (residual) o = __fadd_rn(o, __ldg(residual + obase + m));
+      y[obase + m] = o;
+    }
+  }
+}
+
+cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const float* bias,
+                               const float* residual, float* y, const ConvGeom& g, int group,
+                               const ActParams& act, cudaStream_t st) {
+  const int mg = g.m / group;
+  const int64_t pix = (int64_t)g.n * g.oh * g.ow;
+  if (group == 1 || mg % 8 == 0) {
+    const int mblocks = (g.m + 7) / 8;
+    conv_direct_kernel<8><<<grid_for(pix * mblocks), 256, 0, st>>>(
+        x, x_nchw, w, bias, residual, y, g.n, g.c, g.h, g.w, g.m, g.oh, g.ow, g.kh, g.kw, g.sh,
+        g.sw, g.ph, g.pw, group, act);
+  } else {
+    conv_direct_kernel<1><<<grid_for(pix * g.m), 256, 0, st>>>(
+        x, x_nchw, w, bias, residual, y, g.n, g.c, g.h, g.w, g.m, g.oh, g.ow, g.kh, g.kw, g.sh,
+        g.sw, g.ph, g.pw, group, act);
+  }
+  return cudaGetLastError();
+}
+
+// --------------------------------------------------- ConvTranspose 2x2 s2
+// conv.rs:730-838: each output pixel is one tap of one input pixel; the sum
+// over input channels is a c-ascending fma chain from 0.  The following
+// BatchNormalization (shape.rs:700-733: y = fma(x, a, b)) and activation are
+// fused when present.  wt: [C][M][2][2] (ONNX ConvTranspose layout).
+__global__ void __launch_bounds__(256) convt2x2_kernel(
+    const float* __restrict__ x, const float* __restrict__ wt, const float* __restrict__ bn_a,
+    const float* __restrict__ bn_b, float* __restrict__ y, int N, int H, int W, int C, int M,
+    ActParams act) {
+  const int OH = 2 * H, OW = 2 * W;
+  const int64_t total = (int64_t)N * OH * OW * M;
+  GRID_LOOP(t, total) {
+    const int co = (int)(t % M);
+    int64_t r = t / M;
+    const int ox = (int)(r % OW);
+    r /= OW;
+    const int oy = (int)(r % OH);
+    const int n = (int)(r / OH);
+    const int ky = oy & 1, kx = ox & 1;
+    const float* xp = x + (((int64_t)n * H + (oy >> 1)) * W + (ox >> 1)) * C;
+    float acc = 0.f;
+    for (int ch = 0; ch < C; ++ch)
+      acc = __fmaf_rn(__ldg(xp + ch), __ldg(wt + ((ch * M + co) * 4) + ky * 2 + kx), acc);
+    if (bn_a) acc = __fmaf_rn(acc, __ldg(bn_a + co), __ldg(bn_b + co));
+    y[t] = apply_act(acc, act);
+  }
+}
+
+cudaError_t launch_convt2x2(const float* x, const float* wt, const float* bn_a, const float* bn_b,
+                            float* y, int n, int h, int w, int c, int m, const ActParams& act,
+                            cudaStream_t st) {
+  convt2x2_kernel<<<grid_for((int64_t)n * 4 * h * w * m), 256, 0, st>>>(x, wt, bn_a, bn_b, y, n, h,
+                                                                         w, c, m, act);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ pooling
+// pool2d.rs:10-30 global_avg_pool (f64 sum / plane) on NHWC: one thread per
+// (n, c), summing the plane in index order.
+__global__ void gap_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int N, int HW,
+                                int C) {
+  GRID_LOOP(t, (int64_t)N * C) {
+    const int c = (int)(t % C), n = (int)(t / C);
+    const float* p = x + (int64_t)n * HW * C + c;
+    double s = 0.0;
+    for (int i = 0; i < HW; ++i) s += (double)__ldg(p + (int64_t)i * C);
+    y[t] = (float)(s / (double)HW);
+  }
+}
+
+cudaError_t launch_gap_nhwc(const float* x, float* y, int n, int hw, int c, cudaStream_t st) {
+  gap_nhwc_kernel<<<grid_for((int64_t)n * c), 256, 0, st>>>(x, y, n, hw, c);
+  return cudaGetLastError();
+}
+
+// pool2d.rs:51-260 (max / avg over the kernel window, avg divides by kh*kw).
+__global__ void pool2d_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int N, int H,
+                                   int W, int C, int OH, int OW, int KH, int KW, int SH, int SW,
+                                   int PH, int PW, int is_max) {
+  GRID_LOOP(t, (int64_t)N * OH * OW * C) {
+    const int c = (int)(t % C);
+    int64_t r = t / C;
+    const int ox = (int)(r % OW);
+    r /= OW;
+    const int oy = (int)(r % OH);
+    const int n = (int)(r / OH);
+    float acc = is_max ? -INFINITY : 0.f;
+    for (int ky = 0; ky < KH; ++ky)
+      for (int kx = 0; kx < KW; ++kx) {
+        const int iy = oy * SH - PH + ky, ix = ox * SW - PW + kx;
+        if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
+        const float v = __ldg(x + (((int64_t)n * H + iy) * W + ix) * C + c);
+        if (is_max) acc = v > acc ? v : acc;
+        else acc = __fadd_rn(acc, v);
+      }
+    y[t] = is_max ? acc : __fdiv_rn(acc, (float)(KH * KW));
+  }
+}
+
+cudaError_t launch_pool2d_nhwc(const float* x, float* y, int n, int h, int w, int c, int oh, int ow,
+                               int kh, int kw, int sh, int sw, int ph, int pw, int is_max,
+                               cudaStream_t st) {
+  pool2d_nhwc_kernel<<<grid_for((int64_t)n * oh * ow * c), 256, 0, st>>>(x, y, n, h, w, c, oh, ow, kh,
+                                                                        kw, sh, sw, ph, pw, is_max);
+  return cudaGetLastError();
+}
+
+// resize.rs:8-57 nearest: iy = min((int)((float)oy * H / oh), H - 1).  Writes
+// into a channel slice [c_off, c_off + C) of an output with ldc channels, so
+// the FPN concat needs no separate copy.
+__global__ void resize_nearest_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int N,
+                                           int H, int W, int C, int OH, int OW, int ldc, int c_off) {
+  const int C4 = C >> 2;
+  GRID_LOOP(t, (int64_t)N * OH * OW * C4) {
+    const int c4 = (int)(t % C4);
+    int64_t r = t / C4;
+    const int ox = (int)(r % OW);
+    r /= OW;
+    const int oy = (int)(r % OH);
+    const int n = (int)(r / OH);
+    int iy = (int)__fdiv_rn(__fmul_rn((float)oy, (float)H), (float)OH);
+    int ix = (int)__fdiv_rn(__fmul_rn((float)ox, (float)W), (float)OW);
+    iy = iy < H - 1 ? iy : H - 1;
+    ix = ix < W - 1 ? ix : W - 1;
+    const float4 v = __ldg(reinterpret_cast<const float4*>(x + (((int64_t)n * H + iy) * W + ix) * C) + c4);
+    *reinterpret_cast<float4*>(y + (((int64_t)n * OH + oy) * OW + ox) * ldc + c_off + c4 * 4) = v;
+  }
+}
+
+cudaError_t launch_resize_nearest_nhwc(const float* x, float* y, int n, int h, int w, int c, int oh,
+                                       int ow, int ldc, int c_off, cudaStream_t st) {
+  if ((c & 3) || (ldc & 3) || (c_off & 3)) return cudaErrorInvalidValue;
+  resize_nearest_nhwc_kernel<<<grid_for((int64_t)n * oh * ow * (c / 4)), 256, 0, st>>>(
+      x, y, n, h, w, c, oh, ow, ldc, c_off);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ elementwise
+// elementwise.rs:185-420 broadcast binary op over a strided view.  The
+// output is contiguous in `out_dims` order; a_str / b_str are element
+// strides per output dim (0 where broadcast).  op: 0 add 1 sub 2 mul 3 div
+// 4 pow.  `post` applies an activation to the result.
+__global__ void binary_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                              float* __restrict__ y, StridedDims sd, int op, ActParams post) {
+  GRID_LOOP(t, sd.total) {
+    int64_t rem = t, ia = 0, ib = 0;
+    for (int d = sd.rank - 1; d >= 0; --d) {
+      const int64_t idx = rem % sd.dims[d];
+      rem /= sd.dims[d];
+      ia += idx * sd.sa[d];
+      ib += idx * sd.sb[d];
+    }
+    const float va = __ldg(a + ia), vb = __ldg(b + ib);
+    float r;
+    switch (op) {
+      case 0: r = __fadd_rn(va, vb); break;
+      case 1: r = __fsub_rn(va, vb); break;
+      case 2: r = __fmul_rn(va, vb); break;
+      case 3: r = __fdiv_rn(va, vb); break;
+      default: r = (vb == 2.0f) ? __fmul_rn(va, va) : powf(va, vb); break;
+    }
+    y[t] = apply_act(r, post);
+  }
+}
+
+cudaError_t launch_binary(const float* a, const float* b, float* y, const StridedDims& sd, int op,
+                          const ActParams& post, cudaStream_t st) {
+  binary_kernel<<<grid_for(sd.total), 256, 0, st>>>(a, b, y, sd, op, post);
+  return cudaGetLastError();
+}
+
+// Unary ops on a strided view (sa = input strides): activation kinds plus
+// sqrt (kind 100), clip (kind 101, lo = alpha, hi = beta) and erf (kind 102).
+__global__ void unary_kernel(const float* __restrict__ a, float* __restrict__ y, StridedDims sd,
+                             ActParams act) {
+  GRID_LOOP(t, sd.total) {
+    int64_t rem = t, ia = 0;
+    for (int d = sd.rank - 1; d >= 0; --d) {
+      const int64_t idx = rem % sd.dims[d];
+      rem /= sd.dims[d];
+      ia += idx * sd.sa[d];
+    }
+    const float v = __ldg(a + ia);
+    float r;
+    if (act.kind == 100) r = __fsqrt_rn(v);
+    else if (act.kind == 102) r = erf1(v);
+    else if (act.kind == 101) {
+      const float m = v < act.alpha ? act.alpha : v;
+      r = act.beta < m ? act.beta : m;
+    } else r = apply_act(v, act);
+    y[t] = r;
+  }
+}
+
+cudaError_t launch_unary(const float* a, float* y, const StridedDims& sd, const ActParams& act,
+                         cudaStream_t st) {
+  unary_kernel<<<grid_for(sd.total), 256, 0, st>>>(a, y, sd, act);
+  return cudaGetLastError();
+}
+
+// elementwise.rs:134-165 mul_add_scale on NHWC with a per-channel gate:
+// out = f * g[n, c] + r  (two roundings).  gate_per_n: gate is [N, C].
+__global__ void mul_add_scale_nhwc_kernel(const float* __restrict__ f, const float* __restrict__ g,
+                                          const float* __restrict__ r, float* __restrict__ y,
+                                          int64_t total, int HW, int C, int gate_per_n) {
+  GRID_LOOP(t, total) {
+    const int c = (int)(t % C);
+    const int64_t n = t / ((int64_t)HW * C);
+    const float gv = __ldg(g + (gate_per_n ? n * C : 0) + c);
+    y[t] = __fadd_rn(__fmul_rn(__ldg(f + t), gv), r ? __ldg(r + t) : 0.0f);
+  }
+}
+
+cudaError_t launch_mul_add_scale_nhwc(const float* f, const float* g, const float* r, float* y,
+                                      int64_t total, int hw, int c, int gate_per_n, cudaStream_t st) {
+  mul_add_scale_nhwc_kernel<<<grid_for(total), 256, 0, st>>>(f, g, r, y, total, hw, c, gate_per_n);
+  return cudaGetLastError();
+}
+
+// Strided view -> contiguous copy (Transpose / Slice / Reshape materialise),
+// optionally into a channel slice of a wider buffer (out row = ldo, c_off).
+__global__ void copy_strided_kernel(const float* __restrict__ a, float* __restrict__ y,
+                                    StridedDims sd) {
+  GRID_LOOP(t, sd.total) {
+    int64_t rem = t, ia = 0;
+    for (int d = sd.rank - 1; d >= 0; --d) {
+      const int64_t idx = rem % sd.dims[d];
+      rem /= sd.dims[d];
+      ia += idx * sd.sa[d];
+    }
+    y[t] = __ldg(a + ia);
+  }
+}
+
+cudaError_t launch_copy_strided(const float* a, float* y, const StridedDims& sd, cudaStream_t st) {
+  copy_strided_kernel<<<grid_for(sd.total), 256, 0, st>>>(a, y, sd);
+  return cudaGetLastError();
+}
+
+// Channel-slice copy for Concat(axis=1) on NHWC: y[p, c_off + c] = x[p, c].
+__global__ void copy_channels_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t pix,
+                                     int C, int ldc, int c_off) {
+  GRID_LOOP(t, pix * C) {
+    const int c = (int)(t % C);
+    const int64_t p = t / C;
+    y[p * ldc + c_off + c] = __ldg(x + t);
+  }
+}
+
+cudaError_t launch_copy_channels(const float* x, float* y, int64_t pix, int c, int ldc, int c_off,
+                                 cudaStream_t st) {
+  copy_channels_kernel<<<grid_for(pix * c), 256, 0, st>>>(x, y, pix, c, ldc, c_off);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ reductions
+// shape.rs:510-566 reduce_mean over [outer, mid, inner] with f64 sums.
+__global__ void reduce_mean_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t outer,
+                                   int64_t mid, int64_t inner) {
+  GRID_LOOP(t, outer * inner) {
+    const int64_t o = t / inner, i = t % inner;
+    const float* p = x + o * mid * inner + i;
+    double s = 0.0;
+    for (int64_t m = 0; m < mid; ++m) s += (double)__ldg(p + m * inner);
+    y[t] = (float)(s / (double)mid);
+  }
+}
+
+cudaError_t launch_reduce_mean(const float* x, float* y, int64_t outer, int64_t mid, int64_t inner,
+                               cudaStream_t st) {
+  reduce_mean_kernel<<<grid_for(outer * inner), 256, 0, st>>>(x, y, outer, mid, inner);
+  return cudaGetLastError();
+}
+
+// activation.rs:321-403 softmax_last_dim, one thread per row: 8-lane max,
+// exp1(x - max), per-lane partial sums combined by the hsum8 tree, scalar
+// tail, y = e * (1 / sum).  Bit-identical to the reference row kernel.
+__global__ void softmax_rows_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t rows,
+                                    int inner) {
+  GRID_LOOP(r, rows) {
+    const float* row = x + r * inner;
+    float* out = y + r * inner;
+    int i = 0;
+    float mx;
+    if (inner >= 8) {
+      float vmax[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) vmax[j] = row[0];
+      for (; i + 8 <= inner; i += 8)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float v = row[i + j];
+          if (v > vmax[j]) vmax[j] = v;
+        }
+      mx = vmax[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j)
+        if (vmax[j] > mx) mx = vmax[j];
+    } else {
+      i = 1;
+      mx = row[0];
+    }
+    for (; i < inner; ++i)
+      if (row[i] > mx) mx = row[i];
+    float sum = 0.f;
+    int i2 = 0;
+    if (inner >= 8) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (; i2 + 8 <= inner; i2 += 8)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float e = exp1(__fsub_rn(row[i2 + j], mx));
+          out[i2 + j] = e;
+          acc[j] = __fadd_rn(acc[j], e);
+        }
+      const float t0 = __fadd_rn(acc[0], acc[4]), t1 = __fadd_rn(acc[1], acc[5]);
+      const float t2 = __fadd_rn(acc[2], acc[6]), t3 = __fadd_rn(acc[3], acc[7]);
+      sum = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
+    }
+    for (; i2 < inner; ++i2) {
+      const float e = exp1(__fsub_rn(row[i2], mx));
+      out[i2] = e;
+      sum = __fadd_rn(sum, e);
+    }
+    const float inv = __fdiv_rn(1.0f, sum);
+    for (int j = 0; j < inner; ++j) out[j] = __fmul_rn(out[j], inv);
+  }
+}
+
+cudaError_t launch_softmax_rows(const float* x, float* y, int64_t rows, int inner, cudaStream_t st) {
+  softmax_rows_kernel<<<grid_for(rows, 128), 128, 0, st>>>(x, y, rows, inner);
+  return cudaGetLastError();
+}
+
+// shape.rs:669-697 small batched matmul (attention): per output row, zeroed
+// accumulators, then c[j] = fma(a[k], b[k][j], c[j]) for k ascending.  Fully
+// strided operands (batch index decomposed as b0 * nb1 + b1).
+__global__ void bmm_small_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                 float* __restrict__ c, BmmDims d) {
+  const int64_t total = (int64_t)d.nb0 * d.nb1 * d.m * d.n;
+  GRID_LOOP(t, total) {
+    const int j = (int)(t % d.n);
+    int64_t r = t / d.n;
+    const int i = (int)(r % d.m);
+    r /= d.m;
+    const int b1 = (int)(r % d.nb1), b0 = (int)(r / d.nb1);
+    const float* ap = a + b0 * d.sa0 + b1 * d.sa1 + (int64_t)i * d.sam;
+    const float* bp = b + b0 * d.sb0 + b1 * d.sb1 + (int64_t)j * d.sbn;
+    float acc = 0.f;
+    for (int k = 0; k < d.k; ++k) acc = __fmaf_rn(__ldg(ap + (int64_t)k * d.sak), __ldg(bp + (int64_t)k * d.sbk), acc);
+    c[t] = acc;
+  }
+}
+
+cudaError_t launch_bmm_small(const float* a, const float* b, float* c, const BmmDims& d,
+                             cudaStream_t st) {
+  bmm_small_kernel<<<grid_for((int64_t)d.nb0 * d.nb1 * d.m * d.n), 256, 0, st>>>(a, b, c, d);
+  return cudaGetLastError();
+}
+
+// n_exit3_argmax.comp / rec.rs:34-79: first strict maximum per row, ties to
+// the lowest index; pairs[2r] = value, pairs[2r+1] = index bit pattern.
+// One warp per row.
+__global__ void argmax_pairs_kernel(const float* __restrict__ x, float* __restrict__ pairs,
+                                    int64_t rows, int cols) {
+  const int warps_per_block = blockDim.x >> 5;
+  const int64_t row = (int64_t)blockIdx.x * warps_per_block + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* p = x + row * cols;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int c = lane; c < cols; c += 32) {
+    const float v = __ldg(p + c);
+    if (v > bv) { bv = v; bi = c; }
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  if (lane == 0) {
+    pairs[2 * row] = bv;
+    pairs[2 * row + 1] = __uint_as_float((unsigned)bi);
+  }
+}
+
+cudaError_t launch_argmax_pairs(const float* x, float* pairs, int64_t rows, int cols,
+                                cudaStream_t st) {
+  const int64_t blocks = (rows + 7) / 8;
+  argmax_pairs_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, pairs, rows, cols);
+  return cudaGetLastError();
+}
+
+// BatchNormalization on NHWC (unfused fallback): y = fma(x, a[c], b[c]).
+__global__ void affine_nhwc_kernel(const float* __restrict__ x, const float* __restrict__ a,
+                                   const float* __restrict__ b, float* __restrict__ y,
+                                   int64_t total, int C, ActParams act) {
+  GRID_LOOP(t, total) {
+    const int c = (int)(t % C);
+    y[t] = apply_act(__fmaf_rn(__ldg(x + t), __ldg(a + c), __ldg(b + c)), act);
+  }
+}
+
+cudaError_t launch_affine_nhwc(const float* x, const float* a, const float* b, float* y,
+                               int64_t total, int c, const ActParams& act, cudaStream_t st) {
+  affine_nhwc_kernel<<<grid_for(total), 256, 0, st>>>(x, a, b, y, total, c, act);
+  return cudaGetLastError();
+}
+
+// Strided view -> strided view copy (sa = source strides, sb = destination
+// strides, both in the same logical dim order).
+__global__ void copy_view_kernel(const float* __restrict__ a, float* __restrict__ y, StridedDims sd) {
+  GRID_LOOP(t, sd.total) {
+    int64_t rem = t, ia = 0, ib = 0;
+    for (int d = sd.rank - 1; d >= 0; --d) {
+      const int64_t idx = rem % sd.dims[d];
+      rem /= sd.dims[d];
+      ia += idx * sd.sa[d];
+      ib += idx * sd.sb[d];
+    }
+    y[ib] = __ldg(a + ia);
+  }
+}
+
+cudaError_t launch_copy_view(const float* a, float* y, const StridedDims& sd, cudaStream_t st) {
+  copy_view_kernel<<<grid_for(sd.total), 256, 0, st>>>(a, y, sd);
+  return cudaGetLastError();
+}
+
+// LayerNorm over the last axis, fused from the reference's decomposed chain
+// (executor ReduceMean -> Sub -> Pow 2 -> ReduceMean -> Add eps -> Sqrt ->
+// Div -> Mul gamma -> Add beta; shape.rs:510-566 f64 means, elementwise.rs
+// single roundings).  One thread per row, sequential f64 sums in index order,
+// so every intermediate equals the reference's.
+__global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+                                 const float* __restrict__ beta, float* __restrict__ y,
+                                 int64_t rows, int C, float eps) {
+  GRID_LOOP(r, rows) {
+    const float* p = x + r * C;
+    float* o = y + r * C;
+    double s = 0.0;
+    for (int i = 0; i < C; ++i) s += (double)p[i];
+    const float mean = (float)(s / (double)C);
+    double s2 = 0.0;
+    for (int i = 0; i < C; ++i) {
+      const float d = __fsub_rn(p[i], mean);
+      s2 += (double)__fmul_rn(d, d);
+    }
+    const float var = (float)(s2 / (double)C);
+    const float sd = __fsqrt_rn(__fadd_rn(var, eps));
+    for (int i = 0; i < C; ++i) {
+      float v = __fdiv_rn(__fsub_rn(p[i], mean), sd);
+      if (gamma) v = __fmul_rn(v, __ldg(gamma + i));
+      if (beta) v = __fadd_rn(v, __ldg(beta + i));
+      o[i] = v;
+    }
+  }
+}
+
+cudaError_t launch_layernorm(const float* x, const float* gamma, const float* beta, float* y,
+                             int64_t rows, int c, float eps, cudaStream_t st) {
+  layernorm_kernel<<<grid_for(rows, 128), 128, 0, st>>>(x, gamma, beta, y, rows, c, eps);
+  return cudaGetLastError();
+}
+
+// CTC-head exit on logits: per row the first strict maximum (ties -> lowest
+// index) and its softmax probability 1 / sum_j exp1(l_j - max) (the max's own
+// term is exp1(0) == 1).  One warp per row.  Replaces Softmax + argmax exit
+// (activation.rs:321-403 + n_exit3_argmax.comp) without writing the
+// probabilities.
+__global__ void softmax_argmax_kernel(const float* __restrict__ x, float* __restrict__ pairs,
+                                      int64_t rows, int cols) {
+  const int warps_per_block = blockDim.x >> 5;
+  const int64_t row = (int64_t)blockIdx.x * warps_per_block + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* p = x + row * cols;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int c = lane; c < cols; c += 32) {
+    const float v = __ldg(p + c);
+    if (v > bv) { bv = v; bi = c; }
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+  }
+  float s = 0.f;
+  for (int c = lane; c < cols; c += 32) s = __fadd_rn(s, exp1(__fsub_rn(__ldg(p + c), bv)));
+#pragma unroll
+  for (int off = 16; off; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+  if (lane == 0) {
+    pairs[2 * row] = __fdiv_rn(1.0f, s);
+    pairs[2 * row + 1] = __uint_as_float((unsigned)bi);
+  }
+}
+
+cudaError_t launch_softmax_argmax(const float* x, float* pairs, int64_t rows, int cols,
+                                  cudaStream_t st) {
+  const int64_t blocks = (rows + 7) / 8;
+  softmax_argmax_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, pairs, rows, cols);
+  return cudaGetLastError();
+}
+
+}  // namespace qpc

@@ -1,0 +1,1979 @@
+// Session runtime: graph import, load-time fusion, per-shape planning over
+// strided device views, liveness-based arena reuse, CUDA-graph capture and
+// deferred runs.
+//
+// Reference behaviour this follows:
+//  * DeviceContext::create_session / DeviceSession::run / run_deferred
+//    (crates/qppocr-core/src/device.rs:83-176): weights resident for the
+//    session's lifetime, unsupported ops rejected at create time naming the
+//    node, outputs in graph-output order, two same-shape runs in flight never
+//    share buffers (the Vulkan backend's shadow plans,
+//    crates/qppocr-gpu/src/vulkan/session.rs:291-352).
+//  * Per-shape plan cache with a byte budget and oldest-first eviction
+//    (vulkan/session.rs:369-395); here each plan is one captured CUDA graph.
+//  * Op semantics: crates/qppocr-core/src/executor.rs:433-1580 (cited per op
+//    below); fused epilogue order bias -> act -> residual
+//    (crates/qppocr-core/src/graph/optimize.rs:337-770).
+#include "session.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <numeric>
+#include <set>
+#include <sstream>
+#include <thread>
+
+#include "kernels.h"
+#include "misc.h"
+
+namespace qpc {
+
+// ================================================================ runtime
+static thread_local std::string g_err;
+void set_error(const std::string& m) { g_err = m; }
+const std::string& last_error() { return g_err; }
+
+DevBuf::DevBuf(size_t n) : bytes(n) {
+  if (n) {
+    cudaError_t e = cudaMalloc(&ptr, n);
+    if (e != cudaSuccess) {
+      ptr = nullptr;
+      cudaGetLastError();
+      throw DeviceError{"cudaMalloc(" + std::to_string(n) + " bytes): " + cudaGetErrorString(e)};
+    }
+  }
+}
+DevBuf::~DevBuf() {
+  if (ptr) cudaFree(ptr);
+}
+
+static std::mutex g_dev_mu;
+static std::map<int, DeviceState> g_devs;
+
+DeviceState& device_state(int d) {
+  QPC_CUDA_OR_THROW(cudaSetDevice(d));
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceState& s = g_devs[d];
+  if (!s.err_word) {
+    s.device = d;
+    QPC_CUDA_OR_THROW(cudaMalloc(&s.err_word, sizeof(unsigned int)));
+    QPC_CUDA_OR_THROW(cudaMemset(s.err_word, 0, sizeof(unsigned int)));
+  }
+  return s;
+}
+
+unsigned int take_kernel_error(int d) {
+  DeviceState& s = device_state(d);
+  unsigned int v = 0;
+  QPC_CUDA_OR_THROW(cudaMemcpy(&v, s.err_word, sizeof(v), cudaMemcpyDeviceToHost));
+  if (v) QPC_CUDA_OR_THROW(cudaMemset(s.err_word, 0, sizeof(v)));
+  return v;
+}
+
+// ================================================================ IR
+const Attr* Node::attr(const std::string& n) const {
+  for (auto& a : attrs)
+    if (a.name == n) return &a;
+  return nullptr;
+}
+int64_t Node::geti(const std::string& n, int64_t d) const {
+  const Attr* a = attr(n);
+  return (a && a->kind == QPC_ATTR_INT) ? a->i : d;
+}
+float Node::getf(const std::string& n, float d) const {
+  const Attr* a = attr(n);
+  return (a && a->kind == QPC_ATTR_FLOAT) ? a->f : d;
+}
+std::string Node::gets(const std::string& n, const std::string& d) const {
+  const Attr* a = attr(n);
+  return (a && a->kind == QPC_ATTR_STRING) ? a->s : d;
+}
+std::vector<int64_t> Node::getints(const std::string& n) const {
+  const Attr* a = attr(n);
+  return (a && a->kind == QPC_ATTR_INTS) ? a->ints : std::vector<int64_t>{};
+}
+void Node::seti(const std::string& n, int64_t v) {
+  for (auto& a : attrs)
+    if (a.name == n) { a.kind = QPC_ATTR_INT; a.i = v; return; }
+  Attr a;
+  a.name = n;
+  a.kind = QPC_ATTR_INT;
+  a.i = v;
+  attrs.push_back(a);
+}
+void Node::setf(const std::string& n, float v) {
+  for (auto& a : attrs)
+    if (a.name == n) { a.kind = QPC_ATTR_FLOAT; a.f = v; return; }
+  Attr a;
+  a.name = n;
+  a.kind = QPC_ATTR_FLOAT;
+  a.f = v;
+  attrs.push_back(a);
+}
+
+static std::string shape_str(const std::vector<int64_t>& s) {
+  std::ostringstream o;
+  o << "[";
+  for (size_t i = 0; i < s.size(); ++i) o << (i ? "," : "") << s[i];
+  o << "]";
+  return o.str();
+}
+
+PlanInstance::~PlanInstance() {
+  if (exec) cudaGraphExecDestroy(exec);
+  for (auto& e : ev)
+    if (e) cudaEventDestroy(e);
+  if (stream) cudaStreamDestroy(stream);
+  for (auto& io : ins)
+    if (io.host) cudaFreeHost(io.host);
+  for (auto& io : outs)
+    if (io.host) cudaFreeHost(io.host);
+}
+
+// ================================================================ session
+static const std::set<std::string>& supported_ops() {
+  static const std::set<std::string> ops = {
+      "Conv", "ConvTranspose", "BatchNormalization", "Relu", "Sigmoid", "HardSigmoid",
+      "FusedGelu", "Erf", "Sqrt", "Clip", "MulAddScale", "Add", "Sub", "Mul", "Div", "Pow",
+      "Softmax", "GlobalAveragePool", "AveragePool", "MaxPool", "Resize", "Concat", "Slice",
+      "Transpose", "Reshape", "Squeeze", "Unsqueeze", "Flatten", "ReduceMean", "MatMul",
+      "Identity", "Dropout", "Gather", "Shape", "Cast",
+      // internal (produced by Session::fuse)
+      "QpcLinear", "QpcConvT", "QpcLayerNorm", "QpcCtcHead"};
+  return ops;
+}
+
+Session::Session(int device, const qpc_graph* g, const qpc_tensor* w, int nw, int role,
+                 const qpc_session_options* opts)
+    : device_(device), role_(role) {
+  opts_.math = QPC_MATH_TF32;
+  opts_.argmax_exit = -1;
+  opts_.plan_budget_bytes = 0;
+  opts_.use_cuda_graph = 1;
+  if (opts) opts_ = *opts;
+  if (opts_.plan_budget_bytes <= 0) opts_.plan_budget_bytes = (int64_t)8 << 30;
+  argmax_exit_ = opts_.argmax_exit < 0 ? (role == QPC_ROLE_REC) : (opts_.argmax_exit != 0);
+  device_state(device_);
+  for (int k = 0; k < g->n_nodes; ++k) {
+    const qpc_node& qn = g->nodes[k];
+    Node n;
+    n.op = qn.op_type ? qn.op_type : "";
+    n.name = qn.name ? qn.name : ("node" + std::to_string(k));
+    for (int j = 0; j < qn.n_inputs; ++j) n.in.push_back(qn.inputs[j] ? qn.inputs[j] : "");
+    for (int j = 0; j < qn.n_outputs; ++j) n.out.push_back(qn.outputs[j] ? qn.outputs[j] : "");
+    for (int j = 0; j < qn.n_attrs; ++j) {
+      const qpc_attr& qa = qn.attrs[j];
+      Attr a;
+      a.name = qa.name ? qa.name : "";
+      a.kind = qa.kind;
+      a.f = qa.f;
+      a.i = qa.i;
+      if (qa.s) a.s = qa.s;
+      if (qa.kind == QPC_ATTR_FLOATS && qa.floats) a.floats.assign(qa.floats, qa.floats + qa.n);
+      if (qa.kind == QPC_ATTR_INTS && qa.ints) a.ints.assign(qa.ints, qa.ints + qa.n);
+      n.attrs.push_back(std::move(a));
+    }
+    nodes_.push_back(std::move(n));
+  }
+  for (int k = 0; k < g->n_inputs; ++k) inputs_.push_back(g->inputs[k]);
+  for (int k = 0; k < g->n_outputs; ++k) outputs_.push_back(g->outputs[k]);
+  for (int k = 0; k < nw; ++k) {
+    const qpc_tensor& t = w[k];
+    HostTensor h;
+    h.shape.assign(t.shape, t.shape + t.rank);
+    h.dtype = t.dtype;
+    const int64_t n = h.numel();
+    if (t.dtype == QPC_F32) {
+      h.f.resize(n);
+      if (n) std::memcpy(h.f.data(), t.data, n * sizeof(float));
+    } else if (t.dtype == QPC_I64) {
+      h.i.resize(n);
+      if (n) std::memcpy(h.i.data(), t.data, n * sizeof(int64_t));
+    } else {
+      throw GraphError{std::string("weight ") + t.name + ": unsupported dtype"};
+    }
+    weights_[t.name] = std::move(h);
+  }
+  validate_ops();
+  fuse();
+}
+
+Session::~Session() {
+  cudaSetDevice(device_);
+  for (auto& kv : plans_)
+    for (auto& p : kv.second)
+      if (p->stream) cudaStreamSynchronize(p->stream);
+}
+
+void Session::validate_ops() const {
+  for (const Node& n : nodes_) {
+    if (!supported_ops().count(n.op))
+      throw GraphError{"unsupported op " + n.op + " (node " + n.name + ")"};
+    if (n.op == "Conv") {
+      if (!n.has_in(1) || !weights_.count(n.in[1]))
+        throw GraphError{"Conv " + n.name + ": weight must be an initializer"};
+      for (auto d : n.getints("dilations"))
+        if (d != 1) throw GraphError{"Conv " + n.name + ": dilation != 1 unsupported"};
+    }
+    if (n.op == "ConvTranspose") {
+      const HostTensor* w = weight(n.in[1]);
+      if (!w || w->shape.size() != 4 || w->shape[2] != 2 || w->shape[3] != 2)
+        throw GraphError{"ConvTranspose " + n.name + ": only 2x2 s2 p0 (conv.rs:754-757)"};
+    }
+    if (n.op == "Resize") {
+      const std::string mode = n.gets("mode", "nearest");
+      if (mode != "nearest") throw GraphError{"Resize " + n.name + ": mode " + mode + " unsupported"};
+    }
+  }
+}
+
+const HostTensor* Session::weight(const std::string& name) const {
+  auto it = weights_.find(name);
+  return it == weights_.end() ? nullptr : &it->second;
+}
+
+qpc_caps Session::caps() const {
+  qpc_caps c;
+  c.prefers_host_parallelism = 0;  // GPU executes in parallel internally (device.rs:134)
+  c.bucket_grain = 64;             // width buckets collapse rec shapes (device.rs:139-141)
+  c.batch_grain = 1;               // batch rows are not padded (device.rs:148-157)
+  c.rec_chunk = 256;               // real lines merged per forward
+  c.argmax_pairs = argmax_exit_ ? 1 : 0;
+  return c;
+}
+
+// Device copies of weights, in the layout a kernel wants (built once).
+//   raw        as given
+//   dw         depthwise [C,1,kh,kw] -> tap-major [kh*kw][C]
+//   kxk        dense [M,C,kh,kw] -> tap-major [kh*kw][M][C]
+//   nk         MatMul B [K,N] -> [N,K]
+//   X.hi/X.lo  3xTF32 split of variant X (hi = tf32 truncation, lo = v - hi)
+const float* Session::dweight(const std::string& name, const std::string& variant) {
+  const std::string key = name + "#" + variant;
+  auto it = dev_cache_.find(key);
+  if (it != dev_cache_.end()) return it->second->f();
+  const HostTensor* h = weight(name);
+  if (!h) throw GraphError{"missing initializer " + name};
+  std::vector<float> v;
+  auto base_variant = variant;
+  bool hi = false, lo = false;
+  if (variant.size() > 3 && variant.compare(variant.size() - 3, 3, ".hi") == 0) {
+    hi = true;
+    base_variant = variant.substr(0, variant.size() - 3);
+  } else if (variant.size() > 3 && variant.compare(variant.size() - 3, 3, ".lo") == 0) {
+    lo = true;
+    base_variant = variant.substr(0, variant.size() - 3);
+  }
+  std::vector<float> src;
+  if (h->dtype == QPC_F32) src = h->f;
+  else {
+    src.resize(h->i.size());
+    for (size_t k = 0; k < src.size(); ++k) src[k] = (float)h->i[k];
+  }
+  if (base_variant == "raw") {
+    v = src;
+  } else if (base_variant == "dw") {
+    const int64_t c = h->shape[0], taps = h->shape[2] * h->shape[3];
+    v.resize(c * taps);
+    for (int64_t ch = 0; ch < c; ++ch)
+      for (int64_t t = 0; t < taps; ++t) v[t * c + ch] = src[ch * taps + t];
+  } else if (base_variant == "kxk") {
+    const int64_t m = h->shape[0], c = h->shape[1], taps = h->shape[2] * h->shape[3];
+    v.resize(m * c * taps);
+    for (int64_t mo = 0; mo < m; ++mo)
+      for (int64_t ch = 0; ch < c; ++ch)
+        for (int64_t t = 0; t < taps; ++t) v[(t * m + mo) * c + ch] = src[(mo * c + ch) * taps + t];
+  } else if (base_variant == "nk") {
+    const int64_t k = h->shape[0], n = h->shape[1];
+    v.resize(k * n);
+    for (int64_t a = 0; a < k; ++a)
+      for (int64_t b = 0; b < n; ++b) v[b * k + a] = src[a * n + b];
+  } else {
+    throw GraphError{"internal: unknown weight variant " + variant};
+  }
+  if (hi || lo) {
+    for (auto& x : v) {
+      uint32_t u;
+      std::memcpy(&u, &x, 4);
+      u &= 0xFFFFE000u;
+      float t;
+      std::memcpy(&t, &u, 4);
+      x = hi ? t : (x - t);
+    }
+  }
+  if (v.empty()) v.push_back(0.f);
+  auto buf = std::make_unique<DevBuf>(v.size() * sizeof(float));
+  QPC_CUDA_OR_THROW(cudaMemcpy(buf->ptr, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+  const float* p = buf->f();
+  dev_cache_[key] = std::move(buf);
+  return p;
+}
+
+// ================================================================ fusion
+// Load-time graph rewrites into internal ops, each placed where the last
+// absorbed node stood (all of its inputs exist there).  Only single-consumer
+// intermediates are absorbed, so no other node can observe the change.
+void Session::fuse() {
+  std::vector<Node>& N = nodes_;
+  std::vector<bool> alive(N.size(), true);
+  std::set<std::string> gouts(outputs_.begin(), outputs_.end());
+  auto consumers = [&](const std::string& t) {
+    std::vector<int> r;
+    for (size_t i = 0; i < N.size(); ++i)
+      if (alive[i])
+        for (auto& x : N[i].in)
+          if (x == t) r.push_back((int)i);
+    return r;
+  };
+  auto is_const = [&](const std::string& t) { return !t.empty() && weights_.count(t) > 0; };
+  auto const_scalar = [&](const std::string& t, double* v) {
+    const HostTensor* h = weight(t);
+    if (!h || h->numel() != 1) return false;
+    *v = h->scalar();
+    return true;
+  };
+
+  // Conv fused-activation attribute from the reference optimizer
+  // (optimize.rs:337-427: act 1 = GELU(c1..c3), 2 = ReLU) -> internal codes.
+  for (auto& n : N) {
+    if (n.op != "Conv") continue;
+    const int64_t a = n.geti("act", 0);
+    if (a == 1) {
+      n.seti("qpc_act", ACT_GELU);
+      n.setf("qpc_c1", n.getf("act_c1", 1.4142135f));
+      n.setf("qpc_c2", n.getf("act_c2", 1.0f));
+      n.setf("qpc_c3", n.getf("act_c3", 0.5f));
+    } else if (a == 2) {
+      n.seti("qpc_act", ACT_RELU);
+    }
+  }
+
+  // MatMul(x, W[K,N]) (+ Add(b[N])) -> QpcLinear.  shape.rs:568-653 constant-B path.
+  for (size_t i = 0; i < N.size(); ++i) {
+    if (!alive[i] || N[i].op != "MatMul" || N[i].in.size() != 2) continue;
+    const HostTensor* w = weight(N[i].in[1]);
+    if (!w || w->shape.size() != 2 || (w->shape[0] % 4) != 0) continue;
+    Node lin = N[i];
+    lin.op = "QpcLinear";
+    size_t pos = i;
+    auto cs = consumers(N[i].out[0]);
+    if (!gouts.count(N[i].out[0]) && cs.size() == 1 && N[cs[0]].op == "Add") {
+      Node& ad = N[cs[0]];
+      const std::string other = ad.in[0] == N[i].out[0] ? ad.in[1] : ad.in[0];
+      const HostTensor* b = weight(other);
+      if (b && b->numel() == w->shape[1] && ad.in[0] != ad.in[1]) {
+        lin.in.push_back(other);
+        lin.out = ad.out;
+        alive[i] = false;
+        pos = cs[0];
+      }
+    }
+    N[pos] = lin;
+    alive[pos] = true;
+  }
+
+  // ConvTranspose -> BatchNormalization -> QpcConvT (executor.rs:654-731).
+  for (size_t i = 0; i < N.size(); ++i) {
+    if (!alive[i] || N[i].op != "ConvTranspose") continue;
+    Node ct = N[i];
+    ct.op = "QpcConvT";
+    ct.in.resize(2);
+    size_t pos = i;
+    auto cs = consumers(N[i].out[0]);
+    if (!gouts.count(N[i].out[0]) && cs.size() == 1 && N[cs[0]].op == "BatchNormalization") {
+      Node& bn = N[cs[0]];
+      if (bn.in.size() == 5 && is_const(bn.in[1]) && is_const(bn.in[2]) && is_const(bn.in[3]) &&
+          is_const(bn.in[4])) {
+        for (int k = 1; k < 5; ++k) ct.in.push_back(bn.in[k]);
+        ct.setf("qpc_eps", bn.getf("epsilon", 1e-5f));
+        ct.out = bn.out;
+        alive[i] = false;
+        pos = cs[0];
+      }
+    }
+    N[pos] = ct;
+    alive[pos] = true;
+  }
+
+  // Activation absorption into producers with a fused epilogue.
+  auto producer_ok = [&](const Node& n) {
+    return (n.op == "Conv" || n.op == "QpcLinear" || n.op == "QpcConvT") &&
+           n.geti("qpc_act", 0) == 0 && !n.has_in(3) && n.geti("qpc_has_res", 0) == 0;
+  };
+  bool changed = true;
+  while (changed) {
+    changed = false;
+    for (size_t i = 0; i < N.size(); ++i) {
+      if (!alive[i] || !producer_ok(N[i])) continue;
+      const std::string o = N[i].out[0];
+      if (gouts.count(o)) continue;
+      auto cs = consumers(o);
+      if (cs.size() == 2 && cs[0] != cs[1]) {
+        // x * HardSigmoid(x) (hardswish) / x * Sigmoid(x) (swish)
+        for (int pick = 0; pick < 2 && !changed; ++pick) {
+          Node& h = N[cs[pick]];
+          Node& m = N[cs[1 - pick]];
+          if ((h.op != "HardSigmoid" && h.op != "Sigmoid") || h.in[0] != o || m.op != "Mul") continue;
+          if (!((m.in[0] == o && m.in[1] == h.out[0]) || (m.in[1] == o && m.in[0] == h.out[0])))
+            continue;
+          auto hc = consumers(h.out[0]);
+          if (hc.size() != 1 || gouts.count(h.out[0])) continue;
+          if (h.op == "HardSigmoid") {
+            N[i].seti("qpc_act", ACT_HARDSWISH);
+            N[i].setf("qpc_alpha", h.getf("alpha", 0.2f));
+            N[i].setf("qpc_beta", h.getf("beta", 0.5f));
+          } else {
+            N[i].seti("qpc_act", ACT_SWISH);
+          }
+          N[i].out = m.out;
+          alive[cs[0]] = alive[cs[1]] = false;
+          changed = true;
+        }
+      } else if (cs.size() == 1) {
+        Node& a = N[cs[0]];
+        int kind = 0;
+        if (a.op == "Relu") kind = ACT_RELU;
+        else if (a.op == "Sigmoid") kind = ACT_SIGMOID;
+        else if (a.op == "HardSigmoid") kind = ACT_HARDSIGMOID;
+        else if (a.op == "FusedGelu") kind = ACT_GELU;
+        if (kind && a.in[0] == o) {
+          N[i].seti("qpc_act", kind);
+          if (kind == ACT_HARDSIGMOID) {
+            N[i].setf("qpc_alpha", a.getf("alpha", 0.2f));
+            N[i].setf("qpc_beta", a.getf("beta", 0.5f));
+          }
+          if (kind == ACT_GELU) {
+            N[i].setf("qpc_c1", a.getf("c1", 1.4142135f));
+            N[i].setf("qpc_c2", a.getf("c2", 1.0f));
+            N[i].setf("qpc_c3", a.getf("c3", 0.5f));
+          }
+          N[i].out = a.out;
+          alive[cs[0]] = false;
+          changed = true;
+        }
+      }
+    }
+  }
+
+  // Residual absorption: P -> Add(P.out, R) (fuse_conv_residual semantics,
+  // optimize.rs:662-770: residual added after the activation).
+  for (size_t i = 0; i < N.size(); ++i) {
+    if (!alive[i]) continue;
+    Node& p = N[i];
+    if (!(p.op == "Conv" || p.op == "QpcLinear")) continue;
+    if (p.has_in(3) || p.geti("qpc_has_res", 0)) continue;
+    const std::string o = p.out[0];
+    if (gouts.count(o)) continue;
+    auto cs = consumers(o);
+    if (cs.size() != 1 || N[cs[0]].op != "Add") continue;
+    Node& ad = N[cs[0]];
+    if (ad.in[0] == ad.in[1]) continue;
+    const std::string r = ad.in[0] == o ? ad.in[1] : ad.in[0];
+    if (is_const(r)) continue;
+    Node f = p;
+    if (f.op == "Conv") {
+      f.in.resize(3);  // x, w, bias ("" if none)
+      f.in.push_back(r);
+    } else {
+      if (f.in.size() < 3) f.in.push_back("");
+      f.in.push_back(r);
+    }
+    f.seti("qpc_has_res", 1);
+    f.out = ad.out;
+    alive[i] = false;
+    N[cs[0]] = f;
+  }
+
+  // LayerNorm decomposition (executor ReduceMean/Sub/Pow/ReduceMean/Add/Sqrt/
+  // Div then Mul/Add or MulAddScale; shape.rs:510-566 f64 means) -> QpcLayerNorm.
+  for (size_t i = 0; i < N.size(); ++i) {
+    if (!alive[i] || N[i].op != "ReduceMean") continue;
+    const Node& rm1 = N[i];
+    auto ax = rm1.getints("axes");
+    if (!(ax.size() == 1 && ax[0] == -1) || rm1.geti("keepdims", 1) != 1) continue;
+    const std::string x = rm1.in[0], mean = rm1.out[0];
+    auto c1 = consumers(mean);
+    if (c1.size() != 1 || N[c1[0]].op != "Sub" || N[c1[0]].in[0] != x || N[c1[0]].in[1] != mean)
+      continue;
+    const int isub = c1[0];
+    const std::string d = N[isub].out[0];
+    auto cd = consumers(d);
+    if (cd.size() != 2) continue;
+    int ipow = -1, idiv = -1;
+    for (int k : cd) {
+      if (N[k].op == "Pow" && N[k].in[0] == d) ipow = k;
+      if (N[k].op == "Div" && N[k].in[0] == d) idiv = k;
+    }
+    double e2 = 0;
+    if (ipow < 0 || idiv < 0 || !const_scalar(N[ipow].in[1], &e2) || e2 != 2.0) continue;
+    auto cp = consumers(N[ipow].out[0]);
+    if (cp.size() != 1 || N[cp[0]].op != "ReduceMean") continue;
+    const int irm2 = cp[0];
+    auto ax2 = N[irm2].getints("axes");
+    if (!(ax2.size() == 1 && ax2[0] == -1)) continue;
+    auto cv = consumers(N[irm2].out[0]);
+    if (cv.size() != 1 || N[cv[0]].op != "Add") continue;
+    const int iadd = cv[0];
+    double eps = 0;
+    const std::string eps_name = N[iadd].in[0] == N[irm2].out[0] ? N[iadd].in[1] : N[iadd].in[0];
+    if (!const_scalar(eps_name, &eps)) continue;
+    auto cs2 = consumers(N[iadd].out[0]);
+    if (cs2.size() != 1 || N[cs2[0]].op != "Sqrt") continue;
+    const int isq = cs2[0];
+    if (N[idiv].in[1] != N[isq].out[0]) continue;
+    auto cq = consumers(N[isq].out[0]);
+    if (cq.size() != 1) continue;
+    // affine tail
+    Node ln;
+    ln.op = "QpcLayerNorm";
+    ln.name = rm1.name;
+    ln.in = {x, "", ""};
+    ln.setf("qpc_eps", (float)eps);
+    std::vector<int> absorbed = {(int)i, isub, ipow, irm2, iadd, isq, idiv};
+    int last = idiv;
+    std::string out = N[idiv].out[0];
+    auto cn = consumers(out);
+    if (!gouts.count(out) && cn.size() == 1) {
+      Node& t = N[cn[0]];
+      if (t.op == "MulAddScale" && t.in[0] == out && is_const(t.in[1]) && is_const(t.in[2])) {
+        ln.in[1] = t.in[1];
+        ln.in[2] = t.in[2];
+        absorbed.push_back(cn[0]);
+        last = cn[0];
+        out = t.out[0];
+      } else if (t.op == "Mul" && is_const(t.in[1]) && t.in[0] == out) {
+        auto cm = consumers(t.out[0]);
+        if (!gouts.count(t.out[0]) && cm.size() == 1 && N[cm[0]].op == "Add" &&
+            N[cm[0]].in[0] == t.out[0] && is_const(N[cm[0]].in[1])) {
+          ln.in[1] = t.in[1];
+          ln.in[2] = N[cm[0]].in[1];
+          absorbed.push_back(cn[0]);
+          absorbed.push_back(cm[0]);
+          last = cm[0];
+          out = N[cm[0]].out[0];
+        }
+      }
+    }
+    ln.out = {out};
+    for (int k : absorbed) alive[k] = false;
+    N[last] = ln;
+    alive[last] = true;
+  }
+
+  // Rec CTC head: QpcLinear -> Softmax(last axis) -> graph output, with the
+  // argmax exit on: one fused op emitting (val, idx) pairs
+  // (DeviceSession::rec_argmax_pairs, device.rs:159-163; n_exit3_argmax.comp).
+  if (argmax_exit_) {
+    for (size_t i = 0; i < N.size(); ++i) {
+      if (!alive[i] || N[i].op != "Softmax" || !gouts.count(N[i].out[0])) continue;
+      const int64_t axis = N[i].geti("axis", -1);
+      if (axis != -1) continue;
+      int ip = -1;
+      for (size_t j = 0; j < i; ++j)
+        if (alive[j] && N[j].out.size() && N[j].out[0] == N[i].in[0]) ip = (int)j;
+      if (ip < 0 || N[ip].op != "QpcLinear" || N[ip].has_in(3) || N[ip].geti("qpc_act", 0)) continue;
+      if (consumers(N[ip].out[0]).size() != 1) continue;
+      Node h = N[ip];
+      h.op = "QpcCtcHead";
+      h.out = N[i].out;
+      alive[ip] = false;
+      N[i] = h;
+    }
+  }
+
+  std::vector<Node> kept;
+  for (size_t i = 0; i < N.size(); ++i)
+    if (alive[i]) kept.push_back(std::move(N[i]));
+  nodes_ = std::move(kept);
+}
+
+// ================================================================ planner
+namespace {
+
+struct Val {
+  bool is_const = false;
+  const HostTensor* ct = nullptr;     // host constant (initializer or folded)
+  std::shared_ptr<HostTensor> owned;  // folded constant storage
+  std::vector<int64_t> shape, strides;
+  int buf = -1;                       // arena buffer
+  const float* cptr = nullptr;        // device constant (weights)
+  int64_t off = 0;
+  int64_t numel() const {
+    int64_t n = 1;
+    for (auto d : shape) n *= d;
+    return n;
+  }
+};
+
+std::vector<int64_t> rowmajor_strides(const std::vector<int64_t>& s) {
+  std::vector<int64_t> st(s.size());
+  int64_t acc = 1;
+  for (int i = (int)s.size() - 1; i >= 0; --i) {
+    st[i] = acc;
+    acc *= s[i];
+  }
+  return st;
+}
+std::vector<int64_t> nhwc_strides(const std::vector<int64_t>& s) {
+  const int64_t C = s[1], H = s[2], W = s[3];
+  return {H * W * C, 1, W * C, C};
+}
+bool same_layout(const Val& v, const std::vector<int64_t>& want) {
+  for (size_t i = 0; i < v.shape.size(); ++i)
+    if (v.shape[i] != 1 && v.strides[i] != want[i]) return false;
+  return true;
+}
+bool is_rowmajor(const Val& v) { return same_layout(v, rowmajor_strides(v.shape)); }
+bool is_nhwc(const Val& v) { return v.shape.size() == 4 && same_layout(v, nhwc_strides(v.shape)); }
+
+struct Arena {
+  struct B {
+    std::unique_ptr<DevBuf> mem;
+    int64_t cap = 0;
+    int refs = 0;
+    bool pinned = false;  // graph I/O: never reused
+  };
+  std::vector<B> bufs;
+  int alloc(int64_t elems, bool pinned = false) {
+    elems = std::max<int64_t>(elems, 1);
+    int best = -1;
+    if (!pinned)
+      for (size_t i = 0; i < bufs.size(); ++i)
+        if (bufs[i].refs == 0 && !bufs[i].pinned && bufs[i].cap >= elems &&
+            (best < 0 || bufs[i].cap < bufs[best].cap))
+          best = (int)i;
+    if (best >= 0 && bufs[best].cap <= 2 * elems + (1 << 20)) {
+      bufs[best].refs = 1;
+      return best;
+    }
+    B b;
+    b.mem = std::make_unique<DevBuf>((size_t)(elems + 64) * sizeof(float));
+    b.cap = elems + 64;
+    b.refs = 1;
+    b.pinned = pinned;
+    bufs.push_back(std::move(b));
+    return (int)bufs.size() - 1;
+  }
+  void retain(int b) {
+    if (b >= 0) ++bufs[b].refs;
+  }
+  void release(int b) {
+    if (b >= 0 && bufs[b].refs > 0) --bufs[b].refs;
+  }
+  float* ptr(int b) { return bufs[b].mem->f(); }
+};
+
+ActParams act_of(const Node& n) {
+  ActParams a{};
+  a.kind = (int)n.geti("qpc_act", 0);
+  a.alpha = n.getf("qpc_alpha", 1.0f / 6.0f);
+  a.beta = n.getf("qpc_beta", 0.5f);
+  a.c1 = n.getf("qpc_c1", 1.4142135f);
+  a.c2 = n.getf("qpc_c2", 1.0f);
+  a.c3 = n.getf("qpc_c3", 0.5f);
+  return a;
+}
+
+// ONNX pads / auto_pad -> (ph, pw, peh, pew); executor.rs resolve_pads.
+void resolve_pads(const Node& n, int64_t h, int64_t w, int64_t kh, int64_t kw, int64_t sh,
+                  int64_t sw, int64_t* ph, int64_t* pw, int64_t* peh, int64_t* pew) {
+  const std::string ap = n.gets("auto_pad", "NOTSET");
+  if (ap == "SAME_UPPER" || ap == "SAME_LOWER") {
+    auto one = [&](int64_t in, int64_t k, int64_t s, int64_t* b, int64_t* e) {
+      const int64_t out = (in + s - 1) / s;
+      const int64_t tot = std::max<int64_t>(0, (out - 1) * s + k - in);
+      *b = ap == "SAME_UPPER" ? tot / 2 : tot - tot / 2;
+      *e = tot - *b;
+    };
+    one(h, kh, sh, ph, peh);
+    one(w, kw, sw, pw, pew);
+    return;
+  }
+  auto p = n.getints("pads");
+  if (p.size() == 4) {
+    *ph = p[0];
+    *pw = p[1];
+    *peh = p[2];
+    *pew = p[3];
+  } else {
+    *ph = *pw = *peh = *pew = 0;
+  }
+}
+
+}  // namespace
+
+class Planner {
+ public:
+  Planner(Session& s, PlanInstance& p) : S(s), P(p) {}
+
+  void run(const qpc_tensor* inputs, int n_inputs) {
+    // Remaining uses of each tensor (consumers + graph outputs).
+    for (const Node& n : S.nodes())
+      for (auto& x : n.in)
+        if (!x.empty()) uses_[x]++;
+    for (auto& o : S.graph_outputs()) uses_[o]++;
+
+    // Graph inputs: contiguous row-major device buffers (logical NCHW).
+    for (const std::string& gi : S.graph_inputs()) {
+      const qpc_tensor* t = nullptr;
+      for (int k = 0; k < n_inputs; ++k)
+        if (gi == inputs[k].name) t = &inputs[k];
+      if (!t) throw GraphError{"missing graph input " + gi};
+      if (t->dtype != QPC_F32) throw GraphError{"graph input " + gi + " must be f32"};
+      Val v;
+      v.shape.assign(t->shape, t->shape + t->rank);
+      v.strides = rowmajor_strides(v.shape);
+      v.buf = A.alloc(v.numel(), true);
+      PlanInstance::IO io;
+      io.name = gi;
+      io.shape = v.shape;
+      io.count = v.numel();
+      io.dev = A.ptr(v.buf);
+      P.ins.push_back(io);
+      vals_[gi] = v;
+    }
+    for (size_t i = 0; i < S.nodes().size(); ++i) {
+      const Node& n = S.nodes()[i];
+      try {
+        plan_node(n);
+      } catch (GraphError& e) {
+        throw GraphError{n.op + " " + n.name + ": " + e.msg};
+      }
+      for (auto& x : n.in)
+        if (!x.empty()) use_done(x);
+      for (auto& o : n.out)
+        if (!uses_.count(o) || uses_[o] == 0) drop(o);
+    }
+    // Graph outputs: contiguous row-major, dedicated buffers.
+    for (const std::string& go : S.graph_outputs()) {
+      auto it = vals_.find(go);
+      if (it == vals_.end()) throw GraphError{"graph output " + go + " not produced"};
+      Val v = it->second;
+      if (v.is_const) throw GraphError{"graph output " + go + " is a constant"};
+      Val o;
+      o.shape = v.shape;
+      o.strides = rowmajor_strides(v.shape);
+      o.buf = A.alloc(o.numel(), true);
+      copy_into(v, o, "output " + go);
+      PlanInstance::IO io;
+      io.name = go;
+      io.shape = o.shape;
+      io.count = o.numel();
+      io.dev = A.ptr(o.buf);
+      P.outs.push_back(io);
+    }
+    for (auto& b : A.bufs) {
+      P.bytes += b.mem->bytes;
+      P.bufs.push_back(std::move(b.mem));
+    }
+  }
+
+ private:
+  Session& S;
+  PlanInstance& P;
+  Arena A;
+  std::unordered_map<std::string, Val> vals_;
+  std::unordered_map<std::string, int> uses_;
+
+  // ------------------------------------------------------------ bookkeeping
+  void use_done(const std::string& x) {
+    auto it = uses_.find(x);
+    if (it == uses_.end()) return;
+    if (--it->second == 0) drop(x);
+  }
+  void drop(const std::string& x) {
+    auto it = vals_.find(x);
+    if (it == vals_.end()) return;
+    A.release(it->second.buf);
+    vals_.erase(it);
+  }
+  void define(const std::string& name, Val v) {
+    if (vals_.count(name)) A.release(vals_[name].buf);
+    vals_[name] = std::move(v);
+  }
+  const Val& get(const std::string& name) {
+    auto it = vals_.find(name);
+    if (it != vals_.end()) return it->second;
+    const HostTensor* h = S.weight(name);
+    if (!h) throw GraphError{"missing tensor " + name};
+    Val v;
+    v.is_const = true;
+    v.ct = h;
+    v.shape = h->shape;
+    v.strides = rowmajor_strides(v.shape);
+    vals_[name] = v;
+    uses_[name] += 0;
+    return vals_[name];
+  }
+  const float* dptr(const Val& v, const std::string& name) {
+    if (v.is_const) return S.dweight(name, "raw");
+    return A.ptr(v.buf) + v.off;
+  }
+  float* out_ptr(const Val& v) { return A.ptr(v.buf) + v.off; }
+  Val new_val(const std::vector<int64_t>& shape, bool nhwc) {
+    Val v;
+    v.shape = shape;
+    v.strides = nhwc ? nhwc_strides(shape) : rowmajor_strides(shape);
+    v.buf = A.alloc(v.numel());
+    return v;
+  }
+  Val view_of(const Val& src, std::vector<int64_t> shape, std::vector<int64_t> strides, int64_t off) {
+    Val v;
+    v.shape = std::move(shape);
+    v.strides = std::move(strides);
+    v.buf = src.buf;
+    v.cptr = src.cptr;
+    v.off = off;
+    A.retain(src.buf);
+    return v;
+  }
+  void step(const std::string& kernel, const std::string& node, double bytes, double flops,
+            std::function<cudaError_t(cudaStream_t)> fn) {
+    StepInfo si;
+    si.kernel = kernel;
+    si.node = node;
+    si.bytes = bytes;
+    si.flops = flops;
+    P.info.push_back(si);
+    P.steps.push_back(std::move(fn));
+  }
+
+  // Copy a strided view into another view of the same shape.
+  void copy_into(const Val& src, const Val& dst, const std::string& why) {
+    if (src.is_const) {
+      // constants used as outputs / concat parts: upload then copy
+      throw GraphError{"constant operand not supported in " + why};
+    }
+    StridedDims sd;
+    sd.rank = (int)src.shape.size();
+    if (sd.rank > kMaxDims) throw GraphError{"rank > 6 in " + why};
+    sd.total = src.numel();
+    const bool dst_rm = is_rowmajor(dst);
+    for (int d = 0; d < sd.rank; ++d) {
+      sd.dims[d] = src.shape[d];
+      sd.sa[d] = src.strides[d];
+      sd.sb[d] = dst.strides[d];
+    }
+    const float* a = A.ptr(src.buf) + src.off;
+    float* y = A.ptr(dst.buf) + dst.off;
+    if (dst_rm) {
+      step("copy", why, 8.0 * sd.total, 0, [=](cudaStream_t st) { return launch_copy_strided(a, y, sd, st); });
+    } else {
+      // dst strided: write through a second strided map (sb)
+      step("copy", why, 8.0 * sd.total, 0, [=](cudaStream_t st) { return launch_copy_view(a, y, sd, st); });
+    }
+  }
+  // Ensure a value is laid out as NHWC (4-D) or row-major; returns the value
+  // to use (possibly a fresh copy).
+  Val as_nhwc(const Val& v, const std::string& why) {
+    if (v.is_const) throw GraphError{"constant activation in " + why};
+    if (is_nhwc(v) && (v.off % 4) == 0) {
+      Val r = v;
+      A.retain(r.buf);
+      return r;
+    }
+    Val o = new_val(v.shape, true);
+    copy_into(v, o, why + " (to NHWC)");
+    return o;
+  }
+  Val as_rowmajor(const Val& v, const std::string& why) {
+    if (v.is_const) throw GraphError{"constant activation in " + why};
+    if (is_rowmajor(v) && (v.off % 4) == 0) {
+      Val r = v;
+      A.retain(r.buf);
+      return r;
+    }
+    Val o = new_val(v.shape, false);
+    copy_into(v, o, why + " (to row-major)");
+    return o;
+  }
+  void unref(const Val& v) { A.release(v.buf); }
+
+  // ------------------------------------------------------------ node dispatch
+  void plan_node(const Node& n) {
+    const std::string& op = n.op;
+    if (op == "Conv") return plan_conv(n);
+    if (op == "QpcConvT" || op == "ConvTranspose") return plan_convt(n);
+    if (op == "QpcLinear") return plan_linear(n, false);
+    if (op == "QpcCtcHead") return plan_linear(n, true);
+    if (op == "QpcLayerNorm") return plan_layernorm(n);
+    if (op == "BatchNormalization") return plan_bn(n);
+    if (op == "Relu" || op == "Sigmoid" || op == "HardSigmoid" || op == "FusedGelu" ||
+        op == "Erf" || op == "Sqrt" || op == "Clip")
+      return plan_unary(n);
+    if (op == "Add" || op == "Sub" || op == "Mul" || op == "Div" || op == "Pow") return plan_binary(n);
+    if (op == "MulAddScale") return plan_mul_add_scale(n);
+    if (op == "Softmax") return plan_softmax(n);
+    if (op == "GlobalAveragePool") return plan_gap(n);
+    if (op == "AveragePool" || op == "MaxPool") return plan_pool(n);
+    if (op == "Resize") return plan_resize(n);
+    if (op == "Concat") return plan_concat(n);
+    if (op == "Slice") return plan_slice(n);
+    if (op == "Transpose") return plan_transpose(n);
+    if (op == "Reshape" || op == "Squeeze" || op == "Unsqueeze" || op == "Flatten")
+      return plan_reshape(n);
+    if (op == "ReduceMean") return plan_reduce_mean(n);
+    if (op == "MatMul") return plan_matmul(n);
+    if (op == "Identity" || op == "Dropout") {
+      const Val& x = get(n.in[0]);
+      define(n.out[0], view_of(x, x.shape, x.strides, x.off));
+      return;
+    }
+    if (op == "Gather") return plan_gather(n);
+    if (op == "Shape") {
+      const Val& x = get(n.in[0]);
+      auto h = std::make_shared<HostTensor>();
+      h->dtype = QPC_I64;
+      h->shape = {(int64_t)x.shape.size()};
+      h->i = x.shape;
+      Val v;
+      v.is_const = true;
+      v.owned = h;
+      v.ct = h.get();
+      v.shape = h->shape;
+      v.strides = rowmajor_strides(v.shape);
+      define(n.out[0], v);
+      return;
+    }
+    if (op == "Cast") {
+      const Val& x = get(n.in[0]);
+      if (!x.is_const) {
+        Val v = view_of(x, x.shape, x.strides, x.off);  // f32 -> f32 at run time
+        define(n.out[0], v);
+        return;
+      }
+      Val v = x;
+      define(n.out[0], v);
+      return;
+    }
+    throw GraphError{"no planner for op " + op};
+  }
+
+  std::vector<int64_t> const_ints(const std::string& name) {
+    const Val& v = get(name);
+    if (!v.is_const) throw GraphError{"expected a constant for " + name};
+    std::vector<int64_t> r(v.ct->numel());
+    for (int64_t k = 0; k < (int64_t)r.size(); ++k) r[k] = (int64_t)v.ct->scalar(k);
+    return r;
+  }
+
+  // ------------------------------------------------------------ Conv
+  // executor.rs:433-652 / conv.rs:222-715.  Routing:
+  //   depthwise (group == C == M)        -> dwconv (SIMT, bandwidth bound)
+  //   1x1 s1 p0 g1, C % 4 == 0           -> tcgen05 GEMM, rows = pixels
+  //   kxk s1 g1, C % 4 == 0              -> tcgen05 implicit GEMM (4-D TMA)
+  //   anything else                      -> direct SIMT conv
+  void plan_conv(const Node& n) {
+    const Val& x0 = get(n.in[0]);
+    const HostTensor* w = S.weight(n.in[1]);
+    if (x0.shape.size() != 4 || w->shape.size() != 4) throw GraphError{"only 2-D convolutions"};
+    const int64_t N = x0.shape[0], C = x0.shape[1], H = x0.shape[2], W = x0.shape[3];
+    const int64_t M = w->shape[0], cg = w->shape[1], kh = w->shape[2], kw = w->shape[3];
+    const int64_t group = n.geti("group", 1);
+    auto st = n.getints("strides");
+    const int64_t sh = st.size() == 2 ? st[0] : 1, sw = st.size() == 2 ? st[1] : 1;
+    int64_t ph, pw, peh, pew;
+    resolve_pads(n, H, W, kh, kw, sh, sw, &ph, &pw, &peh, &pew);
+    if (group * cg != C || M % group) throw GraphError{"group mismatch"};
+    const int64_t oh = (H + ph + peh - kh) / sh + 1, ow = (W + pw + pew - kw) / sw + 1;
+    if (oh <= 0 || ow <= 0) throw GraphError{"empty conv output"};
+    const std::vector<int64_t> oshape = {N, M, oh, ow};
+    const bool has_bias = n.has_in(2);
+    const float* bias = has_bias ? S.dweight(n.in[2], "raw") : nullptr;
+    const ActParams act = act_of(n);
+    ConvGeom g{(int)N, (int)H, (int)W, (int)C, (int)oh, (int)ow, (int)M, (int)kh, (int)kw,
+               (int)sh, (int)sw, (int)ph, (int)pw};
+    const bool dw = group > 1 && cg == 1 && M == C;
+    const bool pw1 = group == 1 && kh == 1 && kw == 1 && sh == 1 && sw == 1 && ph == 0 && pw == 0 &&
+                     peh == 0 && pew == 0 && (C % 4) == 0;
+    const bool kxk_tc = group == 1 && sh == 1 && sw == 1 && (C % 4) == 0 && !pw1 && kh * kw > 1;
+    const int math = S.math();
+    const double flops = 2.0 * N * oh * ow * M * cg * kh * kw;
+    const double out_bytes = 4.0 * N * oh * ow * M;
+
+    // Residual: plain tensor, or (res_up) the pre-upsample map of a nearest resize.
+    const bool has_res = n.has_in(3);
+    Val res;
+    if (has_res) {
+      const Val& r0 = get(n.in[3]);
+      if (r0.shape != oshape) throw GraphError{"residual shape " + shape_str(r0.shape) + " != " + shape_str(oshape)};
+      res = as_nhwc(r0, n.name + " residual");
+    }
+    Val y = new_val(oshape, true);
+    float* yp = out_ptr(y);
+    const float* rp = has_res ? out_ptr(res) : nullptr;
+    unsigned int* err = device_state(S.device()).err_word;
+    const std::string nm = n.name;
+    if (dw) {
+      Val x = as_nhwc(x0, nm);
+      const float* xp = out_ptr(x);
+      const float* wt = S.dweight(n.in[1], "dw");
+      const double bytes = 4.0 * N * H * W * C + out_bytes + (has_res ? out_bytes : 0);
+      step("dwconv", nm, bytes, flops,
+           [=](cudaStream_t s) { return launch_dwconv_nhwc(xp, wt, bias, rp, yp, g, act, s); });
+      unref(x);
+    } else if (pw1) {
+      Val x = as_nhwc(x0, nm);
+      const float* xp = out_ptr(x);
+      const bool split = math == QPC_MATH_3XTF32;
+      const float* wb = S.dweight(n.in[1], split ? "raw.hi" : "raw");
+      const float* wl = split ? S.dweight(n.in[1], "raw.lo") : nullptr;
+      GemmEpilogue e;
+      e.bias = bias;
+      e.residual = rp;
+      e.out = yp;
+      e.ldo = (int)M;
+      e.ldr = (int)M;
+      e.act = act;
+      const int64_t rows = N * H * W;
+      const double bytes = 4.0 * rows * C + out_bytes + 4.0 * M * C + (has_res ? out_bytes : 0);
+      step("gemm_tc", nm, bytes, flops, [=](cudaStream_t s) {
+        return launch_gemm_tc(xp, rows, (int)C, (int)C, wb, wl, (int)M, e, math, err, s);
+      });
+      unref(x);
+    } else if (kxk_tc) {
+      Val x = as_nhwc(x0, nm);
+      const float* xp = out_ptr(x);
+      const bool split = math == QPC_MATH_3XTF32;
+      const float* wb = S.dweight(n.in[1], split ? "kxk.hi" : "kxk");
+      const float* wl = split ? S.dweight(n.in[1], "kxk.lo") : nullptr;
+      GemmEpilogue e;
+      e.bias = bias;
+      e.residual = rp;
+      e.out = yp;
+      e.ldo = (int)M;
+      e.ldr = (int)M;
+      e.act = act;
+      const double bytes = 4.0 * N * H * W * C + out_bytes + 4.0 * M * C * kh * kw + (has_res ? out_bytes : 0);
+      step("conv_tc", nm, bytes, flops,
+           [=](cudaStream_t s) { return launch_conv_tc(xp, g, wb, wl, e, math, err, s); });
+      unref(x);
+    } else {
+      const bool nchw_in = is_rowmajor(x0) && !x0.is_const && (x0.off % 4) == 0;
+      Val x = nchw_in ? view_of(x0, x0.shape, x0.strides, x0.off) : as_nhwc(x0, nm);
+      const float* xp = out_ptr(x);
+      const float* wr = S.dweight(n.in[1], "raw");
+      const double bytes = 4.0 * N * H * W * C + out_bytes + (has_res ? out_bytes : 0);
+      const int grp = (int)group;
+      step("conv_direct", nm, bytes, flops, [=](cudaStream_t s) {
+        return launch_conv_direct(xp, nchw_in ? 1 : 0, wr, bias, rp, yp, g, grp, act, s);
+      });
+      unref(x);
+    }
+    if (has_res) unref(res);
+    define(n.out[0], y);
+  }
+
+  // ------------------------------------------------------------ ConvTranspose
+  void plan_convt(const Node& n) {
+    const Val& x0 = get(n.in[0]);
+    const HostTensor* w = S.weight(n.in[1]);
+    if (!w || w->shape.size() != 4 || w->shape[2] != 2 || w->shape[3] != 2)
+      throw GraphError{"ConvTranspose: only 2x2 s2 p0"};
+    auto st = n.getints("strides");
+    if (!(st.empty() || (st.size() == 2 && st[0] == 2 && st[1] == 2)))
+      throw GraphError{"ConvTranspose: stride must be 2"};
+    for (auto p : n.getints("pads"))
+      if (p) throw GraphError{"ConvTranspose: pads must be 0"};
+    const int64_t N = x0.shape[0], C = x0.shape[1], H = x0.shape[2], W = x0.shape[3];
+    if (w->shape[0] != C) throw GraphError{"ConvTranspose: weight C_in mismatch"};
+    const int64_t M = w->shape[1];
+    const float* bn_a = nullptr;
+    const float* bn_b = nullptr;
+    if (n.op == "QpcConvT" && n.in.size() >= 6) {
+      // BatchNormalization folded into the epilogue, shape.rs:700-733:
+      // a = scale / sqrt(var + eps); b = fma(-mean, a, bias); y = fma(x, a, b).
+      const HostTensor* sc = S.weight(n.in[2]);
+      const HostTensor* bi = S.weight(n.in[3]);
+      const HostTensor* me = S.weight(n.in[4]);
+      const HostTensor* va = S.weight(n.in[5]);
+      const float eps = n.getf("qpc_eps", 1e-5f);
+      std::vector<float> a(M), b(M);
+      for (int64_t c = 0; c < M; ++c) {
+        a[c] = sc->f[c] / std::sqrt(va->f[c] + eps);
+        b[c] = std::fma(-me->f[c], a[c], bi->f[c]);
+      }
+      bn_a = upload_temp(a);
+      bn_b = upload_temp(b);
+    }
+    Val x = as_nhwc(x0, n.name);
+    Val y = new_val({N, M, 2 * H, 2 * W}, true);
+    const float* xp = out_ptr(x);
+    float* yp = out_ptr(y);
+    const float* wp = S.dweight(n.in[1], "raw");
+    const ActParams act = act_of(n);
+    const double bytes = 4.0 * (N * H * W * C + N * 4 * H * W * M);
+    step("convt2x2", n.name, bytes, 2.0 * N * 4 * H * W * M * C, [=](cudaStream_t s) {
+      return launch_convt2x2(xp, wp, bn_a, bn_b, yp, (int)N, (int)H, (int)W, (int)C, (int)M, act, s);
+    });
+    unref(x);
+    define(n.out[0], y);
+  }
+
+  std::vector<std::unique_ptr<DevBuf>> temps_;
+  const float* upload_temp(const std::vector<float>& v) {
+    auto b = std::make_unique<DevBuf>(std::max<size_t>(v.size(), 1) * sizeof(float));
+    QPC_CUDA_OR_THROW(cudaMemcpy(b->ptr, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+    const float* p = b->f();
+    P.bufs.push_back(std::move(b));
+    return p;
+  }
+
+  // ------------------------------------------------------------ BN (unfused)
+  void plan_bn(const Node& n) {
+    const Val& x0 = get(n.in[0]);
+    if (x0.shape.size() != 4) throw GraphError{"BatchNormalization: 4-D input expected"};
+    const int64_t C = x0.shape[1];
+    const HostTensor* sc = S.weight(n.in[1]);
+    const HostTensor* bi = S.weight(n.in[2]);
+    const HostTensor* me = S.weight(n.in[3]);
+    const HostTensor* va = S.weight(n.in[4]);
+    if (!sc || !bi || !me || !va) throw GraphError{"BatchNormalization: parameters must be initializers"};
+    const float eps = n.getf("epsilon", 1e-5f);
+    std::vector<float> a(C), b(C);
+    for (int64_t c = 0; c < C; ++c) {
+      a[c] = sc->f[c] / std::sqrt(va->f[c] + eps);
+      b[c] = std::fma(-me->f[c], a[c], bi->f[c]);
+    }
+    const float* ap = upload_temp(a);
+    const float* bp = upload_temp(b);
+    Val x = as_nhwc(x0, n.name);
+    Val y = new_val(x0.shape, true);
+    const float* xp = out_ptr(x);
+    float* yp = out_ptr(y);
+    const int64_t total = x0.numel();
+    ActParams act{};
+    step("affine", n.name, 8.0 * total, 2.0 * total,
+         [=](cudaStream_t s) { return launch_affine_nhwc(xp, ap, bp, yp, total, (int)C, act, s); });
+    unref(x);
+    define(n.out[0], y);
+  }
+
+  // ------------------------------------------------------------ elementwise
+  // Output layout: NHWC when a runtime operand of the output's 4-D shape is
+  // NHWC, else row-major.  Strides are given in the output's physical order.
+  StridedDims make_sd(const std::vector<int64_t>& oshape, bool nhwc, const Val* a, const Val* b) {
+    StridedDims sd;
+    const int r = (int)oshape.size();
+    if (r > kMaxDims) throw GraphError{"rank > 6"};
+    sd.rank = r;
+    sd.total = 1;
+    for (auto d : oshape) sd.total *= d;
+    auto ext = [&](const Val* v, std::vector<int64_t>& s) {
+      s.assign(r, 0);
+      if (!v) return;
+      const int rv = (int)v->shape.size();
+      for (int i = 0; i < r; ++i) {
+        const int j = i - (r - rv);
+        if (j < 0) continue;
+        s[i] = (v->shape[j] == 1 && oshape[i] != 1) ? 0 : v->strides[j];
+        if (v->shape[j] == 1) s[i] = 0;
+      }
+    };
+    std::vector<int64_t> s1, s2;
+    ext(a, s1);
+    ext(b, s2);
+    std::vector<int> perm(r);
+    std::iota(perm.begin(), perm.end(), 0);
+    if (nhwc) perm = {0, 2, 3, 1};
+    for (int d = 0; d < r; ++d) {
+      sd.dims[d] = oshape[perm[d]];
+      sd.sa[d] = s1[perm[d]];
+      sd.sb[d] = s2[perm[d]];
+    }
+    return sd;
+  }
+  std::vector<int64_t> bcast(const std::vector<int64_t>& a, const std::vector<int64_t>& b) {
+    const size_t r = std::max(a.size(), b.size());
+    std::vector<int64_t> o(r);
+    for (size_t i = 0; i < r; ++i) {
+      const int64_t da = i + a.size() >= r ? a[i + a.size() - r] : 1;
+      const int64_t db = i + b.size() >= r ? b[i + b.size() - r] : 1;
+      if (da != db && da != 1 && db != 1) throw GraphError{"broadcast mismatch " + shape_str(a) + " vs " + shape_str(b)};
+      o[i] = std::max(da, db);
+    }
+    return o;
+  }
+  bool pick_nhwc(const std::vector<int64_t>& oshape, const Val& a, const Val* b) {
+    if (oshape.size() != 4) return false;
+    if (!a.is_const && a.shape == oshape && is_nhwc(a)) return true;
+    if (b && !b->is_const && b->shape == oshape && is_nhwc(*b)) return true;
+    return false;
+  }
+  // A device pointer + view for any operand (constants are uploaded raw).
+  Val operand(const std::string& name) {
+    const Val& v = get(name);
+    if (!v.is_const) return v;
+    Val c = v;
+    c.cptr = S.dweight(name, "raw");
+    return c;
+  }
+  const float* optr(const Val& v) { return v.cptr ? v.cptr + v.off : A.ptr(v.buf) + v.off; }
+
+  void plan_unary(const Node& n) {
+    Val x = operand(n.in[0]);
+    ActParams act{};
+    const std::string& op = n.op;
+    if (op == "Relu") act.kind = ACT_RELU;
+    else if (op == "Sigmoid") act.kind = ACT_SIGMOID;
+    else if (op == "HardSigmoid") {
+      act.kind = ACT_HARDSIGMOID;
+      act.alpha = n.getf("alpha", 0.2f);
+      act.beta = n.getf("beta", 0.5f);
+    } else if (op == "FusedGelu") {
+      act.kind = ACT_GELU;
+      act.c1 = n.getf("c1", 1.4142135f);
+      act.c2 = n.getf("c2", 1.0f);
+      act.c3 = n.getf("c3", 0.5f);
+    } else if (op == "Sqrt") act.kind = 100;
+    else if (op == "Erf") act.kind = 102;
+    else if (op == "Clip") {
+      act.kind = 101;
+      act.alpha = n.getf("min", -3.4e38f);
+      act.beta = n.getf("max", 3.4e38f);
+      if (n.has_in(1)) act.alpha = (float)get(n.in[1]).ct->scalar();
+      if (n.has_in(2)) act.beta = (float)get(n.in[2]).ct->scalar();
+    }
+    const bool nhwc = pick_nhwc(x.shape, x, nullptr);
+    Val y = new_val(x.shape, nhwc);
+    StridedDims sd = make_sd(x.shape, nhwc, &x, nullptr);
+    const float* xp = optr(x);
+    float* yp = out_ptr(y);
+    step("unary", n.name, 8.0 * sd.total, sd.total, [=](cudaStream_t s) { return launch_unary(xp, yp, sd, act, s); });
+    define(n.out[0], y);
+  }
+
+  void plan_binary(const Node& n) {
+    Val a = operand(n.in[0]);
+    Val b = operand(n.in[1]);
+    int op = 0;
+    if (n.op == "Sub") op = 1;
+    else if (n.op == "Mul") op = 2;
+    else if (n.op == "Div") op = 3;
+    else if (n.op == "Pow") op = 4;
+    const auto oshape = bcast(a.shape, b.shape);
+    const bool nhwc = pick_nhwc(oshape, a, &b);
+    Val y = new_val(oshape, nhwc);
+    StridedDims sd = make_sd(oshape, nhwc, &a, &b);
+    const float* ap = optr(a);
+    const float* bp = optr(b);
+    float* yp = out_ptr(y);
+    ActParams post{};
+    step("binary", n.name, 12.0 * sd.total, sd.total,
+         [=](cudaStream_t s) { return launch_binary(ap, bp, yp, sd, op, post, s); });
+    define(n.out[0], y);
+  }
+
+  // executor.rs:808-884 MulAddScale: per-channel gate fast path, else Mul then Add.
+  void plan_mul_add_scale(const Node& n) {
+    Val f = operand(n.in[0]);
+    Val g = operand(n.in[1]);
+    Val r = operand(n.in[2]);
+    if (f.shape.size() == 4 && r.shape == f.shape && !f.is_const && !r.is_const && !g.is_const &&
+        (g.numel() == f.shape[1] || g.numel() == f.shape[0] * f.shape[1]) && is_rowmajor(g)) {
+      Val fx = as_nhwc(f, n.name);
+      Val rx = as_nhwc(r, n.name);
+      Val y = new_val(f.shape, true);
+      const float* fp = out_ptr(fx);
+      const float* gp = optr(g);
+      const float* rp = out_ptr(rx);
+      float* yp = out_ptr(y);
+      const int64_t total = f.numel();
+      const int hw = (int)(f.shape[2] * f.shape[3]), c = (int)f.shape[1];
+      const int per_n = g.numel() != f.shape[1] ? 1 : 0;
+      step("mul_add_scale", n.name, 12.0 * total, 2.0 * total,
+           [=](cudaStream_t s) { return launch_mul_add_scale_nhwc(fp, gp, rp, yp, total, hw, c, per_n, s); });
+      unref(fx);
+      unref(rx);
+      define(n.out[0], y);
+      return;
+    }
+    // generic: t = f * g ; y = t + r (two roundings, elementwise.rs:134-181)
+    const auto s1 = bcast(f.shape, g.shape);
+    const bool nh1 = pick_nhwc(s1, f, &g);
+    Val t = new_val(s1, nh1);
+    {
+      StridedDims sd = make_sd(s1, nh1, &f, &g);
+      const float* fp = optr(f);
+      const float* gp = optr(g);
+      float* tp = out_ptr(t);
+      ActParams post{};
+      step("binary", n.name + "/mul", 12.0 * sd.total, sd.total,
+           [=](cudaStream_t s) { return launch_binary(fp, gp, tp, sd, 2, post, s); });
+    }
+    const auto s2 = bcast(s1, r.shape);
+    const bool nh2 = pick_nhwc(s2, t, &r);
+    Val y = new_val(s2, nh2);
+    {
+      StridedDims sd = make_sd(s2, nh2, &t, &r);
+      const float* tp = out_ptr(t);
+      const float* rp = optr(r);
+      float* yp = out_ptr(y);
+      ActParams post{};
+      step("binary", n.name + "/add", 12.0 * sd.total, sd.total,
+           [=](cudaStream_t s) { return launch_binary(tp, rp, yp, sd, 0, post, s); });
+    }
+    unref(t);
+    define(n.out[0], y);
+  }
+
+  // ------------------------------------------------------------ LayerNorm
+  void plan_layernorm(const Node& n) {
+    const Val& x0 = get(n.in[0]);
+    Val x = as_rowmajor(x0, n.name);
+    const int64_t C = x.shape.back();
+    const int64_t rows = x.numel() / C;
+    Val y = new_val(x.shape, false);
+    const float* xp = out_ptr(x);
+    float* yp = out_ptr(y);
+    const float* gp = n.has_in(1) ? S.dweight(n.in[1], "raw") : nullptr;
+    const float* bp = n.has_in(2) ? S.dweight(n.in[2], "raw") : nullptr;
+    const float eps = n.getf("qpc_eps", 1e-5f);
+    step("layernorm", n.name, 8.0 * x.numel(), 8.0 * x.numel(),
+         [=](cudaStream_t s) { return launch_layernorm(xp, gp, bp, yp, rows, (int)C, eps, s); });
+    unref(x);
+    define(n.out[0], y);
+  }
+
+  // ------------------------------------------------------------ Linear / head
+  // QpcLinear(x[..., K], W[K, N], b?, residual?) on the tensor-core GEMM.
+  // QpcCtcHead: the same GEMM followed by the row argmax exit.
+  void plan_linear(const Node& n, bool head) {
+    const Val& x0 = get(n.in[0]);
+    const HostTensor* w = S.weight(n.in[1]);
+    const int64_t K = w->shape[0], Nn = w->shape[1];
+    if (x0.shape.empty() || x0.shape.back() != K) throw GraphError{"MatMul inner dim mismatch"};
+    Val x = as_rowmajor(x0, n.name);
+    const int64_t rows = x.numel() / K;
+    std::vector<int64_t> oshape = x.shape;
+    oshape.back() = Nn;
+    const int math = S.math();
+    const bool split = math == QPC_MATH_3XTF32;
+    const float* wb = S.dweight(n.in[1], split ? "nk.hi" : "nk");
+    const float* wl = split ? S.dweight(n.in[1], "nk.lo") : nullptr;
+    const float* bias = n.has_in(2) ? S.dweight(n.in[2], "raw") : nullptr;
+    Val res;
+    const bool has_res = n.has_in(3);
+    if (has_res) {
+      const Val& r0 = get(n.in[3]);
+      if (r0.shape != oshape) throw GraphError{"residual shape mismatch"};
+      res = as_rowmajor(r0, n.name + " residual");
+    }
+    unsigned int* err = device_state(S.device()).err_word;
+    const double flops = 2.0 * rows * K * Nn;
+    Val y = new_val(oshape, false);
+    GemmEpilogue e;
+    e.bias = bias;
+    e.residual = has_res ? out_ptr(res) : nullptr;
+    e.out = out_ptr(y);
+    e.ldo = (int)Nn;
+    e.ldr = (int)Nn;
+    e.act = act_of(n);
+    const float* xp = out_ptr(x);
+    step(head ? "head_gemm" : "gemm_tc", n.name, 4.0 * (rows * K + rows * Nn + K * Nn), flops,
+         [=](cudaStream_t s) { return launch_gemm_tc(xp, rows, (int)K, (int)K, wb, wl, (int)Nn, e, math, err, s); });
+    unref(x);
+    if (has_res) unref(res);
+    if (!head) {
+      define(n.out[0], y);
+      return;
+    }
+    // argmax exit: (val = softmax prob of the first strict max, idx bits)
+    std::vector<int64_t> pshape = oshape;
+    pshape.back() = 2;
+    Val pr = new_val(pshape, false);
+    const float* lp = out_ptr(y);
+    float* pp = out_ptr(pr);
+    step("head_argmax", n.name, 4.0 * rows * Nn, 3.0 * rows * Nn,
+         [=](cudaStream_t s) { return launch_softmax_argmax(lp, pp, rows, (int)Nn, s); });
+    unref(y);
+    define(n.out[0], pr);
+  }
+
+  // ------------------------------------------------------------ Softmax
+  void plan_softmax(const Node& n) {
+    const Val& x0 = get(n.in[0]);
+    int64_t axis = n.geti("axis", -1);
+    if (axis < 0) axis += (int64_t)x0.shape.size();
+    if (axis != (int64_t)x0.shape.size() - 1) throw GraphError{"Softmax: only the last axis"};
+    Val x = as_rowmajor(x0, n.name);
+    const int64_t inner = x.shape.back(), rows = x.numel() / inner;
+    const bool exit_here = S.argmax_exit() &&
+        std::find(S.graph_outputs().begin(), S.graph_outputs().end(), n.out[0]) != S.graph_outputs().end();
+    const float* xp = out_ptr(x);
+    if (exit_here) {
+      std::vector<int64_t> pshape = x.shape;
+      pshape.back() = 2;
+      Val pr = new_val(pshape, false);
+      float* pp = out_ptr(pr);
+      step("head_argmax", n.name, 4.0 * rows * inner, 3.0 * rows * inner,
+           [=](cudaStream_t s) { return launch_softmax_argmax(xp, pp, rows, (int)inner, s); });
+      unref(x);
+      define(n.out[0], pr);
+      return;
+    }
+    Val y = new_val(x.shape, false);
+    float* yp = out_ptr(y);
+    step("softmax", n.name, 8.0 * x.numel(), 4.0 * x.numel(),
+         [=](cudaStream_t s) { return launch_softmax_rows(xp, yp, rows, (int)inner, s); });
+    unref(x);
+    define(n.out[0], y);
+  }
+
+  // ------------------------------------------------------------ pooling
+  void plan_gap(const Node& n) {
+    const Val& x0 = get(n.in[0]);
+    Val x = as_nhwc(x0, n.name);
+    const int64_t N = x.shape[0], C = x.shape[1], HW = x.shape[2] * x.shape[3];
+    Val y = new_val({N, C, 1, 1}, true);
+    const float* xp = out_ptr(x);
+    float* yp = out_ptr(y);
+    step("gap", n.name, 4.0 * (N * C * HW + N * C), N * C * HW,
+         [=](cudaStream_t s) { return launch_gap_nhwc(xp, yp, (int)N, (int)HW, (int)C, s); });
+    unref(x);
+    define(n.out[0], y);
+  }
+
+  void plan_pool(const Node& n) {
+    const Val& x0 = get(n.in[0]);
+    auto ks = n.getints("kernel_shape");
+    if (ks.size() != 2) throw GraphError{"kernel_shape required"};
+    auto st = n.getints("strides");
+    const int64_t sh = st.size() == 2 ? st[0] : 1, sw = st.size() == 2 ? st[1] : 1;
+    const int64_t N = x0.shape[0], C = x0.shape[1], H = x0.shape[2], W = x0.shape[3];
+    int64_t ph, pw, peh, pew;
+    resolve_pads(n, H, W, ks[0], ks[1], sh, sw, &ph, &pw, &peh, &pew);
+    const int64_t oh = (H + ph + peh - ks[0]) / sh + 1, ow = (W + pw + pew - ks[1]) / sw + 1;
+    Val x = as_nhwc(x0, n.name);
+    Val y = new_val({N, C, oh, ow}, true);
+    const float* xp = out_ptr(x);
+    float* yp = out_ptr(y);
+    const int is_max = n.op == "MaxPool";
+    step("pool2d", n.name, 4.0 * (N * C * H * W + N * C * oh * ow), N * C * oh * ow * ks[0] * ks[1],
+         [=](cudaStream_t s) {
+           return launch_pool2d_nhwc(xp, yp, (int)N, (int)H, (int)W, (int)C, (int)oh, (int)ow,
+                                     (int)ks[0], (int)ks[1], (int)sh, (int)sw, (int)ph, (int)pw,
+                                     is_max, s);
+         });
+    unref(x);
+    define(n.out[0], y);
+  }
+
+  // executor.rs:1070-1183 Resize (nearest): sizes (inputs[3]) or scales (inputs[2]).
+  void plan_resize(const Node& n) {
+    const Val& x0 = get(n.in[0]);
+    int64_t oh, ow;
+    if (n.has_in(3)) {
+      auto sz = const_ints(n.in[3]);
+      oh = sz[sz.size() - 2];
+      ow = sz[sz.size() - 1];
+    } else if (n.has_in(2)) {
+      const Val& sc = get(n.in[2]);
+      const float s_h = (float)sc.ct->scalar(sc.ct->numel() - 2);
+      const float s_w = (float)sc.ct->scalar(sc.ct->numel() - 1);
+      oh = (int64_t)((float)x0.shape[2] * s_h);
+      ow = (int64_t)((float)x0.shape[3] * s_w);
+    } else {
+      throw GraphError{"Resize: no scales/sizes"};
+    }
+    const int64_t N = x0.shape[0], C = x0.shape[1], H = x0.shape[2], W = x0.shape[3];
+    Val x = as_nhwc(x0, n.name);
+    Val y = new_val({N, C, oh, ow}, true);
+    const float* xp = out_ptr(x);
+    float* yp = out_ptr(y);
+    if (C % 4) throw GraphError{"Resize: C % 4 != 0 unsupported"};
+    step("resize", n.name, 4.0 * (N * C * H * W + N * C * oh * ow), 0, [=](cudaStream_t s) {
+      return launch_resize_nearest_nhwc(xp, yp, (int)N, (int)H, (int)W, (int)C, (int)oh, (int)ow,
+                                        (int)C, 0, s);
+    });
+    unref(x);
+    define(n.out[0], y);
+  }
+
+  // ------------------------------------------------------------ Concat
+  void plan_concat(const Node& n) {
+    std::vector<Val> parts;
+    for (auto& nm : n.in) parts.push_back(operand(nm));
+    const int64_t r = (int64_t)parts[0].shape.size();
+    int64_t axis = n.geti("axis", 0);
+    if (axis < 0) axis += r;
+    std::vector<int64_t> oshape = parts[0].shape;
+    oshape[axis] = 0;
+    for (auto& p : parts) {
+      if ((int64_t)p.shape.size() != r) throw GraphError{"Concat rank mismatch"};
+      oshape[axis] += p.shape[axis];
+    }
+    const bool nhwc = r == 4 && axis == 1;
+    Val y = new_val(oshape, nhwc);
+    int64_t off = 0;
+    for (size_t k = 0; k < parts.size(); ++k) {
+      const Val& p = parts[k];
+      if (p.is_const) throw GraphError{"Concat of a constant"};
+      Val dst;
+      dst.shape = p.shape;
+      dst.strides = y.strides;
+      dst.buf = y.buf;
+      dst.off = y.off + off * y.strides[axis];
+      copy_into(p, dst, n.name + "/part" + std::to_string(k));
+      off += p.shape[axis];
+    }
+    define(n.out[0], y);
+  }
+
+  // ------------------------------------------------------------ views
+  void plan_transpose(const Node& n) {
+    const Val& x = get(n.in[0]);
+    auto perm = n.getints("perm");
+    const size_t r = x.shape.size();
+    if (perm.empty()) {
+      perm.resize(r);
+      for (size_t i = 0; i < r; ++i) perm[i] = (int64_t)(r - 1 - i);
+    }
+    std::vector<int64_t> s(r), st(r);
+    for (size_t i = 0; i < r; ++i) {
+      s[i] = x.shape[perm[i]];
+      st[i] = x.strides[perm[i]];
+    }
+    if (x.is_const) throw GraphError{"Transpose of a constant"};
+    define(n.out[0], view_of(x, s, st, x.off));
+  }
+
+  // Try to express `shape` as a strided view of `x` without copying
+  // (merging / splitting dims whose strides are compatible).
+  bool reshape_view(const Val& x, const std::vector<int64_t>& shape, std::vector<int64_t>* out) {
+    // drop size-1 dims of the source
+    std::vector<int64_t> os, ost;
+    for (size_t i = 0; i < x.shape.size(); ++i)
+      if (x.shape[i] != 1) {
+        os.push_back(x.shape[i]);
+        ost.push_back(x.strides[i]);
+      }
+    out->assign(shape.size(), 0);
+    size_t oi = 0, ni = 0;
+    const size_t on = os.size(), nn = shape.size();
+    while (ni < nn && shape[ni] == 1) (*out)[ni++] = 0;
+    while (oi < on && ni < nn) {
+      // group source dims [oi, oj) and target dims [ni, nj) with equal products
+      int64_t np = shape[ni], op = os[oi];
+      size_t oj = oi + 1, nj = ni + 1;
+      while (np != op) {
+        if (np < op) {
+          if (nj >= nn) return false;
+          np *= shape[nj++];
+        } else {
+          if (oj >= on) return false;
+          op *= os[oj++];
+        }
+      }
+      for (size_t k = oi; k + 1 < oj; ++k)
+        if (ost[k] != ost[k + 1] * os[k + 1]) return false;  // source group must be contiguous
+      (*out)[nj - 1] = ost[oj - 1];
+      for (size_t k = nj - 1; k > ni; --k) (*out)[k - 1] = (*out)[k] * shape[k];
+      oi = oj;
+      ni = nj;
+      while (ni < nn && shape[ni] == 1) (*out)[ni++] = 0;
+    }
+    return oi == on && ni == nn;
+  }
+
+  void plan_reshape(const Node& n) {
+    const Val& x = get(n.in[0]);
+    std::vector<int64_t> shape;
+    const int64_t total = x.numel();
+    if (n.op == "Reshape") {
+      auto req = const_ints(n.in[1]);
+      int64_t known = 1, infer = -1;
+      for (size_t i = 0; i < req.size(); ++i) {
+        int64_t d = req[i];
+        if (d == 0 && n.geti("allowzero", 0) == 0) d = x.shape[i];
+        if (d == -1) {
+          infer = (int64_t)i;
+          shape.push_back(1);
+        } else {
+          shape.push_back(d);
+          known *= d;
+        }
+      }
+      if (infer >= 0) shape[infer] = known ? total / known : 0;
+    } else if (n.op == "Flatten") {
+      int64_t axis = n.geti("axis", 1);
+      if (axis < 0) axis += (int64_t)x.shape.size();
+      int64_t a = 1, b = 1;
+      for (int64_t i = 0; i < (int64_t)x.shape.size(); ++i) (i < axis ? a : b) *= x.shape[i];
+      shape = {a, b};
+    } else if (n.op == "Squeeze") {
+      auto axes = n.getints("axes");
+      if (axes.empty() && n.has_in(1)) axes = const_ints(n.in[1]);
+      const int64_t r = (int64_t)x.shape.size();
+      for (auto& a : axes)
+        if (a < 0) a += r;
+      for (int64_t i = 0; i < r; ++i) {
+        const bool sq = axes.empty() ? x.shape[i] == 1 : std::count(axes.begin(), axes.end(), i) > 0;
+        if (!sq) shape.push_back(x.shape[i]);
+      }
+    } else {  // Unsqueeze
+      auto axes = n.getints("axes");
+      if (axes.empty() && n.has_in(1)) axes = const_ints(n.in[1]);
+      const int64_t r = (int64_t)x.shape.size() + (int64_t)axes.size();
+      for (auto& a : axes)
+        if (a < 0) a += r;
+      size_t k = 0;
+      for (int64_t i = 0; i < r; ++i) {
+        if (std::count(axes.begin(), axes.end(), i)) shape.push_back(1);
+        else shape.push_back(x.shape[k++]);
+      }
+    }
+    int64_t chk = 1;
+    for (auto d : shape) chk *= d;
+    if (chk != total) throw GraphError{"reshape numel mismatch " + shape_str(x.shape) + " -> " + shape_str(shape)};
+    if (x.is_const) {
+      Val v = x;
+      auto h = std::make_shared<HostTensor>(*x.ct);
+      h->shape = shape;
+      v.owned = h;
+      v.ct = h.get();
+      v.shape = shape;
+      v.strides = rowmajor_strides(shape);
+      define(n.out[0], v);
+      return;
+    }
+    std::vector<int64_t> st;
+    if (reshape_view(x, shape, &st)) {
+      define(n.out[0], view_of(x, shape, st, x.off));
+      return;
+    }
+    Val c = as_rowmajor(x, n.name);
+    Val v = view_of(c, shape, rowmajor_strides(shape), c.off);
+    unref(c);
+    define(n.out[0], v);
+  }
+
+  void plan_slice(const Node& n) {
+    const Val& x = get(n.in[0]);
+    const int64_t r = (int64_t)x.shape.size();
+    std::vector<int64_t> starts, ends, axes, steps;
+    if (n.has_in(1)) {
+      starts = const_ints(n.in[1]);
+      ends = const_ints(n.in[2]);
+      if (n.has_in(3)) axes = const_ints(n.in[3]);
+      if (n.has_in(4)) steps = const_ints(n.in[4]);
+    } else {
+      starts = n.getints("starts");
+      ends = n.getints("ends");
+      axes = n.getints("axes");
+    }
+    if (axes.empty())
+      for (size_t i = 0; i < starts.size(); ++i) axes.push_back((int64_t)i);
+    if (steps.empty()) steps.assign(starts.size(), 1);
+    std::vector<int64_t> shape = x.shape, st = x.strides;
+    int64_t off = x.off;
+    for (size_t k = 0; k < starts.size(); ++k) {
+      int64_t a = axes[k] < 0 ? axes[k] + r : axes[k];
+      const int64_t dim = x.shape[a], step_ = steps[k];
+      if (step_ <= 0) throw GraphError{"Slice: only positive steps"};
+      int64_t s0 = starts[k] < 0 ? starts[k] + dim : starts[k];
+      int64_t e0 = ends[k] < 0 ? ends[k] + dim : ends[k];
+      s0 = std::clamp<int64_t>(s0, 0, dim);
+      e0 = std::clamp<int64_t>(e0, 0, dim);
+      const int64_t cnt = e0 > s0 ? (e0 - s0 + step_ - 1) / step_ : 0;
+      off += s0 * x.strides[a];
+      shape[a] = cnt;
+      st[a] = x.strides[a] * step_;
+    }
+    if (x.is_const) throw GraphError{"Slice of a constant"};
+    define(n.out[0], view_of(x, shape, st, off));
+  }
+
+  void plan_gather(const Node& n) {
+    const Val& x = get(n.in[0]);
+    const Val& idx = get(n.in[1]);
+    if (!idx.is_const || idx.ct->numel() != 1 || !idx.shape.empty())
+      throw GraphError{"Gather: only a scalar constant index"};
+    const int64_t r = (int64_t)x.shape.size();
+    int64_t axis = n.geti("axis", 0);
+    if (axis < 0) axis += r;
+    int64_t k = (int64_t)idx.ct->scalar();
+    if (k < 0) k += x.shape[axis];
+    std::vector<int64_t> shape, st;
+    for (int64_t i = 0; i < r; ++i)
+      if (i != axis) {
+        shape.push_back(x.shape[i]);
+        st.push_back(x.strides[i]);
+      }
+    if (x.is_const) throw GraphError{"Gather of a constant"};
+    define(n.out[0], view_of(x, shape, st, x.off + k * x.strides[axis]));
+  }
+
+  // shape.rs:510-566 (contiguous reduced axes, f64 sums).
+  void plan_reduce_mean(const Node& n) {
+    const Val& x0 = get(n.in[0]);
+    std::vector<int64_t> axes = n.getints("axes");
+    if (axes.empty() && n.has_in(1)) axes = const_ints(n.in[1]);
+    const int64_t r = (int64_t)x0.shape.size();
+    std::vector<bool> red(r, axes.empty());
+    for (auto a : axes) red[a < 0 ? a + r : a] = true;
+    int64_t outer = 1, mid = 1, inner = 1;
+    int state = 0;
+    for (int64_t i = 0; i < r; ++i) {
+      if (red[i]) {
+        if (state == 2) throw GraphError{"ReduceMean: non-contiguous axes"};
+        mid *= x0.shape[i];
+        state = 1;
+      } else if (state == 0) outer *= x0.shape[i];
+      else {
+        inner *= x0.shape[i];
+        state = 2;
+      }
+    }
+    const bool keep = n.geti("keepdims", 1) != 0;
+    std::vector<int64_t> shape;
+    for (int64_t i = 0; i < r; ++i) {
+      if (!red[i]) shape.push_back(x0.shape[i]);
+      else if (keep) shape.push_back(1);
+    }
+    Val x = as_rowmajor(x0, n.name);
+    Val y = new_val(shape, false);
+    const float* xp = out_ptr(x);
+    float* yp = out_ptr(y);
+    step("reduce_mean", n.name, 4.0 * (x.numel() + y.numel()), x.numel(),
+         [=](cudaStream_t s) { return launch_reduce_mean(xp, yp, outer, mid, inner, s); });
+    unref(x);
+    define(n.out[0], y);
+  }
+
+  // MatMul with a runtime B (attention) or a constant B the GEMM cannot take:
+  // shape.rs:669-697 row outer product, strided operands, up to 2 batch dims.
+  void plan_matmul(const Node& n) {
+    Val a = operand(n.in[0]);
+    Val b = operand(n.in[1]);
+    if (a.shape.size() < 2 || b.shape.size() < 2) throw GraphError{"MatMul rank < 2"};
+    const int ra = (int)a.shape.size(), rb = (int)b.shape.size();
+    const int64_t M = a.shape[ra - 2], K = a.shape[ra - 1], K2 = b.shape[rb - 2], Nn = b.shape[rb - 1];
+    if (K != K2) throw GraphError{"MatMul inner dim mismatch"};
+    std::vector<int64_t> ba(a.shape.begin(), a.shape.end() - 2), bb(b.shape.begin(), b.shape.end() - 2);
+    auto bs = bcast(ba, bb);
+    if (bs.size() > 2) throw GraphError{"MatMul: more than 2 batch dims"};
+    while (bs.size() < 2) bs.insert(bs.begin(), 1);
+    auto bstride = [&](const Val& v, int rv, int which) -> int64_t {
+      // stride of batch dim `which` (0/1 of the 2-dim padded batch) in v
+      const int nb = rv - 2;
+      const int j = which - (2 - nb);
+      if (j < 0) return 0;
+      return v.shape[j] == 1 ? 0 : v.strides[j];
+    };
+    BmmDims d;
+    d.nb0 = (int)bs[0];
+    d.nb1 = (int)bs[1];
+    d.m = (int)M;
+    d.n = (int)Nn;
+    d.k = (int)K;
+    d.sa0 = bstride(a, ra, 0);
+    d.sa1 = bstride(a, ra, 1);
+    d.sam = a.strides[ra - 2];
+    d.sak = a.strides[ra - 1];
+    d.sb0 = bstride(b, rb, 0);
+    d.sb1 = bstride(b, rb, 1);
+    d.sbk = b.strides[rb - 2];
+    d.sbn = b.strides[rb - 1];
+    std::vector<int64_t> oshape;
+    for (size_t i = 0; i < std::max(ba.size(), bb.size()); ++i) oshape.push_back(bs[2 - std::max(ba.size(), bb.size()) + i]);
+    oshape.push_back(M);
+    oshape.push_back(Nn);
+    Val y = new_val(oshape, false);
+    const float* ap = optr(a);
+    const float* bp = optr(b);
+    float* yp = out_ptr(y);
+    const double flops = 2.0 * d.nb0 * d.nb1 * M * Nn * K;
+    step("bmm_small", n.name, 4.0 * (a.numel() + b.numel() + y.numel()), flops,
+         [=](cudaStream_t s) { return launch_bmm_small(ap, bp, yp, d, s); });
+    define(n.out[0], y);
+  }
+};
+
+// ================================================================ plans / runs
+static std::string shape_key(const qpc_tensor* in, int n) {
+  std::ostringstream o;
+  for (int k = 0; k < n; ++k) {
+    o << (in[k].name ? in[k].name : "") << ":";
+    for (int d = 0; d < in[k].rank; ++d) o << in[k].shape[d] << "x";
+    o << ";";
+  }
+  return o.str();
+}
+
+std::unique_ptr<PlanInstance> Session::build(const qpc_tensor* inputs, int n, const std::string& key) {
+  device_state(device_);
+  auto p = std::make_unique<PlanInstance>();
+  p->key = key;
+  QPC_CUDA_OR_THROW(cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking));
+  for (auto& e : p->ev) QPC_CUDA_OR_THROW(cudaEventCreate(&e));
+  {
+    Planner pl(*this, *p);
+    pl.run(inputs, n);
+  }
+  for (auto& io : p->ins)
+    QPC_CUDA_OR_THROW(cudaHostAlloc((void**)&io.host, std::max<int64_t>(io.count, 1) * sizeof(float), cudaHostAllocDefault));
+  for (auto& io : p->outs)
+    QPC_CUDA_OR_THROW(cudaHostAlloc((void**)&io.host, std::max<int64_t>(io.count, 1) * sizeof(float), cudaHostAllocDefault));
+  // Eager validation pass (sets kernel attributes, surfaces launch errors).
+  for (size_t k = 0; k < p->steps.size(); ++k) {
+    cudaError_t e = p->steps[k](p->stream);
+    if (e != cudaSuccess)
+      throw DeviceError{"launch of step " + std::to_string(k) + " (" + p->info[k].kernel + " " +
+                        p->info[k].node + "): " + cudaGetErrorString(e)};
+  }
+  QPC_CUDA_OR_THROW(cudaStreamSynchronize(p->stream));
+  if (unsigned kerr = take_kernel_error(device_))
+    throw DeviceError{"kernel wait timeout during plan validation (flags " + std::to_string(kerr) + ")"};
+  if (opts_.use_cuda_graph) {
+    cudaGraph_t graph = nullptr;
+    QPC_CUDA_OR_THROW(cudaStreamBeginCapture(p->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t cap_err = cudaSuccess;
+    for (size_t k = 0; k < p->steps.size() && cap_err == cudaSuccess; ++k) cap_err = p->steps[k](p->stream);
+    cudaError_t end_err = cudaStreamEndCapture(p->stream, &graph);
+    if (cap_err != cudaSuccess || end_err != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      throw DeviceError{std::string("CUDA graph capture failed: ") +
+                        cudaGetErrorString(cap_err != cudaSuccess ? cap_err : end_err)};
+    }
+    cudaError_t ie = cudaGraphInstantiate(&p->exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) throw DeviceError{std::string("cudaGraphInstantiate: ") + cudaGetErrorString(ie)};
+  }
+  return p;
+}
+
+PlanInstance* Session::acquire(const qpc_tensor* inputs, int n) {
+  const std::string key = shape_key(inputs, n);
+  std::lock_guard<std::mutex> lk(mu_);
+  auto& vec = plans_[key];
+  for (auto& p : vec) {
+    bool expect = false;
+    if (p->busy.compare_exchange_strong(expect, true)) {
+      p->last_used = ++tick_;
+      return p.get();
+    }
+  }
+  // Evict idle plans oldest-first while over budget (vulkan/session.rs:369-395).
+  auto total = [&] {
+    size_t t = 0;
+    for (auto& kv : plans_)
+      for (auto& p : kv.second) t += p->bytes;
+    return t;
+  };
+  while (total() > (size_t)opts_.plan_budget_bytes) {
+    PlanInstance* oldest = nullptr;
+    std::string okey;
+    for (auto& kv : plans_)
+      for (auto& p : kv.second)
+        if (!p->busy && (!oldest || p->last_used < oldest->last_used)) {
+          oldest = p.get();
+          okey = kv.first;
+        }
+    if (!oldest) break;
+    auto& v = plans_[okey];
+    v.erase(std::remove_if(v.begin(), v.end(), [&](auto& q) { return q.get() == oldest; }), v.end());
+  }
+  auto p = build(inputs, n, key);
+  p->busy = true;
+  p->last_used = ++tick_;
+  PlanInstance* raw = p.get();
+  plans_[key].push_back(std::move(p));
+  return raw;
+}
+
+void Session::release(PlanInstance* p) {
+  if (p) p->busy = false;
+}
+
+PlanInstance* Session::launch(const qpc_tensor* inputs, int n) {
+  device_state(device_);
+  PlanInstance* p = acquire(inputs, n);
+  try {
+    QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[0], p->stream));
+    for (auto& io : p->ins) {
+      const qpc_tensor* t = nullptr;
+      for (int k = 0; k < n; ++k)
+        if (io.name == inputs[k].name) t = &inputs[k];
+      std::memcpy(io.host, t->data, io.count * sizeof(float));
+      QPC_CUDA_OR_THROW(cudaMemcpyAsync(io.dev, io.host, io.count * sizeof(float), cudaMemcpyHostToDevice, p->stream));
+    }
+    QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[1], p->stream));
+    if (p->exec) {
+      QPC_CUDA_OR_THROW(cudaGraphLaunch(p->exec, p->stream));
+    } else {
+      for (size_t k = 0; k < p->steps.size(); ++k) QPC_CUDA_OR_THROW(p->steps[k](p->stream));
+    }
+    QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[2], p->stream));
+    for (auto& io : p->outs)
+      QPC_CUDA_OR_THROW(cudaMemcpyAsync(io.host, io.dev, io.count * sizeof(float), cudaMemcpyDeviceToHost, p->stream));
+    QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[3], p->stream));
+  } catch (...) {
+    release(p);
+    throw;
+  }
+  return p;
+}
+
+// Stage inputs once, then replay the compute graph `iters` times back to back;
+// returns device ms per replay (CUDA events on the plan's stream).
+float Session::replay(const qpc_tensor* inputs, int n, int iters) {
+  PlanInstance* p = launch(inputs, n);
+  float ms = 0.f;
+  try {
+    QPC_CUDA_OR_THROW(cudaStreamSynchronize(p->stream));
+    QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[1], p->stream));
+    for (int it = 0; it < iters; ++it) {
+      if (p->exec) QPC_CUDA_OR_THROW(cudaGraphLaunch(p->exec, p->stream));
+      else
+        for (auto& s : p->steps) QPC_CUDA_OR_THROW(s(p->stream));
+    }
+    QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[2], p->stream));
+    QPC_CUDA_OR_THROW(cudaEventSynchronize(p->ev[2]));
+    QPC_CUDA_OR_THROW(cudaEventElapsedTime(&ms, p->ev[1], p->ev[2]));
+    if (unsigned kerr = take_kernel_error(device_))
+      throw DeviceError{"kernel wait timeout (flags " + std::to_string(kerr) + ")"};
+  } catch (...) {
+    release(p);
+    throw;
+  }
+  release(p);
+  return iters > 0 ? ms / iters : 0.f;
+}
+
+// Per-step device times: each step run eagerly between two events, averaged
+// over `iters` passes (QPPOCR_GPU_PROF analogue, vulkan/session.rs:2073-2139).
+void Session::profile(const qpc_tensor* inputs, int n, int iters) {
+  PlanInstance* p = launch(inputs, n);
+  try {
+    QPC_CUDA_OR_THROW(cudaStreamSynchronize(p->stream));
+    const size_t ns = p->steps.size();
+    std::vector<cudaEvent_t> evs(ns + 1);
+    for (auto& e : evs) QPC_CUDA_OR_THROW(cudaEventCreate(&e));
+    std::vector<double> acc(ns, 0.0);
+    for (int it = 0; it < iters; ++it) {
+      QPC_CUDA_OR_THROW(cudaEventRecord(evs[0], p->stream));
+      for (size_t k = 0; k < ns; ++k) {
+        QPC_CUDA_OR_THROW(p->steps[k](p->stream));
+        QPC_CUDA_OR_THROW(cudaEventRecord(evs[k + 1], p->stream));
+      }
+      QPC_CUDA_OR_THROW(cudaEventSynchronize(evs[ns]));
+      for (size_t k = 0; k < ns; ++k) {
+        float ms = 0;
+        QPC_CUDA_OR_THROW(cudaEventElapsedTime(&ms, evs[k], evs[k + 1]));
+        acc[k] += ms;
+      }
+    }
+    for (auto& e : evs) cudaEventDestroy(e);
+    prof_ = p->info;
+    for (size_t k = 0; k < ns; ++k) prof_[k].ms = (float)(acc[k] / std::max(iters, 1));
+  } catch (...) {
+    release(p);
+    throw;
+  }
+  release(p);
+}
+
+}  // namespace qpc

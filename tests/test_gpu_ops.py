@@ -1,0 +1,102 @@
+"""Operator-level parity on the B200 through the C ABI (device pointers)
+against the CPU oracle.  Tolerances: the reference's max|d|/max|ref| metric;
+bit-exact for the depthwise kernel (same fma chain), 1e-3 for TF32 tensor-core
+GEMMs, 1e-5 for the 3xTF32 mode."""
+import numpy as np
+import pytest
+
+import oracle as orc
+import qppocr_b200 as q
+
+pytestmark = pytest.mark.gpu
+
+TOL_TF32 = 1e-3
+TOL_3XTF32 = 1e-5
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return np.abs(a - b).max() / max(np.abs(b).max(), 1e-6)
+
+
+def dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("n,h,w,c,k,s,act,res", [
+    (1, 160, 160, 64, 3, (1, 1), "hswish", False),
+    (2, 33, 31, 16, 3, (2, 2), "hswish", True),
+    (1, 40, 40, 24, 5, (1, 1), "relu", False),
+    (1, 41, 37, 32, 5, (2, 2), None, True),
+    (3, 12, 80, 64, 3, (2, 1), "hswish", False),
+    (1, 9, 9, 8, 7, (1, 1), "sigmoid", False),
+    (1, 1, 1, 4, 3, (1, 1), None, False),
+    (1, 10, 10, 6, 3, (1, 1), "swish", True),   # C % 4 != 0 -> generic kernel
+])
+def test_dwconv_bit_exact(cuda_ctx, n, h, w, c, k, s, act, res):
+    import torch
+    rng = np.random.Generator(np.random.PCG64(7))
+    x = rng.uniform(-1, 1, (n, h, w, c)).astype(np.float32)
+    wt = (rng.standard_normal((c, 1, k, k)) * 0.3).astype(np.float32)
+    b = rng.standard_normal(c).astype(np.float32) * 0.1
+    p = (k - 1) // 2
+    oh = (h + 2 * p - k) // s[0] + 1
+    ow = (w + 2 * p - k) // s[1] + 1
+    r = rng.uniform(-1, 1, (n, oh, ow, c)).astype(np.float32) if res else None
+    tap = np.ascontiguousarray(wt.reshape(c, k * k).T)
+    y = q.op_dwconv_nhwc(dev(x), dev(tap), k, k, s, (p, p, p, p), bias=dev(b), act=act,
+                         residual=dev(r) if res else None)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    # reference: NCHW depthwise (conv.rs:45-71) then act then residual
+    ref = orc.conv2d(np.transpose(x, (0, 3, 1, 2)), wt, b, s, (p, p, p, p), c)
+    if act == "hswish":
+        ref = orc.binary("Mul", ref, orc.hardsigmoid(ref, np.float32(1 / 6), 0.5))
+    elif act == "relu":
+        ref = orc.relu(ref)
+    elif act == "sigmoid":
+        ref = orc.sigmoid(ref)
+    elif act == "swish":
+        ref = orc.binary("Mul", ref, orc.sigmoid(ref))
+    ref = np.transpose(ref, (0, 2, 3, 1))
+    if res:
+        ref = orc.binary("Add", ref, r)
+    assert got.shape == ref.shape
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), rel(got, ref)
+    assert q.kernel_error(0) == 0
+
+
+@pytest.mark.parametrize("m,k,n", [(6400, 16, 32), (6400, 64, 128), (25600, 128, 256),
+                                   (6400, 256, 512), (6400, 512, 512), (1000, 120, 360),
+                                   (77, 36, 24), (300, 480, 120), (129, 120, 18709)])
+@pytest.mark.parametrize("math", ["tf32", "3xtf32"])
+def test_gemm_parity(cuda_ctx, m, k, n, math):
+    import torch
+    from qppocr_b200 import nets
+    x, w, b = nets.gemm_case(m, k, n)
+    r = np.random.Generator(np.random.PCG64(2)).uniform(-1, 1, (m, n)).astype(np.float32)
+    wn = np.ascontiguousarray(w.T)   # [N, K]
+    wd = dev(wn)
+    lo = None
+    if math == "3xtf32":
+        hi, lo = q.op_split_tf32(wd)
+        wd = hi
+    y = q.op_gemm(dev(x), wd, bias=dev(b), act="hswish", residual=dev(r), math=math, w_lo=lo)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    ref = orc.conv1x1_nhwc(x, w, b)
+    ref = orc.binary("Add", orc.binary("Mul", ref, orc.hardsigmoid(ref, np.float32(1 / 6), 0.5)), r)
+    tol = TOL_TF32 if math == "tf32" else TOL_3XTF32
+    e = rel(got, ref)
+    assert e < tol, e
+    assert q.kernel_error(0) == 0
+
+
+def test_gemm_rejects_unaligned_k(cuda_ctx):
+    import torch
+    x = torch.zeros((8, 6), device="cuda")
+    w = torch.zeros((4, 6), device="cuda")
+    with pytest.raises(q.GraphError):
+        q.op_gemm(x, w)
