@@ -190,6 +190,15 @@ int qpc_session_profile_step(const qpc_session* s, int idx, const char** kernel,
 int qpc_session_replay(qpc_session* s, const qpc_tensor* inputs, int n_inputs, int iters,
                        float* ms_per_replay);
 
+/* The session's node list after load-time fusion: op ("Conv", "QpcLinear",
+ * "QpcLayerNorm", ...), node name and first output tensor.  Making those
+ * outputs graph outputs of a second session changes no fusion, so every
+ * fused node can be compared on its own (dump-compare stepping,
+ * QPPOCR_GPU_DUMP_CMP, crates/qppocr-gpu/src/vulkan/session.rs:542-600). */
+int qpc_session_node_count(const qpc_session* s, int* n);
+int qpc_session_node(const qpc_session* s, int idx, const char** op, const char** name,
+                     const char** output);
+
 /* ------------------------------------------------ operator entry points
  * Device-pointer entry points for single operators (the qppocr-kernels
  * functions the session composes), for callers that manage device memory
@@ -213,14 +222,16 @@ int qpc_op_dwconv_nhwc(const float* x, int n, int h, int w, int c, const float* 
  * y[M,N] = act(x[M,K] * w[N,K]^T + bias) + residual.  Replaces the 1x1 path
  * of conv2d_res_into (conv.rs:264-460 -> sgemm_res, gemm.rs:53-66, 223-466),
  * conv1x1_nhwc (conv.rs:856-901) and constant-B matmul (shape.rs:568-653).
- * math: qpc_math.  w_lo: for QPC_MATH_3XTF32, w minus its tf32 truncation
- * (see qpc_op_split_tf32); ignored for TF32. */
+ * math: qpc_math.  x is rounded to tf32 (nearest) on chip; w should already
+ * be tf32-rounded: pass the `hi` part of qpc_op_split_tf32 as w, and for
+ * QPC_MATH_3XTF32 its `lo` part as w_lo (ignored for TF32). */
 int qpc_op_gemm(const float* x, int64_t m, int k, const float* w, const float* w_lo, int n,
                 const float* bias, int act, const float* act_p, const float* residual, float* y,
                 int math, void* stream);
 
-/* Split fp32 device values into tf32 hi (truncation) and lo = v - hi parts,
- * the load-time weight preparation of the 3xTF32 mode. */
+/* Split fp32 device values into tf32 parts hi = rn(v) and lo = rn(v - hi)
+ * (round to nearest, ties away): the load-time weight preparation of both
+ * math modes. */
 int qpc_op_split_tf32(const float* v, int64_t count, float* hi, float* lo, void* stream);
 
 /* Device fault / timeout flag raised by kernels with bounded waits on the

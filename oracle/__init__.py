@@ -355,105 +355,110 @@ def run_graph(graph, weights: Dict[str, np.ndarray], inputs: Dict[str, np.ndarra
         return weights[name]
 
     for n in graph.nodes:
-        op = n.op_type
-        a = n.attrs
-        if op == "Conv":
-            x, w = get(n.inputs[0]), get(n.inputs[1])
-            bias = get(n.inputs[2]) if len(n.inputs) > 2 and n.inputs[2] else None
-            res = get(n.inputs[3]) if len(n.inputs) > 3 and n.inputs[3] else None
-            st = a.get("strides", [1, 1])
-            kh, kw = w.shape[2], w.shape[3]
-            pads = _resolve_pads(n, x.shape[2], x.shape[3], kh, kw, st[0], st[1])
-            act = int(a.get("act", 0))
-            act_c = [a.get("act_c1", 1.4142135), a.get("act_c2", 1.0), a.get("act_c3", 0.5)]
-            y = conv2d(x, w, bias, st, pads, int(a.get("group", 1)), act, act_c, res)
-        elif op == "ConvTranspose":
-            y = convtranspose2d(get(n.inputs[0]), get(n.inputs[1]))
-        elif op == "BatchNormalization":
-            y = batchnorm(get(n.inputs[0]), *(get(n.inputs[k]) for k in range(1, 5)), eps=a.get("epsilon", 1e-5))
-        elif op == "Relu":
-            y = relu(get(n.inputs[0]))
-        elif op == "Sigmoid":
-            y = sigmoid(get(n.inputs[0]))
-        elif op == "HardSigmoid":
-            y = hardsigmoid(get(n.inputs[0]), a.get("alpha", 0.2), a.get("beta", 0.5))
-        elif op == "Sqrt":
-            y = sqrt(get(n.inputs[0]))
-        elif op in _BINOPS:
-            y = binary(op, get(n.inputs[0]), get(n.inputs[1]))
-        elif op == "MulAddScale":
-            f, g, r = (get(i) for i in n.inputs)
-            if f.ndim == 4 and g.size == f.shape[1] and r.shape == f.shape and f.size:
-                y = mul_add_scale(f, g, r)
-            else:
-                y = binary("Add", binary("Mul", f, g), r)
-        elif op == "Softmax":
-            x = get(n.inputs[0])
-            axis = int(a.get("axis", -1))
-            if axis not in (-1, x.ndim - 1):
-                raise NotImplementedError("softmax axis")
-            y = softmax_last(x)
-        elif op == "GlobalAveragePool":
-            y = global_avg_pool(get(n.inputs[0]))
-        elif op in ("AveragePool", "MaxPool"):
-            x = get(n.inputs[0])
-            ks = a["kernel_shape"]
-            st = a.get("strides", [1, 1])
-            ph, pw, peh, pew = _resolve_pads(n, x.shape[2], x.shape[3], ks[0], ks[1], st[0], st[1])
-            y = pool2d(x, ks[0], ks[1], st[0], st[1], ph, pw, peh, pew, op == "MaxPool")
-        elif op == "Resize":
-            x = get(n.inputs[0])
-            if len(n.inputs) >= 4 and n.inputs[3]:
-                sz = get(n.inputs[3]).astype(np.int64)
-                oh, ow = int(sz[-2]), int(sz[-1])
-            else:
-                sc = get(n.inputs[2]).astype(np.float32)
-                oh = int(np.float32(x.shape[2]) * sc[-2])
-                ow = int(np.float32(x.shape[3]) * sc[-1])
-            y = resize_nearest(x, oh, ow)
-        elif op == "Concat":
-            y = np.concatenate([get(i) for i in n.inputs], axis=int(a.get("axis", 0)))
-        elif op == "Slice":
-            x = get(n.inputs[0])
-            starts = get(n.inputs[1]).astype(np.int64)
-            ends = get(n.inputs[2]).astype(np.int64)
-            axes = get(n.inputs[3]).astype(np.int64) if len(n.inputs) > 3 and n.inputs[3] else range(len(starts))
-            sl = [slice(None)] * x.ndim
-            for s0, e0, ax in zip(starts, ends, axes):
-                sl[int(ax)] = slice(int(s0), int(e0))
-            y = np.ascontiguousarray(x[tuple(sl)])
-        elif op == "Transpose":
-            y = np.ascontiguousarray(np.transpose(get(n.inputs[0]), a.get("perm")))
-        elif op == "Reshape":
-            x = get(n.inputs[0])
-            shp = [int(v) for v in get(n.inputs[1])]
-            shp = [x.shape[i] if d == 0 else d for i, d in enumerate(shp)]
-            y = x.reshape(shp)
-        elif op == "Squeeze":
-            x = get(n.inputs[0])
-            axes = a.get("axes") or [int(v) for v in get(n.inputs[1])]
-            y = np.squeeze(x, axis=tuple(int(v) for v in axes))
-        elif op == "Unsqueeze":
-            x = get(n.inputs[0])
-            axes = a.get("axes") or [int(v) for v in get(n.inputs[1])]
-            y = np.expand_dims(x, tuple(int(v) for v in axes))
-        elif op == "ReduceMean":
-            x = get(n.inputs[0])
-            axes = [int(v) % x.ndim for v in a.get("axes", range(x.ndim))]
-            lo, hi = min(axes), max(axes)
-            outer = int(np.prod(x.shape[:lo]))
-            mid = int(np.prod(x.shape[lo:hi + 1]))
-            inner = int(np.prod(x.shape[hi + 1:]))
-            y = reduce_mean(x, outer, mid, inner)
-            shp = [d if i not in axes else 1 for i, d in enumerate(x.shape)]
-            if not int(a.get("keepdims", 1)):
-                shp = [d for i, d in enumerate(x.shape) if i not in axes]
-            y = y.reshape(shp)
-        elif op == "MatMul":
-            y = matmul(get(n.inputs[0]), get(n.inputs[1]))
-        elif op in ("Identity", "Dropout"):
-            y = get(n.inputs[0])
-        else:
-            raise NotImplementedError(f"oracle executor: op {op}")
-        vals[n.outputs[0]] = np.ascontiguousarray(y, dtype=np.float32)
+        vals[n.outputs[0]] = eval_node(n, get)
     return [vals[o] for o in graph.outputs]
+
+
+def eval_node(n, get) -> np.ndarray:
+    """One node of the reference executor; `get(name)` supplies its inputs."""
+    op = n.op_type
+    a = n.attrs
+    if op == "Conv":
+        x, w = get(n.inputs[0]), get(n.inputs[1])
+        bias = get(n.inputs[2]) if len(n.inputs) > 2 and n.inputs[2] else None
+        res = get(n.inputs[3]) if len(n.inputs) > 3 and n.inputs[3] else None
+        st = a.get("strides", [1, 1])
+        kh, kw = w.shape[2], w.shape[3]
+        pads = _resolve_pads(n, x.shape[2], x.shape[3], kh, kw, st[0], st[1])
+        act = int(a.get("act", 0))
+        act_c = [a.get("act_c1", 1.4142135), a.get("act_c2", 1.0), a.get("act_c3", 0.5)]
+        y = conv2d(x, w, bias, st, pads, int(a.get("group", 1)), act, act_c, res)
+    elif op == "ConvTranspose":
+        y = convtranspose2d(get(n.inputs[0]), get(n.inputs[1]))
+    elif op == "BatchNormalization":
+        y = batchnorm(get(n.inputs[0]), *(get(n.inputs[k]) for k in range(1, 5)), eps=a.get("epsilon", 1e-5))
+    elif op == "Relu":
+        y = relu(get(n.inputs[0]))
+    elif op == "Sigmoid":
+        y = sigmoid(get(n.inputs[0]))
+    elif op == "HardSigmoid":
+        y = hardsigmoid(get(n.inputs[0]), a.get("alpha", 0.2), a.get("beta", 0.5))
+    elif op == "Sqrt":
+        y = sqrt(get(n.inputs[0]))
+    elif op in _BINOPS:
+        y = binary(op, get(n.inputs[0]), get(n.inputs[1]))
+    elif op == "MulAddScale":
+        f, g, r = (get(i) for i in n.inputs)
+        if f.ndim == 4 and g.size == f.shape[1] and r.shape == f.shape and f.size:
+            y = mul_add_scale(f, g, r)
+        else:
+            y = binary("Add", binary("Mul", f, g), r)
+    elif op == "Softmax":
+        x = get(n.inputs[0])
+        axis = int(a.get("axis", -1))
+        if axis not in (-1, x.ndim - 1):
+            raise NotImplementedError("softmax axis")
+        y = softmax_last(x)
+    elif op == "GlobalAveragePool":
+        y = global_avg_pool(get(n.inputs[0]))
+    elif op in ("AveragePool", "MaxPool"):
+        x = get(n.inputs[0])
+        ks = a["kernel_shape"]
+        st = a.get("strides", [1, 1])
+        ph, pw, peh, pew = _resolve_pads(n, x.shape[2], x.shape[3], ks[0], ks[1], st[0], st[1])
+        y = pool2d(x, ks[0], ks[1], st[0], st[1], ph, pw, peh, pew, op == "MaxPool")
+    elif op == "Resize":
+        x = get(n.inputs[0])
+        if len(n.inputs) >= 4 and n.inputs[3]:
+            sz = get(n.inputs[3]).astype(np.int64)
+            oh, ow = int(sz[-2]), int(sz[-1])
+        else:
+            sc = get(n.inputs[2]).astype(np.float32)
+            oh = int(np.float32(x.shape[2]) * sc[-2])
+            ow = int(np.float32(x.shape[3]) * sc[-1])
+        y = resize_nearest(x, oh, ow)
+    elif op == "Concat":
+        y = np.concatenate([get(i) for i in n.inputs], axis=int(a.get("axis", 0)))
+    elif op == "Slice":
+        x = get(n.inputs[0])
+        starts = get(n.inputs[1]).astype(np.int64)
+        ends = get(n.inputs[2]).astype(np.int64)
+        axes = get(n.inputs[3]).astype(np.int64) if len(n.inputs) > 3 and n.inputs[3] else range(len(starts))
+        sl = [slice(None)] * x.ndim
+        for s0, e0, ax in zip(starts, ends, axes):
+            sl[int(ax)] = slice(int(s0), int(e0))
+        y = np.ascontiguousarray(x[tuple(sl)])
+    elif op == "Transpose":
+        y = np.ascontiguousarray(np.transpose(get(n.inputs[0]), a.get("perm")))
+    elif op == "Reshape":
+        x = get(n.inputs[0])
+        shp = [int(v) for v in get(n.inputs[1])]
+        shp = [x.shape[i] if d == 0 else d for i, d in enumerate(shp)]
+        y = x.reshape(shp)
+    elif op == "Squeeze":
+        x = get(n.inputs[0])
+        axes = a.get("axes") or [int(v) for v in get(n.inputs[1])]
+        y = np.squeeze(x, axis=tuple(int(v) for v in axes))
+    elif op == "Unsqueeze":
+        x = get(n.inputs[0])
+        axes = a.get("axes") or [int(v) for v in get(n.inputs[1])]
+        y = np.expand_dims(x, tuple(int(v) for v in axes))
+    elif op == "ReduceMean":
+        x = get(n.inputs[0])
+        axes = [int(v) % x.ndim for v in a.get("axes", range(x.ndim))]
+        lo, hi = min(axes), max(axes)
+        outer = int(np.prod(x.shape[:lo]))
+        mid = int(np.prod(x.shape[lo:hi + 1]))
+        inner = int(np.prod(x.shape[hi + 1:]))
+        y = reduce_mean(x, outer, mid, inner)
+        shp = [d if i not in axes else 1 for i, d in enumerate(x.shape)]
+        if not int(a.get("keepdims", 1)):
+            shp = [d for i, d in enumerate(x.shape) if i not in axes]
+        y = y.reshape(shp)
+    elif op == "MatMul":
+        y = matmul(get(n.inputs[0]), get(n.inputs[1]))
+    elif op in ("Identity", "Dropout"):
+        y = get(n.inputs[0])
+    else:
+        raise NotImplementedError(f"oracle executor: op {op}")
+    return np.ascontiguousarray(y, dtype=np.float32)

@@ -94,7 +94,7 @@ EXPORTED = (
     "qpc_session_caps", "qpc_run_async", "qpc_complete", "qpc_ticket_output_count",
     "qpc_ticket_output", "qpc_ticket_release", "qpc_run", "qpc_ticket_device_ms",
     "qpc_session_destroy", "qpc_session_profile", "qpc_session_profile_step",
-    "qpc_session_replay", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_split_tf32",
+    "qpc_session_replay", "qpc_session_node_count", "qpc_session_node", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_split_tf32",
     "qpc_kernel_error",
 )
 
@@ -134,6 +134,9 @@ def lib():
                                            ctypes.POINTER(ctypes.c_float)]
     L.qpc_session_replay.argtypes = [P, ctypes.POINTER(QpcTensor), ctypes.c_int, ctypes.c_int,
                                      ctypes.POINTER(ctypes.c_float)]
+    L.qpc_session_node_count.argtypes = [P, ctypes.POINTER(ctypes.c_int)]
+    L.qpc_session_node.argtypes = [P, ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
+                                   ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_char_p)]
     L.qpc_op_dwconv_nhwc.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P,
                                      ctypes.c_int, ctypes.c_int, P, P, P, ctypes.c_int, P, P, P, P]
     L.qpc_op_gemm.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P, ctypes.c_int, P,
@@ -350,6 +353,17 @@ class CudaSession:
             _check(lib().qpc_session_profile_step(self._h, k, ctypes.byref(kern), ctypes.byref(node),
                                                   ctypes.byref(by), ctypes.byref(fl), ctypes.byref(ms)))
             out.append((kern.value.decode(), node.value.decode(), by.value, fl.value, ms.value))
+        return out
+
+    def fused_nodes(self):
+        """(op, name, output) of every node after load-time fusion."""
+        n = ctypes.c_int(0)
+        _check(lib().qpc_session_node_count(self._h, ctypes.byref(n)))
+        out = []
+        for k in range(n.value):
+            op, nm, o = ctypes.c_char_p(), ctypes.c_char_p(), ctypes.c_char_p()
+            _check(lib().qpc_session_node(self._h, k, ctypes.byref(op), ctypes.byref(nm), ctypes.byref(o)))
+            out.append((op.value.decode(), nm.value.decode(), o.value.decode()))
         return out
 
     def replay(self, inputs, iters: int) -> float:

@@ -53,9 +53,9 @@ __global__ void split_tf32_kernel(const float* v, int64_t n, float* hi, float* l
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float x = v[i];
-    const float h = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    const float h = tf32_rna(x);
     hi[i] = h;
-    lo[i] = __fsub_rn(x, h);
+    lo[i] = tf32_rna(__fsub_rn(x, h));
   }
 }
 
@@ -265,6 +265,25 @@ int qpc_session_replay(qpc_session* s, const qpc_tensor* inputs, int n_inputs, i
     *ms_per_replay = s->impl->replay(inputs, n_inputs, iters);
     return (int)OK;
   });
+}
+
+// Fused plan nodes (after load-time fusion), for per-node dump-compare
+// (QPPOCR_GPU_DUMP_CMP analogue, vulkan/session.rs:542-600).
+int qpc_session_node_count(const qpc_session* s, int* n) {
+  if (!s || !n) return E_INVALID;
+  *n = (int)s->impl->nodes().size();
+  return OK;
+}
+
+int qpc_session_node(const qpc_session* s, int idx, const char** op, const char** name,
+                     const char** output) {
+  if (!s) return E_INVALID;
+  const auto& v = s->impl->nodes();
+  if (idx < 0 || idx >= (int)v.size()) return E_INVALID;
+  if (op) *op = v[idx].op.c_str();
+  if (name) *name = v[idx].name.c_str();
+  if (output) *output = v[idx].out.empty() ? "" : v[idx].out[0].c_str();
+  return OK;
 }
 
 // ---- operator entry points

@@ -10,10 +10,15 @@
 //   K-major) are staged by TMA with 128-byte swizzle into a STAGES-deep ring.
 // * One elected lane issues tcgen05.mma kind::tf32 (M=128, N=BN, K=8); the
 //   accumulator lives in TMEM and never touches registers during the K loop.
-// * MATH_3XTF32 (fp32-accurate mode): B arrives pre-split (hi = tf32
-//   truncation, lo = B - hi, prepared at load time); A is split on chip by two
-//   converter warps, and each k-step issues hi*hi + hi*lo + lo*hi.
-// * Epilogue: 4 warps read their 32 TMEM lanes (tcgen05.ld 32x32b), add bias,
+// * Operands are rounded to tf32 to nearest (the tensor core itself would
+//   truncate, biasing every product toward zero): B at load time, A on chip
+//   by four converter warps between the TMA landing and the MMA.
+// * MATH_3XTF32 (fp32-accurate mode): B arrives pre-split (hi = rn(B),
+//   lo = rn(B - hi)); A is split the same way on chip; each k-step issues
+//   lo*hi + hi*lo + hi*hi.  The tensor core's fp32 accumulation drifts toward
+//   zero with K, so partial sums over CH k-blocks are promoted into fp32
+//   registers with IEEE round-to-nearest adds (TMEM is drained per chunk).
+// * Epilogue: warps 2-5 read their 32 TMEM lanes (tcgen05.ld 32x32b), add bias,
 //   apply the fused activation, add the residual (optionally through a
 //   nearest-upsample index map) and store fp32 rows.
 // * A_MODE 1 (k x k, stride 1 conv): the A tile is a 4-D TMA box
@@ -79,19 +84,26 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& args, const float
   }
 }
 
+constexpr int NUM_THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 convert + epilogue
+constexpr int CH = 1;             // k-blocks per promotion chunk (3xTF32)
+constexpr int LAG = 1;            // converter runs this many k-blocks ahead of a drain
+
 template <int BN, int STAGES, bool SPLIT, int A_MODE>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmBlo, const GemmArgs args) {
   using SM = Smem<BN, SPLIT>;
-  constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  // 3xTF32 ping-pongs two accumulators so the MMA runs on while a chunk drains.
+  constexpr uint32_t TMEM_COLS = SPLIT ? 2 * BN : (BN < 32 ? 32 : BN);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t split_bar[STAGES];
+  __shared__ __align__(8) uint64_t conv_bar[STAGES];
   __shared__ __align__(8) uint64_t acc_bar;
+  __shared__ __align__(8) uint64_t chunk_full[2];
+  __shared__ __align__(8) uint64_t chunk_free[2];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
 
@@ -117,9 +129,13 @@ __global__ void __launch_bounds__(128, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
-      mbar_init(&split_bar[s], 64);
+      mbar_init(&conv_bar[s], 128);
     }
     mbar_init(&acc_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&chunk_full[b], 1);
+      mbar_init(&chunk_free[b], 128);
+    }
     abort_flag = 0;
     fence_barrier_init();
     prefetch_tensormap(&tmA);
@@ -135,127 +151,181 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_after();
   const uint32_t tmem_d = tmem_base_slot;
   const int nkb = args.nkb;
+  const int nchunks = (nkb + CH - 1) / CH;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer
-    const uint32_t bytes = SPLIT ? (A_TILE_BYTES + 2 * SM::B_TILE) : (A_TILE_BYTES + SM::B_TILE);
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-      if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.err)) { abort_flag = 1; break; }
-      uint8_t* st = smem + s * SM::STAGE;
-      mbar_arrive_expect_tx(&full_bar[s], bytes);
-      if (A_MODE == 0) {
-        tma_load_2d(st, &tmA, &full_bar[s], kb * BK, m_blk * BM);
-        tma_load_2d(st + A_TILE_BYTES, &tmB, &full_bar[s], kb * BK, n0);
-        if (SPLIT) tma_load_2d(st + 2 * A_TILE_BYTES + SM::B_TILE, &tmBlo, &full_bar[s], kb * BK, n0);
-      } else {
-        const int tap = kb / args.cblocks, cb = kb % args.cblocks;
-        const int ky = tap / args.kw, kx = tap % args.kw;
-        tma_load_4d(st, &tmA, &full_bar[s], cb * BK, ox0 + kx - args.pw, oy0 + ky - args.ph, img);
-        tma_load_4d(st + A_TILE_BYTES, &tmB, &full_bar[s], cb * BK, n0, tap, 0);
-        if (SPLIT)
-          tma_load_4d(st + 2 * A_TILE_BYTES + SM::B_TILE, &tmBlo, &full_bar[s], cb * BK, n0, tap, 0);
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      const uint32_t bytes = SPLIT ? (A_TILE_BYTES + 2 * SM::B_TILE) : (A_TILE_BYTES + SM::B_TILE);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+        if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.err)) { abort_flag = 1; break; }
+        uint8_t* st = smem + s * SM::STAGE;
+        mbar_arrive_expect_tx(&full_bar[s], bytes);
+        if (A_MODE == 0) {
+          tma_load_2d(st, &tmA, &full_bar[s], kb * BK, m_blk * BM);
+          tma_load_2d(st + A_TILE_BYTES, &tmB, &full_bar[s], kb * BK, n0);
+          if (SPLIT) tma_load_2d(st + 2 * A_TILE_BYTES + SM::B_TILE, &tmBlo, &full_bar[s], kb * BK, n0);
+        } else {
+          const int tap = kb / args.cblocks, cb = kb % args.cblocks;
+          const int ky = tap / args.kw, kx = tap % args.kw;
+          tma_load_4d(st, &tmA, &full_bar[s], cb * BK, ox0 + kx - args.pw, oy0 + ky - args.ph, img);
+          tma_load_4d(st + A_TILE_BYTES, &tmB, &full_bar[s], cb * BK, n0, tap, 0);
+          if (SPLIT)
+            tma_load_4d(st + 2 * A_TILE_BYTES + SM::B_TILE, &tmBlo, &full_bar[s], cb * BK, n0, tap, 0);
+        }
       }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
-    constexpr uint32_t idesc = idesc_tf32(BM, BN);
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc = idesc_tf32(BM, BN);
+      bool ok = true;
+      for (int kb = 0; kb < nkb && ok; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+        const bool first = SPLIT ? (kb % CH) == 0 : kb == 0;
+        const int chunk = kb / CH, buf = chunk & 1;
+        // accumulator `buf` is reused by chunk c once chunk c - 2 has drained
+        if (SPLIT && first && chunk >= 2 &&
+            !mbar_wait(&chunk_free[buf], (uint32_t)((chunk >> 1) - 1) & 1u, args.err)) {
+          ok = false;
+          break;
+        }
+        const uint32_t d_tmem = tmem_d + (SPLIT ? (uint32_t)(buf * BN) : 0u);
+        if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + s * SM::STAGE);
+        const uint32_t b_addr = a_addr + A_TILE_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < BK / 8; ++ks) {
+          const uint32_t acc = (!first || ks > 0) ? 1u : 0u;
+          const uint64_t ad = sw128_kmajor_desc(a_addr + ks * 32);
+          const uint64_t bd = sw128_kmajor_desc(b_addr + ks * 32);
+          if (SPLIT) {
+            const uint64_t alo = sw128_kmajor_desc(b_addr + SM::B_TILE + ks * 32);
+            const uint64_t blo = sw128_kmajor_desc(b_addr + SM::B_TILE + A_TILE_BYTES + ks * 32);
+            mma_tf32(d_tmem, alo, bd, idesc, acc);
+            mma_tf32(d_tmem, ad, blo, idesc, 1u);
+            mma_tf32(d_tmem, ad, bd, idesc, 1u);
+          } else {
+            mma_tf32(d_tmem, ad, bd, idesc, acc);
+          }
+        }
+        mma_commit(&empty_bar[s]);   // frees the stage once these MMAs have read it
+        if (SPLIT && ((kb % CH) == CH - 1 || kb == nkb - 1)) mma_commit(&chunk_full[buf]);
+      }
+      if (!ok) abort_flag = 1;
+      if (!SPLIT) mma_commit(&acc_bar);   // accumulator complete (or abandoned)
+    }
+  } else {
+    // ---------------- warps 2-5: convert A on chip, then the epilogue.
+    // TMEM lane quarter of this warp = warp % 4; its rows are 32 * (warp % 4) + lane.
+    const int t = threadIdx.x - 64;
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_base = tmem_d + ((uint32_t)(q * 32) << 16);
+    float accr[SPLIT ? BN : 1];
+#pragma unroll
+    for (int j = 0; j < (SPLIT ? BN : 1); ++j) accr[j] = 0.f;
     bool ok = true;
-    for (int kb = 0; kb < nkb && ok; ++kb) {
+    int drained = 0;
+    // Promotion of a finished chunk: TMEM partial sum -> fp32 registers (RN adds).
+    auto drain = [&](int c) {
+      const int b = c & 1;
+      if (!ok || !mbar_wait(&chunk_full[b], (uint32_t)(c >> 1) & 1u, args.err)) { ok = false; return; }
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < (SPLIT ? BN : 16); c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16_nowait(lane_base + (uint32_t)(b * BN) + c0, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          accr[(c0 + j) % (SPLIT ? BN : 1)] =
+              __fadd_rn(accr[(c0 + j) % (SPLIT ? BN : 1)], __uint_as_float(v[j]));
+      }
+      tc_fence_before();
+      mbar_arrive(&chunk_free[b]);
+    };
+    for (int kb = 0; kb < nkb; ++kb) {
       const int s = kb % STAGES;
       const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
       if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
-      if (SPLIT && !mbar_wait(&split_bar[s], ph, args.err)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t a_addr = smem_u32(smem + s * SM::STAGE);
-      const uint32_t b_addr = a_addr + A_TILE_BYTES;
-#pragma unroll
-      for (int ks = 0; ks < BK / 8; ++ks) {
-        const uint32_t acc = (kb > 0 || ks > 0) ? 1u : 0u;
-        const uint64_t ad = sw128_kmajor_desc(a_addr + ks * 32);
-        const uint64_t bd = sw128_kmajor_desc(b_addr + ks * 32);
-        if (SPLIT) {
-          const uint64_t alo = sw128_kmajor_desc(b_addr + SM::B_TILE + ks * 32);
-          const uint64_t blo = sw128_kmajor_desc(b_addr + SM::B_TILE + A_TILE_BYTES + ks * 32);
-          mma_tf32(tmem_d, alo, bd, idesc, acc);
-          mma_tf32(tmem_d, ad, blo, idesc, 1u);
-          mma_tf32(tmem_d, ad, bd, idesc, 1u);
-        } else {
-          mma_tf32(tmem_d, ad, bd, idesc, acc);
-        }
-      }
-      mma_commit(&empty_bar[s]);   // frees the stage once these MMAs have read it
-    }
-    if (!ok) abort_flag = 1;
-    mma_commit(&acc_bar);          // accumulator complete (or abandoned)
-  } else if (SPLIT && warp >= 2) {
-    // ---------------- on-chip 3xTF32 split of A: hi = tf32 truncation in
-    // place, lo = A - hi into its own tile.  Elementwise, so the TMA swizzle
-    // needs no attention.
-    const int t = threadIdx.x - 64;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-      if (!mbar_wait(&full_bar[s], ph, args.err)) { abort_flag = 1; break; }
       float4* a = reinterpret_cast<float4*>(smem + s * SM::STAGE);
       float4* lo = reinterpret_cast<float4*>(smem + s * SM::STAGE + A_TILE_BYTES + SM::B_TILE);
-#pragma unroll 4
-      for (int i = t; i < A_TILE_BYTES / 16; i += 64) {
-        float4 v = a[i], h, l;
-        h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-        h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-        h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-        h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-        l.x = __fsub_rn(v.x, h.x);
-        l.y = __fsub_rn(v.y, h.y);
-        l.z = __fsub_rn(v.z, h.z);
-        l.w = __fsub_rn(v.w, h.w);
+#pragma unroll
+      for (int i = t; i < A_TILE_BYTES / 16; i += 128) {
+        const float4 v = a[i];
+        float4 h;
+        h.x = tf32_rna(v.x);
+        h.y = tf32_rna(v.y);
+        h.z = tf32_rna(v.z);
+        h.w = tf32_rna(v.w);
         a[i] = h;
-        lo[i] = l;
+        if (SPLIT) {
+          float4 l;
+          l.x = tf32_rna(__fsub_rn(v.x, h.x));
+          l.y = tf32_rna(__fsub_rn(v.y, h.y));
+          l.z = tf32_rna(__fsub_rn(v.z, h.z));
+          l.w = tf32_rna(__fsub_rn(v.w, h.w));
+          lo[i] = l;
+        }
       }
       fence_proxy_async_smem();
-      mbar_arrive(&split_bar[s]);
+      mbar_arrive(&conv_bar[s]);
+      if (SPLIT)
+        while (ok && drained < nchunks && min((drained + 1) * CH, nkb) - 1 <= kb - LAG) drain(drained++);
     }
-  }
-  __syncwarp();
-
-  // ---------------- epilogue: all 4 warps
-  const bool acc_ok = mbar_wait(&acc_bar, 0, args.err);
-  tc_fence_after();
-  if (acc_ok && !abort_flag) {
-    const int r = warp * 32 + lane;   // TMEM lane == tile row
-    int64_t orow = -1, rrow = -1;
-    if (A_MODE == 0) {
-      const int64_t m = (int64_t)m_blk * BM + r;
-      if (m < args.M) orow = m;
-    } else {
-      const int oy = oy0 + r / args.tw, ox = ox0 + r % args.tw;
-      if (oy < args.oh && ox < args.ow) orow = ((int64_t)img * args.oh + oy) * args.ow + ox;
-    }
-    if (orow >= 0) {
-      rrow = orow;
-      const GemmEpilogue& e = args.epi;
-      if (e.residual && e.rh > 0) {
-        // nearest resize source row, resize.rs:43-50: (int)((float)o * in / out)
-        const int64_t pix = orow;
-        const int x = (int)(pix % e.ow);
-        const int y = (int)((pix / e.ow) % e.oh);
-        const int64_t nn = pix / ((int64_t)e.ow * e.oh);
-        int iy = (int)__fdiv_rn(__fmul_rn((float)y, (float)e.rh), (float)e.oh);
-        int ix = (int)__fdiv_rn(__fmul_rn((float)x, (float)e.rw), (float)e.ow);
-        iy = iy < e.rh - 1 ? iy : e.rh - 1;
-        ix = ix < e.rw - 1 ? ix : e.rw - 1;
-        rrow = (nn * e.rh + iy) * e.rw + ix;
+    if (SPLIT)
+      while (ok && drained < nchunks) drain(drained++);
+    if (!SPLIT) ok = ok && mbar_wait(&acc_bar, 0, args.err);
+    tc_fence_after();
+    if (ok && !abort_flag) {
+      int64_t orow = -1, rrow = -1;
+      if (A_MODE == 0) {
+        const int64_t m = (int64_t)m_blk * BM + r;
+        if (m < args.M) orow = m;
+      } else {
+        const int oy = oy0 + r / args.tw, ox = ox0 + r % args.tw;
+        if (oy < args.oh && ox < args.ow) orow = ((int64_t)img * args.oh + oy) * args.ow + ox;
       }
-    }
-    const uint32_t lane_base = tmem_d + ((uint32_t)(warp * 32) << 16);
+      if (orow >= 0) {
+        rrow = orow;
+        const GemmEpilogue& e = args.epi;
+        if (e.residual && e.rh > 0) {
+          // nearest resize source row, resize.rs:43-50: (int)((float)o * in / out)
+          const int64_t pix = orow;
+          const int x = (int)(pix % e.ow);
+          const int y = (int)((pix / e.ow) % e.oh);
+          const int64_t nn = pix / ((int64_t)e.ow * e.oh);
+          int iy = (int)__fdiv_rn(__fmul_rn((float)y, (float)e.rh), (float)e.oh);
+          int ix = (int)__fdiv_rn(__fmul_rn((float)x, (float)e.rw), (float)e.ow);
+          iy = iy < e.rh - 1 ? iy : e.rh - 1;
+          ix = ix < e.rw - 1 ? ix : e.rw - 1;
+          rrow = (nn * e.rh + iy) * e.rw + ix;
+        }
+      }
+      if (SPLIT) {
+#pragma unroll
+        for (int c = 0; c < BN; c += 16) {
+          if (n0 + c < args.N && orow >= 0) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = accr[(c + j) % (SPLIT ? BN : 1)];
+            epilogue_store<BN>(args, v, orow, rrow, n0 + c);
+          }
+        }
+      } else {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      if (n0 + c >= args.N) break;
-      float v[16];
-      tmem_ld16(lane_base + c, v);   // warp-collective; every lane participates
-      if (orow >= 0) epilogue_store<BN>(args, v, orow, rrow, n0 + c);
+        for (int c = 0; c < BN; c += 16) {
+          if (n0 + c >= args.N) break;
+          float v[16];
+          tmem_ld16(lane_base + c, v);   // warp-collective; every lane participates
+          if (orow >= 0) epilogue_store<BN>(args, v, orow, rrow, n0 + c);
+        }
+      }
     }
   }
   tc_fence_before();
@@ -313,7 +383,7 @@ cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  kern<<<grid, 128, smem, st>>>(a, b, blo, args);
+  kern<<<grid, NUM_THREADS, smem, st>>>(a, b, blo, args);
   return cudaGetLastError();
 }
 
@@ -331,17 +401,17 @@ cudaError_t dispatch(int bn, bool split, const CUtensorMap& a, const CUtensorMap
   }
   switch (bn) {
     case 32: return run_kernel<32, 4, true, A_MODE>(a, b, blo, args, grid, st);
-    case 64: return run_kernel<64, 3, true, A_MODE>(a, b, blo, args, grid, st);
-    case 128: return run_kernel<128, 3, true, A_MODE>(a, b, blo, args, grid, st);
-    default: return run_kernel<256, 2, true, A_MODE>(a, b, blo, args, grid, st);
+    case 64: return run_kernel<64, 4, true, A_MODE>(a, b, blo, args, grid, st);
+    default: return run_kernel<128, 3, true, A_MODE>(a, b, blo, args, grid, st);
   }
 }
 
-// Output tile width: the smallest N tile that covers N with the least padding.
-int pick_bn(int n) {
+// Output tile width: the smallest N tile that covers N with the least padding
+// (3xTF32 keeps its promoted accumulator in registers: at most 128 columns).
+int pick_bn(int n, bool split) {
   if (n <= 32) return 32;
   if (n <= 64) return 64;
-  if (n <= 128) return 128;
+  if (n <= 128 || split) return 128;
   // Wider: minimise padded columns, prefer 256 on ties (fewer A re-reads).
   const int c128 = ((n + 127) / 128) * 128, c256 = ((n + 255) / 256) * 256;
   return c256 <= c128 ? 256 : 128;
@@ -358,7 +428,7 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
     return cudaErrorInvalidValue;
   const bool split = math == MATH_3XTF32;
   if (split && !b_lo) return cudaErrorInvalidValue;
-  const int bn = pick_bn(N);
+  const int bn = pick_bn(N, split);
   CUtensorMap ma, mb, mblo;
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
@@ -400,7 +470,7 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
     if (cost < best_cost) { best_cost = cost; best_tw = tw; }
   }
   const int tw = best_tw, th = 128 / tw;
-  const int bn = pick_bn(g.m);
+  const int bn = pick_bn(g.m, split);
   CUtensorMap ma, mb, mblo;
   {
     const uint64_t dims[4] = {(uint64_t)g.c, (uint64_t)g.w, (uint64_t)g.h, (uint64_t)g.n};

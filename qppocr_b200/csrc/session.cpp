@@ -249,7 +249,17 @@ qpc_caps Session::caps() const {
 //   dw         depthwise [C,1,kh,kw] -> tap-major [kh*kw][C]
 //   kxk        dense [M,C,kh,kw] -> tap-major [kh*kw][M][C]
 //   nk         MatMul B [K,N] -> [N,K]
-//   X.hi/X.lo  3xTF32 split of variant X (hi = tf32 truncation, lo = v - hi)
+//   X.rn       variant X rounded to tf32, nearest (TF32-mode B operand)
+//   X.hi/X.lo  3xTF32 split of variant X: hi = rn(v), lo = rn(v - hi)
+static float tf32_rn_host(float x) {
+  uint32_t u;
+  std::memcpy(&u, &x, 4);
+  u = (u + 0x1000u) & 0xFFFFE000u;  // round to nearest, ties away (cvt.rna.tf32.f32)
+  float r;
+  std::memcpy(&r, &u, 4);
+  return r;
+}
+
 const float* Session::dweight(const std::string& name, const std::string& variant) {
   const std::string key = name + "#" + variant;
   auto it = dev_cache_.find(key);
@@ -258,12 +268,15 @@ const float* Session::dweight(const std::string& name, const std::string& varian
   if (!h) throw GraphError{"missing initializer " + name};
   std::vector<float> v;
   auto base_variant = variant;
-  bool hi = false, lo = false;
+  bool hi = false, lo = false, rn = false;
   if (variant.size() > 3 && variant.compare(variant.size() - 3, 3, ".hi") == 0) {
     hi = true;
     base_variant = variant.substr(0, variant.size() - 3);
   } else if (variant.size() > 3 && variant.compare(variant.size() - 3, 3, ".lo") == 0) {
     lo = true;
+    base_variant = variant.substr(0, variant.size() - 3);
+  } else if (variant.size() > 3 && variant.compare(variant.size() - 3, 3, ".rn") == 0) {
+    rn = true;
     base_variant = variant.substr(0, variant.size() - 3);
   }
   std::vector<float> src;
@@ -293,14 +306,10 @@ const float* Session::dweight(const std::string& name, const std::string& varian
   } else {
     throw GraphError{"internal: unknown weight variant " + variant};
   }
-  if (hi || lo) {
+  if (hi || lo || rn) {
     for (auto& x : v) {
-      uint32_t u;
-      std::memcpy(&u, &x, 4);
-      u &= 0xFFFFE000u;
-      float t;
-      std::memcpy(&t, &u, 4);
-      x = hi ? t : (x - t);
+      const float h = tf32_rn_host(x);
+      x = lo ? tf32_rn_host(x - h) : h;
     }
   }
   if (v.empty()) v.push_back(0.f);
@@ -1018,7 +1027,7 @@ class Planner {
       Val x = as_nhwc(x0, nm);
       const float* xp = out_ptr(x);
       const bool split = math == QPC_MATH_3XTF32;
-      const float* wb = S.dweight(n.in[1], split ? "raw.hi" : "raw");
+      const float* wb = S.dweight(n.in[1], split ? "raw.hi" : "raw.rn");
       const float* wl = split ? S.dweight(n.in[1], "raw.lo") : nullptr;
       GemmEpilogue e;
       e.bias = bias;
@@ -1037,7 +1046,7 @@ class Planner {
       Val x = as_nhwc(x0, nm);
       const float* xp = out_ptr(x);
       const bool split = math == QPC_MATH_3XTF32;
-      const float* wb = S.dweight(n.in[1], split ? "kxk.hi" : "kxk");
+      const float* wb = S.dweight(n.in[1], split ? "kxk.hi" : "kxk.rn");
       const float* wl = split ? S.dweight(n.in[1], "kxk.lo") : nullptr;
       GemmEpilogue e;
       e.bias = bias;
@@ -1351,7 +1360,7 @@ class Planner {
     oshape.back() = Nn;
     const int math = S.math();
     const bool split = math == QPC_MATH_3XTF32;
-    const float* wb = S.dweight(n.in[1], split ? "nk.hi" : "nk");
+    const float* wb = S.dweight(n.in[1], split ? "nk.hi" : "nk.rn");
     const float* wl = split ? S.dweight(n.in[1], "nk.lo") : nullptr;
     const float* bias = n.has_in(2) ? S.dweight(n.in[2], "raw") : nullptr;
     Val res;

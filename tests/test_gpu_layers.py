@@ -1,0 +1,81 @@
+"""Per-node parity with teacher forcing (dump-compare stepping, as the
+reference's QPPOCR_GPU_DUMP_CMP does, vulkan/session.rs:542-600).
+
+Every fused node's output is exposed as a graph output; the oracle evaluates
+each reference node on the GPU's own inputs to that node, so each kernel's
+error is measured alone rather than after amplification by the layers before
+it.  Tolerance per node: max|d|/max|ref| < 1e-3 (TF32), < 1e-5 (3xTF32)."""
+import copy
+
+import numpy as np
+import pytest
+
+import oracle as orc
+import qppocr_b200 as q
+from qppocr_b200 import nets
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"tf32": 1e-3, "3xtf32": 1e-5}
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return np.abs(a - b).max() / max(np.abs(b).max(), 1e-6)
+
+
+def per_node(ctx, builder, x, math, role, **kw):
+    g, w = builder(**kw)
+    g = q.optimize(g, w)
+    s0 = ctx.create_session(g, w, role=role, math=math, argmax_exit=False)
+    fused = s0.fused_nodes()
+    s0.close()
+    outs = list(dict.fromkeys([o for _, _, o in fused] + list(g.outputs)))
+    g2 = copy.deepcopy(g)
+    g2.outputs = outs
+    s = ctx.create_session(g2, w, role=role, math=math, argmax_exit=False)
+    assert [f[0] for f in s.fused_nodes()] == [f[0] for f in fused]  # same fusion
+    gpu = dict(zip(outs, s.run({"x": x})))
+    s.close()
+    vals = {"x": x}
+    errs = {}
+
+    def get(name):
+        if name in gpu:
+            return gpu[name]
+        if name in vals:
+            return vals[name]
+        return w[name]
+
+    for n in g.nodes:
+        y = orc.eval_node(n, get)
+        vals[n.outputs[0]] = y
+        if n.outputs[0] in gpu:
+            errs[n.outputs[0]] = (n.op_type, rel(gpu[n.outputs[0]], y))
+    return fused, errs
+
+
+@pytest.mark.parametrize("math", ["tf32", "3xtf32"])
+def test_det_per_node(cuda_ctx, math):
+    fused, errs = per_node(cuda_ctx, nets.build_det, nets.det_input(2, 128, 160), math, "det")
+    ops = [f[0] for f in fused]
+    assert "QpcConvT" in ops and ops.count("Conv") >= 40
+    worst = max(errs.items(), key=lambda kv: kv[1][1])
+    assert worst[1][1] < TOL[math], worst
+
+
+@pytest.mark.parametrize("math", ["tf32", "3xtf32"])
+def test_rec_per_node(cuda_ctx, math):
+    fused, errs = per_node(cuda_ctx, nets.build_rec, nets.rec_input(4), math, "rec")
+    ops = [f[0] for f in fused]
+    assert ops.count("QpcLayerNorm") == 5 and ops.count("QpcLinear") >= 9
+    worst = max(errs.items(), key=lambda kv: kv[1][1])
+    assert worst[1][1] < TOL[math], worst
+
+
+@pytest.mark.parametrize("math", ["tf32", "3xtf32"])
+def test_cls_per_node(cuda_ctx, math):
+    fused, errs = per_node(cuda_ctx, nets.build_cls, nets.cls_input(8), math, "cls")
+    worst = max(errs.items(), key=lambda kv: kv[1][1])
+    assert worst[1][1] < TOL[math], worst

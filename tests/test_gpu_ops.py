@@ -78,11 +78,10 @@ def test_gemm_parity(cuda_ctx, m, k, n, math):
     x, w, b = nets.gemm_case(m, k, n)
     r = np.random.Generator(np.random.PCG64(2)).uniform(-1, 1, (m, n)).astype(np.float32)
     wn = np.ascontiguousarray(w.T)   # [N, K]
-    wd = dev(wn)
-    lo = None
-    if math == "3xtf32":
-        hi, lo = q.op_split_tf32(wd)
-        wd = hi
+    hi, lo = q.op_split_tf32(dev(wn))   # RN tf32 weight preparation (both modes)
+    wd = hi
+    if math == "tf32":
+        lo = None
     y = q.op_gemm(dev(x), wd, bias=dev(b), act="hswish", residual=dev(r), math=math, w_lo=lo)
     torch.cuda.synchronize()
     got = y.cpu().numpy()
