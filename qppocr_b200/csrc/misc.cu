@@ -85,11 +85,86 @@ __global__ void __launch_bounds__(256) conv_direct_kernel(
   }
 }
 
+// Small-C dense conv (stems: C <= 4): one thread per output pixel computes
+// all M channels; weights live in shared memory as [k][M] so every thread
+// reads the same word (broadcast).  Same per-element chain as above; for
+// M % 4 == 0 there are no bias-seeded tail rows.
+template <int M>
+__global__ void __launch_bounds__(256) conv_small_c_kernel(
+    const float* __restrict__ x, int x_nchw, const float* __restrict__ w,
+    const float* __restrict__ bias, const float* __restrict__ residual, float* __restrict__ y,
+    int N, int C, int H, int W, int OH, int OW, int KH, int KW, int SH, int SW, int PH, int PW,
+    ActParams act) {
+  extern __shared__ float wsm[];
+  const int K = C * KH * KW;
+  for (int i = threadIdx.x; i < K * M; i += blockDim.x) {
+    const int k = i / M, m = i % M;
+    wsm[i] = w[m * K + k];
+  }
+  __syncthreads();
+  const int64_t total = (int64_t)N * OH * OW;
+  GRID_LOOP(t, total) {
+    const int ox = (int)(t % OW);
+    int64_t r = t / OW;
+    const int oy = (int)(r % OH);
+    const int n = (int)(r / OH);
+    float acc[M];
+#pragma unroll
+    for (int i = 0; i < M; ++i) acc[i] = 0.f;
+    int k = 0;
+    for (int ch = 0; ch < C; ++ch)
+      for (int ky = 0; ky < KH; ++ky) {
+        const int iy = oy * SH - PH + ky;
+        for (int kx = 0; kx < KW; ++kx, ++k) {
+          const int ix = ox * SW - PW + kx;
+          float v = 0.f;
+          if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+            v = x_nchw ? __ldg(x + (((int64_t)n * C + ch) * H + iy) * W + ix)
+                       : __ldg(x + (((int64_t)n * H + iy) * W + ix) * C + ch);
+          const float* wk = wsm + k * M;
+#pragma unroll
+          for (int i = 0; i < M; ++i) acc[i] = __fmaf_rn(wk[i], v, acc[i]);
+        }
+      }
+    float* yo = y + t * M;
+    const float* ro = residual ? residual + t * M : nullptr;
+#pragma unroll
+    for (int i = 0; i < M; i += 4) {
+      float4 o;
+      float* op = reinterpret_cast<float*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float v = acc[i + j];
+        if (bias) v = __fadd_rn(v, __ldg(bias + i + j));
+        v = apply_act(v, act);
+        if (ro) v = __fadd_rn(v, __ldg(ro + i + j));
+        op[j] = v;
+      }
+      *reinterpret_cast<float4*>(yo + i) = o;
+    }
+  }
+}
+
 cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const float* bias,
                                const float* residual, float* y, const ConvGeom& g, int group,
                                const ActParams& act, cudaStream_t st) {
   const int mg = g.m / group;
   const int64_t pix = (int64_t)g.n * g.oh * g.ow;
+  if (group == 1 && g.c <= 4 && (g.m == 8 || g.m == 16 || g.m == 32)) {
+    const size_t smem = (size_t)g.c * g.kh * g.kw * g.m * sizeof(float);
+#define QPC_SMALLC(M_)                                                                            \
+  if (g.m == M_) {                                                                                \
+    conv_small_c_kernel<M_><<<grid_for(pix), 256, smem, st>>>(x, x_nchw, w, bias, residual, y,    \
+                                                             g.n, g.c, g.h, g.w, g.oh, g.ow,      \
+                                                             g.kh, g.kw, g.sh, g.sw, g.ph, g.pw,  \
+                                                             act);                                \
+    return cudaGetLastError();                                                                    \
+  }
+    QPC_SMALLC(8)
+    QPC_SMALLC(16)
+    QPC_SMALLC(32)
+#undef QPC_SMALLC
+  }
   if (group == 1 || mg % 8 == 0) {
     const int mblocks = (g.m + 7) / 8;
     conv_direct_kernel<8><<<grid_for(pix * mblocks), 256, 0, st>>>(
@@ -131,9 +206,68 @@ __global__ void __launch_bounds__(256) convt2x2_kernel(
   }
 }
 
+// Same arithmetic, one thread per INPUT pixel: its C channels are read once
+// and all 4 taps x M outputs are produced (each a c-ascending chain from 0).
+template <int C, int M>
+__global__ void __launch_bounds__(256) convt2x2_pix_kernel(
+    const float* __restrict__ x, const float* __restrict__ wt, const float* __restrict__ bn_a,
+    const float* __restrict__ bn_b, float* __restrict__ y, int N, int H, int W, ActParams act) {
+  __shared__ float wsm[C * M * 4];
+  for (int i = threadIdx.x; i < C * M * 4; i += blockDim.x) wsm[i] = wt[i];
+  __syncthreads();
+  const int OW = 2 * W;
+  const int64_t total = (int64_t)N * H * W;
+  GRID_LOOP(p, total) {
+    const int ix = (int)(p % W);
+    int64_t r = p / W;
+    const int iy = (int)(r % H);
+    const int n = (int)(r / H);
+    float xv[C];
+    const float4* xp = reinterpret_cast<const float4*>(x + p * C);
+#pragma unroll
+    for (int c4 = 0; c4 < C / 4; ++c4) {
+      const float4 v = __ldg(xp + c4);
+      xv[4 * c4] = v.x;
+      xv[4 * c4 + 1] = v.y;
+      xv[4 * c4 + 2] = v.z;
+      xv[4 * c4 + 3] = v.w;
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int oy = 2 * iy + (t >> 1), ox = 2 * ix + (t & 1);
+      float* yo = y + (((int64_t)n * 2 * H + oy) * OW + ox) * M;
+      float out[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float acc = 0.f;
+#pragma unroll
+        for (int ch = 0; ch < C; ++ch) acc = __fmaf_rn(xv[ch], wsm[(ch * M + m) * 4 + t], acc);
+        if (bn_a) acc = __fmaf_rn(acc, __ldg(bn_a + m), __ldg(bn_b + m));
+        out[m] = apply_act(acc, act);
+      }
+      if (M % 4 == 0) {
+#pragma unroll
+        for (int m = 0; m < M; m += 4)
+          *reinterpret_cast<float4*>(yo + m) = make_float4(out[m], out[m + 1], out[m + 2], out[m + 3]);
+      } else {
+#pragma unroll
+        for (int m = 0; m < M; ++m) yo[m] = out[m];
+      }
+    }
+  }
+}
+
 cudaError_t launch_convt2x2(const float* x, const float* wt, const float* bn_a, const float* bn_b,
                             float* y, int n, int h, int w, int c, int m, const ActParams& act,
                             cudaStream_t st) {
+  if (c == 24 && m == 24) {
+    convt2x2_pix_kernel<24, 24><<<grid_for((int64_t)n * h * w, 256), 256, 0, st>>>(x, wt, bn_a, bn_b, y, n, h, w, act);
+    return cudaGetLastError();
+  }
+  if (c == 24 && m == 1) {
+    convt2x2_pix_kernel<24, 1><<<grid_for((int64_t)n * h * w, 256), 256, 0, st>>>(x, wt, bn_a, bn_b, y, n, h, w, act);
+    return cudaGetLastError();
+  }
   convt2x2_kernel<<<grid_for((int64_t)n * 4 * h * w * m), 256, 0, st>>>(x, wt, bn_a, bn_b, y, n, h,
                                                                          w, c, m, act);
   return cudaGetLastError();
@@ -332,8 +466,23 @@ __global__ void copy_channels_kernel(const float* __restrict__ x, float* __restr
   }
 }
 
+__global__ void copy_channels4_kernel(const float4* __restrict__ x, float* __restrict__ y, int64_t pix,
+                                      int C4, int ldc, int c_off) {
+  GRID_LOOP(t, pix * C4) {
+    const int c4 = (int)(t % C4);
+    const int64_t p = t / C4;
+    *reinterpret_cast<float4*>(y + p * ldc + c_off + 4 * c4) = __ldg(x + t);
+  }
+}
+
 cudaError_t launch_copy_channels(const float* x, float* y, int64_t pix, int c, int ldc, int c_off,
                                  cudaStream_t st) {
+  if ((c & 3) == 0 && (ldc & 3) == 0 && (c_off & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    copy_channels4_kernel<<<grid_for(pix * (c / 4)), 256, 0, st>>>(reinterpret_cast<const float4*>(x), y,
+                                                                  pix, c / 4, ldc, c_off);
+    return cudaGetLastError();
+  }
   copy_channels_kernel<<<grid_for(pix * c), 256, 0, st>>>(x, y, pix, c, ldc, c_off);
   return cudaGetLastError();
 }

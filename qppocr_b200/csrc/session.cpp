@@ -408,8 +408,9 @@ void Session::fuse() {
 
   // Activation absorption into producers with a fused epilogue.
   auto producer_ok = [&](const Node& n) {
-    return (n.op == "Conv" || n.op == "QpcLinear" || n.op == "QpcConvT") &&
-           n.geti("qpc_act", 0) == 0 && !n.has_in(3) && n.geti("qpc_has_res", 0) == 0;
+    if (n.geti("qpc_act", 0) != 0 || n.geti("qpc_has_res", 0) != 0) return false;
+    if (n.op == "QpcConvT") return true;  // inputs 2..5 are BN parameters, not a residual
+    return (n.op == "Conv" || n.op == "QpcLinear") && !n.has_in(3);
   };
   bool changed = true;
   while (changed) {
@@ -719,9 +720,15 @@ class Planner {
 
   void run(const qpc_tensor* inputs, int n_inputs) {
     // Remaining uses of each tensor (consumers + graph outputs).
-    for (const Node& n : S.nodes())
+    for (size_t i = 0; i < S.nodes().size(); ++i) {
+      const Node& n = S.nodes()[i];
       for (auto& x : n.in)
-        if (!x.empty()) uses_[x]++;
+        if (!x.empty()) {
+          uses_[x]++;
+          consumers_[x].push_back((int)i);
+        }
+      for (auto& o : n.out) producer_[o] = (int)i;
+    }
     for (auto& o : S.graph_outputs()) uses_[o]++;
 
     // Graph inputs: contiguous row-major device buffers (logical NCHW).
@@ -764,13 +771,19 @@ class Planner {
       Val o;
       o.shape = v.shape;
       o.strides = rowmajor_strides(v.shape);
-      o.buf = A.alloc(o.numel(), true);
-      copy_into(v, o, "output " + go);
+      if (is_rowmajor(v) && (v.off % 4) == 0) {
+        o.buf = v.buf;  // already in host order: read it back directly
+        o.off = v.off;
+        A.bufs[v.buf].pinned = true;
+      } else {
+        o.buf = A.alloc(o.numel(), true);
+        copy_into(v, o, "output " + go);
+      }
       PlanInstance::IO io;
       io.name = go;
       io.shape = o.shape;
       io.count = o.numel();
-      io.dev = A.ptr(o.buf);
+      io.dev = A.ptr(o.buf) + o.off;
       P.outs.push_back(io);
     }
     for (auto& b : A.bufs) {
@@ -785,6 +798,69 @@ class Planner {
   Arena A;
   std::unordered_map<std::string, Val> vals_;
   std::unordered_map<std::string, int> uses_;
+  std::unordered_map<std::string, std::vector<int>> consumers_;
+  std::unordered_map<std::string, int> producer_;
+  std::unordered_map<std::string, Val> concat_bufs_;  // Concat output -> buffer allocated early
+
+  // Channel count of a 4-D tensor from its producer chain (before it exists).
+  int64_t channels_of(const std::string& name, int depth = 0) {
+    auto v = vals_.find(name);
+    if (v != vals_.end() && v->second.shape.size() == 4) return v->second.shape[1];
+    auto p = producer_.find(name);
+    if (p == producer_.end() || depth > 64) return -1;
+    const Node& n = S.nodes()[p->second];
+    if (n.op == "Conv") return S.weight(n.in[1])->shape[0];
+    if (n.op == "QpcConvT" || n.op == "ConvTranspose") return S.weight(n.in[1])->shape[1];
+    if (n.op == "Concat") {
+      int64_t t = 0;
+      for (auto& x : n.in) {
+        const int64_t c = channels_of(x, depth + 1);
+        if (c < 0) return -1;
+        t += c;
+      }
+      return t;
+    }
+    static const std::set<std::string> same = {"Resize", "Relu", "Sigmoid", "HardSigmoid", "Add", "Sub",
+                                               "Mul", "Div", "MulAddScale", "BatchNormalization",
+                                               "AveragePool", "MaxPool", "Identity", "Clip"};
+    if (same.count(n.op)) return channels_of(n.in[0], depth + 1);
+    return -1;
+  }
+
+  // If `o` (4-D, NHWC-produced) feeds only a channel Concat, return the view of
+  // its slice in the Concat's buffer (allocated now, at the first part, so no
+  // buffer that is live in between can alias it).
+  bool concat_slot(const std::string& o, const std::vector<int64_t>& oshape, Val* dst) {
+    auto cit = consumers_.find(o);
+    if (cit == consumers_.end() || cit->second.size() != 1) return false;
+    const Node& c = S.nodes()[cit->second[0]];
+    if (c.op != "Concat" || oshape.size() != 4) return false;
+    for (auto& go : S.graph_outputs())
+      if (go == o) return false;
+    int64_t axis = c.geti("axis", 0);
+    if (axis < 0) axis += 4;
+    if (axis != 1) return false;
+    int64_t off = -1, total = 0;
+    for (auto& x : c.in) {
+      if (x == o) {
+        if (off >= 0) return false;  // same tensor twice
+        off = total;
+      }
+      const int64_t ch = channels_of(x);
+      if (ch < 0) return false;
+      total += ch;
+    }
+    if (off < 0 || (off % 4) || (total % 4)) return false;
+    auto it = concat_bufs_.find(c.out[0]);
+    if (it == concat_bufs_.end()) {
+      std::vector<int64_t> full = {oshape[0], total, oshape[2], oshape[3]};
+      it = concat_bufs_.emplace(c.out[0], new_val(full, true)).first;
+    }
+    const Val& f = it->second;
+    if (f.shape[0] != oshape[0] || f.shape[2] != oshape[2] || f.shape[3] != oshape[3]) return false;
+    *dst = view_of(f, oshape, f.strides, f.off + off);
+    return true;
+  }
 
   // ------------------------------------------------------------ bookkeeping
   void use_done(const std::string& x) {
@@ -1010,7 +1086,11 @@ class Planner {
       if (r0.shape != oshape) throw GraphError{"residual shape " + shape_str(r0.shape) + " != " + shape_str(oshape)};
       res = as_nhwc(r0, n.name + " residual");
     }
-    Val y = new_val(oshape, true);
+    Val y;
+    const bool epi_path = (pw1 || kxk_tc) && !dw;
+    int64_t ldo = M;
+    if (epi_path && concat_slot(n.out[0], oshape, &y)) ldo = y.strides[3];
+    else y = new_val(oshape, true);
     float* yp = out_ptr(y);
     const float* rp = has_res ? out_ptr(res) : nullptr;
     unsigned int* err = device_state(S.device()).err_word;
@@ -1033,7 +1113,7 @@ class Planner {
       e.bias = bias;
       e.residual = rp;
       e.out = yp;
-      e.ldo = (int)M;
+      e.ldo = (int)ldo;
       e.ldr = (int)M;
       e.act = act;
       const int64_t rows = N * H * W;
@@ -1052,7 +1132,7 @@ class Planner {
       e.bias = bias;
       e.residual = rp;
       e.out = yp;
-      e.ldo = (int)M;
+      e.ldo = (int)ldo;
       e.ldr = (int)M;
       e.act = act;
       const double bytes = 4.0 * N * H * W * C + out_bytes + 4.0 * M * C * kh * kw + (has_res ? out_bytes : 0);
@@ -1489,13 +1569,17 @@ class Planner {
     }
     const int64_t N = x0.shape[0], C = x0.shape[1], H = x0.shape[2], W = x0.shape[3];
     Val x = as_nhwc(x0, n.name);
-    Val y = new_val({N, C, oh, ow}, true);
+    const std::vector<int64_t> oshape = {N, C, oh, ow};
+    Val y;
+    int64_t ldc = C;
+    if (concat_slot(n.out[0], oshape, &y)) ldc = y.strides[3];
+    else y = new_val(oshape, true);
     const float* xp = out_ptr(x);
     float* yp = out_ptr(y);
     if (C % 4) throw GraphError{"Resize: C % 4 != 0 unsupported"};
     step("resize", n.name, 4.0 * (N * C * H * W + N * C * oh * ow), 0, [=](cudaStream_t s) {
       return launch_resize_nearest_nhwc(xp, yp, (int)N, (int)H, (int)W, (int)C, (int)oh, (int)ow,
-                                        (int)C, 0, s);
+                                        (int)ldc, 0, s);
     });
     unref(x);
     define(n.out[0], y);
@@ -1515,7 +1599,15 @@ class Planner {
       oshape[axis] += p.shape[axis];
     }
     const bool nhwc = r == 4 && axis == 1;
-    Val y = new_val(oshape, nhwc);
+    Val y;
+    auto pre = concat_bufs_.find(n.out[0]);
+    if (pre != concat_bufs_.end()) {
+      y = pre->second;  // takes over the early allocation's reference
+      concat_bufs_.erase(pre);
+      if (y.shape != oshape) throw GraphError{"internal: concat buffer shape"};
+    } else {
+      y = new_val(oshape, nhwc);
+    }
     int64_t off = 0;
     for (size_t k = 0; k < parts.size(); ++k) {
       const Val& p = parts[k];
@@ -1525,7 +1617,21 @@ class Planner {
       dst.strides = y.strides;
       dst.buf = y.buf;
       dst.off = y.off + off * y.strides[axis];
-      copy_into(p, dst, n.name + "/part" + std::to_string(k));
+      const bool in_place = p.buf == dst.buf && p.off == dst.off && p.strides == dst.strides;
+      if (!in_place) {
+        if (nhwc && is_nhwc(p) && (p.off % 4) == 0 && (p.shape[1] % 4) == 0 && (oshape[1] % 4) == 0 &&
+            (off % 4) == 0) {
+          const float* src = out_ptr(p);
+          float* dp = A.ptr(y.buf) + y.off;
+          const int64_t pix = p.shape[0] * p.shape[2] * p.shape[3];
+          const int pc = (int)p.shape[1], ldc = (int)oshape[1], coff = (int)off;
+          step("copy", n.name + "/part" + std::to_string(k), 8.0 * p.numel(), 0, [=](cudaStream_t st) {
+            return launch_copy_channels(src, dp, pix, pc, ldc, coff, st);
+          });
+        } else {
+          copy_into(p, dst, n.name + "/part" + std::to_string(k));
+        }
+      }
       off += p.shape[axis];
     }
     define(n.out[0], y);
