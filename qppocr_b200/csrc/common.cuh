@@ -116,6 +116,39 @@ __device__ __forceinline__ float apply_act(float v, const ActParams& a) {
   }
 }
 
+// Activation over a register array: one (uniform) switch per array, not per
+// element, so the epilogue's inner loops stay branch-free.
+template <int N>
+__device__ __forceinline__ void apply_act_n(float (&v)[N], const ActParams& a) {
+  switch (a.kind) {
+    case ACT_NONE: return;
+    case ACT_RELU:
+#pragma unroll
+      for (int j = 0; j < N; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;
+      return;
+    case ACT_HARDSWISH:
+#pragma unroll
+      for (int j = 0; j < N; ++j) v[j] = __fmul_rn(v[j], hardsigmoid(v[j], a.alpha, a.beta));
+      return;
+    case ACT_HARDSIGMOID:
+#pragma unroll
+      for (int j = 0; j < N; ++j) v[j] = hardsigmoid(v[j], a.alpha, a.beta);
+      return;
+    case ACT_SIGMOID:
+#pragma unroll
+      for (int j = 0; j < N; ++j) v[j] = sigmoid1(v[j]);
+      return;
+    case ACT_SWISH:
+#pragma unroll
+      for (int j = 0; j < N; ++j) v[j] = __fmul_rn(v[j], sigmoid1(v[j]));
+      return;
+    default:
+#pragma unroll
+      for (int j = 0; j < N; ++j) v[j] = apply_act(v[j], a);
+      return;
+  }
+}
+
 // ------------------------------------------------------------- smem / PTX
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -193,6 +226,39 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
       "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+
+// TMA tiled stores from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          (uint64_t)map),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1,
+                                             int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          (uint64_t)map),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until at most N committed bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// Named barrier among `count` threads (ids 1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {

@@ -54,15 +54,20 @@ __global__ void __launch_bounds__(256) dwconv_nhwc_kernel(
     }
     const float4 b4 = bias ? __ldg(reinterpret_cast<const float4*>(bias) + c4)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    float vals[4 * RUN];
+#pragma unroll
+    for (int i = 0; i < RUN; ++i) {
+      vals[4 * i] = __fadd_rn(acc[i].x, b4.x);
+      vals[4 * i + 1] = __fadd_rn(acc[i].y, b4.y);
+      vals[4 * i + 2] = __fadd_rn(acc[i].z, b4.z);
+      vals[4 * i + 3] = __fadd_rn(acc[i].w, b4.w);
+    }
+    apply_act_n(vals, act);
 #pragma unroll
     for (int i = 0; i < RUN; ++i) {
       const int ox = ox0 + i;
       if (ox >= OW) break;
-      float4 o;
-      o.x = apply_act(__fadd_rn(acc[i].x, b4.x), act);
-      o.y = apply_act(__fadd_rn(acc[i].y, b4.y), act);
-      o.z = apply_act(__fadd_rn(acc[i].z, b4.z), act);
-      o.w = apply_act(__fadd_rn(acc[i].w, b4.w), act);
+      float4 o = make_float4(vals[4 * i], vals[4 * i + 1], vals[4 * i + 2], vals[4 * i + 3]);
       const int64_t oidx = ((int64_t)(n * OH + oy) * OW + ox) * C4 + c4;
       if (residual) {
         const float4 rr = __ldg(reinterpret_cast<const float4*>(residual) + oidx);

@@ -18,7 +18,10 @@
 //   lo*hi + hi*lo + hi*hi.  The tensor core's fp32 accumulation drifts toward
 //   zero with K, so partial sums over CH k-blocks are promoted into fp32
 //   registers with IEEE round-to-nearest adds (TMEM is drained per chunk).
-// * Epilogue: warps 2-5 read their 32 TMEM lanes (tcgen05.ld 32x32b), add bias,
+// * Persistent: one CTA per SM walks output tiles round-robin; TMA, A
+//   conversion and MMA run ahead across tiles while the epilogue drains the
+//   other of two TMEM accumulators.
+// * Epilogue: warps 4-7 read their 32 TMEM lanes (tcgen05.ld 32x32b), add bias,
 //   apply the fused activation, add the residual (optionally through a
 //   nearest-upsample index map) and store fp32 rows.
 // * A_MODE 1 (k x k, stride 1 conv): the A tile is a 4-D TMA box
@@ -38,11 +41,14 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 32;                  // fp32 elements per 128-byte swizzle row
 constexpr int A_TILE_BYTES = BM * BK * 4;
+constexpr int OUT_STAGE_BYTES = BM * 32 * 4;  // one 128 x 32 fp32 output chunk (16 KB)
 
 struct GemmArgs {
   int M, N, K;          // M = output rows (pixels/tokens), N = output channels
   unsigned int* err;    // device error word for bounded-wait timeouts
   int nkb;              // number of 32-wide k-blocks
+  int m_tiles;          // output row tiles (128 rows each)
+  int tma_store;        // 1: output tiles leave through smem staging + TMA store
   GemmEpilogue epi;
   // A_MODE 1 geometry
   int taps, kw, ph, pw, cblocks;
@@ -63,14 +69,13 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& args, const float
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int col = col0 + j;
-    float t = v[j];
-    if (col < args.N) {
-      if (e.bias) t = __fadd_rn(t, __ldg(e.bias + col));
-      t = apply_act(t, e.act);
-      if (e.residual) t = __fadd_rn(t, __ldg(e.residual + rrow * e.ldr + col));
-    }
-    o[j] = t;
+    o[j] = (e.bias && col < args.N) ? __fadd_rn(v[j], __ldg(e.bias + col)) : v[j];
   }
+  apply_act_n(o, e.act);
+  if (e.residual)
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (col0 + j < args.N) o[j] = __fadd_rn(o[j], __ldg(e.residual + rrow * e.ldr + col0 + j));
   float* dst = e.out + orow * e.ldo + e.col_off + col0;
   const bool vec_ok = ((e.ldo | e.col_off) & 3) == 0 && col0 + 16 <= args.N;
   if (vec_ok) {
@@ -84,64 +89,181 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& args, const float
   }
 }
 
-constexpr int NUM_THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 convert + epilogue
-constexpr int CH = 1;             // k-blocks per promotion chunk (3xTF32)
-constexpr int LAG = 1;            // converter runs this many k-blocks ahead of a drain
 
+// Output row (pixel / token) and residual row of tile row `r`; -1 if the row
+// lies outside the output.
+struct RowMap {
+  int64_t orow, rrow;
+};
+
+template <int A_MODE>
+__device__ __forceinline__ RowMap row_map(const GemmArgs& args, int m_blk, int img, int oy0, int ox0,
+                                          int r) {
+  RowMap m{-1, -1};
+  if (A_MODE == 0) {
+    const int64_t row = (int64_t)m_blk * BM + r;
+    if (row < args.M) m.orow = row;
+  } else {
+    const int oy = oy0 + r / args.tw, ox = ox0 + r % args.tw;
+    if (oy < args.oh && ox < args.ow) m.orow = ((int64_t)img * args.oh + oy) * args.ow + ox;
+  }
+  m.rrow = m.orow;
+  const GemmEpilogue& e = args.epi;
+  if (m.orow >= 0 && e.residual && e.rh > 0) {
+    // nearest resize source row, resize.rs:43-50: (int)((float)o * in / out)
+    const int x = (int)(m.orow % e.ow);
+    const int y = (int)((m.orow / e.ow) % e.oh);
+    const int64_t nn = m.orow / ((int64_t)e.ow * e.oh);
+    int iy = (int)__fdiv_rn(__fmul_rn((float)y, (float)e.rh), (float)e.oh);
+    int ix = (int)__fdiv_rn(__fmul_rn((float)x, (float)e.rw), (float)e.ow);
+    iy = iy < e.rh - 1 ? iy : e.rh - 1;
+    ix = ix < e.rw - 1 ? ix : e.rw - 1;
+    m.rrow = (nn * e.rh + iy) * e.rw + ix;
+  }
+  return m;
+}
+
+// Epilogue of one tile through shared memory: for each 32-column chunk the
+// residual (if any) is loaded cooperatively (8 threads per 128-byte row
+// segment), every thread finishes its row (bias, activation, residual) into a
+// 128B-swizzled staging buffer, and one thread writes the chunk with a TMA
+// store.  Two staging buffers alternate; a buffer is rewritten only after the
+// store issued from it two chunks earlier has finished reading it.
+template <int BN, int A_MODE, class Fetch>
+__device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorMap* tm_out,
+                                           uint8_t* stage, uint32_t& chunk_ctr, int m_blk, int n0,
+                                           int img, int oy0, int ox0, int r, int t, Fetch&& fetch) {
+  const GemmEpilogue& e = args.epi;
+  const RowMap mine = row_map<A_MODE>(args, m_blk, img, oy0, ox0, r);
+#pragma unroll 1
+  for (int cc = 0; cc < BN; cc += 32) {
+    if (n0 + cc >= args.N) break;
+    float* sb = reinterpret_cast<float*>(stage + (chunk_ctr & 1u) * OUT_STAGE_BYTES);
+    if (t == 0) bulk_wait_group_read<1>();
+    named_bar_sync(1, 128);
+    if (e.residual) {
+#pragma unroll 2
+      for (int i = t; i < BM * 8; i += 128) {
+        const int row = i >> 3, c4 = i & 7;
+        const int col = n0 + cc + c4 * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        const RowMap rm = row_map<A_MODE>(args, m_blk, img, oy0, ox0, row);
+        if (rm.orow >= 0 && col < args.N)
+          v = __ldg(reinterpret_cast<const float4*>(e.residual + rm.rrow * e.ldr + col));
+        *reinterpret_cast<float4*>(sb + row * 32 + ((c4 ^ (row & 7)) << 2)) = v;
+      }
+      named_bar_sync(1, 128);
+    }
+    float v[32];
+    fetch(cc, v);
+    if (e.bias) {
+      // columns past N are clipped by the TMA store; keep their reads in bounds
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const int col = n0 + cc + j;
+        if (col < args.N) {
+          const float4 b4 = __ldg(reinterpret_cast<const float4*>(e.bias + col));
+          v[j] = __fadd_rn(v[j], b4.x);
+          v[j + 1] = __fadd_rn(v[j + 1], b4.y);
+          v[j + 2] = __fadd_rn(v[j + 2], b4.z);
+          v[j + 3] = __fadd_rn(v[j + 3], b4.w);
+        }
+      }
+    }
+    apply_act_n(v, e.act);
+    float* myrow = sb + r * 32;
+#pragma unroll
+    for (int c4 = 0; c4 < 8; ++c4) {
+      float4* slot = reinterpret_cast<float4*>(myrow + ((c4 ^ (r & 7)) << 2));
+      float4 o = make_float4(v[c4 * 4], v[c4 * 4 + 1], v[c4 * 4 + 2], v[c4 * 4 + 3]);
+      if (e.residual) {
+        const float4 rv = *slot;
+        o.x = __fadd_rn(o.x, rv.x);
+        o.y = __fadd_rn(o.y, rv.y);
+        o.z = __fadd_rn(o.z, rv.z);
+        o.w = __fadd_rn(o.w, rv.w);
+      }
+      *slot = o;
+    }
+    (void)mine;
+    fence_proxy_async_smem();
+    named_bar_sync(1, 128);
+    if (t == 0) {
+      if (A_MODE == 0) tma_store_2d(tm_out, sb, n0 + cc, m_blk * BM);
+      else tma_store_4d(tm_out, sb, n0 + cc, ox0, oy0, img);
+      bulk_commit_group();
+    }
+    ++chunk_ctr;
+  }
+}
+
+constexpr int NUM_THREADS = 256;  // w0 TMA, w1 MMA, w2-3 convert A, w4-7 epilogue
+constexpr int CH = 1;             // k-blocks per promotion chunk (3xTF32)
+
+struct TileCoord {
+  int m_blk, n0, img, oy0, ox0;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(const GemmArgs& a, int tile, int n_tiles, int bn) {
+  TileCoord c;
+  c.m_blk = tile / n_tiles;
+  c.n0 = (tile % n_tiles) * bn;
+  c.img = c.oy0 = c.ox0 = 0;
+  if (a.tiles_x > 0) {
+    const int per_img = a.tiles_x * a.tiles_y;
+    c.img = c.m_blk / per_img;
+    const int rem = c.m_blk % per_img;
+    c.oy0 = (rem / a.tiles_x) * a.th;
+    c.ox0 = (rem % a.tiles_x) * a.tw;
+  }
+  return c;
+}
+
+// Persistent, warp-specialised tcgen05 GEMM.  Each CTA walks tiles
+// blockIdx.x, blockIdx.x + gridDim.x, ...; the TMA ring, the A conversion and
+// the MMAs run ahead across tile boundaries while the epilogue warps drain the
+// previous tile from the other TMEM accumulator.
 template <int BN, int STAGES, bool SPLIT, int A_MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmBlo, const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmOut,
+                   const GemmArgs args) {
   using SM = Smem<BN, SPLIT>;
-  // 3xTF32 ping-pongs two accumulators so the MMA runs on while a chunk drains.
-  constexpr uint32_t TMEM_COLS = SPLIT ? 2 * BN : (BN < 32 ? 32 : BN);
+  // Two accumulators: consecutive tiles (TF32) or consecutive K chunks (3xTF32).
+  constexpr uint32_t TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
   __shared__ __align__(8) uint64_t conv_bar[STAGES];
-  __shared__ __align__(8) uint64_t acc_bar;
-  __shared__ __align__(8) uint64_t chunk_full[2];
-  __shared__ __align__(8) uint64_t chunk_free[2];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_slot;
-  __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // Tile coordinates.  Consecutive CTAs walk the N tiles of one M block so
-  // the A rows they share are still in L2.
   const int n_tiles = (args.N + BN - 1) / BN;
-  const int m_blk = blockIdx.x / n_tiles;
-  const int n_blk = blockIdx.x % n_tiles;
-  const int n0 = n_blk * BN;
-  int img = 0, oy0 = 0, ox0 = 0;
-  if (A_MODE == 1) {
-    const int per_img = args.tiles_x * args.tiles_y;
-    img = m_blk / per_img;
-    const int rem = m_blk % per_img;
-    oy0 = (rem / args.tiles_x) * args.th;
-    ox0 = (rem % args.tiles_x) * args.tw;
-  }
+  const int total_tiles = args.m_tiles * n_tiles;
+  const int nkb = args.nkb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
-      mbar_init(&conv_bar[s], 128);
+      mbar_init(&conv_bar[s], 64);
     }
-    mbar_init(&acc_bar, 1);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&chunk_full[b], 1);
-      mbar_init(&chunk_free[b], 128);
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
     }
-    abort_flag = 0;
     fence_barrier_init();
     prefetch_tensormap(&tmA);
     prefetch_tensormap(&tmB);
     if (SPLIT) prefetch_tensormap(&tmBlo);
+    if (args.tma_store) prefetch_tensormap(&tmOut);
   }
+  uint8_t* out_stage = smem + STAGES * SM::STAGE;  // 2 x 16 KB, 1024-aligned
   if (warp == 0) {
     tmem_alloc(&tmem_base_slot, TMEM_COLS);
     tmem_relinquish();
@@ -150,30 +272,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_d = tmem_base_slot;
-  const int nkb = args.nkb;
-  const int nchunks = (nkb + CH - 1) / CH;
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
       const uint32_t bytes = SPLIT ? (A_TILE_BYTES + 2 * SM::B_TILE) : (A_TILE_BYTES + SM::B_TILE);
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-        if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.err)) { abort_flag = 1; break; }
-        uint8_t* st = smem + s * SM::STAGE;
-        mbar_arrive_expect_tx(&full_bar[s], bytes);
-        if (A_MODE == 0) {
-          tma_load_2d(st, &tmA, &full_bar[s], kb * BK, m_blk * BM);
-          tma_load_2d(st + A_TILE_BYTES, &tmB, &full_bar[s], kb * BK, n0);
-          if (SPLIT) tma_load_2d(st + 2 * A_TILE_BYTES + SM::B_TILE, &tmBlo, &full_bar[s], kb * BK, n0);
-        } else {
-          const int tap = kb / args.cblocks, cb = kb % args.cblocks;
-          const int ky = tap / args.kw, kx = tap % args.kw;
-          tma_load_4d(st, &tmA, &full_bar[s], cb * BK, ox0 + kx - args.pw, oy0 + ky - args.ph, img);
-          tma_load_4d(st + A_TILE_BYTES, &tmB, &full_bar[s], cb * BK, n0, tap, 0);
-          if (SPLIT)
-            tma_load_4d(st + 2 * A_TILE_BYTES + SM::B_TILE, &tmBlo, &full_bar[s], cb * BK, n0, tap, 0);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        const TileCoord tc = tile_coord(args, tile, n_tiles, BN);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.err)) { ok = false; break; }
+          uint8_t* st = smem + s * SM::STAGE;
+          mbar_arrive_expect_tx(&full_bar[s], bytes);
+          if (A_MODE == 0) {
+            tma_load_2d(st, &tmA, &full_bar[s], kb * BK, tc.m_blk * BM);
+            tma_load_2d(st + A_TILE_BYTES, &tmB, &full_bar[s], kb * BK, tc.n0);
+            if (SPLIT) tma_load_2d(st + 2 * A_TILE_BYTES + SM::B_TILE, &tmBlo, &full_bar[s], kb * BK, tc.n0);
+          } else {
+            const int tap = kb / args.cblocks, cb = kb % args.cblocks;
+            const int ky = tap / args.kw, kx = tap % args.kw;
+            tma_load_4d(st, &tmA, &full_bar[s], cb * BK, tc.ox0 + kx - args.pw, tc.oy0 + ky - args.ph, tc.img);
+            tma_load_4d(st + A_TILE_BYTES, &tmB, &full_bar[s], cb * BK, tc.n0, tap, 0);
+            if (SPLIT)
+              tma_load_4d(st + 2 * A_TILE_BYTES + SM::B_TILE, &tmBlo, &full_bar[s], cb * BK, tc.n0, tap, 0);
+          }
         }
       }
     }
@@ -181,125 +306,108 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       // ---------------- MMA issuer
       constexpr uint32_t idesc = idesc_tf32(BM, BN);
+      uint32_t it = 0, acc_i = 0;  // acc_i: accumulator fills (tiles, or chunks in 3xTF32)
       bool ok = true;
-      for (int kb = 0; kb < nkb && ok; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-        const bool first = SPLIT ? (kb % CH) == 0 : kb == 0;
-        const int chunk = kb / CH, buf = chunk & 1;
-        // accumulator `buf` is reused by chunk c once chunk c - 2 has drained
-        if (SPLIT && first && chunk >= 2 &&
-            !mbar_wait(&chunk_free[buf], (uint32_t)((chunk >> 1) - 1) & 1u, args.err)) {
-          ok = false;
-          break;
-        }
-        const uint32_t d_tmem = tmem_d + (SPLIT ? (uint32_t)(buf * BN) : 0u);
-        if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + s * SM::STAGE);
-        const uint32_t b_addr = a_addr + A_TILE_BYTES;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
+          const bool first = SPLIT ? (kb % CH) == 0 : kb == 0;
+          const uint32_t buf = acc_i & 1u;
+          if (first && acc_i >= 2 && !mbar_wait(&acc_empty[buf], ((acc_i >> 1) - 1) & 1u, args.err)) {
+            ok = false;
+            break;
+          }
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_d + buf * BN;
+          const uint32_t a_addr = smem_u32(smem + s * SM::STAGE);
+          const uint32_t b_addr = a_addr + A_TILE_BYTES;
 #pragma unroll
-        for (int ks = 0; ks < BK / 8; ++ks) {
-          const uint32_t acc = (!first || ks > 0) ? 1u : 0u;
-          const uint64_t ad = sw128_kmajor_desc(a_addr + ks * 32);
-          const uint64_t bd = sw128_kmajor_desc(b_addr + ks * 32);
-          if (SPLIT) {
-            const uint64_t alo = sw128_kmajor_desc(b_addr + SM::B_TILE + ks * 32);
-            const uint64_t blo = sw128_kmajor_desc(b_addr + SM::B_TILE + A_TILE_BYTES + ks * 32);
-            mma_tf32(d_tmem, alo, bd, idesc, acc);
-            mma_tf32(d_tmem, ad, blo, idesc, 1u);
-            mma_tf32(d_tmem, ad, bd, idesc, 1u);
-          } else {
-            mma_tf32(d_tmem, ad, bd, idesc, acc);
+          for (int ks = 0; ks < BK / 8; ++ks) {
+            const uint32_t acc = (!first || ks > 0) ? 1u : 0u;
+            const uint64_t ad = sw128_kmajor_desc(a_addr + ks * 32);
+            const uint64_t bd = sw128_kmajor_desc(b_addr + ks * 32);
+            if (SPLIT) {
+              const uint64_t alo = sw128_kmajor_desc(b_addr + SM::B_TILE + ks * 32);
+              const uint64_t blo = sw128_kmajor_desc(b_addr + SM::B_TILE + A_TILE_BYTES + ks * 32);
+              mma_tf32(d_tmem, alo, bd, idesc, acc);
+              mma_tf32(d_tmem, ad, blo, idesc, 1u);
+              mma_tf32(d_tmem, ad, bd, idesc, 1u);
+            } else {
+              mma_tf32(d_tmem, ad, bd, idesc, acc);
+            }
+          }
+          mma_commit(&empty_bar[s]);  // frees the stage once these MMAs have read it
+          const bool last = SPLIT ? ((kb % CH) == CH - 1 || kb == nkb - 1) : kb == nkb - 1;
+          if (last) {
+            mma_commit(&acc_full[buf]);
+            ++acc_i;
           }
         }
-        mma_commit(&empty_bar[s]);   // frees the stage once these MMAs have read it
-        if (SPLIT && ((kb % CH) == CH - 1 || kb == nkb - 1)) mma_commit(&chunk_full[buf]);
       }
-      if (!ok) abort_flag = 1;
-      if (!SPLIT) mma_commit(&acc_bar);   // accumulator complete (or abandoned)
+    }
+  } else if (warp < 4) {
+    // ---------------- converters: round A to tf32 (nearest) in place; in
+    // 3xTF32 also write lo = rn(A - hi).  Elementwise, so the swizzle is moot.
+    const int t = threadIdx.x - 64;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1u;
+        if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
+        float4* a = reinterpret_cast<float4*>(smem + s * SM::STAGE);
+        float4* lo = reinterpret_cast<float4*>(smem + s * SM::STAGE + A_TILE_BYTES + SM::B_TILE);
+#pragma unroll 4
+        for (int i = t; i < A_TILE_BYTES / 16; i += 64) {
+          const float4 v = a[i];
+          float4 h;
+          h.x = tf32_rna(v.x);
+          h.y = tf32_rna(v.y);
+          h.z = tf32_rna(v.z);
+          h.w = tf32_rna(v.w);
+          a[i] = h;
+          if (SPLIT) {
+            float4 l;
+            l.x = tf32_rna(__fsub_rn(v.x, h.x));
+            l.y = tf32_rna(__fsub_rn(v.y, h.y));
+            l.z = tf32_rna(__fsub_rn(v.z, h.z));
+            l.w = tf32_rna(__fsub_rn(v.w, h.w));
+            lo[i] = l;
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&conv_bar[s]);
+      }
     }
   } else {
-    // ---------------- warps 2-5: convert A on chip, then the epilogue.
-    // TMEM lane quarter of this warp = warp % 4; its rows are 32 * (warp % 4) + lane.
-    const int t = threadIdx.x - 64;
+    // ---------------- epilogue warps 4-7: TMEM lane quarter q = warp % 4.
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const uint32_t lane_base = tmem_d + ((uint32_t)(q * 32) << 16);
-    float accr[SPLIT ? BN : 1];
-#pragma unroll
-    for (int j = 0; j < (SPLIT ? BN : 1); ++j) accr[j] = 0.f;
+    const GemmEpilogue& e = args.epi;
+    uint32_t acc_i = 0, chunk_ctr = 0;
     bool ok = true;
-    int drained = 0;
-    // Promotion of a finished chunk: TMEM partial sum -> fp32 registers (RN adds).
-    auto drain = [&](int c) {
-      const int b = c & 1;
-      if (!ok || !mbar_wait(&chunk_full[b], (uint32_t)(c >> 1) & 1u, args.err)) { ok = false; return; }
-      tc_fence_after();
-#pragma unroll
-      for (int c0 = 0; c0 < (SPLIT ? BN : 16); c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16_nowait(lane_base + (uint32_t)(b * BN) + c0, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          accr[(c0 + j) % (SPLIT ? BN : 1)] =
-              __fadd_rn(accr[(c0 + j) % (SPLIT ? BN : 1)], __uint_as_float(v[j]));
-      }
-      tc_fence_before();
-      mbar_arrive(&chunk_free[b]);
-    };
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-      if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
-      float4* a = reinterpret_cast<float4*>(smem + s * SM::STAGE);
-      float4* lo = reinterpret_cast<float4*>(smem + s * SM::STAGE + A_TILE_BYTES + SM::B_TILE);
-#pragma unroll
-      for (int i = t; i < A_TILE_BYTES / 16; i += 128) {
-        const float4 v = a[i];
-        float4 h;
-        h.x = tf32_rna(v.x);
-        h.y = tf32_rna(v.y);
-        h.z = tf32_rna(v.z);
-        h.w = tf32_rna(v.w);
-        a[i] = h;
-        if (SPLIT) {
-          float4 l;
-          l.x = tf32_rna(__fsub_rn(v.x, h.x));
-          l.y = tf32_rna(__fsub_rn(v.y, h.y));
-          l.z = tf32_rna(__fsub_rn(v.z, h.z));
-          l.w = tf32_rna(__fsub_rn(v.w, h.w));
-          lo[i] = l;
-        }
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&conv_bar[s]);
-      if (SPLIT)
-        while (ok && drained < nchunks && min((drained + 1) * CH, nkb) - 1 <= kb - LAG) drain(drained++);
-    }
-    if (SPLIT)
-      while (ok && drained < nchunks) drain(drained++);
-    if (!SPLIT) ok = ok && mbar_wait(&acc_bar, 0, args.err);
-    tc_fence_after();
-    if (ok && !abort_flag) {
+    float accr[SPLIT ? BN : 1];
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      const TileCoord tc = tile_coord(args, tile, n_tiles, BN);
       int64_t orow = -1, rrow = -1;
       if (A_MODE == 0) {
-        const int64_t m = (int64_t)m_blk * BM + r;
+        const int64_t m = (int64_t)tc.m_blk * BM + r;
         if (m < args.M) orow = m;
       } else {
-        const int oy = oy0 + r / args.tw, ox = ox0 + r % args.tw;
-        if (oy < args.oh && ox < args.ow) orow = ((int64_t)img * args.oh + oy) * args.ow + ox;
+        const int oy = tc.oy0 + r / args.tw, ox = tc.ox0 + r % args.tw;
+        if (oy < args.oh && ox < args.ow) orow = ((int64_t)tc.img * args.oh + oy) * args.ow + ox;
       }
       if (orow >= 0) {
         rrow = orow;
-        const GemmEpilogue& e = args.epi;
         if (e.residual && e.rh > 0) {
           // nearest resize source row, resize.rs:43-50: (int)((float)o * in / out)
-          const int64_t pix = orow;
-          const int x = (int)(pix % e.ow);
-          const int y = (int)((pix / e.ow) % e.oh);
-          const int64_t nn = pix / ((int64_t)e.ow * e.oh);
+          const int x = (int)(orow % e.ow);
+          const int y = (int)((orow / e.ow) % e.oh);
+          const int64_t nn = orow / ((int64_t)e.ow * e.oh);
           int iy = (int)__fdiv_rn(__fmul_rn((float)y, (float)e.rh), (float)e.oh);
           int ix = (int)__fdiv_rn(__fmul_rn((float)x, (float)e.rw), (float)e.ow);
           iy = iy < e.rh - 1 ? iy : e.rh - 1;
@@ -307,27 +415,83 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           rrow = (nn * e.rh + iy) * e.rw + ix;
         }
       }
-      if (SPLIT) {
+      if (!SPLIT) {
+        const uint32_t buf = acc_i & 1u;
+        if (!mbar_wait(&acc_full[buf], (acc_i >> 1) & 1u, args.err)) { ok = false; break; }
+        tc_fence_after();
+        if (args.tma_store) {
+          store_tile<BN, A_MODE>(args, &tmOut, out_stage, chunk_ctr, tc.m_blk, tc.n0, tc.img, tc.oy0,
+                                 tc.ox0, r, threadIdx.x - 128, [&](int c, float (&v)[32]) {
+                                   uint32_t a[16], b[16];
+                                   tmem_ld16_nowait(lane_base + buf * BN + c, a);
+                                   tmem_ld16_nowait(lane_base + buf * BN + c + 16, b);
+                                   tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < BN; c += 16) {
-          if (n0 + c < args.N && orow >= 0) {
+                                   for (int j = 0; j < 16; ++j) {
+                                     v[j] = __uint_as_float(a[j]);
+                                     v[16 + j] = __uint_as_float(b[j]);
+                                   }
+                                 });
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            if (tc.n0 + c >= args.N) break;
             float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = accr[(c + j) % (SPLIT ? BN : 1)];
-            epilogue_store<BN>(args, v, orow, rrow, n0 + c);
+            tmem_ld16(lane_base + buf * BN + c, v);  // warp-collective
+            if (orow >= 0) epilogue_store<BN>(args, v, orow, rrow, tc.n0 + c);
           }
         }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+        ++acc_i;
       } else {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          if (n0 + c >= args.N) break;
-          float v[16];
-          tmem_ld16(lane_base + c, v);   // warp-collective; every lane participates
-          if (orow >= 0) epilogue_store<BN>(args, v, orow, rrow, n0 + c);
+#pragma unroll
+        for (int j = 0; j < BN; ++j) accr[j % (SPLIT ? BN : 1)] = 0.f;
+        const int nchunks = (nkb + CH - 1) / CH;
+        for (int ck = 0; ck < nchunks; ++ck) {
+          // promotion: TMEM partial sum of this chunk -> fp32 registers (RN adds)
+          const uint32_t buf = acc_i & 1u;
+          if (!mbar_wait(&acc_full[buf], (acc_i >> 1) & 1u, args.err)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int c0 = 0; c0 < (SPLIT ? BN : 16); c0 += 16) {
+            uint32_t v[16];
+            tmem_ld16_nowait(lane_base + buf * BN + c0, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              accr[(c0 + j) % (SPLIT ? BN : 1)] =
+                  __fadd_rn(accr[(c0 + j) % (SPLIT ? BN : 1)], __uint_as_float(v[j]));
+          }
+          tc_fence_before();
+          mbar_arrive(&acc_empty[buf]);
+          ++acc_i;
+        }
+        if (!ok) break;
+        if (args.tma_store) {
+          store_tile<BN, A_MODE>(args, &tmOut, out_stage, chunk_ctr, tc.m_blk, tc.n0, tc.img, tc.oy0,
+                                 tc.ox0, r, threadIdx.x - 128, [&](int c, float (&v)[32]) {
+#pragma unroll
+                                   for (int cb = 0; cb < BN; cb += 32)
+                                     if (cb == c)
+#pragma unroll
+                                       for (int j = 0; j < 32; ++j) v[j] = accr[(cb + j) % (SPLIT ? BN : 1)];
+                                 });
+        } else {
+#pragma unroll
+          for (int c = 0; c < BN; c += 16) {
+            if (tc.n0 + c < args.N && orow >= 0) {
+              float v[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = accr[(c + j) % (SPLIT ? BN : 1)];
+              epilogue_store<BN>(args, v, orow, rrow, tc.n0 + c);
+            }
+          }
         }
       }
     }
   }
+  if (args.tma_store && threadIdx.x == 128) bulk_wait_group<0>();  // stores out of smem before exit
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem_d, TMEM_COLS);
@@ -372,37 +536,50 @@ bool make_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims
   return r == CUDA_SUCCESS;
 }
 
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
+
 template <int BN, int STAGES, bool SPLIT, int A_MODE>
 cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& blo,
-                       const GemmArgs& args, int grid, cudaStream_t st) {
+                       const CUtensorMap& out, const GemmArgs& args, int tiles, cudaStream_t st) {
   auto kern = gemm_tc_kernel<BN, STAGES, SPLIT, A_MODE>;
-  const int smem = STAGES * Smem<BN, SPLIT>::STAGE + 1024;
+  const int smem = STAGES * Smem<BN, SPLIT>::STAGE + 2 * OUT_STAGE_BYTES + 1024;
   static bool attr_set = false;  // per instantiation
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  kern<<<grid, NUM_THREADS, smem, st>>>(a, b, blo, args);
+  const int grid = tiles < sm_count() ? tiles : sm_count();
+  kern<<<grid, NUM_THREADS, smem, st>>>(a, b, blo, out, args);
   return cudaGetLastError();
 }
 
 template <int A_MODE>
 cudaError_t dispatch(int bn, bool split, const CUtensorMap& a, const CUtensorMap& b,
-                     const CUtensorMap& blo, const GemmArgs& args, int grid_m, cudaStream_t st) {
-  const int grid = grid_m * ((args.N + bn - 1) / bn);
+                     const CUtensorMap& blo, const CUtensorMap& out, GemmArgs args, int grid_m,
+                     cudaStream_t st) {
+  args.m_tiles = grid_m;
+  const int tiles = grid_m * ((args.N + bn - 1) / bn);
   if (!split) {
     switch (bn) {
-      case 32: return run_kernel<32, 4, false, A_MODE>(a, b, blo, args, grid, st);
-      case 64: return run_kernel<64, 4, false, A_MODE>(a, b, blo, args, grid, st);
-      case 128: return run_kernel<128, 3, false, A_MODE>(a, b, blo, args, grid, st);
-      default: return run_kernel<256, 3, false, A_MODE>(a, b, blo, args, grid, st);
+      case 32: return run_kernel<32, 6, false, A_MODE>(a, b, blo, out, args, tiles, st);
+      case 64: return run_kernel<64, 6, false, A_MODE>(a, b, blo, out, args, tiles, st);
+      case 128: return run_kernel<128, 5, false, A_MODE>(a, b, blo, out, args, tiles, st);
+      default: return run_kernel<256, 3, false, A_MODE>(a, b, blo, out, args, tiles, st);
     }
   }
   switch (bn) {
-    case 32: return run_kernel<32, 4, true, A_MODE>(a, b, blo, args, grid, st);
-    case 64: return run_kernel<64, 4, true, A_MODE>(a, b, blo, args, grid, st);
-    default: return run_kernel<128, 3, true, A_MODE>(a, b, blo, args, grid, st);
+    case 32: return run_kernel<32, 4, true, A_MODE>(a, b, blo, out, args, tiles, st);
+    case 64: return run_kernel<64, 4, true, A_MODE>(a, b, blo, out, args, tiles, st);
+    default: return run_kernel<128, 3, true, A_MODE>(a, b, blo, out, args, tiles, st);
   }
 }
 
@@ -451,8 +628,17 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
   args.nkb = (K + BK - 1) / BK;
   args.epi = epi;
   args.err = err;
+  CUtensorMap mo = ma;
+  const float* obase = epi.out + epi.col_off;
+  if ((N % 4) == 0 && (epi.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(obase) & 15) == 0 &&
+      (!epi.residual || (epi.ldr % 4) == 0)) {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)epi.ldo * 4};
+    const uint32_t box[2] = {32, BM};
+    args.tma_store = make_map(&mo, obase, 2, dims, strides, box) ? 1 : 0;
+  }
   const int grid_m = (int)((M + BM - 1) / BM);
-  return dispatch<0>(bn, split, ma, mb, mblo, args, grid_m, st);
+  return dispatch<0>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
 }
 
 cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, const float* wk_lo,
@@ -507,8 +693,18 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
   args.tiles_y = (g.oh + th - 1) / th;
   args.epi = epi;
   args.err = err;
+  CUtensorMap mo = ma;
+  const float* obase = epi.out + epi.col_off;
+  if ((g.m % 4) == 0 && (epi.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(obase) & 15) == 0 &&
+      (!epi.residual || (epi.ldr % 4) == 0)) {
+    const uint64_t dims[4] = {(uint64_t)g.m, (uint64_t)g.ow, (uint64_t)g.oh, (uint64_t)g.n};
+    const uint64_t strides[3] = {(uint64_t)epi.ldo * 4, (uint64_t)epi.ldo * g.ow * 4,
+                                 (uint64_t)epi.ldo * g.ow * g.oh * 4};
+    const uint32_t box[4] = {32, (uint32_t)tw, (uint32_t)th, 1};
+    args.tma_store = make_map(&mo, obase, 4, dims, strides, box) ? 1 : 0;
+  }
   const int grid_m = g.n * args.tiles_x * args.tiles_y;
-  return dispatch<1>(bn, split, ma, mb, mblo, args, grid_m, st);
+  return dispatch<1>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
 }
 
 }  // namespace qpc
