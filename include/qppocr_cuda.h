@@ -229,6 +229,17 @@ int qpc_op_gemm(const float* x, int64_t m, int k, const float* w, const float* w
                 const float* bias, int act, const float* act_p, const float* residual, float* y,
                 int math, void* stream);
 
+/* Fused CTC head with the argmax exit (rec MatMul 120 -> V + bias + Softmax +
+ * per-timestep argmax; crates/qppocr-core/src/pipeline/rec.rs:34-120 and
+ * crates/qppocr-gpu/shaders/n_exit3_argmax.comp): for each of `rows` rows of
+ * x[rows, k], pairs[2r] = softmax probability of the first strict maximum of
+ * x * w^T + bias (ties -> lowest class), pairs[2r+1] = its class index as an
+ * f32 bit pattern.  w is [n, k] tf32-rounded (and w_lo as for qpc_op_gemm).
+ * The logits are never written: a scratch buffer of per-column-tile partials
+ * (rows * ceil(n / 128) * 16 bytes) is allocated and freed stream-ordered. */
+int qpc_op_ctc_head(const float* x, int64_t rows, int k, const float* w, const float* w_lo, int n,
+                    const float* bias, int math, float* pairs, void* stream);
+
 /* Split fp32 device values into tf32 parts hi = rn(v) and lo = rn(v - hi)
  * (round to nearest, ties away): the load-time weight preparation of both
  * math modes. */

@@ -94,7 +94,7 @@ EXPORTED = (
     "qpc_session_caps", "qpc_run_async", "qpc_complete", "qpc_ticket_output_count",
     "qpc_ticket_output", "qpc_ticket_release", "qpc_run", "qpc_ticket_device_ms",
     "qpc_session_destroy", "qpc_session_profile", "qpc_session_profile_step",
-    "qpc_session_replay", "qpc_session_node_count", "qpc_session_node", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_split_tf32",
+    "qpc_session_replay", "qpc_session_node_count", "qpc_session_node", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_ctc_head", "qpc_op_split_tf32",
     "qpc_kernel_error",
 )
 
@@ -142,6 +142,8 @@ def lib():
     L.qpc_op_gemm.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P, ctypes.c_int, P,
                               P, P, ctypes.c_int, P]
     L.qpc_op_split_tf32.argtypes = [P, ctypes.c_int64, P, P, P]
+    L.qpc_op_ctc_head.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P, ctypes.c_int,
+                                  P, P]
     L.qpc_kernel_error.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]
     _lib = L
     return L
@@ -463,6 +465,17 @@ def op_gemm(x, w, n=None, bias=None, act=None, act_p=None, residual=None, math="
     _check(lib().qpc_op_gemm(_dptr(x), m, k, _dptr(w), _dptr(w_lo), nn, _dptr(bias), ACT[act],
                              ctypes.cast(ap, ctypes.c_void_p) if ap is not None else None,
                              _dptr(residual), _dptr(y), MATH[math], stream))
+    return y
+
+
+def op_ctc_head(x, w, bias=None, math="tf32", w_lo=None, out=None, stream=None):
+    """(value, index-bits) pairs [rows, 2] of softmax(x w^T + bias) per row."""
+    import torch
+    rows, k = x.shape
+    n = w.shape[0]
+    y = out if out is not None else torch.empty((rows, 2), dtype=torch.float32, device=x.device)
+    _check(lib().qpc_op_ctc_head(_dptr(x), rows, k, _dptr(w), _dptr(w_lo), n, _dptr(bias), MATH[math],
+                                 _dptr(y), stream))
     return y
 
 

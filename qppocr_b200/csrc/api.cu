@@ -332,6 +332,33 @@ int qpc_op_gemm(const float* x, int64_t m, int k, const float* w, const float* w
   });
 }
 
+int qpc_op_ctc_head(const float* x, int64_t rows, int k, const float* w, const float* w_lo, int n,
+                    const float* bias, int math, float* pairs, void* stream) {
+  if (!x || !w || !pairs || rows < 0 || k <= 0 || n <= 0) {
+    set_error("invalid argument");
+    return E_INVALID;
+  }
+  return guarded([&] {
+    if (k % 4) throw GraphError{"ctc head: K must be a multiple of 4 (16-byte TMA row pitch)"};
+    if (math == QPC_MATH_3XTF32 && !w_lo) throw GraphError{"ctc head: 3xTF32 needs w_lo"};
+    if (rows == 0) return (int)OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int ntiles = gemm_tc_col_tiles(n, math);
+    void* part = nullptr;
+    QPC_CUDA_OR_THROW(cudaMallocAsync(&part, (size_t)ntiles * rows * sizeof(float4), st));
+    GemmEpilogue e;
+    e.bias = bias;
+    e.partials = static_cast<float4*>(part);
+    e.ldo = n;
+    unsigned int* err = device_state(current_device()).err_word;
+    cudaError_t le = launch_gemm_tc(x, rows, k, k, w, w_lo, n, e, math, err, st);
+    if (le == cudaSuccess) le = launch_argmax_combine(static_cast<float4*>(part), ntiles, rows, pairs, st);
+    cudaFreeAsync(part, st);
+    QPC_CUDA_OR_THROW(le);
+    return (int)OK;
+  });
+}
+
 int qpc_op_split_tf32(const float* v, int64_t count, float* hi, float* lo, void* stream) {
   if (!v || !hi || !lo || count < 0) return E_INVALID;
   return guarded([&] {

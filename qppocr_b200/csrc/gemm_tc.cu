@@ -131,10 +131,16 @@ __device__ __forceinline__ RowMap row_map(const GemmArgs& args, int m_blk, int i
 // store issued from it two chunks earlier has finished reading it.
 template <int BN, int A_MODE, class Fetch>
 __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorMap* tm_out,
-                                           uint8_t* stage, uint32_t& chunk_ctr, int m_blk, int n0,
-                                           int img, int oy0, int ox0, int r, int t, Fetch&& fetch) {
+                                           uint8_t* stage, int64_t* s_rrow, uint32_t& chunk_ctr,
+                                           int m_blk, int n0, int img, int oy0, int ox0, int r,
+                                           int t, Fetch&& fetch) {
   const GemmEpilogue& e = args.epi;
-  const RowMap mine = row_map<A_MODE>(args, m_blk, img, oy0, ox0, r);
+  if (e.residual) {
+    // residual source row of every tile row, once per tile (read after the
+    // first barrier below)
+    const RowMap mine = row_map<A_MODE>(args, m_blk, img, oy0, ox0, r);
+    s_rrow[r] = mine.orow >= 0 ? mine.rrow : -1;
+  }
 #pragma unroll 1
   for (int cc = 0; cc < BN; cc += 32) {
     if (n0 + cc >= args.N) break;
@@ -147,9 +153,9 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
         const int row = i >> 3, c4 = i & 7;
         const int col = n0 + cc + c4 * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        const RowMap rm = row_map<A_MODE>(args, m_blk, img, oy0, ox0, row);
-        if (rm.orow >= 0 && col < args.N)
-          v = __ldg(reinterpret_cast<const float4*>(e.residual + rm.rrow * e.ldr + col));
+        const int64_t rr = s_rrow[row];
+        if (rr >= 0 && col < args.N)
+          v = __ldg(reinterpret_cast<const float4*>(e.residual + rr * e.ldr + col));
         *reinterpret_cast<float4*>(sb + row * 32 + ((c4 ^ (row & 7)) << 2)) = v;
       }
       named_bar_sync(1, 128);
@@ -185,7 +191,6 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
       }
       *slot = o;
     }
-    (void)mine;
     fence_proxy_async_smem();
     named_bar_sync(1, 128);
     if (t == 0) {
@@ -195,6 +200,74 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
     }
     ++chunk_ctr;
   }
+}
+
+// Row-argmax epilogue for one tile (CTC head): per row, the first strict
+// maximum of logits + bias over this tile's columns, its column, and the sum
+// of exp(l - max) over the tile, in one online pass over 32-column chunks
+// (fast exp; the combine step rescales across tiles).
+template <int BN, class Fetch>
+__device__ __forceinline__ void argmax_tile(const GemmArgs& args, int64_t orow, int n0, int n_blk,
+                                            Fetch&& fetch) {
+  const GemmEpilogue& e = args.epi;
+  float m = -INFINITY, s = 0.f;
+  int mi = n0;
+#pragma unroll 1
+  for (int cc = 0; cc < BN; cc += 32) {
+    const int c0 = n0 + cc;
+    if (c0 >= args.N) break;
+    float v[32];
+    fetch(cc, v);
+    const int valid = args.N - c0;  // columns >= valid are padding
+    if (e.bias) {
+      const float4* b4 = reinterpret_cast<const float4*>(e.bias + c0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 b;
+        if (4 * j + 3 < valid) {
+          b = __ldg(b4 + j);
+        } else {  // partial trailing quad: stay inside the bias array
+          b.x = 4 * j < valid ? __ldg(e.bias + c0 + 4 * j) : 0.f;
+          b.y = 4 * j + 1 < valid ? __ldg(e.bias + c0 + 4 * j + 1) : 0.f;
+          b.z = 4 * j + 2 < valid ? __ldg(e.bias + c0 + 4 * j + 2) : 0.f;
+          b.w = 0.f;
+        }
+        v[4 * j] = __fadd_rn(v[4 * j], b.x);
+        v[4 * j + 1] = __fadd_rn(v[4 * j + 1], b.y);
+        v[4 * j + 2] = __fadd_rn(v[4 * j + 2], b.z);
+        v[4 * j + 3] = __fadd_rn(v[4 * j + 3], b.w);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j >= valid) v[j] = -INFINITY;
+    // chunk max and its first column (ascending scan keeps the lowest on ties)
+    float cm = v[0];
+    int cj = 0;
+#pragma unroll
+    for (int j = 1; j < 32; ++j) {
+      const bool gt = v[j] > cm;
+      cm = gt ? v[j] : cm;
+      cj = gt ? j : cj;
+    }
+    float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      p0 += __expf(v[j] - cm);
+      p1 += __expf(v[j + 1] - cm);
+      p2 += __expf(v[j + 2] - cm);
+      p3 += __expf(v[j + 3] - cm);
+    }
+    const float cs = (p0 + p1) + (p2 + p3);
+    if (cm > m) {
+      s = s * __expf(m - cm) + cs;
+      m = cm;
+      mi = c0 + cj;
+    } else {
+      s += cs * __expf(cm - m);
+    }
+  }
+  if (orow >= 0) e.partials[(int64_t)n_blk * args.M + orow] = make_float4(m, __uint_as_float((unsigned)mi), s, 0.f);
 }
 
 constexpr int NUM_THREADS = 256;  // w0 TMA, w1 MMA, w2-3 convert A, w4-7 epilogue
@@ -240,6 +313,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_slot;
+  __shared__ int64_t s_rrow[BM];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -419,8 +493,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t buf = acc_i & 1u;
         if (!mbar_wait(&acc_full[buf], (acc_i >> 1) & 1u, args.err)) { ok = false; break; }
         tc_fence_after();
-        if (args.tma_store) {
-          store_tile<BN, A_MODE>(args, &tmOut, out_stage, chunk_ctr, tc.m_blk, tc.n0, tc.img, tc.oy0,
+        if (e.partials) {
+          argmax_tile<BN>(args, orow, tc.n0, tc.n0 / BN, [&](int c, float (&v)[32]) {
+            uint32_t a[16], b[16];
+            tmem_ld16_nowait(lane_base + buf * BN + c, a);
+            tmem_ld16_nowait(lane_base + buf * BN + c + 16, b);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              v[j] = __uint_as_float(a[j]);
+              v[16 + j] = __uint_as_float(b[j]);
+            }
+          });
+        } else if (args.tma_store) {
+          store_tile<BN, A_MODE>(args, &tmOut, out_stage, s_rrow, chunk_ctr, tc.m_blk, tc.n0, tc.img, tc.oy0,
                                  tc.ox0, r, threadIdx.x - 128, [&](int c, float (&v)[32]) {
                                    uint32_t a[16], b[16];
                                    tmem_ld16_nowait(lane_base + buf * BN + c, a);
@@ -468,8 +554,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ++acc_i;
         }
         if (!ok) break;
-        if (args.tma_store) {
-          store_tile<BN, A_MODE>(args, &tmOut, out_stage, chunk_ctr, tc.m_blk, tc.n0, tc.img, tc.oy0,
+        if (e.partials) {
+          argmax_tile<BN>(args, orow, tc.n0, tc.n0 / BN, [&](int c, float (&v)[32]) {
+#pragma unroll
+            for (int cb = 0; cb < BN; cb += 32)
+              if (cb == c)
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = accr[(cb + j) % (SPLIT ? BN : 1)];
+          });
+        } else if (args.tma_store) {
+          store_tile<BN, A_MODE>(args, &tmOut, out_stage, s_rrow, chunk_ctr, tc.m_blk, tc.n0, tc.img, tc.oy0,
                                  tc.ox0, r, threadIdx.x - 128, [&](int c, float (&v)[32]) {
 #pragma unroll
                                    for (int cb = 0; cb < BN; cb += 32)
@@ -596,6 +690,44 @@ int pick_bn(int n, bool split) {
 
 }  // namespace
 
+int gemm_tc_col_tiles(int N, int math) {
+  const int bn = pick_bn(N, math == MATH_3XTF32);
+  return (N + bn - 1) / bn;
+}
+
+namespace {
+__global__ void argmax_combine_kernel(const float4* __restrict__ partials, int n_tiles, int64_t M,
+                                      float* __restrict__ pairs) {
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < M;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    float best = -INFINITY;
+    unsigned idx = 0;
+    for (int t = 0; t < n_tiles; ++t) {  // tiles ascend in column: strict > keeps the lowest
+      const float4 p = partials[(int64_t)t * M + r];
+      if (p.x > best) {
+        best = p.x;
+        idx = __float_as_uint(p.y);
+      }
+    }
+    float s = 0.f;
+    for (int t = 0; t < n_tiles; ++t) {
+      const float4 p = partials[(int64_t)t * M + r];
+      s += p.z * __expf(p.x - best);
+    }
+    pairs[2 * r] = 1.0f / s;
+    pairs[2 * r + 1] = __uint_as_float(idx);
+  }
+}
+}  // namespace
+
+cudaError_t launch_argmax_combine(const float4* partials, int n_tiles, int64_t M, float* pairs,
+                                  cudaStream_t st) {
+  int64_t blocks = (M + 127) / 128;
+  if (blocks < 1) blocks = 1;
+  argmax_combine_kernel<<<(unsigned)blocks, 128, 0, st>>>(partials, n_tiles, M, pairs);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const float* b,
                            const float* b_lo, int N, const GemmEpilogue& epi, int math,
                            unsigned int* err, cudaStream_t st) {
@@ -630,7 +762,7 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
   args.err = err;
   CUtensorMap mo = ma;
   const float* obase = epi.out + epi.col_off;
-  if ((N % 4) == 0 && (epi.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(obase) & 15) == 0 &&
+  if (!epi.partials && (N % 4) == 0 && (epi.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(obase) & 15) == 0 &&
       (!epi.residual || (epi.ldr % 4) == 0)) {
     const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)epi.ldo * 4};

@@ -42,6 +42,10 @@ struct GemmEpilogue {
   // nearest-upsample residual: output rows are pixels of an (n, oh, ow) map;
   // the residual is an (n, rh, rw) map. rh == 0 disables the remap.
   int oh = 0, ow = 0, rh = 0, rw = 0;
+  // Row-argmax epilogue (CTC head): instead of storing D, each output tile
+  // writes per row (max, argmax bits, sum exp(l - max)) of its columns to
+  // partials[n_tile * M + row] (float4); nothing is written to `out`.
+  float4* partials = nullptr;
 };
 
 enum MathMode : int { MATH_TF32 = 0, MATH_3XTF32 = 1 };
@@ -55,6 +59,16 @@ enum MathMode : int { MATH_TF32 = 0, MATH_3XTF32 = 1 };
 cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const float* b,
                            const float* b_lo, int N, const GemmEpilogue& epi, int math,
                            unsigned int* err, cudaStream_t st);
+
+// Number of output-column tiles launch_gemm_tc uses for N (sizes the
+// row-argmax partials buffer: n_tiles * M float4).
+int gemm_tc_col_tiles(int N, int math);
+
+// Combines row-argmax partials into (value, index-bits) pairs: the first
+// strict maximum over all columns (ties -> lowest column) and its softmax
+// probability 1 / sum_j exp(l_j - max).
+cudaError_t launch_argmax_combine(const float4* partials, int n_tiles, int64_t M, float* pairs,
+                                  cudaStream_t st);
 
 // kxk stride-1 dense conv as implicit GEMM on tcgen05: A tiles are 4-D TMA
 // boxes of the NHWC input shifted per tap (out-of-bounds rows/cols read as

@@ -274,21 +274,34 @@ cudaError_t launch_convt2x2(const float* x, const float* wt, const float* bn_a, 
 }
 
 // ------------------------------------------------------------ pooling
-// pool2d.rs:10-30 global_avg_pool (f64 sum / plane) on NHWC: one thread per
-// (n, c), summing the plane in index order.
-__global__ void gap_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int N, int HW,
-                                int C) {
-  GRID_LOOP(t, (int64_t)N * C) {
-    const int c = (int)(t % C), n = (int)(t / C);
+// pool2d.rs:10-30 global_avg_pool (f64 sum / plane) on NHWC.  A block owns
+// (n, 32 channels); its 8 warps sum strided slices of the plane in f64 and the
+// 8 partial f64 sums are added in a fixed order.  f64 partial sums of f32
+// values are exact far beyond the f32 result's precision, so the rounded mean
+// equals the sequential sum's except at ties ~1e-16 apart.
+__global__ void __launch_bounds__(256) gap_nhwc_kernel(const float* __restrict__ x,
+                                                       float* __restrict__ y, int N, int HW, int C) {
+  __shared__ double part[8][32];
+  const int cblocks = (C + 31) / 32;
+  const int n = blockIdx.x / cblocks, c = (blockIdx.x % cblocks) * 32 + (threadIdx.x & 31);
+  const int w = threadIdx.x >> 5;
+  double s = 0.0;
+  if (c < C) {
     const float* p = x + (int64_t)n * HW * C + c;
-    double s = 0.0;
-    for (int i = 0; i < HW; ++i) s += (double)__ldg(p + (int64_t)i * C);
-    y[t] = (float)(s / (double)HW);
+    for (int i = w; i < HW; i += 8) s += (double)__ldg(p + (int64_t)i * C);
+  }
+  part[w][threadIdx.x & 31] = s;
+  __syncthreads();
+  if (w == 0 && c < C) {
+    double t = 0.0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += part[k][threadIdx.x];
+    y[(int64_t)n * C + c] = (float)(t / (double)HW);
   }
 }
 
 cudaError_t launch_gap_nhwc(const float* x, float* y, int n, int hw, int c, cudaStream_t st) {
-  gap_nhwc_kernel<<<grid_for((int64_t)n * c), 256, 0, st>>>(x, y, n, hw, c);
+  gap_nhwc_kernel<<<n * ((c + 31) / 32), 256, 0, st>>>(x, y, n, hw, c);
   return cudaGetLastError();
 }
 

@@ -312,7 +312,10 @@ const float* Session::dweight(const std::string& name, const std::string& varian
       x = lo ? tf32_rn_host(x - h) : h;
     }
   }
-  if (v.empty()) v.push_back(0.f);
+  // 16 zero floats of padding: vector loads of a trailing partial chunk
+  // (bias of a 32-column tile) stay inside the allocation.
+  const size_t real = v.size();
+  v.resize(real + 16, 0.f);
   auto buf = std::make_unique<DevBuf>(v.size() * sizeof(float));
   QPC_CUDA_OR_THROW(cudaMemcpy(buf->ptr, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
   const float* p = buf->f();
@@ -1452,32 +1455,47 @@ class Planner {
     }
     unsigned int* err = device_state(S.device()).err_word;
     const double flops = 2.0 * rows * K * Nn;
-    Val y = new_val(oshape, false);
-    GemmEpilogue e;
-    e.bias = bias;
-    e.residual = has_res ? out_ptr(res) : nullptr;
-    e.out = out_ptr(y);
-    e.ldo = (int)Nn;
-    e.ldr = (int)Nn;
-    e.act = act_of(n);
     const float* xp = out_ptr(x);
-    step(head ? "head_gemm" : "gemm_tc", n.name, 4.0 * (rows * K + rows * Nn + K * Nn), flops,
-         [=](cudaStream_t s) { return launch_gemm_tc(xp, rows, (int)K, (int)K, wb, wl, (int)Nn, e, math, err, s); });
-    unref(x);
-    if (has_res) unref(res);
     if (!head) {
+      Val y = new_val(oshape, false);
+      GemmEpilogue e;
+      e.bias = bias;
+      e.residual = has_res ? out_ptr(res) : nullptr;
+      e.out = out_ptr(y);
+      e.ldo = (int)Nn;
+      e.ldr = (int)Nn;
+      e.act = act_of(n);
+      step("gemm_tc", n.name, 4.0 * (rows * K + rows * Nn + K * Nn), flops, [=](cudaStream_t s) {
+        return launch_gemm_tc(xp, rows, (int)K, (int)K, wb, wl, (int)Nn, e, math, err, s);
+      });
+      unref(x);
+      if (has_res) unref(res);
       define(n.out[0], y);
       return;
     }
-    // argmax exit: (val = softmax prob of the first strict max, idx bits)
+    // CTC head with the argmax exit: the GEMM epilogue reduces each row of
+    // logits per column tile to (max, argmax, sum exp) partials (scratch), the
+    // combine step emits (val = softmax prob of the first strict max, idx bits).
+    if (has_res) throw GraphError{"CTC head with a residual"};
+    const int ntiles = gemm_tc_col_tiles((int)Nn, math);
+    Val part = new_val({(int64_t)ntiles * rows * 4}, false);
+    float4* pp4 = reinterpret_cast<float4*>(out_ptr(part));
+    GemmEpilogue e;
+    e.bias = bias;
+    e.partials = pp4;
+    e.out = nullptr;
+    e.ldo = (int)Nn;
+    e.act = act_of(n);
+    step("head_gemm", n.name, 4.0 * (rows * K + K * Nn) + 16.0 * ntiles * rows, flops,
+         [=](cudaStream_t s) { return launch_gemm_tc(xp, rows, (int)K, (int)K, wb, wl, (int)Nn, e, math, err, s); });
+    unref(x);
     std::vector<int64_t> pshape = oshape;
     pshape.back() = 2;
     Val pr = new_val(pshape, false);
-    const float* lp = out_ptr(y);
-    float* pp = out_ptr(pr);
-    step("head_argmax", n.name, 4.0 * rows * Nn, 3.0 * rows * Nn,
-         [=](cudaStream_t s) { return launch_softmax_argmax(lp, pp, rows, (int)Nn, s); });
-    unref(y);
+    float* prp = out_ptr(pr);
+    step("head_combine", n.name, 16.0 * ntiles * rows + 8.0 * rows, 0,
+         [=](cudaStream_t s) { return launch_argmax_combine(pp4, ntiles, rows, prp, s); });
+    unref(part);
     define(n.out[0], pr);
   }
 

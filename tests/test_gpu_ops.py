@@ -99,3 +99,30 @@ def test_gemm_rejects_unaligned_k(cuda_ctx):
     w = torch.zeros((4, 6), device="cuda")
     with pytest.raises(q.GraphError):
         q.op_gemm(x, w)
+
+
+@pytest.mark.parametrize("rows,n", [(10240, 18709), (77, 1000), (300, 37)])
+@pytest.mark.parametrize("math", ["tf32", "3xtf32"])
+def test_ctc_head_parity(cuda_ctx, rows, n, math):
+    """Fused head vs oracle: logits = x W + b -> softmax (activation.rs:321-403)
+    -> first strict argmax (rec.rs:34-79).  Indices identical except rows whose
+    top-2 probabilities differ by less than the tolerance; values within it."""
+    import torch
+    rng = np.random.Generator(np.random.PCG64(11))
+    k = 120
+    x = rng.uniform(-1, 1, (rows, k)).astype(np.float32)
+    w = (rng.standard_normal((k, n)) * np.sqrt(1.0 / k)).astype(np.float32)
+    b = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    hi, lo = q.op_split_tf32(dev(np.ascontiguousarray(w.T)))
+    pairs = q.op_ctc_head(dev(x), hi, bias=dev(b), math=math, w_lo=lo if math == "3xtf32" else None)
+    torch.cuda.synchronize()
+    got = pairs.cpu().numpy()
+    probs = orc.softmax_last(orc.binary("Add", orc.sgemm(x, w), b))
+    ref = orc.argmax_pairs(probs)
+    tol = TOL_TF32 if math == "tf32" else TOL_3XTF32
+    gi, ri = got[:, 1].view(np.uint32), ref[:, 1].view(np.uint32)
+    top2 = np.sort(probs, axis=1)[:, -2:]
+    gap = top2[:, 1] - top2[:, 0]
+    assert not ((gi != ri) & (gap >= tol * probs.max())).any()
+    assert rel(got[:, 0], ref[:, 0]) < 10 * tol
+    assert q.kernel_error(0) == 0
