@@ -240,6 +240,19 @@ int qpc_op_gemm(const float* x, int64_t m, int k, const float* w, const float* w
 int qpc_op_ctc_head(const float* x, int64_t rows, int k, const float* w, const float* w_lo, int n,
                     const float* bias, int math, float* pairs, void* stream);
 
+/* qpc_op_ctc_head without any device allocation.  No counterpart in the
+ * reference: it exists for callers that cannot let a library allocate GPU
+ * memory (an engine that owns all device memory in its own pool, or a serving
+ * loop that must not call the CUDA allocator once running).  Same arguments
+ * and result as qpc_op_ctc_head; the partials live in a fixed array compiled
+ * into this library (32 MiB per device, held until process exit).
+ * Limits: rows * ceil(n / 128) <= 2^21, else QPC_ERR_INVALID.  All calls on a
+ * device share that array: calls whose kernels overlap on the GPU race.  The
+ * first call on a device looks up the array's address (cudaGetSymbolAddress);
+ * make it before any stream capture. */
+int qpc_op_ctc_head_noalloc(const float* x, int64_t rows, int k, const float* w, const float* w_lo,
+                            int n, const float* bias, int math, float* pairs, void* stream);
+
 /* Split fp32 device values into tf32 parts hi = rn(v) and lo = rn(v - hi)
  * (round to nearest, ties away): the load-time weight preparation of both
  * math modes. */

@@ -94,7 +94,8 @@ EXPORTED = (
     "qpc_session_caps", "qpc_run_async", "qpc_complete", "qpc_ticket_output_count",
     "qpc_ticket_output", "qpc_ticket_release", "qpc_run", "qpc_ticket_device_ms",
     "qpc_session_destroy", "qpc_session_profile", "qpc_session_profile_step",
-    "qpc_session_replay", "qpc_session_node_count", "qpc_session_node", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_ctc_head", "qpc_op_split_tf32",
+    "qpc_session_replay", "qpc_session_node_count", "qpc_session_node", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_ctc_head", "qpc_op_ctc_head_noalloc",
+    "qpc_op_split_tf32",
     "qpc_kernel_error",
 )
 
@@ -144,6 +145,8 @@ def lib():
     L.qpc_op_split_tf32.argtypes = [P, ctypes.c_int64, P, P, P]
     L.qpc_op_ctc_head.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P, ctypes.c_int,
                                   P, P]
+    L.qpc_op_ctc_head_noalloc.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P,
+                                          ctypes.c_int, P, P]
     L.qpc_kernel_error.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]
     _lib = L
     return L
