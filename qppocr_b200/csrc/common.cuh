@@ -343,10 +343,11 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t smem_addr) {
 // fp32 -> tf32 with round-to-nearest (ties away), as a 32-bit container with
 // the low 13 mantissa bits zero.  The tensor core would otherwise truncate,
 // which biases every product toward zero.
+// Integer form: add half an ulp of tf32 to the magnitude bits, clear the low
+// 13 bits (ties away from zero; identical to cvt.rna.tf32.f32 for finite
+// values) -- two full-rate integer ops instead of a conversion instruction.
 __device__ __forceinline__ float tf32_rna(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
 // Issue one 32x32b x16 TMEM load without waiting (pair with tmem_ld_wait).

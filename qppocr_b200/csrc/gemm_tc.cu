@@ -131,9 +131,9 @@ __device__ __forceinline__ RowMap row_map(const GemmArgs& args, int m_blk, int i
 // store issued from it two chunks earlier has finished reading it.
 template <int BN, int A_MODE, class Fetch>
 __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorMap* tm_out,
-                                           uint8_t* stage, int64_t* s_rrow, uint32_t& chunk_ctr,
-                                           int m_blk, int n0, int img, int oy0, int ox0, int r,
-                                           int t, Fetch&& fetch) {
+                                           uint8_t* stage, int64_t* s_rrow, int bar_id,
+                                           uint32_t& chunk_ctr, int m_blk, int n0, int img, int oy0,
+                                           int ox0, int r, int t, Fetch&& fetch) {
   const GemmEpilogue& e = args.epi;
   if (e.residual) {
     // residual source row of every tile row, once per tile (read after the
@@ -146,7 +146,7 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
     if (n0 + cc >= args.N) break;
     float* sb = reinterpret_cast<float*>(stage + (chunk_ctr & 1u) * OUT_STAGE_BYTES);
     if (t == 0) bulk_wait_group_read<1>();
-    named_bar_sync(1, 128);
+    named_bar_sync(bar_id, 128);
     if (e.residual) {
 #pragma unroll 2
       for (int i = t; i < BM * 8; i += 128) {
@@ -158,7 +158,7 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
           v = __ldg(reinterpret_cast<const float4*>(e.residual + rr * e.ldr + col));
         *reinterpret_cast<float4*>(sb + row * 32 + ((c4 ^ (row & 7)) << 2)) = v;
       }
-      named_bar_sync(1, 128);
+      named_bar_sync(bar_id, 128);
     }
     float v[32];
     fetch(cc, v);
@@ -192,7 +192,7 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
       *slot = o;
     }
     fence_proxy_async_smem();
-    named_bar_sync(1, 128);
+    named_bar_sync(bar_id, 128);
     if (t == 0) {
       if (A_MODE == 0) tma_store_2d(tm_out, sb, n0 + cc, m_blk * BM);
       else tma_store_4d(tm_out, sb, n0 + cc, ox0, oy0, img);
@@ -270,7 +270,21 @@ __device__ __forceinline__ void argmax_tile(const GemmArgs& args, int64_t orow, 
   if (orow >= 0) e.partials[(int64_t)n_blk * args.M + orow] = make_float4(m, __uint_as_float((unsigned)mi), s, 0.f);
 }
 
-constexpr int NUM_THREADS = 256;  // w0 TMA, w1 MMA, w2-3 convert A, w4-7 epilogue
+// Warp roles: w0 TMA producer, w1 MMA issuer, w2-3 convert A, then 4-warp
+// epilogue groups.  TF32 runs two epilogue groups that take alternate tiles
+// (their serial TMEM -> smem -> TMA-store chains overlap); 3xTF32 keeps one
+// group, whose registers hold the promoted accumulator.
+template <bool SPLIT>
+struct Roles {
+  static constexpr int EPI_GROUPS = SPLIT ? 1 : 2;
+  static constexpr int THREADS = 128 + 128 * EPI_GROUPS;
+};
+// TMEM accumulators: 4 for N tiles <= 128 columns (the MMA can run up to 3
+// tiles ahead of the epilogue), 2 otherwise; 3xTF32 ping-pongs 2 chunk buffers.
+template <int BN, bool SPLIT>
+struct Accs {
+  static constexpr int NBUF = SPLIT ? 2 : (BN <= 128 ? 4 : 2);
+};
 constexpr int CH = 1;             // k-blocks per promotion chunk (3xTF32)
 
 struct TileCoord {
@@ -297,23 +311,24 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& a, int tile, int
 // the MMAs run ahead across tile boundaries while the epilogue warps drain the
 // previous tile from the other TMEM accumulator.
 template <int BN, int STAGES, bool SPLIT, int A_MODE>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(Roles<SPLIT>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmOut,
                    const GemmArgs args) {
   using SM = Smem<BN, SPLIT>;
-  // Two accumulators: consecutive tiles (TF32) or consecutive K chunks (3xTF32).
-  constexpr uint32_t TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
+  constexpr int NBUF = Accs<BN, SPLIT>::NBUF;
+  constexpr int NGRP = Roles<SPLIT>::EPI_GROUPS;
+  constexpr uint32_t TMEM_COLS = (NBUF * BN < 32) ? 32 : NBUF * BN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
   __shared__ __align__(8) uint64_t conv_bar[STAGES];
-  __shared__ __align__(8) uint64_t acc_full[2];
-  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t acc_full[NBUF];
+  __shared__ __align__(8) uint64_t acc_empty[NBUF];
   __shared__ uint32_t tmem_base_slot;
-  __shared__ int64_t s_rrow[BM];
+  __shared__ int64_t s_rrow[NGRP][BM];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -327,7 +342,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&empty_bar[s], 1);
       mbar_init(&conv_bar[s], 64);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NBUF; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 128);
     }
@@ -385,8 +400,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
         for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
           const bool first = SPLIT ? (kb % CH) == 0 : kb == 0;
-          const uint32_t buf = acc_i & 1u;
-          if (first && acc_i >= 2 && !mbar_wait(&acc_empty[buf], ((acc_i >> 1) - 1) & 1u, args.err)) {
+          const uint32_t buf = acc_i % NBUF;
+          if (first && acc_i >= (uint32_t)NBUF &&
+              !mbar_wait(&acc_empty[buf], ((acc_i / NBUF) - 1) & 1u, args.err)) {
             ok = false;
             break;
           }
@@ -457,15 +473,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue warps 4-7: TMEM lane quarter q = warp % 4.
+    // ---------------- epilogue groups (warps 4-7, 8-11): TMEM lane quarter
+    // q = warp % 4; group `grp` takes local tiles grp, grp + NGRP, ...
     const int q = warp & 3;
+    const int grp = (warp - 4) >> 2;
     const int r = q * 32 + lane;
+    const int gt = threadIdx.x - 128 - grp * 128;  // thread index within the group
     const uint32_t lane_base = tmem_d + ((uint32_t)(q * 32) << 16);
     const GemmEpilogue& e = args.epi;
-    uint32_t acc_i = 0, chunk_ctr = 0;
+    uint8_t* my_stage = out_stage + grp * 2 * OUT_STAGE_BYTES;
+    uint32_t acc_i = grp, chunk_ctr = 0;
     bool ok = true;
     float accr[SPLIT ? BN : 1];
-    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+    for (int tile = blockIdx.x + grp * gridDim.x; tile < total_tiles && ok; tile += NGRP * gridDim.x) {
       const TileCoord tc = tile_coord(args, tile, n_tiles, BN);
       int64_t orow = -1, rrow = -1;
       if (A_MODE == 0) {
@@ -490,8 +510,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (!SPLIT) {
-        const uint32_t buf = acc_i & 1u;
-        if (!mbar_wait(&acc_full[buf], (acc_i >> 1) & 1u, args.err)) { ok = false; break; }
+        const uint32_t buf = acc_i % NBUF;
+        if (!mbar_wait(&acc_full[buf], (acc_i / NBUF) & 1u, args.err)) { ok = false; break; }
         tc_fence_after();
         if (e.partials) {
           argmax_tile<BN>(args, orow, tc.n0, tc.n0 / BN, [&](int c, float (&v)[32]) {
@@ -506,8 +526,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
           });
         } else if (args.tma_store) {
-          store_tile<BN, A_MODE>(args, &tmOut, out_stage, s_rrow, chunk_ctr, tc.m_blk, tc.n0, tc.img, tc.oy0,
-                                 tc.ox0, r, threadIdx.x - 128, [&](int c, float (&v)[32]) {
+          store_tile<BN, A_MODE>(args, &tmOut, my_stage, s_rrow[grp], 1 + grp, chunk_ctr, tc.m_blk, tc.n0, tc.img,
+                                 tc.oy0, tc.ox0, r, gt, [&](int c, float (&v)[32]) {
                                    uint32_t a[16], b[16];
                                    tmem_ld16_nowait(lane_base + buf * BN + c, a);
                                    tmem_ld16_nowait(lane_base + buf * BN + c + 16, b);
@@ -529,15 +549,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[buf]);
-        ++acc_i;
+        acc_i += NGRP;
       } else {
 #pragma unroll
         for (int j = 0; j < BN; ++j) accr[j % (SPLIT ? BN : 1)] = 0.f;
         const int nchunks = (nkb + CH - 1) / CH;
         for (int ck = 0; ck < nchunks; ++ck) {
           // promotion: TMEM partial sum of this chunk -> fp32 registers (RN adds)
-          const uint32_t buf = acc_i & 1u;
-          if (!mbar_wait(&acc_full[buf], (acc_i >> 1) & 1u, args.err)) { ok = false; break; }
+          const uint32_t buf = acc_i % NBUF;
+          if (!mbar_wait(&acc_full[buf], (acc_i / NBUF) & 1u, args.err)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int c0 = 0; c0 < (SPLIT ? BN : 16); c0 += 16) {
@@ -563,8 +583,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int j = 0; j < 32; ++j) v[j] = accr[(cb + j) % (SPLIT ? BN : 1)];
           });
         } else if (args.tma_store) {
-          store_tile<BN, A_MODE>(args, &tmOut, out_stage, s_rrow, chunk_ctr, tc.m_blk, tc.n0, tc.img, tc.oy0,
-                                 tc.ox0, r, threadIdx.x - 128, [&](int c, float (&v)[32]) {
+          store_tile<BN, A_MODE>(args, &tmOut, my_stage, s_rrow[grp], 1 + grp, chunk_ctr, tc.m_blk, tc.n0, tc.img,
+                                 tc.oy0, tc.ox0, r, gt, [&](int c, float (&v)[32]) {
 #pragma unroll
                                    for (int cb = 0; cb < BN; cb += 32)
                                      if (cb == c)
@@ -585,7 +605,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
   }
-  if (args.tma_store && threadIdx.x == 128) bulk_wait_group<0>();  // stores out of smem before exit
+  if (args.tma_store && threadIdx.x >= 128 && ((threadIdx.x - 128) & 127) == 0)
+    bulk_wait_group<0>();  // each epilogue group's stores out of smem before exit
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem_d, TMEM_COLS);
@@ -644,7 +665,7 @@ template <int BN, int STAGES, bool SPLIT, int A_MODE>
 cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& blo,
                        const CUtensorMap& out, const GemmArgs& args, int tiles, cudaStream_t st) {
   auto kern = gemm_tc_kernel<BN, STAGES, SPLIT, A_MODE>;
-  const int smem = STAGES * Smem<BN, SPLIT>::STAGE + 2 * OUT_STAGE_BYTES + 1024;
+  const int smem = STAGES * Smem<BN, SPLIT>::STAGE + Roles<SPLIT>::EPI_GROUPS * 2 * OUT_STAGE_BYTES + 1024;
   static bool attr_set = false;  // per instantiation
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -652,7 +673,7 @@ cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
     attr_set = true;
   }
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, NUM_THREADS, smem, st>>>(a, b, blo, out, args);
+  kern<<<grid, Roles<SPLIT>::THREADS, smem, st>>>(a, b, blo, out, args);
   return cudaGetLastError();
 }
 
@@ -664,16 +685,16 @@ cudaError_t dispatch(int bn, bool split, const CUtensorMap& a, const CUtensorMap
   const int tiles = grid_m * ((args.N + bn - 1) / bn);
   if (!split) {
     switch (bn) {
-      case 32: return run_kernel<32, 6, false, A_MODE>(a, b, blo, out, args, tiles, st);
+      case 32: return run_kernel<32, 7, false, A_MODE>(a, b, blo, out, args, tiles, st);
       case 64: return run_kernel<64, 6, false, A_MODE>(a, b, blo, out, args, tiles, st);
-      case 128: return run_kernel<128, 5, false, A_MODE>(a, b, blo, out, args, tiles, st);
+      case 128: return run_kernel<128, 4, false, A_MODE>(a, b, blo, out, args, tiles, st);
       default: return run_kernel<256, 3, false, A_MODE>(a, b, blo, out, args, tiles, st);
     }
   }
   switch (bn) {
     case 32: return run_kernel<32, 4, true, A_MODE>(a, b, blo, out, args, tiles, st);
     case 64: return run_kernel<64, 4, true, A_MODE>(a, b, blo, out, args, tiles, st);
-    default: return run_kernel<128, 3, true, A_MODE>(a, b, blo, out, args, tiles, st);
+    default: return run_kernel<128, 2, true, A_MODE>(a, b, blo, out, args, tiles, st);
   }
 }
 
