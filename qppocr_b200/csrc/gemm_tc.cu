@@ -24,6 +24,13 @@
 // * Epilogue: warps 4-7 read their 32 TMEM lanes (tcgen05.ld 32x32b), add bias,
 //   apply the fused activation, add the residual (optionally through a
 //   nearest-upsample index map) and store fp32 rows.
+// * A_MODE 2 (k x k, stride 1, output rows >= 64 wide): a tile is one output
+//   row of 128 pixels; per (kernel row, 32-channel block) one TMA box brings a
+//   128 + kw - 1 pixel halo row, and tap kx reads it shifted by kx rows (a
+//   descriptor start kx * 128 bytes in; the 128-byte swizzle is a function of
+//   the absolute shared-memory address, so the shifted view reads the rows
+//   the TMA wrote, with base offset 0), so each input pixel crosses L2 -> SM
+//   once per kernel row instead of once per tap.
 // * A_MODE 1 (k x k, stride 1 conv): the A tile is a 4-D TMA box
 //   [1][TH][TW][32ch] of the NHWC input shifted by the tap offset; rows and
 //   columns outside the image are zero-filled by TMA, which is exactly the
@@ -55,10 +62,21 @@ struct GemmArgs {
   int oh, ow, tw, th, tiles_x, tiles_y;
 };
 
-template <int BN, bool SPLIT>
+// A_MODE 2 (halo row): one output row of 128 pixels per tile; the A stage is a
+// 128 + kw - 1 pixel halo row (136 rows reserved, 17 KB) and B holds the kw
+// taps of one kernel row, room for MAX_KW_HALO taps.  The host routes only
+// kernels with kw <= MAX_KW_HALO here: the B box is kw taps deep.
+constexpr int MAX_KW_HALO = 3;
+constexpr int HALO_ROWS = 136;
+constexpr int HALO_BYTES = HALO_ROWS * BK * 4;
+static_assert(BM + MAX_KW_HALO - 1 <= HALO_ROWS, "halo row does not fit its buffer");
+
+template <int BN, bool SPLIT, int A_MODE>
 struct Smem {
+  static constexpr int A_BYTES = A_MODE == 2 ? HALO_BYTES : A_TILE_BYTES;
   static constexpr int B_TILE = BN * BK * 4;
-  static constexpr int STAGE = A_TILE_BYTES + B_TILE + (SPLIT ? (A_TILE_BYTES + B_TILE) : 0);
+  static constexpr int B_BYTES = (A_MODE == 2 ? MAX_KW_HALO : 1) * B_TILE;
+  static constexpr int STAGE = A_BYTES + B_BYTES + (SPLIT ? (A_BYTES + B_BYTES) : 0);
 };
 
 template <int BN>
@@ -315,7 +333,7 @@ __global__ void __launch_bounds__(Roles<SPLIT>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmOut,
                    const GemmArgs args) {
-  using SM = Smem<BN, SPLIT>;
+  using SM = Smem<BN, SPLIT, A_MODE>;
   constexpr int NBUF = Accs<BN, SPLIT>::NBUF;
   constexpr int NGRP = Roles<SPLIT>::EPI_GROUPS;
   constexpr uint32_t TMEM_COLS = (NBUF * BN < 32) ? 32 : NBUF * BN;
@@ -365,7 +383,9 @@ __global__ void __launch_bounds__(Roles<SPLIT>::THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
-      const uint32_t bytes = SPLIT ? (A_TILE_BYTES + 2 * SM::B_TILE) : (A_TILE_BYTES + SM::B_TILE);
+      const uint32_t a_bytes = A_MODE == 2 ? (uint32_t)(BM + args.kw - 1) * BK * 4 : A_TILE_BYTES;
+      const uint32_t b_bytes = (A_MODE == 2 ? args.kw : 1) * SM::B_TILE;
+      const uint32_t bytes = SPLIT ? (a_bytes + 2 * b_bytes) : (a_bytes + b_bytes);
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
@@ -378,15 +398,22 @@ __global__ void __launch_bounds__(Roles<SPLIT>::THREADS, 1)
           mbar_arrive_expect_tx(&full_bar[s], bytes);
           if (A_MODE == 0) {
             tma_load_2d(st, &tmA, &full_bar[s], kb * BK, tc.m_blk * BM);
-            tma_load_2d(st + A_TILE_BYTES, &tmB, &full_bar[s], kb * BK, tc.n0);
-            if (SPLIT) tma_load_2d(st + 2 * A_TILE_BYTES + SM::B_TILE, &tmBlo, &full_bar[s], kb * BK, tc.n0);
+            tma_load_2d(st + SM::A_BYTES, &tmB, &full_bar[s], kb * BK, tc.n0);
+            if (SPLIT) tma_load_2d(st + 2 * SM::A_BYTES + SM::B_BYTES, &tmBlo, &full_bar[s], kb * BK, tc.n0);
+          } else if (A_MODE == 2) {
+            // halo row of input row oy + ky - ph, columns ox0 - pw .. ox0 - pw + 128 + kw - 2
+            const int ky = kb / args.cblocks, cb = kb % args.cblocks;
+            tma_load_4d(st, &tmA, &full_bar[s], cb * BK, tc.ox0 - args.pw, tc.oy0 + ky - args.ph, tc.img);
+            tma_load_4d(st + SM::A_BYTES, &tmB, &full_bar[s], cb * BK, tc.n0, ky * args.kw, 0);
+            if (SPLIT)
+              tma_load_4d(st + 2 * SM::A_BYTES + SM::B_BYTES, &tmBlo, &full_bar[s], cb * BK, tc.n0, ky * args.kw, 0);
           } else {
             const int tap = kb / args.cblocks, cb = kb % args.cblocks;
             const int ky = tap / args.kw, kx = tap % args.kw;
             tma_load_4d(st, &tmA, &full_bar[s], cb * BK, tc.ox0 + kx - args.pw, tc.oy0 + ky - args.ph, tc.img);
-            tma_load_4d(st + A_TILE_BYTES, &tmB, &full_bar[s], cb * BK, tc.n0, tap, 0);
+            tma_load_4d(st + SM::A_BYTES, &tmB, &full_bar[s], cb * BK, tc.n0, tap, 0);
             if (SPLIT)
-              tma_load_4d(st + 2 * A_TILE_BYTES + SM::B_TILE, &tmBlo, &full_bar[s], cb * BK, tc.n0, tap, 0);
+              tma_load_4d(st + 2 * SM::A_BYTES + SM::B_BYTES, &tmBlo, &full_bar[s], cb * BK, tc.n0, tap, 0);
           }
         }
       }
@@ -412,20 +439,27 @@ __global__ void __launch_bounds__(Roles<SPLIT>::THREADS, 1)
           tc_fence_after();
           const uint32_t d_tmem = tmem_d + buf * BN;
           const uint32_t a_addr = smem_u32(smem + s * SM::STAGE);
-          const uint32_t b_addr = a_addr + A_TILE_BYTES;
+          const uint32_t b_addr = a_addr + SM::A_BYTES;
+          const uint32_t alo_addr = b_addr + SM::B_BYTES;
+          const uint32_t blo_addr = alo_addr + SM::A_BYTES;
+          // A_MODE 2: tap kx of this kernel row is the halo shifted by kx rows
+          const int ntap = A_MODE == 2 ? args.kw : 1;
+          for (int kx = 0; kx < ntap; ++kx) {
+            const uint32_t a_off = (uint32_t)kx * 128u, b_off = (uint32_t)kx * SM::B_TILE;
 #pragma unroll
-          for (int ks = 0; ks < BK / 8; ++ks) {
-            const uint32_t acc = (!first || ks > 0) ? 1u : 0u;
-            const uint64_t ad = sw128_kmajor_desc(a_addr + ks * 32);
-            const uint64_t bd = sw128_kmajor_desc(b_addr + ks * 32);
-            if (SPLIT) {
-              const uint64_t alo = sw128_kmajor_desc(b_addr + SM::B_TILE + ks * 32);
-              const uint64_t blo = sw128_kmajor_desc(b_addr + SM::B_TILE + A_TILE_BYTES + ks * 32);
-              mma_tf32(d_tmem, alo, bd, idesc, acc);
-              mma_tf32(d_tmem, ad, blo, idesc, 1u);
-              mma_tf32(d_tmem, ad, bd, idesc, 1u);
-            } else {
-              mma_tf32(d_tmem, ad, bd, idesc, acc);
+            for (int ks = 0; ks < BK / 8; ++ks) {
+              const uint32_t acc = (!first || kx > 0 || ks > 0) ? 1u : 0u;
+              const uint64_t ad = sw128_kmajor_desc(a_addr + a_off + ks * 32);
+              const uint64_t bd = sw128_kmajor_desc(b_addr + b_off + ks * 32);
+              if (SPLIT) {
+                const uint64_t alo = sw128_kmajor_desc(alo_addr + a_off + ks * 32);
+                const uint64_t blo = sw128_kmajor_desc(blo_addr + b_off + ks * 32);
+                mma_tf32(d_tmem, alo, bd, idesc, acc);
+                mma_tf32(d_tmem, ad, blo, idesc, 1u);
+                mma_tf32(d_tmem, ad, bd, idesc, 1u);
+              } else {
+                mma_tf32(d_tmem, ad, bd, idesc, acc);
+              }
             }
           }
           mma_commit(&empty_bar[s]);  // frees the stage once these MMAs have read it
@@ -449,9 +483,10 @@ __global__ void __launch_bounds__(Roles<SPLIT>::THREADS, 1)
         const uint32_t ph = (it / STAGES) & 1u;
         if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
         float4* a = reinterpret_cast<float4*>(smem + s * SM::STAGE);
-        float4* lo = reinterpret_cast<float4*>(smem + s * SM::STAGE + A_TILE_BYTES + SM::B_TILE);
+        float4* lo = reinterpret_cast<float4*>(smem + s * SM::STAGE + SM::A_BYTES + SM::B_BYTES);
+        const int n4 = A_MODE == 2 ? (BM + args.kw - 1) * (BK / 4) : A_TILE_BYTES / 16;
 #pragma unroll 4
-        for (int i = t; i < A_TILE_BYTES / 16; i += 64) {
+        for (int i = t; i < n4; i += 64) {
           const float4 v = a[i];
           float4 h;
           h.x = tf32_rna(v.x);
@@ -661,11 +696,28 @@ int sm_count() {
   return n;
 }
 
-template <int BN, int STAGES, bool SPLIT, int A_MODE>
+// Ring depth: as many stages as fit next to the output staging buffers and
+// the 1 KB alignment slack in 224 KB of dynamic shared memory (the 227 KB
+// per-block limit less up to 3 KB of static barriers and row caches), at
+// most 8.  An instantiation with room for fewer than 2 stages is not built.
+template <int BN, bool SPLIT, int A_MODE>
+constexpr int stages_raw() {
+  return (224 * 1024 - Roles<SPLIT>::EPI_GROUPS * 2 * OUT_STAGE_BYTES - 1024) / Smem<BN, SPLIT, A_MODE>::STAGE;
+}
+template <int BN, bool SPLIT, int A_MODE>
+constexpr int stages_for() {
+  return stages_raw<BN, SPLIT, A_MODE>() > 8 ? 8 : stages_raw<BN, SPLIT, A_MODE>();
+}
+
+template <int BN, bool SPLIT, int A_MODE>
 cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& blo,
                        const CUtensorMap& out, const GemmArgs& args, int tiles, cudaStream_t st) {
+  if constexpr (stages_raw<BN, SPLIT, A_MODE>() < 2) {
+    return cudaErrorInvalidValue;
+  } else {
+  constexpr int STAGES = stages_for<BN, SPLIT, A_MODE>();
   auto kern = gemm_tc_kernel<BN, STAGES, SPLIT, A_MODE>;
-  const int smem = STAGES * Smem<BN, SPLIT>::STAGE + Roles<SPLIT>::EPI_GROUPS * 2 * OUT_STAGE_BYTES + 1024;
+  const int smem = STAGES * Smem<BN, SPLIT, A_MODE>::STAGE + Roles<SPLIT>::EPI_GROUPS * 2 * OUT_STAGE_BYTES + 1024;
   static bool attr_set = false;  // per instantiation
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -675,6 +727,7 @@ cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
   const int grid = tiles < sm_count() ? tiles : sm_count();
   kern<<<grid, Roles<SPLIT>::THREADS, smem, st>>>(a, b, blo, out, args);
   return cudaGetLastError();
+  }
 }
 
 template <int A_MODE>
@@ -685,16 +738,16 @@ cudaError_t dispatch(int bn, bool split, const CUtensorMap& a, const CUtensorMap
   const int tiles = grid_m * ((args.N + bn - 1) / bn);
   if (!split) {
     switch (bn) {
-      case 32: return run_kernel<32, 7, false, A_MODE>(a, b, blo, out, args, tiles, st);
-      case 64: return run_kernel<64, 6, false, A_MODE>(a, b, blo, out, args, tiles, st);
-      case 128: return run_kernel<128, 4, false, A_MODE>(a, b, blo, out, args, tiles, st);
-      default: return run_kernel<256, 3, false, A_MODE>(a, b, blo, out, args, tiles, st);
+      case 32: return run_kernel<32, false, A_MODE>(a, b, blo, out, args, tiles, st);
+      case 64: return run_kernel<64, false, A_MODE>(a, b, blo, out, args, tiles, st);
+      case 128: return run_kernel<128, false, A_MODE>(a, b, blo, out, args, tiles, st);
+      default: return run_kernel<256, false, A_MODE>(a, b, blo, out, args, tiles, st);
     }
   }
   switch (bn) {
-    case 32: return run_kernel<32, 4, true, A_MODE>(a, b, blo, out, args, tiles, st);
-    case 64: return run_kernel<64, 4, true, A_MODE>(a, b, blo, out, args, tiles, st);
-    default: return run_kernel<128, 2, true, A_MODE>(a, b, blo, out, args, tiles, st);
+    case 32: return run_kernel<32, true, A_MODE>(a, b, blo, out, args, tiles, st);
+    case 64: return run_kernel<64, true, A_MODE>(a, b, blo, out, args, tiles, st);
+    default: return run_kernel<128, true, A_MODE>(a, b, blo, out, args, tiles, st);
   }
 }
 
@@ -800,6 +853,10 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
   if (g.sh != 1 || g.sw != 1 || (g.c & 3)) return cudaErrorInvalidValue;
   const bool split = math == MATH_3XTF32;
   if (split && !wk_lo) return cudaErrorInvalidValue;
+  // Halo-row mode (A_MODE 2) for rows at least 64 wide and kernels at most
+  // MAX_KW_HALO wide: one 128-pixel output row per tile, each input pixel
+  // staged once per kernel row.
+  const bool halo = g.ow >= 64 && g.kw <= MAX_KW_HALO && g.m <= (split ? 64 : 128);
   // Tile shape TH x TW = 128 output pixels; choose TW to waste the fewest.
   int best_tw = 16;
   int64_t best_cost = INT64_MAX;
@@ -808,14 +865,14 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
     const int64_t cost = (int64_t)((g.ow + tw - 1) / tw) * tw * ((g.oh + th - 1) / th) * th;
     if (cost < best_cost) { best_cost = cost; best_tw = tw; }
   }
-  const int tw = best_tw, th = 128 / tw;
+  const int tw = halo ? 128 : best_tw, th = halo ? 1 : 128 / tw;
   const int bn = pick_bn(g.m, split);
   CUtensorMap ma, mb, mblo;
   {
     const uint64_t dims[4] = {(uint64_t)g.c, (uint64_t)g.w, (uint64_t)g.h, (uint64_t)g.n};
     const uint64_t strides[3] = {(uint64_t)g.c * 4, (uint64_t)g.c * g.w * 4,
                                  (uint64_t)g.c * g.w * g.h * 4};
-    const uint32_t box[4] = {BK, (uint32_t)tw, (uint32_t)th, 1};
+    const uint32_t box[4] = {BK, (uint32_t)(halo ? tw + g.kw - 1 : tw), (uint32_t)th, 1};
     if (!make_map(&ma, x, 4, dims, strides, box)) return cudaErrorInvalidValue;
   }
   {
@@ -823,7 +880,7 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
     const uint64_t dims[4] = {(uint64_t)g.c, (uint64_t)g.m, (uint64_t)taps, 1};
     const uint64_t strides[3] = {(uint64_t)g.c * 4, (uint64_t)g.c * g.m * 4,
                                  (uint64_t)g.c * g.m * taps * 4};
-    const uint32_t box[4] = {BK, (uint32_t)bn, 1, 1};
+    const uint32_t box[4] = {BK, (uint32_t)bn, (uint32_t)(halo ? g.kw : 1), 1};
     if (!make_map(&mb, wk, 4, dims, strides, box)) return cudaErrorInvalidValue;
     if (split && !make_map(&mblo, wk_lo, 4, dims, strides, box)) return cudaErrorInvalidValue;
     if (!split) mblo = mb;
@@ -834,7 +891,7 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
   args.M = g.n * g.oh * g.ow;
   args.cblocks = (g.c + BK - 1) / BK;
   args.taps = g.kh * g.kw;
-  args.nkb = args.taps * args.cblocks;
+  args.nkb = (halo ? g.kh : args.taps) * args.cblocks;
   args.kw = g.kw;
   args.ph = g.ph;
   args.pw = g.pw;
@@ -857,6 +914,7 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
     args.tma_store = make_map(&mo, obase, 4, dims, strides, box) ? 1 : 0;
   }
   const int grid_m = g.n * args.tiles_x * args.tiles_y;
+  if (halo) return dispatch<2>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
   return dispatch<1>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
 }
 

@@ -1,0 +1,55 @@
+"""k x k stride-1 convolutions on the tensor-core implicit GEMM, one Conv node
+per graph, against the oracle's conv (qppocr-kernels conv.rs im2col + panel
+GEMM), metric max|d|/max|ref| (reference tests/kernels.rs:51-77).
+
+The cases cover both implicit-GEMM tilings: output rows >= 64 wide take the
+halo-row tiling (one 128-pixel row per tile, kernel taps as shifted views of
+one staged halo row), narrower rows the 2-D pixel-tile tiling.  Edges cover
+left/right/top/bottom padding, rows that end mid-tile, channel counts that
+are not a multiple of the 32-channel block, 5x5 kernels, output channel
+counts above the halo limit, and a fused ReLU + residual epilogue."""
+import numpy as np
+import pytest
+
+import oracle as orc
+import qppocr_b200 as q
+from qppocr_b200 import nets
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"tf32": 1e-3, "3xtf32": 1e-5}
+
+# (batch, cin, cout, k, h, w, act, residual)
+CASES = [
+    (2, 96, 24, 3, 40, 240, None, False),    # halo, DBFPN-like, 2 row tiles (128 + 112)
+    (1, 64, 64, 3, 17, 128, "relu", True),   # halo, exact row tile, fused relu + residual
+    (1, 20, 40, 3, 9, 200, None, False),     # halo, ragged channel block (20 of 32)
+    (1, 32, 100, 5, 12, 70, "relu", False),  # 5x5: wider than the halo buffer, tile path
+    (1, 24, 32, (1, 3), 8, 100, None, False), # halo, one kernel row
+    (1, 24, 32, (3, 1), 8, 100, None, False), # halo, one tap per kernel row
+    (1, 48, 136, 3, 10, 96, None, False),    # above the halo N limit: tile path
+    (2, 96, 24, 3, 30, 30, None, False),     # tile path, narrow rows
+]
+
+
+def build_conv(cin, cout, k, act, residual, seed=11):
+    b = nets.Builder(seed, "cv")
+    y = b.conv("x", cin, cout, k, bias=True, bn=True, act=act)
+    if residual:
+        y = b.node("Add", [y, "x"])
+    return b.graph(["x"], [y], [[1, cin, 0, 0]])
+
+
+@pytest.mark.parametrize("math", ["tf32", "3xtf32"])
+@pytest.mark.parametrize("case", CASES, ids=[f"{c[1]}x{c[2]}k{c[3]}_{c[4]}x{c[5]}".replace(" ", "") for c in CASES])
+def test_conv_kxk(cuda_ctx, case, math):
+    n, cin, cout, k, h, w, act, residual = case
+    g, wts = build_conv(cin, cout, k, act, residual)
+    g = q.optimize(g, wts)
+    x = np.random.Generator(np.random.PCG64(7)).uniform(-1, 1, (n, cin, h, w)).astype(np.float32)
+    ref = orc.run_graph(g, wts, {"x": x})[0]
+    s = cuda_ctx.create_session(g, wts, role="other", math=math)
+    got = s.run({"x": x})[0]
+    assert got.shape == ref.shape == (n, cout, h, w)
+    err = np.abs(got.astype(np.float64) - ref).max() / max(np.abs(ref).max(), 1e-6)
+    assert err < TOL[math], err
