@@ -162,6 +162,12 @@ int qpc_complete(qpc_ticket* ticket, int timeout_ms);
 int qpc_ticket_output_count(const qpc_ticket* ticket, int* count);
 int qpc_ticket_output(const qpc_ticket* ticket, int index, const float** data,
                       const int64_t** shape, int* rank);
+/* Copy output `index` of a completed ticket into the caller's buffer `dst`
+ * (`count` floats, the output's element count) with the library's host copy
+ * threads.  This is the copy into the fresh host Tensor that
+ * DeviceSession::run returns (device.rs:130); a binding may instead copy
+ * from qpc_ticket_output's pointer itself. */
+int qpc_ticket_output_copy(const qpc_ticket* ticket, int index, float* dst, int64_t count);
 int qpc_ticket_release(qpc_ticket* ticket);
 
 /* DeviceSession::run (device.rs:130): run_async + complete(no bound). */

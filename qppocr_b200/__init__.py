@@ -92,7 +92,7 @@ class QpcCaps(ctypes.Structure):
 EXPORTED = (
     "qpc_last_error", "qpc_device_count", "qpc_device_info", "qpc_session_create",
     "qpc_session_caps", "qpc_run_async", "qpc_complete", "qpc_ticket_output_count",
-    "qpc_ticket_output", "qpc_ticket_release", "qpc_run", "qpc_ticket_device_ms",
+    "qpc_ticket_output", "qpc_ticket_output_copy", "qpc_ticket_release", "qpc_run", "qpc_ticket_device_ms",
     "qpc_session_destroy", "qpc_session_profile", "qpc_session_profile_step",
     "qpc_session_replay", "qpc_session_node_count", "qpc_session_node", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_ctc_head", "qpc_op_ctc_head_noalloc",
     "qpc_op_split_tf32",
@@ -123,6 +123,7 @@ def lib():
     L.qpc_ticket_output.argtypes = [P, ctypes.c_int, ctypes.POINTER(ctypes.POINTER(ctypes.c_float)),
                                     ctypes.POINTER(ctypes.POINTER(ctypes.c_int64)),
                                     ctypes.POINTER(ctypes.c_int)]
+    L.qpc_ticket_output_copy.argtypes = [P, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64]
     L.qpc_ticket_release.argtypes = [P]
     L.qpc_ticket_device_ms.argtypes = [P, ctypes.POINTER(ctypes.c_float)]
     L.qpc_session_destroy.argtypes = [P]
@@ -281,7 +282,9 @@ class DeferredRun:
             _check(L.qpc_ticket_output(self._t, k, ctypes.byref(data), ctypes.byref(shp), ctypes.byref(rank)))
             shape = tuple(shp[i] for i in range(rank.value))
             cnt = int(np.prod(shape)) if shape else 1
-            outs.append(np.ctypeslib.as_array(data, shape=(cnt,)).reshape(shape).copy())
+            out = np.empty(shape, np.float32)
+            _check(L.qpc_ticket_output_copy(self._t, k, out.ctypes.data, cnt))
+            outs.append(out)
         ms = ctypes.c_float(0)
         _check(L.qpc_ticket_device_ms(self._t, ctypes.byref(ms)))
         self.device_ms = ms.value

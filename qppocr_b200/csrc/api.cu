@@ -7,6 +7,7 @@
 
 #include "kernels.h"
 #include "session.h"
+#include "host_copy.h"
 
 using namespace qpc;
 
@@ -192,6 +193,22 @@ int qpc_ticket_output(const qpc_ticket* t, int index, const float** data, const 
   if (data) *data = io.host;
   if (shape) *shape = io.shape.data();
   if (rank) *rank = (int)io.shape.size();
+  return OK;
+}
+
+int qpc_ticket_output_copy(const qpc_ticket* t, int index, float* dst, int64_t count) {
+  if (!t || !t->plan || !dst || index < 0 || index >= (int)t->plan->outs.size()) return E_INVALID;
+  if (!t->completed) {
+    set_error("ticket not completed");
+    return E_INVALID;
+  }
+  const auto& io = t->plan->outs[index];
+  if (count != io.count) {
+    set_error("output " + std::to_string(index) + " has " + std::to_string(io.count) + " elements, not " +
+              std::to_string(count));
+    return E_INVALID;
+  }
+  qpc::parallel_copy(dst, io.host, (size_t)count * sizeof(float));
   return OK;
 }
 

@@ -15,6 +15,7 @@
 //    below); fused epilogue order bias -> act -> residual
 //    (crates/qppocr-core/src/graph/optimize.rs:337-770).
 #include "session.h"
+#include "host_copy.h"
 
 #include <algorithm>
 #include <chrono>
@@ -2030,8 +2031,7 @@ PlanInstance* Session::launch(const qpc_tensor* inputs, int n) {
       const qpc_tensor* t = nullptr;
       for (int k = 0; k < n; ++k)
         if (io.name == inputs[k].name) t = &inputs[k];
-      std::memcpy(io.host, t->data, io.count * sizeof(float));
-      QPC_CUDA_OR_THROW(cudaMemcpyAsync(io.dev, io.host, io.count * sizeof(float), cudaMemcpyHostToDevice, p->stream));
+      QPC_CUDA_OR_THROW(staged_h2d(io.dev, io.host, t->data, io.count * sizeof(float), p->stream));
     }
     QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[1], p->stream));
     if (p->exec) {
