@@ -647,6 +647,205 @@ __global__ void __launch_bounds__(Roles<SPLIT>::THREADS, 1)
   if (warp == 0) tmem_dealloc(tmem_d, TMEM_COLS);
 }
 
+// Row-band implicit GEMM for k x k stride-1 convs (kw <= MAX_KW_HALO, one
+// column tile of N <= BN output channels, TF32).  A tile is RB output rows of
+// 128 pixels.  The whole filter (taps x channel blocks x BN x 32 floats,
+// tf32-rounded on the host) is loaded into shared memory once per CTA, and
+// the ring streams only input halo rows: stage (j, cb) is input row
+// oy0 - ph + j, channels cb*32..cb*32+31, columns ox0 - pw .. ox0 - pw + 128
+// + kw - 2.  Every staged row feeds each of the kh output rows it touches
+// (output row i = j - ky, all kw taps as shifted views), so an input pixel
+// crosses L2 -> SM (RB + kh - 1) / RB times per output row instead of kh
+// times, and no weights are restaged.  Accumulators: RB x BN TMEM columns per
+// tile, two tiles in flight.  Warps: w0 TMA, w1 MMA, w2-3 tf32 rounding of A,
+// w4-7 epilogue (one 128-pixel row chunk at a time through store_tile).
+template <int BN, int STAGES, int RB>
+__global__ void __launch_bounds__(256, 1)
+    conv_band_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmOut, const GemmArgs args, int w_bytes) {
+  constexpr int B_TILE = BN * BK * 4;
+  constexpr uint32_t TMEM_COLS = 2 * RB * BN;
+  static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512, "band accumulators do not fit TMEM");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t conv_bar[STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t w_full;
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ int64_t s_rrow[BM];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total_tiles = args.m_tiles;
+  const int kw = args.kw, kh = args.taps / args.kw, cblocks = args.cblocks;
+  const int nkb = (RB + kh - 1) * cblocks;
+  uint8_t* wsm = smem;                   // resident filter
+  uint8_t* ring = smem + w_bytes;        // STAGES x HALO_BYTES
+  uint8_t* out_stage = ring + STAGES * HALO_BYTES;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+      mbar_init(&conv_bar[s], 64);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(&w_full, 1);
+    fence_barrier_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmW);
+    if (args.tma_store) prefetch_tensormap(&tmOut);
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = tmem_base_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: the filter once, then halo rows
+      mbar_arrive_expect_tx(&w_full, (uint32_t)w_bytes);
+      for (int tap = 0; tap < args.taps; ++tap)
+        for (int cb = 0; cb < cblocks; ++cb)
+          tma_load_4d(wsm + (tap * cblocks + cb) * B_TILE, &tmW, &w_full, cb * BK, 0, tap, 0);
+      const uint32_t a_bytes = (uint32_t)(BM + kw - 1) * BK * 4;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        const TileCoord tc = tile_coord(args, tile, 1, BN);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int j = kb / cblocks, cb = kb % cblocks;
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full_bar[s], a_bytes);
+          tma_load_4d(ring + s * HALO_BYTES, &tmA, &full_bar[s], cb * BK, tc.ox0 - args.pw,
+                      tc.oy0 - args.ph + j, tc.img);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc = idesc_tf32(BM, BN);
+      bool ok = mbar_wait(&w_full, 0, args.err);
+      const uint32_t w_addr = smem_u32(wsm);
+      uint32_t it = 0, acc_i = 0;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++acc_i) {
+        const TileCoord tc = tile_coord(args, tile, 1, BN);
+        const int rows = min(RB, args.oh - tc.oy0);
+        const uint32_t buf = acc_i & 1u;
+        if (acc_i >= 2 && !mbar_wait(&acc_empty[buf], ((acc_i >> 1) - 1) & 1u, args.err)) break;
+        const uint32_t d_base = tmem_d + buf * (RB * BN);
+        for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
+          const int j = kb / cblocks, cb = kb % cblocks;
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(ring + s * HALO_BYTES);
+          for (int ky = 0; ky < kh; ++ky) {
+            const int i = j - ky;  // output row of this tile fed by kernel row ky
+            if (i < 0 || i >= rows) continue;
+            const uint32_t d = d_base + i * BN;
+            for (int kx = 0; kx < kw; ++kx) {
+              const uint32_t b_addr = w_addr + ((ky * kw + kx) * cblocks + cb) * B_TILE;
+#pragma unroll
+              for (int ks = 0; ks < BK / 8; ++ks) {
+                const uint32_t acc = (ky | cb | kx | ks) ? 1u : 0u;
+                mma_tf32(d, sw128_kmajor_desc(a_addr + kx * 128 + ks * 32),
+                         sw128_kmajor_desc(b_addr + ks * 32), idesc, acc);
+              }
+            }
+          }
+          mma_commit(&empty_bar[s]);
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[buf]);
+      }
+    }
+  } else if (warp < 4) {
+    // ---------------- converters: round the halo row to tf32 (nearest) in place
+    const int t = threadIdx.x - 64;
+    const int n4 = (BM + kw - 1) * (BK / 4);
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1u;
+        if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
+        float4* a = reinterpret_cast<float4*>(ring + s * HALO_BYTES);
+#pragma unroll 4
+        for (int i = t; i < n4; i += 64) {
+          const float4 v = a[i];
+          a[i] = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&conv_bar[s]);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 4-7): TMEM lane r = pixel ox0 + r
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int gt = threadIdx.x - 128;
+    const uint32_t lane_base = tmem_d + ((uint32_t)(q * 32) << 16);
+    uint32_t acc_i = 0, chunk_ctr = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++acc_i) {
+      const TileCoord tc = tile_coord(args, tile, 1, BN);
+      const int rows = min(RB, args.oh - tc.oy0);
+      const uint32_t buf = acc_i & 1u;
+      if (!mbar_wait(&acc_full[buf], (acc_i >> 1) & 1u, args.err)) break;
+      tc_fence_after();
+      for (int i = 0; i < rows; ++i) {
+        const uint32_t col0 = buf * (RB * BN) + i * BN;
+        auto fetch = [&](int c, float (&v)[32]) {
+          uint32_t a[16], b[16];
+          tmem_ld16_nowait(lane_base + col0 + c, a);
+          tmem_ld16_nowait(lane_base + col0 + c + 16, b);
+          tmem_ld_wait();
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            v[jj] = __uint_as_float(a[jj]);
+            v[16 + jj] = __uint_as_float(b[jj]);
+          }
+        };
+        if (args.tma_store) {
+          store_tile<BN, 1>(args, &tmOut, out_stage, s_rrow, 1, chunk_ctr, 0, 0, tc.img, tc.oy0 + i, tc.ox0,
+                            r, gt, fetch);
+        } else {
+          const RowMap m = row_map<1>(args, 0, tc.img, tc.oy0 + i, tc.ox0, r);
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            if (c >= args.N) break;
+            float v[16];
+            tmem_ld16(lane_base + col0 + c, v);  // warp-collective
+            if (m.orow >= 0) epilogue_store<BN>(args, v, m.orow, m.rrow, c);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  if (args.tma_store && threadIdx.x == 128) bulk_wait_group<0>();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_d, TMEM_COLS);
+}
+
 // ----------------------------------------------------------- host helpers
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -751,6 +950,29 @@ cudaError_t dispatch(int bn, bool split, const CUtensorMap& a, const CUtensorMap
   }
 }
 
+// Row-band conv: STAGES halo rows in the ring next to the resident filter and
+// one epilogue group's two output staging buffers.
+constexpr int BAND_STAGES = 4;
+constexpr int BAND_RB = 4;
+constexpr int BAND_W_MAX = 224 * 1024 - BAND_STAGES * HALO_BYTES - 2 * OUT_STAGE_BYTES - 1024;
+
+template <int BN>
+cudaError_t run_band(const CUtensorMap& a, const CUtensorMap& w, const CUtensorMap& out,
+                     const GemmArgs& args, int w_bytes, cudaStream_t st) {
+  auto kern = conv_band_kernel<BN, BAND_STAGES, BAND_RB>;
+  const int smem = w_bytes + BAND_STAGES * HALO_BYTES + 2 * OUT_STAGE_BYTES + 1024;
+  if (w_bytes > BAND_W_MAX) return cudaErrorInvalidValue;
+  static int attr_set = 0;  // per instantiation: the largest size set so far
+  if (smem > attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set = smem;
+  }
+  const int grid = args.m_tiles < sm_count() ? args.m_tiles : sm_count();
+  kern<<<grid, 256, smem, st>>>(a, w, out, args, w_bytes);
+  return cudaGetLastError();
+}
+
 // Output tile width: the smallest N tile that covers N with the least padding
 // (3xTF32 keeps its promoted accumulator in registers: at most 128 columns).
 int pick_bn(int n, bool split) {
@@ -853,6 +1075,61 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
   if (g.sh != 1 || g.sw != 1 || (g.c & 3)) return cudaErrorInvalidValue;
   const bool split = math == MATH_3XTF32;
   if (split && !wk_lo) return cudaErrorInvalidValue;
+  // Row-band mode: TF32, rows at least 64 wide, kernels at most MAX_KW_HALO
+  // wide, one column tile, and a filter that fits in shared memory.
+  {
+    const int bn = pick_bn(g.m, false);
+    const int cblocks = (g.c + BK - 1) / BK;
+    const int64_t w_bytes = (int64_t)g.kh * g.kw * cblocks * bn * BK * 4;
+    if (!split && g.ow >= 64 && g.kw <= MAX_KW_HALO && g.m <= 64 && w_bytes <= BAND_W_MAX) {
+      CUtensorMap ma, mw, mo;
+      {
+        const uint64_t dims[4] = {(uint64_t)g.c, (uint64_t)g.w, (uint64_t)g.h, (uint64_t)g.n};
+        const uint64_t strides[3] = {(uint64_t)g.c * 4, (uint64_t)g.c * g.w * 4,
+                                     (uint64_t)g.c * g.w * g.h * 4};
+        const uint32_t box[4] = {BK, (uint32_t)(BM + g.kw - 1), 1, 1};
+        if (!make_map(&ma, x, 4, dims, strides, box)) return cudaErrorInvalidValue;
+      }
+      {
+        const int taps = g.kh * g.kw;
+        const uint64_t dims[4] = {(uint64_t)g.c, (uint64_t)g.m, (uint64_t)taps, 1};
+        const uint64_t strides[3] = {(uint64_t)g.c * 4, (uint64_t)g.c * g.m * 4,
+                                     (uint64_t)g.c * g.m * taps * 4};
+        const uint32_t box[4] = {BK, (uint32_t)bn, 1, 1};
+        if (!make_map(&mw, wk, 4, dims, strides, box)) return cudaErrorInvalidValue;
+      }
+      GemmArgs args{};
+      args.N = g.m;
+      args.K = g.c * g.kh * g.kw;
+      args.M = g.n * g.oh * g.ow;
+      args.cblocks = cblocks;
+      args.taps = g.kh * g.kw;
+      args.kw = g.kw;
+      args.ph = g.ph;
+      args.pw = g.pw;
+      args.oh = g.oh;
+      args.ow = g.ow;
+      args.tw = BM;
+      args.th = BAND_RB;
+      args.tiles_x = (g.ow + BM - 1) / BM;
+      args.tiles_y = (g.oh + BAND_RB - 1) / BAND_RB;
+      args.m_tiles = g.n * args.tiles_x * args.tiles_y;
+      args.epi = epi;
+      args.err = err;
+      mo = ma;
+      const float* obase = epi.out + epi.col_off;
+      if ((g.m % 4) == 0 && (epi.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(obase) & 15) == 0 &&
+          (!epi.residual || (epi.ldr % 4) == 0)) {
+        const uint64_t dims[4] = {(uint64_t)g.m, (uint64_t)g.ow, (uint64_t)g.oh, (uint64_t)g.n};
+        const uint64_t strides[3] = {(uint64_t)epi.ldo * 4, (uint64_t)epi.ldo * g.ow * 4,
+                                     (uint64_t)epi.ldo * g.ow * g.oh * 4};
+        const uint32_t box[4] = {32, (uint32_t)BM, 1, 1};
+        args.tma_store = make_map(&mo, obase, 4, dims, strides, box) ? 1 : 0;
+      }
+      if (bn == 32) return run_band<32>(ma, mw, mo, args, (int)w_bytes, st);
+      return run_band<64>(ma, mw, mo, args, (int)w_bytes, st);
+    }
+  }
   // Halo-row mode (A_MODE 2) for rows at least 64 wide and kernels at most
   // MAX_KW_HALO wide: one 128-pixel output row per tile, each input pixel
   // staged once per kernel row.

@@ -500,6 +500,27 @@ void Session::fuse() {
     N[cs[0]] = f;
   }
 
+  // Upsampled residual: a Conv's residual that is the output of a nearest
+  // Resize used only there is read from the Resize's input through the
+  // epilogue's nearest-source row remap (resize.rs:43-50), so the upsampled
+  // map is never written (DBFPN: out_k = in_k + up(out_{k+1})).
+  for (size_t i = 0; i < N.size(); ++i) {
+    if (!alive[i] || N[i].op != "Conv" || !N[i].geti("qpc_has_res", 0) || !N[i].has_in(3)) continue;
+    const std::string r = N[i].in[3];
+    if (gouts.count(r)) continue;
+    auto rc = consumers(r);
+    if (rc.size() != 1) continue;
+    for (size_t k = 0; k < N.size(); ++k) {
+      if (!alive[k] || N[k].op != "Resize" || N[k].out.empty() || N[k].out[0] != r) continue;
+      if (N[k].gets("mode", "nearest") != "nearest" || N[k].in.empty() || is_const(N[k].in[0])) break;
+      Node& c = N[i];
+      c.in[3] = N[k].in[0];
+      c.seti("qpc_res_up", 1);  // the upsampled size is the conv's output size
+      alive[k] = false;
+      break;
+    }
+  }
+
   // LayerNorm decomposition (executor ReduceMean/Sub/Pow/ReduceMean/Add/Sqrt/
   // Div then Mul/Add or MulAddScale; shape.rs:510-566 f64 means) -> QpcLayerNorm.
   for (size_t i = 0; i < N.size(); ++i) {
@@ -1082,16 +1103,44 @@ class Planner {
     const double flops = 2.0 * N * oh * ow * M * cg * kh * kw;
     const double out_bytes = 4.0 * N * oh * ow * M;
 
-    // Residual: plain tensor, or (res_up) the pre-upsample map of a nearest resize.
+    // Residual: plain tensor, or (qpc_res_up) the pre-upsample map of a
+    // nearest resize to the output size, read through the epilogue's remap
+    // on the tensor-core paths and upsampled by a resize step elsewhere.
     const bool has_res = n.has_in(3);
+    const bool res_up = has_res && n.geti("qpc_res_up", 0) != 0;
+    const bool epi_path = (pw1 || kxk_tc) && !dw;
     Val res;
+    int res_h = 0, res_w = 0;  // > 0: remap from a res_h x res_w map
     if (has_res) {
       const Val& r0 = get(n.in[3]);
-      if (r0.shape != oshape) throw GraphError{"residual shape " + shape_str(r0.shape) + " != " + shape_str(oshape)};
-      res = as_nhwc(r0, n.name + " residual");
+      if (res_up) {
+        if (r0.shape.size() != 4 || r0.shape[0] != N || r0.shape[1] != M)
+          throw GraphError{"upsampled residual shape " + shape_str(r0.shape) + " vs " + shape_str(oshape)};
+        res = as_nhwc(r0, n.name + " residual");
+        if (epi_path) {
+          res_h = (int)r0.shape[2];
+          res_w = (int)r0.shape[3];
+        } else {
+          if (M % 4) throw GraphError{"upsampled residual: M % 4 != 0 unsupported"};
+          Val up = new_val(oshape, true);
+          const float* sp = out_ptr(res);
+          float* dp = out_ptr(up);
+          const int rh = (int)r0.shape[2], rw = (int)r0.shape[3];
+          step("resize", n.name + " residual", 4.0 * (N * M * rh * rw + N * M * oh * ow), 0,
+               [=](cudaStream_t s) {
+                 return launch_resize_nearest_nhwc(sp, dp, (int)N, rh, rw, (int)M, (int)oh, (int)ow,
+                                                   (int)M, 0, s);
+               });
+          unref(res);
+          res = up;
+        }
+      } else {
+        if (r0.shape != oshape) throw GraphError{"residual shape " + shape_str(r0.shape) + " != " + shape_str(oshape)};
+        res = as_nhwc(r0, n.name + " residual");
+      }
     }
+    const double res_bytes = has_res ? (res_h > 0 ? 4.0 * N * M * res_h * res_w : out_bytes) : 0.0;
     Val y;
-    const bool epi_path = (pw1 || kxk_tc) && !dw;
     int64_t ldo = M;
     if (epi_path && concat_slot(n.out[0], oshape, &y)) ldo = y.strides[3];
     else y = new_val(oshape, true);
@@ -1120,8 +1169,14 @@ class Planner {
       e.ldo = (int)ldo;
       e.ldr = (int)M;
       e.act = act;
+      if (res_h > 0) {
+        e.rh = res_h;
+        e.rw = res_w;
+        e.oh = (int)oh;
+        e.ow = (int)ow;
+      }
       const int64_t rows = N * H * W;
-      const double bytes = 4.0 * rows * C + out_bytes + 4.0 * M * C + (has_res ? out_bytes : 0);
+      const double bytes = 4.0 * rows * C + out_bytes + 4.0 * M * C + res_bytes;
       step("gemm_tc", nm, bytes, flops, [=](cudaStream_t s) {
         return launch_gemm_tc(xp, rows, (int)C, (int)C, wb, wl, (int)M, e, math, err, s);
       });
@@ -1139,7 +1194,13 @@ class Planner {
       e.ldo = (int)ldo;
       e.ldr = (int)M;
       e.act = act;
-      const double bytes = 4.0 * N * H * W * C + out_bytes + 4.0 * M * C * kh * kw + (has_res ? out_bytes : 0);
+      if (res_h > 0) {
+        e.rh = res_h;
+        e.rw = res_w;
+        e.oh = (int)oh;
+        e.ow = (int)ow;
+      }
+      const double bytes = 4.0 * N * H * W * C + out_bytes + 4.0 * M * C * kh * kw + res_bytes;
       step("conv_tc", nm, bytes, flops,
            [=](cudaStream_t s) { return launch_conv_tc(xp, g, wb, wl, e, math, err, s); });
       unref(x);

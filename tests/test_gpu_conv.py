@@ -2,9 +2,12 @@
 per graph, against the oracle's conv (qppocr-kernels conv.rs im2col + panel
 GEMM), metric max|d|/max|ref| (reference tests/kernels.rs:51-77).
 
-The cases cover both implicit-GEMM tilings: output rows >= 64 wide take the
-halo-row tiling (one 128-pixel row per tile, kernel taps as shifted views of
-one staged halo row), narrower rows the 2-D pixel-tile tiling.  Edges cover
+The cases cover the three implicit-GEMM tilings: in TF32, output rows >= 64
+wide with at most 64 output channels and a filter that fits in shared memory
+take the row-band tiling (4 output rows per tile, resident filter); other
+rows >= 64 wide take the halo-row tiling (one 128-pixel row per tile, kernel
+taps as shifted views of one staged halo row); narrower rows the 2-D
+pixel-tile tiling.  Edges cover
 left/right/top/bottom padding, rows that end mid-tile, channel counts that
 are not a multiple of the 32-channel block, 5x5 kernels, output channel
 counts above the halo limit, and a fused ReLU + residual epilogue."""
@@ -21,9 +24,10 @@ TOL = {"tf32": 1e-3, "3xtf32": 1e-5}
 
 # (batch, cin, cout, k, h, w, act, residual)
 CASES = [
-    (2, 96, 24, 3, 40, 240, None, False),    # halo, DBFPN-like, 2 row tiles (128 + 112)
-    (1, 64, 64, 3, 17, 128, "relu", True),   # halo, exact row tile, fused relu + residual
-    (1, 20, 40, 3, 9, 200, None, False),     # halo, ragged channel block (20 of 32)
+    (2, 96, 24, 3, 40, 240, None, False),    # band (tf32) / halo, DBFPN-like, 2 row tiles (128 + 112)
+    (1, 64, 64, 3, 17, 128, "relu", True),   # halo (filter too big for band), relu + residual
+    (1, 32, 32, 3, 13, 150, "relu", True),   # band, 13 rows = 3 full bands + 1, relu + residual
+    (1, 20, 40, 3, 9, 200, None, False),     # band N=40 (64-col tile), ragged channel block (20 of 32)
     (1, 32, 100, 5, 12, 70, "relu", False),  # 5x5: wider than the halo buffer, tile path
     (1, 24, 32, (1, 3), 8, 100, None, False), # halo, one kernel row
     (1, 24, 32, (3, 1), 8, 100, None, False), # halo, one tap per kernel row
@@ -51,5 +55,32 @@ def test_conv_kxk(cuda_ctx, case, math):
     s = cuda_ctx.create_session(g, wts, role="other", math=math)
     got = s.run({"x": x})[0]
     assert got.shape == ref.shape == (n, cout, h, w)
+    err = np.abs(got.astype(np.float64) - ref).max() / max(np.abs(ref).max(), 1e-6)
+    assert err < TOL[math], err
+
+
+UP_CASES = [(1, 32, 24, 1, 20, 30, 2), (1, 32, 24, 3, 16, 96, 2), (2, 16, 16, 1, 24, 24, 4)]
+
+
+@pytest.mark.parametrize("math", ["tf32", "3xtf32"])
+@pytest.mark.parametrize("case", UP_CASES, ids=[f"k{c[3]}_{c[4]}x{c[5]}_up{c[6]}" for c in UP_CASES])
+def test_conv_upsampled_residual(cuda_ctx, case, math):
+    """Conv + Add(Resize_nearest(z)): the resize is absorbed into the conv's
+    epilogue (residual rows read through the nearest-source remap), so the
+    upsampled map is never written; results match the unfused oracle."""
+    n, cin, cout, k, h, w, up = case
+    b = nets.Builder(13, "up")
+    y = b.conv("x", cin, cout, k, bias=True, bn=False, act="relu")
+    r = b.resize2("z", float(up))
+    y = b.node("Add", [y, r])
+    g, wts = b.graph(["x", "z"], [y], [[1, cin, 0, 0], [1, cout, 0, 0]])
+    g = q.optimize(g, wts)
+    rng = np.random.Generator(np.random.PCG64(9))
+    x = rng.uniform(-1, 1, (n, cin, h, w)).astype(np.float32)
+    z = rng.uniform(-1, 1, (n, cout, h // up, w // up)).astype(np.float32)
+    ref = orc.run_graph(g, wts, {"x": x, "z": z})[0]
+    s = cuda_ctx.create_session(g, wts, role="other", math=math)
+    assert [f[0] for f in s.fused_nodes()] == ["Conv"]
+    got = s.run({"x": x, "z": z})[0]
     err = np.abs(got.astype(np.float64) - ref).max() / max(np.abs(ref).max(), 1e-6)
     assert err < TOL[math], err
