@@ -165,21 +165,31 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
     float* sb = reinterpret_cast<float*>(stage + (chunk_ctr & 1u) * OUT_STAGE_BYTES);
     if (t == 0) bulk_wait_group_read<1>();
     named_bar_sync(bar_id, 128);
+    float v[32];
     if (e.residual) {
-#pragma unroll 2
-      for (int i = t; i < BM * 8; i += 128) {
+      // all 8 loads of this thread in flight at once, then into the swizzled
+      // staging buffer (while the TMEM fetch below is outstanding)
+      float4 rv[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = t + k * 128;
         const int row = i >> 3, c4 = i & 7;
         const int col = n0 + cc + c4 * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         const int64_t rr = s_rrow[row];
-        if (rr >= 0 && col < args.N)
-          v = __ldg(reinterpret_cast<const float4*>(e.residual + rr * e.ldr + col));
-        *reinterpret_cast<float4*>(sb + row * 32 + ((c4 ^ (row & 7)) << 2)) = v;
+        rv[k] = (rr >= 0 && col < args.N) ? __ldg(reinterpret_cast<const float4*>(e.residual + rr * e.ldr + col))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = t + k * 128;
+        const int row = i >> 3, c4 = i & 7;
+        *reinterpret_cast<float4*>(sb + row * 32 + ((c4 ^ (row & 7)) << 2)) = rv[k];
+      }
+      fetch(cc, v);
       named_bar_sync(bar_id, 128);
+    } else {
+      fetch(cc, v);
     }
-    float v[32];
-    fetch(cc, v);
     if (e.bias) {
       // columns past N are clipped by the TMA store; keep their reads in bounds
 #pragma unroll

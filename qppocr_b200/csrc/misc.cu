@@ -145,11 +145,115 @@ __global__ void __launch_bounds__(256) conv_small_c_kernel(
   }
 }
 
+// Stem specialisation (C = 3, 3x3, stride 2, NCHW input, NHWC output): a
+// block makes an 8 x 64 output tile; its 3 x 17 x 129 input window is staged
+// in shared memory with coalesced row loads (zeros outside the image), and
+// each thread makes 2 horizontally adjacent pixels, so every broadcast weight
+// read feeds 2 FMAs.  Per element the chain is the generic kernel's: acc = 0,
+// fma over k = (ch, ky, kx) ascending, then + bias, act, + residual.
+template <int M>
+__global__ void __launch_bounds__(256) conv_stem3s2_kernel(
+    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
+    const float* __restrict__ residual, float* __restrict__ y, int N, int H, int W, int OH, int OW,
+    int PH, int PW, ActParams act) {
+  constexpr int TH = 8, TW = 64, IR = 2 * TH + 1, IC = 2 * TW + 1, ICP = IC + 3;
+  __shared__ __align__(16) float wsm[27 * M];
+  __shared__ float xs[3][IR][ICP];
+  for (int i = threadIdx.x; i < 27 * M; i += 256) {
+    const int k = i / M, m = i % M;
+    wsm[i] = w[m * 27 + k];
+  }
+  const int tiles_x = (OW + TW - 1) / TW, tiles_y = (OH + TH - 1) / TH;
+  const int64_t tiles = (int64_t)N * tiles_y * tiles_x;
+  const int tr = threadIdx.x >> 5, tc = threadIdx.x & 31;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int bx = (int)(tile % tiles_x);
+    const int64_t rr = tile / tiles_x;
+    const int by = (int)(rr % tiles_y);
+    const int n = (int)(rr / tiles_y);
+    const int oy0 = by * TH, ox0 = bx * TW;
+    const int iy0 = oy0 * 2 - PH, ix0 = ox0 * 2 - PW;
+    __syncthreads();  // previous tile consumed (and weights staged)
+    for (int i = threadIdx.x; i < 3 * IR * IC; i += 256) {
+      const int col = i % IC;
+      const int row = (i / IC) % IR;
+      const int ch = i / (IC * IR);
+      const int iy = iy0 + row, ix = ix0 + col;
+      float v = 0.f;
+      if (iy >= 0 && iy < H && ix >= 0 && ix < W) v = __ldg(x + (((int64_t)n * 3 + ch) * H + iy) * W + ix);
+      xs[ch][row][col] = v;
+    }
+    __syncthreads();
+    float a0[M], a1[M];
+#pragma unroll
+    for (int i = 0; i < M; ++i) a0[i] = a1[i] = 0.f;
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch)
+#pragma unroll
+      for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+          const int k = (ch * 3 + ky) * 3 + kx;
+          const float v0 = xs[ch][2 * tr + ky][4 * tc + kx];
+          const float v1 = xs[ch][2 * tr + ky][4 * tc + 2 + kx];
+          const float4* wk = reinterpret_cast<const float4*>(wsm + k * M);
+#pragma unroll
+          for (int i4 = 0; i4 < M / 4; ++i4) {
+            const float4 wv = wk[i4];
+            a0[4 * i4] = __fmaf_rn(wv.x, v0, a0[4 * i4]);
+            a0[4 * i4 + 1] = __fmaf_rn(wv.y, v0, a0[4 * i4 + 1]);
+            a0[4 * i4 + 2] = __fmaf_rn(wv.z, v0, a0[4 * i4 + 2]);
+            a0[4 * i4 + 3] = __fmaf_rn(wv.w, v0, a0[4 * i4 + 3]);
+            a1[4 * i4] = __fmaf_rn(wv.x, v1, a1[4 * i4]);
+            a1[4 * i4 + 1] = __fmaf_rn(wv.y, v1, a1[4 * i4 + 1]);
+            a1[4 * i4 + 2] = __fmaf_rn(wv.z, v1, a1[4 * i4 + 2]);
+            a1[4 * i4 + 3] = __fmaf_rn(wv.w, v1, a1[4 * i4 + 3]);
+          }
+        }
+    const int oy = oy0 + tr;
+#pragma unroll
+    for (int px = 0; px < 2; ++px) {
+      const int ox = ox0 + 2 * tc + px;
+      if (oy >= OH || ox >= OW) continue;
+      const int64_t t = ((int64_t)n * OH + oy) * OW + ox;
+      float o[M];
+#pragma unroll
+      for (int i = 0; i < M; ++i) o[i] = px ? a1[i] : a0[i];
+      if (bias)
+#pragma unroll
+        for (int i = 0; i < M; ++i) o[i] = __fadd_rn(o[i], __ldg(bias + i));
+      apply_act_n(o, act);
+      if (residual)
+#pragma unroll
+        for (int i = 0; i < M; ++i) o[i] = __fadd_rn(o[i], __ldg(residual + t * M + i));
+      float4* yo = reinterpret_cast<float4*>(y + t * M);
+#pragma unroll
+      for (int i4 = 0; i4 < M / 4; ++i4)
+        yo[i4] = make_float4(o[4 * i4], o[4 * i4 + 1], o[4 * i4 + 2], o[4 * i4 + 3]);
+    }
+  }
+}
+
 cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const float* bias,
                                const float* residual, float* y, const ConvGeom& g, int group,
                                const ActParams& act, cudaStream_t st) {
   const int mg = g.m / group;
   const int64_t pix = (int64_t)g.n * g.oh * g.ow;
+  if (group == 1 && x_nchw && g.c == 3 && g.kh == 3 && g.kw == 3 && g.sh == 2 && g.sw == 2 &&
+      (g.m == 8 || g.m == 16 || g.m == 32)) {
+    const int64_t tiles = (int64_t)g.n * ((g.oh + 7) / 8) * ((g.ow + 63) / 64);
+    const int grid = (int)(tiles < 148 * 8 ? tiles : 148 * 8);
+#define QPC_STEM(M_)                                                                              \
+  if (g.m == M_) {                                                                                \
+    conv_stem3s2_kernel<M_><<<grid, 256, 0, st>>>(x, w, bias, residual, y, g.n, g.h, g.w, g.oh,   \
+                                                  g.ow, g.ph, g.pw, act);                          \
+    return cudaGetLastError();                                                                    \
+  }
+    QPC_STEM(8)
+    QPC_STEM(16)
+    QPC_STEM(32)
+#undef QPC_STEM
+  }
   if (group == 1 && g.c <= 4 && (g.m == 8 || g.m == 16 || g.m == 32)) {
     const size_t smem = (size_t)g.c * g.kh * g.kw * g.m * sizeof(float);
 #define QPC_SMALLC(M_)                                                                            \
@@ -257,11 +361,86 @@ __global__ void __launch_bounds__(256) convt2x2_pix_kernel(
   }
 }
 
+// Same arithmetic again, organised for wide outputs (M % 4 == 0): thread j of
+// a pixel slot owns tap t = j / (M/4) and output channels 4*(j % (M/4)) ..+3,
+// and keeps those C x 4 weights in registers.  A block stages PIX input pixels
+// in shared memory (coalesced float4 loads) and its SLOTS pixel slots walk
+// them; per pixel a thread reads the C inputs as broadcast float4s and makes
+// 4 outputs (each the c-ascending chain from 0, then BN fma, then act).  The
+// M threads of one pixel write its 4 output pixels as 2 runs of 2*M floats.
+template <int C, int M, int SLOTS, int PIX>
+__global__ void __launch_bounds__(SLOTS * M) convt2x2_wide_kernel(
+    const float* __restrict__ x, const float* __restrict__ wt, const float* __restrict__ bn_a,
+    const float* __restrict__ bn_b, float* __restrict__ y, int N, int H, int W, ActParams act) {
+  static_assert(C % 4 == 0 && M % 4 == 0, "vector widths");
+  constexpr int G = M / 4;  // float4 groups per tap
+  __shared__ __align__(16) float xs[PIX * C];
+  const int j = threadIdx.x % M, slot = threadIdx.x / M;
+  const int t = j / G, m0 = 4 * (j % G);
+  float w[C][4];
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[c][i] = __ldg(wt + (c * M + m0 + i) * 4 + t);
+  float4 ba = make_float4(1.f, 1.f, 1.f, 1.f), bb = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (bn_a) {
+    ba = __ldg(reinterpret_cast<const float4*>(bn_a + m0));
+    bb = __ldg(reinterpret_cast<const float4*>(bn_b + m0));
+  }
+  const int OW = 2 * W;
+  const int64_t total = (int64_t)N * H * W;
+  for (int64_t p0 = (int64_t)blockIdx.x * PIX; p0 < total; p0 += (int64_t)gridDim.x * PIX) {
+    const int np = (int)(total - p0 < PIX ? total - p0 : PIX);
+    __syncthreads();  // previous chunk fully consumed
+    const float4* src = reinterpret_cast<const float4*>(x + p0 * C);
+    for (int i = threadIdx.x; i < np * (C / 4); i += SLOTS * M)
+      reinterpret_cast<float4*>(xs)[i] = __ldg(src + i);
+    __syncthreads();
+    for (int k = slot; k < np; k += SLOTS) {
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      const float4* xp = reinterpret_cast<const float4*>(xs + k * C);
+#pragma unroll
+      for (int c4 = 0; c4 < C / 4; ++c4) {
+        const float4 v = xp[c4];
+        const float xv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = 4 * c4 + q;
+          a0 = __fmaf_rn(xv[q], w[c][0], a0);
+          a1 = __fmaf_rn(xv[q], w[c][1], a1);
+          a2 = __fmaf_rn(xv[q], w[c][2], a2);
+          a3 = __fmaf_rn(xv[q], w[c][3], a3);
+        }
+      }
+      if (bn_a) {
+        a0 = __fmaf_rn(a0, ba.x, bb.x);
+        a1 = __fmaf_rn(a1, ba.y, bb.y);
+        a2 = __fmaf_rn(a2, ba.z, bb.z);
+        a3 = __fmaf_rn(a3, ba.w, bb.w);
+      }
+      float o[4] = {a0, a1, a2, a3};
+      apply_act_n(o, act);
+      const int64_t p = p0 + k;
+      const int ix = (int)(p % W);
+      const int64_t r = p / W;
+      const int iy = (int)(r % H);
+      const int n = (int)(r / H);
+      const int oy = 2 * iy + (t >> 1), ox = 2 * ix + (t & 1);
+      *reinterpret_cast<float4*>(y + (((int64_t)n * 2 * H + oy) * OW + ox) * M + m0) =
+          make_float4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 cudaError_t launch_convt2x2(const float* x, const float* wt, const float* bn_a, const float* bn_b,
                             float* y, int n, int h, int w, int c, int m, const ActParams& act,
                             cudaStream_t st) {
   if (c == 24 && m == 24) {
-    convt2x2_pix_kernel<24, 24><<<grid_for((int64_t)n * h * w, 256), 256, 0, st>>>(x, wt, bn_a, bn_b, y, n, h, w, act);
+    constexpr int SLOTS = 8, PIX = 256;
+    const int64_t chunks = ((int64_t)n * h * w + PIX - 1) / PIX;
+    const int grid = (int)(chunks < 148 * 8 ? chunks : 148 * 8);
+    convt2x2_wide_kernel<24, 24, SLOTS, PIX><<<grid > 0 ? grid : 1, SLOTS * 24, 0, st>>>(
+        x, wt, bn_a, bn_b, y, n, h, w, act);
     return cudaGetLastError();
   }
   if (c == 24 && m == 1) {
