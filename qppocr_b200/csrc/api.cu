@@ -320,8 +320,9 @@ int qpc_op_dwconv_nhwc(const float* x, int n, int h, int w, int c, const float* 
     g.oh = (h + pads[0] + pads[2] - kh) / g.sh + 1;
     g.ow = (w + pads[1] + pads[3] - kw) / g.sw + 1;
     if (g.oh <= 0 || g.ow <= 0) throw GraphError{"dwconv: empty output"};
+    unsigned int* err = device_state(current_device()).err_word;
     QPC_CUDA_OR_THROW(launch_dwconv_nhwc(x, w_tap_major, bias, residual, y, g, act_from(act, act_p),
-                                         (cudaStream_t)stream));
+                                         (cudaStream_t)stream, err));
     return (int)OK;
   });
 }

@@ -875,10 +875,16 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// fp32 tensor map, 128-byte swizzle, zero fill out of bounds.
-// dims / box innermost first; strides in bytes for dims 1..rank-1.
 bool make_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
               const uint64_t* strides, const uint32_t* box) {
+  return make_tensor_map(map, base, rank, dims, strides, box, true);
+}
+
+}  // namespace
+
+// fp32 tensor map, zero fill out of bounds.
+bool make_tensor_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides, const uint32_t* box, bool swizzle128) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t gd[5], gs[4];
@@ -890,10 +896,13 @@ bool make_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims
   }
   for (int i = 0; i < rank - 1; ++i) gs[i] = strides[i];
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<void*>(base),
-                  gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
+
+namespace {
 
 int sm_count() {
   static int n = 0;

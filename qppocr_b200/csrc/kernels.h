@@ -20,13 +20,22 @@ struct ConvGeom {
   int ph, pw;            // begin pads (end pads are implied by oh/ow)
 };
 
+// Tiled fp32 tensor map through the driver's cuTensorMapEncodeTiled (looked
+// up once via the runtime).  dims / box innermost first, strides in bytes for
+// dims 1..rank-1; out-of-bounds elements load as zero.  swizzle128: 128-byte
+// swizzle (tensor-core operands) instead of the plain row layout.
+bool make_tensor_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides, const uint32_t* box, bool swizzle128);
+
 // Depthwise conv (group == C, one filter per channel), NHWC in/out.
 // wt is tap-major [kh*kw][C].  out = act(sum_taps + bias) (+ residual).
 // Restates conv.rs:45-71 (fma from 0, ky outer / kx inner, bias after) with
 // the fused activation and residual of conv.rs:673-713.
+// `err`: device error word for the tiled kernel's bounded waits (null: the
+// untiled kernel, which has no waits).
 cudaError_t launch_dwconv_nhwc(const float* x, const float* wt, const float* bias,
                                const float* residual, float* y, const ConvGeom& g,
-                               const ActParams& act, cudaStream_t st);
+                               const ActParams& act, cudaStream_t st, unsigned int* err = nullptr);
 
 // GEMM epilogue: out[r, col] = act(acc + bias[col]) + residual[r', col]
 // where r' = r, or, for a nearest-upsample residual (FPN top-down add fused

@@ -505,7 +505,7 @@ void Session::fuse() {
   // epilogue's nearest-source row remap (resize.rs:43-50), so the upsampled
   // map is never written (DBFPN: out_k = in_k + up(out_{k+1})).
   for (size_t i = 0; i < N.size(); ++i) {
-    if (!alive[i] || N[i].op != "Conv" || !N[i].geti("qpc_has_res", 0) || !N[i].has_in(3)) continue;
+    if (!alive[i] || N[i].op != "Conv" || !N[i].has_in(3)) continue;  // in[3]: residual
     const std::string r = N[i].in[3];
     if (gouts.count(r)) continue;
     auto rc = consumers(r);
@@ -1154,7 +1154,7 @@ class Planner {
       const float* wt = S.dweight(n.in[1], "dw");
       const double bytes = 4.0 * N * H * W * C + out_bytes + (has_res ? out_bytes : 0);
       step("dwconv", nm, bytes, flops,
-           [=](cudaStream_t s) { return launch_dwconv_nhwc(xp, wt, bias, rp, yp, g, act, s); });
+           [=](cudaStream_t s) { return launch_dwconv_nhwc(xp, wt, bias, rp, yp, g, act, s, err); });
       unref(x);
     } else if (pw1) {
       Val x = as_nhwc(x0, nm);

@@ -34,6 +34,14 @@ def dev(a):
     (1, 9, 9, 8, 7, (1, 1), "sigmoid", False),
     (1, 1, 1, 4, 3, (1, 1), None, False),
     (1, 10, 10, 6, 3, (1, 1), "swish", True),   # C % 4 != 0 -> generic kernel
+    # TMA-tiled kernel (C % 16 == 0): several channel chunks, partial tiles,
+    # 16- and 32-channel chunks, both strides, both kernel sizes
+    (2, 70, 45, 96, 5, (1, 1), "hswish", True),
+    (1, 64, 100, 48, 3, (1, 1), "relu", False),
+    (2, 37, 29, 32, 3, (2, 2), "hswish", False),
+    (1, 23, 50, 64, 5, (2, 2), None, True),
+    (3, 8, 33, 16, 5, (1, 1), "sigmoid", False),
+    (1, 3, 2, 32, 3, (1, 1), "hswish", True),
 ])
 def test_dwconv_bit_exact(cuda_ctx, n, h, w, c, k, s, act, res):
     import torch
