@@ -156,7 +156,20 @@ def barrier(world):
         dist.barrier()
 
 
-def roofline(profile, hbm, tf):
+# DRAM bytes (read + write) per launch of each kernel family, per image (det)
+# or per line (rec), measured by ncu on the full-size bench workload (det
+# batch 64, rec batch 256; profiles/det_b64_launch_list.md).  The roofline's
+# `traffic` is this times the batch, for the dominant family.
+DET_TRAFFIC_PER_IMAGE = {"gemm_tc": 10497110, "conv_tc": 12623699, "dwconv": 15400158,
+                         "convt2x2": 26141910, "conv_direct": 25001176, "resize": 5674939,
+                         "binary": 2067942, "gap": 1383408}
+REC_TRAFFIC_PER_LINE = {"gemm_tc": 116109, "dwconv": 277567, "head_gemm": 54866, "bmm_small": 58286,
+                        "layernorm": 19268, "softmax": 57083, "conv_direct": 212710, "pool2d": 232163,
+                        "head_combine": 94134, "binary": 23152, "copy": 19274}
+TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, profiles/det_b64_launch_list.md, scaled by batch"
+
+
+def roofline(profile, hbm, tf, traffic_per_unit=None, units=1):
     """Dominant kernel family by device time; achieved = algorithmic bytes (or
     flops) per launch / mean launch duration (CUDA events, this process)."""
     fam = {}
@@ -176,8 +189,12 @@ def roofline(profile, hbm, tf):
         ach = by / (ms * 1e-3) / 1e9
         peak, unit, bound = hbm, "GB/s", "hbm"
     shares = {k: round(v[2] / total_ms, 4) for k, v in sorted(fam.items(), key=lambda kv: -kv[1][2])}
+    traffic = None
+    if traffic_per_unit and kern in traffic_per_unit:
+        traffic = int(traffic_per_unit[kern] * units)
     return {"kernel": kern, "bound": bound, "achieved": round(ach, 1), "peak": peak, "unit": unit,
-            "frac": round(ach / peak, 4), "traffic": None, "launches_per_step": n,
+            "frac": round(ach / peak, 4), "traffic": traffic,
+            "traffic_source": TRAFFIC_SOURCE if traffic is not None else None, "launches_per_step": n,
             "bytes_per_launch": by / n, "flops_per_launch": fl / n, "ms_per_launch": ms / n,
             "share_of_step": round(ms / total_ms, 4), "family_shares": shares}
 
@@ -345,7 +362,7 @@ def main():
 
     prof = det.profile({"x": x}, iters=2)
     launches = len(prof)
-    rl = roofline(prof, hbm, tf)
+    rl = roofline(prof, hbm, tf, DET_TRAFFIC_PER_IMAGE, B)
     rl["peak_source"] = peak_src
 
     # e2e through the public API: host inputs, H2D + compute + D2H every step
@@ -370,7 +387,7 @@ def main():
         re2e = max_over_ranks(e2e_seconds(rs, {"x": xr}, args.steps, world), world)
         rec = {"metric": "rec_lines_per_s", "value": round(world * args.rec_batch / (rms / 1000.0), 1),
                "unit": "lines/s", "ms_per_step": round(rms, 3), "batch": args.rec_batch,
-               "roofline": roofline(rprof, hbm, tf),
+               "roofline": roofline(rprof, hbm, tf, REC_TRAFFIC_PER_LINE, args.rec_batch),
                "e2e": {"value": round(world * args.rec_batch / re2e, 1), "unit": "lines/s",
                        "h2d_bytes_per_step": int(xr.nbytes),
                        "d2h_bytes_per_step": int(args.rec_batch * 40 * 2 * 4), "timing": E2E_TIMING},
