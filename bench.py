@@ -131,20 +131,15 @@ def dist_init():
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device("cuda", local))
     return world, rank, local
 
 
 def max_over_ranks(x, world):
-    if world == 1:
-        return x
-    import torch
-    import torch.distributed as dist
+    from qppocr_b200.shard import max_over_ranks as mor
 
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return mor(x, world, "cuda")
 
 
 def barrier(world):
@@ -320,10 +315,13 @@ def main():
     ap.add_argument("--no-rec", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    world, rank, local = dist_init()
     if args.impl == "reference":
-        run_reference(args, world, rank)
+        # CPU only: rank 0 times the reference path, other ranks exit at once
+        # (no process group: the reference arm has no collective)
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        run_reference(args, world, int(os.environ.get("RANK", "0")))
         return
+    world, rank, local = dist_init()
 
     import numpy as np
     import torch
@@ -339,6 +337,11 @@ def main():
     g, w = nets.build_det()
     g = q.optimize(g, w)
     B = args.batch
+    # this rank's contiguous share of the global batch (units are independent)
+    from qppocr_b200.shard import shard_bounds
+
+    img0, img1 = shard_bounds(world * B, world, rank)
+    assert img1 - img0 == B
     x = nets.det_input(B, DET_HW, DET_HW, seed=3 + rank)
     det = ctx.create_session(g, w, role="det", math=args.math)
     det.run({"x": x})                       # plan build + graph capture
