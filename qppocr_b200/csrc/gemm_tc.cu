@@ -35,6 +35,7 @@
 //   [1][TH][TW][32ch] of the NHWC input shifted by the tap offset; rows and
 //   columns outside the image are zero-filled by TMA, which is exactly the
 //   conv's zero padding.  k order is tap-major then channel.
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -163,13 +164,14 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
   for (int cc = 0; cc < BN; cc += 32) {
     if (n0 + cc >= args.N) break;
     float* sb = reinterpret_cast<float*>(stage + (chunk_ctr & 1u) * OUT_STAGE_BYTES);
-    if (t == 0) bulk_wait_group_read<1>();
-    named_bar_sync(bar_id, 128);
+    // Everything that does not touch the staging buffer first (TMEM fetch,
+    // residual loads, bias, activation), so it overlaps the wait for the
+    // store issued from this buffer two chunks ago.
     float v[32];
+    fetch(cc, v);
+    float4 rv[8];
     if (e.residual) {
-      // all 8 loads of this thread in flight at once, then into the swizzled
-      // staging buffer (while the TMEM fetch below is outstanding)
-      float4 rv[8];
+      if (cc == 0) named_bar_sync(bar_id, 128);  // s_rrow of this tile published
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int i = t + k * 128;
@@ -179,16 +181,6 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
         rv[k] = (rr >= 0 && col < args.N) ? __ldg(reinterpret_cast<const float4*>(e.residual + rr * e.ldr + col))
                                           : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int i = t + k * 128;
-        const int row = i >> 3, c4 = i & 7;
-        *reinterpret_cast<float4*>(sb + row * 32 + ((c4 ^ (row & 7)) << 2)) = rv[k];
-      }
-      fetch(cc, v);
-      named_bar_sync(bar_id, 128);
-    } else {
-      fetch(cc, v);
     }
     if (e.bias) {
       // columns past N are clipped by the TMA store; keep their reads in bounds
@@ -205,17 +197,28 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
       }
     }
     apply_act_n(v, e.act);
+    if (t == 0) bulk_wait_group_read<1>();
+    named_bar_sync(bar_id, 128);  // staging buffer free
+    if (e.residual) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = t + k * 128;
+        const int row = i >> 3, c4 = i & 7;
+        *reinterpret_cast<float4*>(sb + row * 32 + ((c4 ^ (row & 7)) << 2)) = rv[k];
+      }
+      named_bar_sync(bar_id, 128);
+    }
     float* myrow = sb + r * 32;
 #pragma unroll
     for (int c4 = 0; c4 < 8; ++c4) {
       float4* slot = reinterpret_cast<float4*>(myrow + ((c4 ^ (r & 7)) << 2));
       float4 o = make_float4(v[c4 * 4], v[c4 * 4 + 1], v[c4 * 4 + 2], v[c4 * 4 + 3]);
       if (e.residual) {
-        const float4 rv = *slot;
-        o.x = __fadd_rn(o.x, rv.x);
-        o.y = __fadd_rn(o.y, rv.y);
-        o.z = __fadd_rn(o.z, rv.z);
-        o.w = __fadd_rn(o.w, rv.w);
+        const float4 rv4 = *slot;
+        o.x = __fadd_rn(o.x, rv4.x);
+        o.y = __fadd_rn(o.y, rv4.y);
+        o.z = __fadd_rn(o.z, rv4.z);
+        o.w = __fadd_rn(o.w, rv4.w);
       }
       *slot = o;
     }
@@ -856,6 +859,225 @@ __global__ void __launch_bounds__(256, 1)
   if (warp == 0) tmem_dealloc(tmem_d, TMEM_COLS);
 }
 
+// Tap-folded row-band implicit GEMM for k x k stride-1 convs with M <= 32
+// output channels (TF32).  A 128 x N x 8 TF32 MMA costs the same for N = 32
+// as for N = 128, so the kw taps of one kernel row go into N: B rows are
+// (kx, m) pairs (NF = kw*M rounded up to 16) and one MMA over an unshifted
+// 128-pixel input row j produces, for every input pixel p, all kw tap
+// products P[p][kx][m] of kernel row ky = j - i for output row i.  Output
+// pixel t of the tile is sum_kx P[t + kx][kx][m]: the epilogue takes slice
+// kx = 0 from its own TMEM lane and slices kx >= 1 from lanes t + kx through
+// shared memory, so a tile row yields TWO = 128 - (kw - 1) outputs.  Per
+// output row: kh * cblocks * 4 MMAs instead of kh * kw * cblocks * 4.
+// Accumulator i of a tile sums ky and channels on the tensor core; the kx
+// slices are added in fp32 (slice 0, then 1, then 2) in the epilogue.
+// The filter stays in shared memory ([kh][cblocks] tiles of NF rows).
+// Warps: w0 TMA, w1 MMA, w2-3 tf32 rounding of A, w4-7 epilogue.
+template <int STAGES>
+__global__ void __launch_bounds__(256, 1)
+    conv_fold_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmOut, const GemmArgs args, int w_bytes, int nf,
+                     int rb) {
+  constexpr int MAXNF = 96;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t conv_bar[STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t w_full;
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ int64_t s_rrow[BM];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total_tiles = args.m_tiles;
+  const int kw = args.kw, kh = args.taps / args.kw, cblocks = args.cblocks, M = args.N;
+  const int nkb = (rb + kh - 1) * cblocks;
+  const int xst = (kw - 1) * M + 1;                       // exchange row stride (odd)
+  uint8_t* wsm = smem;                                    // [kh][cblocks] x NF x 128 B
+  uint8_t* ring = smem + w_bytes;                         // STAGES x 16 KB
+  float* exch = reinterpret_cast<float*>(ring + STAGES * A_TILE_BYTES);  // 128 x xst
+  uint8_t* out_stage = reinterpret_cast<uint8_t*>(exch) +
+                       ((BM * xst * 4 + 1023) / 1024) * 1024;            // 2 x 16 KB
+  const uint32_t tmem_cols = 512;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+      mbar_init(&conv_bar[s], 64);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(&w_full, 1);
+    fence_barrier_init();
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmW);
+    if (args.tma_store) prefetch_tensormap(&tmOut);
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_slot, tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = tmem_base_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: the folded filter once, then input rows
+      mbar_arrive_expect_tx(&w_full, (uint32_t)w_bytes);
+      for (int ky = 0; ky < kh; ++ky)
+        for (int cb = 0; cb < cblocks; ++cb)
+          tma_load_4d(wsm + (ky * cblocks + cb) * nf * 128, &tmW, &w_full, cb * BK, 0, ky, 0);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+        const TileCoord tc = tile_coord(args, tile, 1, 32);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int j = kb / cblocks, cb = kb % cblocks;
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full_bar[s], A_TILE_BYTES);
+          tma_load_4d(ring + s * A_TILE_BYTES, &tmA, &full_bar[s], cb * BK, tc.ox0 - args.pw,
+                      tc.oy0 - args.ph + j, tc.img);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      const uint32_t idesc = idesc_tf32(BM, nf);
+      bool ok = mbar_wait(&w_full, 0, args.err);
+      const uint32_t w_addr = smem_u32(wsm);
+      uint32_t it = 0, acc_i = 0;
+      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++acc_i) {
+        const TileCoord tc = tile_coord(args, tile, 1, 32);
+        const int rows = min(rb, args.oh - tc.oy0);
+        const uint32_t buf = acc_i & 1u;
+        if (acc_i >= 2 && !mbar_wait(&acc_empty[buf], ((acc_i >> 1) - 1) & 1u, args.err)) break;
+        const uint32_t d_base = tmem_d + buf * (uint32_t)(rb * nf);
+        for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
+          const int j = kb / cblocks, cb = kb % cblocks;
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(ring + s * A_TILE_BYTES);
+          for (int ky = 0; ky < kh; ++ky) {
+            const int i = j - ky;  // output row of this tile fed by kernel row ky
+            if (i < 0 || i >= rows) continue;
+            const uint32_t d = d_base + i * nf;
+            const uint32_t b_addr = w_addr + (ky * cblocks + cb) * nf * 128;
+#pragma unroll
+            for (int ks = 0; ks < BK / 8; ++ks) {
+              const uint32_t acc = (ky | cb | ks) ? 1u : 0u;
+              mma_tf32(d, sw128_kmajor_desc(a_addr + ks * 32), sw128_kmajor_desc(b_addr + ks * 32), idesc, acc);
+            }
+          }
+          mma_commit(&empty_bar[s]);
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[buf]);
+      }
+    }
+  } else if (warp < 4) {
+    // ---------------- converters: round the input row to tf32 (nearest) in place
+    const int t = threadIdx.x - 64;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1u;
+        if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
+        float4* a = reinterpret_cast<float4*>(ring + s * A_TILE_BYTES);
+#pragma unroll 4
+        for (int i = t; i < A_TILE_BYTES / 16; i += 64) {
+          const float4 v = a[i];
+          a[i] = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&conv_bar[s]);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 4-7): TMEM lane r = input pixel ox0 - pw + r,
+    // which is also output pixel ox0 + r's kx = 0 slice
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int gt = threadIdx.x - 128;
+    const uint32_t lane_base = tmem_d + ((uint32_t)(q * 32) << 16);
+    const int r1 = min(r + 1, BM - 1), r2 = min(r + 2, BM - 1);  // rows >= TWO are not stored
+    uint32_t acc_i = 0, chunk_ctr = 0;
+    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++acc_i) {
+      const TileCoord tc = tile_coord(args, tile, 1, 32);
+      const int rows = min(rb, args.oh - tc.oy0);
+      const uint32_t buf = acc_i & 1u;
+      if (!mbar_wait(&acc_full[buf], (acc_i >> 1) & 1u, args.err)) break;
+      tc_fence_after();
+      for (int i = 0; i < rows; ++i) {
+        const uint32_t col0 = buf * (uint32_t)(rb * nf) + i * nf;
+        uint32_t raw[MAXNF / 16][16];
+#pragma unroll
+        for (int c = 0; c < MAXNF / 16; ++c)
+          if (c * 16 < nf) tmem_ld16_nowait(lane_base + col0 + c * 16, raw[c]);
+        tmem_ld_wait();
+        float row[MAXNF];
+#pragma unroll
+        for (int c = 0; c < MAXNF; ++c) row[c] = __uint_as_float(raw[c / 16][c % 16]);
+        named_bar_sync(2, 128);  // the previous row's readers are done with `exch`
+#pragma unroll
+        for (int c = 0; c < MAXNF; ++c)
+          if (c >= M && c < kw * M) exch[r * xst + (c - M)] = row[c];
+        named_bar_sync(2, 128);
+        auto fetch = [&](int cc, float (&v)[32]) {
+#pragma unroll
+          for (int m = 0; m < 32; ++m) {
+            float o = 0.f;
+            if (m < M) {
+              o = row[m];
+              if (kw > 1) o = __fadd_rn(o, exch[r1 * xst + m]);
+              if (kw > 2) o = __fadd_rn(o, exch[r2 * xst + M + m]);
+            }
+            v[m] = o;
+          }
+        };
+        if (args.tma_store) {
+          store_tile<32, 1>(args, &tmOut, out_stage, s_rrow, 1, chunk_ctr, 0, 0, tc.img, tc.oy0 + i, tc.ox0,
+                            r, gt, fetch);
+        } else {
+          const RowMap m = row_map<1>(args, 0, tc.img, tc.oy0 + i, tc.ox0, r);
+          float v[32];
+          fetch(0, v);
+          if (m.orow >= 0 && r < args.tw) {
+            float v16[16];
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v16[jj] = v[jj];
+            epilogue_store<32>(args, v16, m.orow, m.rrow, 0);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v16[jj] = v[16 + jj];
+            if (M > 16) epilogue_store<32>(args, v16, m.orow, m.rrow, 16);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  if (args.tma_store && threadIdx.x == 128) bulk_wait_group<0>();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_d, tmem_cols);
+}
+
 // ----------------------------------------------------------- host helpers
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -992,6 +1214,18 @@ cudaError_t run_band(const CUtensorMap& a, const CUtensorMap& w, const CUtensorM
   return cudaGetLastError();
 }
 
+// Tap-folded conv: shared-memory layout and limits.
+constexpr int FOLD_STAGES = 4;
+int fold_nf(const ConvGeom& g) { return ((g.kw * g.m + 15) / 16) * 16; }
+int fold_smem(const ConvGeom& g, int* w_bytes_out) {
+  const int cblocks = (g.c + BK - 1) / BK;
+  const int w_bytes = g.kh * cblocks * fold_nf(g) * 128;
+  const int xst = (g.kw - 1) * g.m + 1;
+  const int exch = ((BM * xst * 4 + 1023) / 1024) * 1024;
+  if (w_bytes_out) *w_bytes_out = w_bytes;
+  return w_bytes + FOLD_STAGES * A_TILE_BYTES + exch + 2 * OUT_STAGE_BYTES + 1024;
+}
+
 // Output tile width: the smallest N tile that covers N with the least padding
 // (3xTF32 keeps its promoted accumulator in registers: at most 128 columns).
 int pick_bn(int n, bool split) {
@@ -1004,6 +1238,11 @@ int pick_bn(int n, bool split) {
 }
 
 }  // namespace
+
+bool conv_fold_ok(const ConvGeom& g) {
+  return g.sh == 1 && g.sw == 1 && (g.c % 4) == 0 && g.kw <= 3 && g.kh <= 7 && g.m <= 32 &&
+         g.ow >= 48 && fold_smem(g, nullptr) <= 224 * 1024;
+}
 
 int gemm_tc_col_tiles(int N, int math) {
   const int bn = pick_bn(N, math == MATH_3XTF32);
@@ -1090,10 +1329,70 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
 
 cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, const float* wk_lo,
                            const GemmEpilogue& epi, int math, unsigned int* err,
-                           cudaStream_t st) {
+                           cudaStream_t st, const float* wk_fold) {
   if (g.sh != 1 || g.sw != 1 || (g.c & 3)) return cudaErrorInvalidValue;
   const bool split = math == MATH_3XTF32;
   if (split && !wk_lo) return cudaErrorInvalidValue;
+  if (!split && wk_fold && conv_fold_ok(g)) {
+    // Tap-folded kernel: TWO = 128 - (kw - 1) output pixels per tile row.
+    const int nf = fold_nf(g);
+    const int two = BM - (g.kw - 1);
+    const int rb = std::min(4, 256 / nf);
+    int w_bytes = 0;
+    const int smem = fold_smem(g, &w_bytes);
+    CUtensorMap ma, mw, mo;
+    {
+      const uint64_t dims[4] = {(uint64_t)g.c, (uint64_t)g.w, (uint64_t)g.h, (uint64_t)g.n};
+      const uint64_t strides[3] = {(uint64_t)g.c * 4, (uint64_t)g.c * g.w * 4,
+                                   (uint64_t)g.c * g.w * g.h * 4};
+      const uint32_t box[4] = {BK, BM, 1, 1};
+      if (!make_map(&ma, x, 4, dims, strides, box)) return cudaErrorInvalidValue;
+    }
+    {
+      const uint64_t dims[4] = {(uint64_t)g.c, (uint64_t)nf, (uint64_t)g.kh, 1};
+      const uint64_t strides[3] = {(uint64_t)g.c * 4, (uint64_t)g.c * nf * 4, (uint64_t)g.c * nf * g.kh * 4};
+      const uint32_t box[4] = {BK, (uint32_t)nf, 1, 1};
+      if (!make_map(&mw, wk_fold, 4, dims, strides, box)) return cudaErrorInvalidValue;
+    }
+    GemmArgs args{};
+    args.N = g.m;
+    args.K = g.c * g.kh * g.kw;
+    args.M = g.n * g.oh * g.ow;
+    args.cblocks = (g.c + BK - 1) / BK;
+    args.taps = g.kh * g.kw;
+    args.kw = g.kw;
+    args.ph = g.ph;
+    args.pw = g.pw;
+    args.oh = g.oh;
+    args.ow = g.ow;
+    args.tw = two;
+    args.th = rb;
+    args.tiles_x = (g.ow + two - 1) / two;
+    args.tiles_y = (g.oh + rb - 1) / rb;
+    args.m_tiles = g.n * args.tiles_x * args.tiles_y;
+    args.epi = epi;
+    args.err = err;
+    mo = ma;
+    const float* obase = epi.out + epi.col_off;
+    if ((g.m % 4) == 0 && (epi.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(obase) & 15) == 0 &&
+        (!epi.residual || (epi.ldr % 4) == 0)) {
+      const uint64_t dims[4] = {(uint64_t)g.m, (uint64_t)g.ow, (uint64_t)g.oh, (uint64_t)g.n};
+      const uint64_t strides[3] = {(uint64_t)epi.ldo * 4, (uint64_t)epi.ldo * g.ow * 4,
+                                   (uint64_t)epi.ldo * g.ow * g.oh * 4};
+      const uint32_t box[4] = {32, (uint32_t)two, 1, 1};
+      args.tma_store = make_map(&mo, obase, 4, dims, strides, box) ? 1 : 0;
+    }
+    auto kern = conv_fold_kernel<FOLD_STAGES>;
+    static int attr_set = 0;
+    if (smem > attr_set) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return e;
+      attr_set = smem;
+    }
+    const int grid = args.m_tiles < sm_count() ? args.m_tiles : sm_count();
+    kern<<<grid, 256, smem, st>>>(ma, mw, mo, args, w_bytes, nf, rb);
+    return cudaGetLastError();
+  }
   // Row-band mode: TF32, rows at least 64 wide, kernels at most MAX_KW_HALO
   // wide, one column tile, and a filter that fits in shared memory.
   {

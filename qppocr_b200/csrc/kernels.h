@@ -83,9 +83,15 @@ cudaError_t launch_argmax_combine(const float4* partials, int n_tiles, int64_t M
 // boxes of the NHWC input shifted per tap (out-of-bounds rows/cols read as
 // the zero padding).  wk is tap-major [kh*kw][M][C] (and wk_lo its 3xTF32
 // residue).  Epilogue as launch_gemm_tc with out rows = output pixels.
+// wk_fold (optional, TF32 only): the kx-folded filter [kh][roundup16(kw*M)][C]
+// (tf32-rounded) for the tap-folded kernel, used when conv_fold_ok(g).
 cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, const float* wk_lo,
                            const GemmEpilogue& epi, int math, unsigned int* err,
-                           cudaStream_t st);
+                           cudaStream_t st, const float* wk_fold = nullptr);
+
+// Whether the tap-folded TF32 kernel takes this conv (kw <= 3, M <= 32,
+// output rows >= 48 wide, stride 1, filter within the shared-memory budget).
+bool conv_fold_ok(const ConvGeom& g);
 
 // Direct (SIMT) dense conv for shapes the tensor-core path does not take
 // (C % 4 != 0 stems, strided kxk).  Input is NCHW when x_nchw != 0 (graph

@@ -249,6 +249,7 @@ qpc_caps Session::caps() const {
 //   raw        as given
 //   dw         depthwise [C,1,kh,kw] -> tap-major [kh*kw][C]
 //   kxk        dense [M,C,kh,kw] -> tap-major [kh*kw][M][C]
+//   kxf        dense [M,C,kh,kw] -> kx-folded [kh][roundup16(kw*M)][C]
 //   nk         MatMul B [K,N] -> [N,K]
 //   X.rn       variant X rounded to tf32, nearest (TF32-mode B operand)
 //   X.hi/X.lo  3xTF32 split of variant X: hi = rn(v), lo = rn(v - hi)
@@ -299,6 +300,17 @@ const float* Session::dweight(const std::string& name, const std::string& varian
     for (int64_t mo = 0; mo < m; ++mo)
       for (int64_t ch = 0; ch < c; ++ch)
         for (int64_t t = 0; t < taps; ++t) v[(t * m + mo) * c + ch] = src[(mo * c + ch) * taps + t];
+  } else if (base_variant == "kxf") {
+    // kx-folded rows of one kernel row: [kh][NF][C], row kx*M + m of kernel
+    // row ky = W[m][c][ky][kx]; NF = kw*M rounded up to 16, zero rows after.
+    const int64_t m = h->shape[0], c = h->shape[1], kh = h->shape[2], kw = h->shape[3];
+    const int64_t nf = ((kw * m + 15) / 16) * 16;
+    v.assign(kh * nf * c, 0.f);
+    for (int64_t ky = 0; ky < kh; ++ky)
+      for (int64_t kx = 0; kx < kw; ++kx)
+        for (int64_t mo = 0; mo < m; ++mo)
+          for (int64_t ch = 0; ch < c; ++ch)
+            v[(ky * nf + kx * m + mo) * c + ch] = src[((mo * c + ch) * kh + ky) * kw + kx];
   } else if (base_variant == "nk") {
     const int64_t k = h->shape[0], n = h->shape[1];
     v.resize(k * n);
@@ -1187,6 +1199,7 @@ class Planner {
       const bool split = math == QPC_MATH_3XTF32;
       const float* wb = S.dweight(n.in[1], split ? "kxk.hi" : "kxk.rn");
       const float* wl = split ? S.dweight(n.in[1], "kxk.lo") : nullptr;
+      const float* wf = (!split && conv_fold_ok(g)) ? S.dweight(n.in[1], "kxf.rn") : nullptr;
       GemmEpilogue e;
       e.bias = bias;
       e.residual = rp;
@@ -1202,7 +1215,7 @@ class Planner {
       }
       const double bytes = 4.0 * N * H * W * C + out_bytes + 4.0 * M * C * kh * kw + res_bytes;
       step("conv_tc", nm, bytes, flops,
-           [=](cudaStream_t s) { return launch_conv_tc(xp, g, wb, wl, e, math, err, s); });
+           [=](cudaStream_t s) { return launch_conv_tc(xp, g, wb, wl, e, math, err, s, wf); });
       unref(x);
     } else {
       const bool nchw_in = is_rowmajor(x0) && !x0.is_const && (x0.off % 4) == 0;
