@@ -98,7 +98,13 @@ typedef struct {
   int n_outputs;
 } qpc_graph;
 
-enum qpc_dtype { QPC_F32 = 0, QPC_I64 = 1 }; /* tensor.rs:10-18 DType */
+/* tensor.rs:10-18 DType.  QPC_U8_IMAGE (run inputs only; no counterpart in
+ * the reference's DType) is a batch of n x h x w x 3 uint8 RGB images given
+ * for an f32 graph input of shape [n, 3, h, w]: the session normalises it on
+ * the device exactly as the reference engine prepares the det input,
+ * v = u8 * (1/255), (v - 0.5) * (1/0.5), HWC -> CHW (engine.rs:963-982), so
+ * a run moves a quarter of the bytes across the host and PCIe. */
+enum qpc_dtype { QPC_F32 = 0, QPC_I64 = 1, QPC_U8_IMAGE = 2 };
 
 /* A host tensor (tensor.rs:28-40): initializers and run inputs. */
 typedef struct {
@@ -263,6 +269,32 @@ int qpc_op_ctc_head_noalloc(const float* x, int64_t rows, int k, const float* w,
  * (round to nearest, ties away): the load-time weight preparation of both
  * math modes. */
 int qpc_op_split_tf32(const float* v, int64_t count, float* hi, float* lo, void* stream);
+
+/* ------------------------------------------------ det / rec pre and post
+ * Device versions of the host code on either side of the networks, bit-exact
+ * with it.  Device pointers; images are n x h x w x 3 uint8 (HWC, as the
+ * reference's `Image`), masks n x h x w uint8. */
+
+/* resize_bilinear_img / resize_bilinear_rgb_u8 (crates/qppocr-core/src/
+ * pipeline/image.rs:50-117, crates/qppocr-kernels/src/resize.rs:158-210): the
+ * det input resize and the rec line resize, n images sh x sw -> dh x dw. */
+int qpc_op_resize_bilinear_rgb_u8(const uint8_t* src, int n, int sh, int sw, uint8_t* dst, int dh, int dw,
+                                  void* stream);
+
+/* Det input preparation (crates/qppocr-core/src/pipeline/engine.rs:930-982):
+ * resize to dh x dw (skipped when the sizes are equal, as there), then
+ * v = u8 * (1/255), (v - 0.5) * (1/0.5) into planar n x 3 x dh x dw f32 -
+ * the det session's input tensor. */
+int qpc_op_det_preprocess(const uint8_t* src, int n, int sh, int sw, float* dst, int dh, int dw, void* stream);
+
+/* DB post-processing mask (crates/qppocr-core/src/pipeline/geometry.rs:
+ * 286-296 with qppocr-kernels resize.rs:213-245 dilate2x2_max): mask =
+ * pred > thresh, then, when `dilate`, the 2x2 dilation (window [y-1, y] x
+ * [x-1, x], out-of-bounds samples ignored).  pred: n x h x w probabilities;
+ * the mask feeds the host's connected components.  With pred == NULL,
+ * mask_in (uint8) is dilated instead. */
+int qpc_op_db_mask(const float* pred, const uint8_t* mask_in, uint8_t* mask, int n, int h, int w, float thresh,
+                   int dilate, void* stream);
 
 /* Device fault / timeout flag raised by kernels with bounded waits on the
  * current device since the last call (0 = none); clears it. */

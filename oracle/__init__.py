@@ -330,6 +330,75 @@ def argmax_pairs(p):
     return out
 
 
+# ------------------------------------------------------ det / rec pre and post
+U8P = ctypes.POINTER(ctypes.c_uint8)
+
+
+def _u8(a):
+    return a.ctypes.data_as(U8P)
+
+
+def resize_bilinear_rgb_u8(src, dh, dw):
+    """resize.rs:158-210 on [n, sh, sw, 3] uint8 -> [n, dh, dw, 3] uint8."""
+    src = np.ascontiguousarray(src, np.uint8)
+    n, sh, sw, _ = src.shape
+    out = np.empty((n, dh, dw, 3), np.uint8)
+    lib().orc_resize_bilinear_rgb_u8(_u8(src), ctypes.c_int64(n), ctypes.c_int64(sh), ctypes.c_int64(sw),
+                                     _u8(out), ctypes.c_int64(dh), ctypes.c_int64(dw))
+    return out
+
+
+def det_normalize(img):
+    """engine.rs:963-982 on [n, h, w, 3] uint8 -> [n, 3, h, w] float32."""
+    img = np.ascontiguousarray(img, np.uint8)
+    n, h, w, _ = img.shape
+    out = np.empty((n, 3, h, w), np.float32)
+    lib().orc_det_normalize(_u8(img), ctypes.c_int64(n), ctypes.c_int64(h), ctypes.c_int64(w), _f(out))
+    return out
+
+
+def dilate2x2(mask):
+    """resize.rs:213-245 on [n, h, w] uint8."""
+    mask = np.ascontiguousarray(mask, np.uint8)
+    n, h, w = mask.shape
+    out = np.empty_like(mask)
+    lib().orc_dilate2x2(_u8(mask), ctypes.c_int64(n), ctypes.c_int64(h), ctypes.c_int64(w), _u8(out))
+    return out
+
+
+def db_mask(pred, thresh, dilate=True):
+    """geometry.rs:286-296: (pred > thresh), then the 2x2 dilation; [n, h, w]."""
+    pred = _c(pred)
+    n, h, w = pred.shape
+    out = np.empty((n, h, w), np.uint8)
+    lib().orc_db_mask(_f(pred), ctypes.c_int64(n), ctypes.c_int64(h), ctypes.c_int64(w),
+                      ctypes.c_float(thresh), ctypes.c_int(1 if dilate else 0), _u8(out))
+    return out
+
+
+def ctc_decode(probs, charset=None):
+    """rec.rs:34-79 greedy CTC over one line's [T, C] probabilities: per step
+    the first strict maximum; emit when best != 0 and best != previous; conf =
+    f64 mean of the emitted steps' values.  Returns (indices, conf); with a
+    charset, indices past it are not emitted as text (but count for conf)."""
+    probs = np.asarray(probs, np.float32)
+    out, conf_sum, conf_n, prev = [], 0.0, 0, -1
+    for t in range(probs.shape[0]):
+        row = probs[t]
+        best, bv = 0, row[0]
+        for c in range(1, row.shape[0]):
+            if row[c] > bv:
+                best, bv = c, row[c]
+        if best != 0 and best != prev:
+            if charset is None or best < len(charset):
+                out.append(best)
+            conf_sum += float(bv)
+            conf_n += 1
+        prev = best
+    conf = np.float32(conf_sum / conf_n) if conf_n else np.float32(0.0)
+    return out, conf
+
+
 # ------------------------------------------------------------------ executor
 def _resolve_pads(node, h, w, kh, kw, sh, sw):
     ap = node.attrs.get("auto_pad", "NOTSET")

@@ -832,4 +832,95 @@ void orc_transpose(const float* x, const int64_t* shape, const int32_t* perm, in
   }, 4096);
 }
 
+// ------------------------------------------------ det / rec pre and post
+// qppocr-kernels resize.rs:158-210 resize_bilinear_rgb_u8 (and its scalar
+// reference, tests/rsz_par.rs:5-36): half-pixel source coordinates clamped at
+// 0, first term two multiplies, the other three fused multiply-adds, then
+// (val + 0.5) clamped to [0, 255] and truncated.  n images of sh x sw x 3.
+void orc_resize_bilinear_rgb_u8(const uint8_t* src, int64_t n, int64_t sh, int64_t sw, uint8_t* dst,
+                                int64_t dh, int64_t dw) {
+  const float sx = (float)sw / (float)dw, sy = (float)sh / (float)dh;
+  std::vector<int64_t> x0(dw), x1(dw);
+  std::vector<float> fx(dw);
+  for (int64_t x = 0; x < dw; ++x) {
+    const float v = std::max(((float)x + 0.5f) * sx - 0.5f, 0.0f);
+    const int64_t i0 = std::min((int64_t)v, sw - 1);
+    x0[x] = i0;
+    x1[x] = std::min(i0 + 1, sw - 1);
+    fx[x] = v - (float)i0;
+  }
+  parallel_for(n * dh, [&](int64_t b, int64_t e) {
+    for (int64_t ry = b; ry < e; ++ry) {
+      const int64_t img = ry / dh, y = ry % dh;
+      const float v = std::max(((float)y + 0.5f) * sy - 0.5f, 0.0f);
+      const int64_t j0 = std::min((int64_t)v, sh - 1), j1 = std::min(j0 + 1, sh - 1);
+      const float fy = v - (float)j0;
+      const uint8_t* r0 = src + (img * sh + j0) * sw * 3;
+      const uint8_t* r1 = src + (img * sh + j1) * sw * 3;
+      uint8_t* out = dst + (img * dh + y) * dw * 3;
+      for (int64_t x = 0; x < dw; ++x) {
+        const int64_t a = x0[x] * 3, bb = x1[x] * 3;
+        const float lx = fx[x];
+        for (int ch = 0; ch < 3; ++ch) {
+          const float p00 = r0[a + ch], p01 = r0[bb + ch], p10 = r1[a + ch], p11 = r1[bb + ch];
+          float t = p00 * (1.0f - lx) * (1.0f - fy);
+          t = std::fma(p01 * lx, 1.0f - fy, t);
+          t = std::fma(p10 * (1.0f - lx), fy, t);
+          const float val = std::fma(p11 * lx, fy, t);
+          out[x * 3 + ch] = (uint8_t)std::min(std::max(val + 0.5f, 0.0f), 255.0f);
+        }
+      }
+    }
+  }, 16);
+}
+
+// engine.rs:963-982 det input: v = u8 * (1/255), (v - 0.5) * (1/0.5), HWC ->
+// planar CHW.  n images of h x w x 3.
+void orc_det_normalize(const uint8_t* src, int64_t n, int64_t h, int64_t w, float* dst) {
+  const float scale = 1.0f / 255.0f, mean = 0.5f, istd = 1.0f / 0.5f;
+  parallel_for(n * 3 * h, [&](int64_t b, int64_t e) {
+    for (int64_t r = b; r < e; ++r) {
+      const int64_t img = r / (3 * h), c = (r / h) % 3, y = r % h;
+      const uint8_t* row = src + (img * h + y) * w * 3;
+      float* d = dst + ((img * 3 + c) * h + y) * w;
+      for (int64_t x = 0; x < w; ++x) {
+        const float v = (float)row[x * 3 + c] * scale;
+        d[x] = (v - mean) * istd;
+      }
+    }
+  }, 64);
+}
+
+// resize.rs:213-245 dilate2x2_max (cv2.dilate 2x2, anchor (1,1)): out[y][x] =
+// max of the in-bounds samples of [y-1, y] x [x-1, x].  n masks of h x w.
+void orc_dilate2x2(const uint8_t* m, int64_t n, int64_t h, int64_t w, uint8_t* out) {
+  parallel_for(n * h, [&](int64_t b, int64_t e) {
+    for (int64_t r = b; r < e; ++r) {
+      const int64_t img = r / h, y = r % h;
+      const uint8_t* cur = m + (img * h + y) * w;
+      const uint8_t* up = y > 0 ? cur - w : nullptr;
+      uint8_t* o = out + (img * h + y) * w;
+      for (int64_t x = 0; x < w; ++x) {
+        uint8_t v = cur[x];
+        if (x > 0) v = std::max(v, cur[x - 1]);
+        if (up) {
+          v = std::max(v, up[x]);
+          if (x > 0) v = std::max(v, up[x - 1]);
+        }
+        o[x] = v;
+      }
+    }
+  }, 64);
+}
+
+// geometry.rs:286-296 db_postprocess binarize (pred > thresh -> 1), then the
+// 2x2 dilation when use_dilation.
+void orc_db_mask(const float* pred, int64_t n, int64_t h, int64_t w, float thresh, int dilate,
+                 uint8_t* out) {
+  std::vector<uint8_t> m((size_t)(n * h * w));
+  for (int64_t i = 0; i < n * h * w; ++i) m[i] = pred[i] > thresh ? 1 : 0;
+  if (dilate) orc_dilate2x2(m.data(), n, h, w, out);
+  else std::memcpy(out, m.data(), m.size());
+}
+
 }  // extern "C"

@@ -95,7 +95,7 @@ EXPORTED = (
     "qpc_ticket_output", "qpc_ticket_output_copy", "qpc_ticket_release", "qpc_run", "qpc_ticket_device_ms",
     "qpc_session_destroy", "qpc_session_profile", "qpc_session_profile_step",
     "qpc_session_replay", "qpc_session_node_count", "qpc_session_node", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_ctc_head", "qpc_op_ctc_head_noalloc",
-    "qpc_op_split_tf32",
+    "qpc_op_split_tf32", "qpc_op_resize_bilinear_rgb_u8", "qpc_op_det_preprocess", "qpc_op_db_mask",
     "qpc_kernel_error",
 )
 
@@ -144,6 +144,10 @@ def lib():
     L.qpc_op_gemm.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P, ctypes.c_int, P,
                               P, P, ctypes.c_int, P]
     L.qpc_op_split_tf32.argtypes = [P, ctypes.c_int64, P, P, P]
+    I = ctypes.c_int
+    L.qpc_op_resize_bilinear_rgb_u8.argtypes = [P, I, I, I, P, I, I, P]
+    L.qpc_op_det_preprocess.argtypes = [P, I, I, I, P, I, I, P]
+    L.qpc_op_db_mask.argtypes = [P, P, P, I, I, I, ctypes.c_float, I, P]
     L.qpc_op_ctc_head.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P, ctypes.c_int,
                                   P, P]
     L.qpc_op_ctc_head_noalloc.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P,
@@ -215,6 +219,11 @@ def _tensor(keep: _Keep, name: str, arr: np.ndarray) -> QpcTensor:
     if arr.dtype == np.int64 or arr.dtype == np.int32:
         arr = keep.add(np.ascontiguousarray(arr, np.int64))
         dt = 1
+    elif arr.dtype == np.uint8:
+        # n x h x w x 3 images for an [n, 3, h, w] f32 input, normalised on
+        # the device (engine.rs:963-982); run inputs only
+        arr = keep.add(np.ascontiguousarray(arr))
+        dt = 2
     else:
         arr = keep.add(np.ascontiguousarray(arr, np.float32))
         dt = 0
@@ -491,6 +500,38 @@ def op_split_tf32(v, stream=None):
     lo = torch.empty_like(v)
     _check(lib().qpc_op_split_tf32(_dptr(v), v.numel(), _dptr(hi), _dptr(lo), stream))
     return hi, lo
+
+
+def op_resize_bilinear_rgb_u8(src, dh: int, dw: int, stream=None):
+    """[n, sh, sw, 3] uint8 device tensor -> [n, dh, dw, 3] (resize.rs:158-210)."""
+    import torch
+    n, sh, sw, _ = src.shape
+    dst = torch.empty((n, dh, dw, 3), dtype=torch.uint8, device=src.device)
+    _check(lib().qpc_op_resize_bilinear_rgb_u8(_dptr(src), n, sh, sw, _dptr(dst), dh, dw, stream))
+    return dst
+
+
+def op_det_preprocess(src, dh: int, dw: int, stream=None):
+    """[n, sh, sw, 3] uint8 device images -> det input [n, 3, dh, dw] f32
+    (engine.rs:930-982)."""
+    import torch
+    n, sh, sw, _ = src.shape
+    dst = torch.empty((n, 3, dh, dw), dtype=torch.float32, device=src.device)
+    _check(lib().qpc_op_det_preprocess(_dptr(src), n, sh, sw, _dptr(dst), dh, dw, stream))
+    return dst
+
+
+def op_db_mask(pred=None, thresh: float = 0.3, dilate: bool = True, mask_in=None, stream=None):
+    """DB mask (geometry.rs:286-296): [n, h, w] probabilities (or an existing
+    uint8 mask to dilate) -> [n, h, w] uint8."""
+    import torch
+    src = pred if pred is not None else mask_in
+    n, h, w = src.shape
+    out = torch.empty((n, h, w), dtype=torch.uint8, device=src.device)
+    _check(lib().qpc_op_db_mask(_dptr(pred) if pred is not None else None,
+                                _dptr(mask_in) if mask_in is not None else None, _dptr(out), n, h, w,
+                                ctypes.c_float(thresh), 1 if dilate else 0, stream))
+    return out
 
 
 def kernel_error(device: int = 0) -> int:

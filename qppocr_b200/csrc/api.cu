@@ -389,6 +389,41 @@ int qpc_op_split_tf32(const float* v, int64_t count, float* hi, float* lo, void*
   });
 }
 
+int qpc_op_resize_bilinear_rgb_u8(const uint8_t* src, int n, int sh, int sw, uint8_t* dst, int dh, int dw,
+                                  void* stream) {
+  if (!src || !dst || n < 0 || sh <= 0 || sw <= 0 || dh <= 0 || dw <= 0) {
+    set_error("invalid argument");
+    return E_INVALID;
+  }
+  return guarded([&] {
+    QPC_CUDA_OR_THROW(launch_resize_bilinear_rgb_u8(src, n, sh, sw, dst, dh, dw, (cudaStream_t)stream));
+    return (int)OK;
+  });
+}
+
+int qpc_op_det_preprocess(const uint8_t* src, int n, int sh, int sw, float* dst, int dh, int dw, void* stream) {
+  if (!src || !dst || n < 0 || sh <= 0 || sw <= 0 || dh <= 0 || dw <= 0) {
+    set_error("invalid argument");
+    return E_INVALID;
+  }
+  return guarded([&] {
+    QPC_CUDA_OR_THROW(launch_det_preprocess(src, n, sh, sw, dst, dh, dw, (cudaStream_t)stream));
+    return (int)OK;
+  });
+}
+
+int qpc_op_db_mask(const float* pred, const uint8_t* mask_in, uint8_t* mask, int n, int h, int w, float thresh,
+                   int dilate, void* stream) {
+  if ((!pred && !mask_in) || !mask || n < 0 || h <= 0 || w <= 0) {
+    set_error("invalid argument");
+    return E_INVALID;
+  }
+  return guarded([&] {
+    QPC_CUDA_OR_THROW(launch_db_mask(pred, mask_in, mask, n, h, w, thresh, dilate, (cudaStream_t)stream));
+    return (int)OK;
+  });
+}
+
 int qpc_kernel_error(int device, unsigned int* flags) {
   if (!flags) return E_INVALID;
   return guarded([&] {

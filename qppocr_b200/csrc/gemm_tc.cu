@@ -302,19 +302,22 @@ __device__ __forceinline__ void argmax_tile(const GemmArgs& args, int64_t orow, 
 }
 
 // Warp roles: w0 TMA producer, w1 MMA issuer, w2-3 convert A, then 4-warp
-// epilogue groups.  TF32 runs two epilogue groups that take alternate tiles
-// (their serial TMEM -> smem -> TMA-store chains overlap); 3xTF32 keeps one
-// group, whose registers hold the promoted accumulator.
-template <bool SPLIT>
+// epilogue groups that take tiles round-robin (their serial TMEM -> smem ->
+// TMA-store chains overlap).  TF32 runs 4 groups for N tiles <= 64 columns,
+// where a tile carries little work and the chain's latency sets the pace, and
+// 2 otherwise; 3xTF32 keeps one group, whose registers hold the promoted
+// accumulator.
+template <int BN, bool SPLIT>
 struct Roles {
-  static constexpr int EPI_GROUPS = SPLIT ? 1 : 2;
+  static constexpr int EPI_GROUPS = SPLIT ? 1 : (BN <= 64 ? 4 : 2);
   static constexpr int THREADS = 128 + 128 * EPI_GROUPS;
 };
-// TMEM accumulators: 4 for N tiles <= 128 columns (the MMA can run up to 3
-// tiles ahead of the epilogue), 2 otherwise; 3xTF32 ping-pongs 2 chunk buffers.
+// TMEM accumulators: 8 for 32-column tiles, 4 up to 128 columns, 2 otherwise
+// (the MMA runs ahead of the epilogue groups by NBUF - groups tiles);
+// 3xTF32 ping-pongs 2 chunk buffers.
 template <int BN, bool SPLIT>
 struct Accs {
-  static constexpr int NBUF = SPLIT ? 2 : (BN <= 128 ? 4 : 2);
+  static constexpr int NBUF = SPLIT ? 2 : (BN <= 32 ? 8 : (BN <= 128 ? 4 : 2));
 };
 constexpr int CH = 1;             // k-blocks per promotion chunk (3xTF32)
 
@@ -342,13 +345,13 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& a, int tile, int
 // the MMAs run ahead across tile boundaries while the epilogue warps drain the
 // previous tile from the other TMEM accumulator.
 template <int BN, int STAGES, bool SPLIT, int A_MODE>
-__global__ void __launch_bounds__(Roles<SPLIT>::THREADS, 1)
+__global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmOut,
                    const GemmArgs args) {
   using SM = Smem<BN, SPLIT, A_MODE>;
   constexpr int NBUF = Accs<BN, SPLIT>::NBUF;
-  constexpr int NGRP = Roles<SPLIT>::EPI_GROUPS;
+  constexpr int NGRP = Roles<BN, SPLIT>::EPI_GROUPS;
   constexpr uint32_t TMEM_COLS = (NBUF * BN < 32) ? 32 : NBUF * BN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1142,7 +1145,7 @@ int sm_count() {
 // most 8.  An instantiation with room for fewer than 2 stages is not built.
 template <int BN, bool SPLIT, int A_MODE>
 constexpr int stages_raw() {
-  return (224 * 1024 - Roles<SPLIT>::EPI_GROUPS * 2 * OUT_STAGE_BYTES - 1024) / Smem<BN, SPLIT, A_MODE>::STAGE;
+  return (224 * 1024 - Roles<BN, SPLIT>::EPI_GROUPS * 2 * OUT_STAGE_BYTES - 1024) / Smem<BN, SPLIT, A_MODE>::STAGE;
 }
 template <int BN, bool SPLIT, int A_MODE>
 constexpr int stages_for() {
@@ -1157,7 +1160,7 @@ cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
   } else {
   constexpr int STAGES = stages_for<BN, SPLIT, A_MODE>();
   auto kern = gemm_tc_kernel<BN, STAGES, SPLIT, A_MODE>;
-  const int smem = STAGES * Smem<BN, SPLIT, A_MODE>::STAGE + Roles<SPLIT>::EPI_GROUPS * 2 * OUT_STAGE_BYTES + 1024;
+  const int smem = STAGES * Smem<BN, SPLIT, A_MODE>::STAGE + Roles<BN, SPLIT>::EPI_GROUPS * 2 * OUT_STAGE_BYTES + 1024;
   static bool attr_set = false;  // per instantiation
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1165,7 +1168,7 @@ cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
     attr_set = true;
   }
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, Roles<SPLIT>::THREADS, smem, st>>>(a, b, blo, out, args);
+  kern<<<grid, Roles<BN, SPLIT>::THREADS, smem, st>>>(a, b, blo, out, args);
   return cudaGetLastError();
   }
 }

@@ -102,4 +102,18 @@ cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const
                                const float* residual, float* y, const ConvGeom& g, int group,
                                const ActParams& act, cudaStream_t st);
 
+// ---- det / rec pre and post (prepost.cu), bit-exact with the reference's
+// host code.  Images are n x h x w x 3 uint8 (HWC), masks n x h x w uint8.
+// Bilinear RGB u8 resize (qppocr-kernels resize.rs:158-210).
+cudaError_t launch_resize_bilinear_rgb_u8(const uint8_t* src, int n, int sh, int sw, uint8_t* dst, int dh,
+                                          int dw, cudaStream_t st);
+// Det input (engine.rs:930-982): resize to dh x dw (skipped when equal), then
+// (u8 / 255 - 0.5) * 2 into planar n x 3 x dh x dw f32.
+cudaError_t launch_det_preprocess(const uint8_t* src, int n, int sh, int sw, float* dst, int dh, int dw,
+                                  cudaStream_t st);
+// DB mask (geometry.rs:286-296): pred > thresh (or an existing u8 mask when
+// pred is null), then the 2x2 dilation when `dilate`.
+cudaError_t launch_db_mask(const float* pred, const uint8_t* mask_in, uint8_t* out, int n, int h, int w,
+                           float thresh, int dilate, cudaStream_t st);
+
 }  // namespace qpc

@@ -774,16 +774,39 @@ class Planner {
       for (int k = 0; k < n_inputs; ++k)
         if (gi == inputs[k].name) t = &inputs[k];
       if (!t) throw GraphError{"missing graph input " + gi};
-      if (t->dtype != QPC_F32) throw GraphError{"graph input " + gi + " must be f32"};
+      if (t->dtype != QPC_F32 && t->dtype != QPC_U8_IMAGE)
+        throw GraphError{"graph input " + gi + " must be f32 (or a u8 image batch)"};
       Val v;
-      v.shape.assign(t->shape, t->shape + t->rank);
-      v.strides = rowmajor_strides(v.shape);
-      v.buf = A.alloc(v.numel(), true);
       PlanInstance::IO io;
       io.name = gi;
-      io.shape = v.shape;
-      io.count = v.numel();
-      io.dev = A.ptr(v.buf);
+      io.dtype = t->dtype;
+      if (t->dtype == QPC_U8_IMAGE) {
+        // n x h x w x 3 u8 images for an [n, 3, h, w] f32 input: staged as
+        // bytes, normalised on the device as the reference engine does
+        if (t->rank != 4 || t->shape[3] != 3) throw GraphError{"u8 image input " + gi + " must be n x h x w x 3"};
+        const int64_t n = t->shape[0], h = t->shape[1], w = t->shape[2];
+        v.shape = {n, 3, h, w};
+        v.strides = rowmajor_strides(v.shape);
+        v.buf = A.alloc(v.numel(), true);
+        io.shape.assign(t->shape, t->shape + t->rank);
+        io.bytes = (size_t)(n * h * w * 3);
+        io.count = (int64_t)((io.bytes + 3) / 4);
+        const int u8buf = A.alloc(io.count, true);
+        io.dev = A.ptr(u8buf);
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(io.dev);
+        float* dst = A.ptr(v.buf);
+        step("det_preprocess", gi, (double)io.bytes + 4.0 * v.numel(), 0, [=](cudaStream_t s) {
+          return launch_det_preprocess(src, (int)n, (int)h, (int)w, dst, (int)h, (int)w, s);
+        });
+      } else {
+        v.shape.assign(t->shape, t->shape + t->rank);
+        v.strides = rowmajor_strides(v.shape);
+        v.buf = A.alloc(v.numel(), true);
+        io.shape = v.shape;
+        io.count = v.numel();
+        io.bytes = (size_t)io.count * sizeof(float);
+        io.dev = A.ptr(v.buf);
+      }
       P.ins.push_back(io);
       vals_[gi] = v;
     }
@@ -2004,7 +2027,7 @@ class Planner {
 static std::string shape_key(const qpc_tensor* in, int n) {
   std::ostringstream o;
   for (int k = 0; k < n; ++k) {
-    o << (in[k].name ? in[k].name : "") << ":";
+    o << (in[k].name ? in[k].name : "") << ":d" << in[k].dtype << ":";
     for (int d = 0; d < in[k].rank; ++d) o << in[k].shape[d] << "x";
     o << ";";
   }
@@ -2022,7 +2045,7 @@ std::unique_ptr<PlanInstance> Session::build(const qpc_tensor* inputs, int n, co
     pl.run(inputs, n);
   }
   for (auto& io : p->ins)
-    QPC_CUDA_OR_THROW(cudaHostAlloc((void**)&io.host, std::max<int64_t>(io.count, 1) * sizeof(float), cudaHostAllocDefault));
+    QPC_CUDA_OR_THROW(cudaHostAlloc((void**)&io.host, std::max<size_t>(io.bytes, 4), cudaHostAllocDefault));
   for (auto& io : p->outs)
     QPC_CUDA_OR_THROW(cudaHostAlloc((void**)&io.host, std::max<int64_t>(io.count, 1) * sizeof(float), cudaHostAllocDefault));
   // Eager validation pass (sets kernel attributes, surfaces launch errors).
@@ -2105,7 +2128,8 @@ PlanInstance* Session::launch(const qpc_tensor* inputs, int n) {
       const qpc_tensor* t = nullptr;
       for (int k = 0; k < n; ++k)
         if (io.name == inputs[k].name) t = &inputs[k];
-      QPC_CUDA_OR_THROW(staged_h2d(io.dev, io.host, t->data, io.count * sizeof(float), p->stream));
+      if (t->dtype != io.dtype) throw GraphError{"input " + io.name + ": dtype differs from the plan's"};
+      QPC_CUDA_OR_THROW(staged_h2d(io.dev, io.host, t->data, io.bytes, p->stream));
     }
     QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[1], p->stream));
     if (p->exec) {

@@ -75,6 +75,8 @@ struct PlanInstance {
     float* dev = nullptr;
     int64_t count = 0;
     float* host = nullptr;  // pinned
+    size_t bytes = 0;       // bytes moved per run (inputs: u8 images are 1 byte per value)
+    int dtype = 0;          // qpc_dtype of the run tensor
   };
   std::vector<IO> ins, outs;
   std::atomic<bool> busy{false};
