@@ -368,11 +368,20 @@ def main():
     rl = roofline(prof, hbm, tf, DET_TRAFFIC_PER_IMAGE, B)
     rl["peak_source"] = peak_src
 
-    # e2e through the public API: host inputs, H2D + compute + D2H every step
-    e2e_s = max_over_ranks(e2e_seconds(det, {"x": x}, args.steps, world), world)
+    # e2e through the public API: host inputs, H2D + compute + D2H every step.
+    # Headline: u8 HWC images (what the reference engine's det stage starts
+    # from), normalised on the device as engine.rs:963-982 does on the host;
+    # beside it the same with the f32 network input tensor.
+    img = np.random.Generator(np.random.PCG64(30 + rank)).integers(0, 256, (B, DET_HW, DET_HW, 3),
+                                                                   dtype=np.uint8)
+    e2e_s = max_over_ranks(e2e_seconds(det, {"x": img}, args.steps, world), world)
     e2e = {"value": round(world * B / e2e_s, 2), "unit": "img/s",
-           "h2d_bytes_per_step": int(x.nbytes), "d2h_bytes_per_step": int(B * DET_HW * DET_HW * 4),
+           "h2d_bytes_per_step": int(img.nbytes), "d2h_bytes_per_step": int(B * DET_HW * DET_HW * 4),
+           "input": "u8 HWC images, normalised on the device in the plan (engine.rs:963-982)",
            "timing": E2E_TIMING}
+    e2e_f = max_over_ranks(e2e_seconds(det, {"x": x}, args.steps, world), world)
+    e2e_f32 = {"value": round(world * B / e2e_f, 2), "unit": "img/s", "h2d_bytes_per_step": int(x.nbytes),
+               "d2h_bytes_per_step": int(B * DET_HW * DET_HW * 4), "input": "f32 NCHW network input"}
 
     # ---------------------------------------------------------------- rec
     rec = None
@@ -414,7 +423,7 @@ def main():
                        "math": args.math, "global_batch": world * B,
                        "parallelism": f"dp{world} (replicas, image shards)",
                        "l2": "inputs 708 MB/step > 126 MB L2, no flush"},
-            "roofline": rl, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "roofline": rl, "cpu_baseline": cpu, "e2e": e2e, "e2e_f32_input": e2e_f32, "clocks": clk,
             "gpu_launches": launches * args.steps, "rec": rec,
         }
         print(json.dumps(line), flush=True)

@@ -142,46 +142,47 @@ __device__ __forceinline__ RowMap row_map(const GemmArgs& args, int m_blk, int i
   return m;
 }
 
-// Epilogue of one tile through shared memory: for each 32-column chunk the
-// residual (if any) is loaded cooperatively (8 threads per 128-byte row
-// segment), every thread finishes its row (bias, activation, residual) into a
+// Epilogue of one tile through shared memory: for each 32-column chunk every
+// thread finishes its own row (bias, activation, residual: its row's 128-byte
+// residual segment, loaded before the TMEM fetch so the two overlap) into a
 // 128B-swizzled staging buffer, and one thread writes the chunk with a TMA
 // store.  Two staging buffers alternate; a buffer is rewritten only after the
 // store issued from it two chunks earlier has finished reading it.
+// Residual row of tile row r (-1 outside the output).
+template <int A_MODE>
+__device__ __forceinline__ int64_t residual_row(const GemmArgs& args, int m_blk, int img, int oy0, int ox0, int r) {
+  const RowMap mine = row_map<A_MODE>(args, m_blk, img, oy0, ox0, r);
+  return mine.orow >= 0 ? mine.rrow : -1;
+}
+
+// The 32 residual values of row `rrow`, columns col0..col0+31 (zeros past N).
+__device__ __forceinline__ void load_residual(const GemmArgs& args, int64_t rrow, int col0, float4 (&rv)[8]) {
+  const float* rp = args.epi.residual + rrow * args.epi.ldr + col0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    rv[k] = (rrow >= 0 && col0 + 4 * k < args.N) ? __ldg(reinterpret_cast<const float4*>(rp) + k)
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
 template <int BN, int A_MODE, class Fetch>
 __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorMap* tm_out,
                                            uint8_t* stage, int64_t* s_rrow, int bar_id,
                                            uint32_t& chunk_ctr, int m_blk, int n0, int img, int oy0,
                                            int ox0, int r, int t, Fetch&& fetch) {
+  (void)s_rrow;
   const GemmEpilogue& e = args.epi;
-  if (e.residual) {
-    // residual source row of every tile row, once per tile (read after the
-    // first barrier below)
-    const RowMap mine = row_map<A_MODE>(args, m_blk, img, oy0, ox0, r);
-    s_rrow[r] = mine.orow >= 0 ? mine.rrow : -1;
-  }
+  const int64_t rrow = e.residual ? residual_row<A_MODE>(args, m_blk, img, oy0, ox0, r) : -1;
 #pragma unroll 1
   for (int cc = 0; cc < BN; cc += 32) {
     if (n0 + cc >= args.N) break;
     float* sb = reinterpret_cast<float*>(stage + (chunk_ctr & 1u) * OUT_STAGE_BYTES);
-    // Everything that does not touch the staging buffer first (TMEM fetch,
-    // residual loads, bias, activation), so it overlaps the wait for the
-    // store issued from this buffer two chunks ago.
+    // Everything that does not touch the staging buffer first (residual
+    // loads, TMEM fetch, bias, activation, residual add), so it overlaps the
+    // wait for the store issued from this buffer two chunks ago.
+    float4 rv[8];
+    if (e.residual) load_residual(args, rrow, n0 + cc, rv);
     float v[32];
     fetch(cc, v);
-    float4 rv[8];
-    if (e.residual) {
-      if (cc == 0) named_bar_sync(bar_id, 128);  // s_rrow of this tile published
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int i = t + k * 128;
-        const int row = i >> 3, c4 = i & 7;
-        const int col = n0 + cc + c4 * 4;
-        const int64_t rr = s_rrow[row];
-        rv[k] = (rr >= 0 && col < args.N) ? __ldg(reinterpret_cast<const float4*>(e.residual + rr * e.ldr + col))
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
     if (e.bias) {
       // columns past N are clipped by the TMA store; keep their reads in bounds
 #pragma unroll
@@ -197,31 +198,22 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
       }
     }
     apply_act_n(v, e.act);
-    if (t == 0) bulk_wait_group_read<1>();
-    named_bar_sync(bar_id, 128);  // staging buffer free
     if (e.residual) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const int i = t + k * 128;
-        const int row = i >> 3, c4 = i & 7;
-        *reinterpret_cast<float4*>(sb + row * 32 + ((c4 ^ (row & 7)) << 2)) = rv[k];
+        v[4 * k] = __fadd_rn(v[4 * k], rv[k].x);
+        v[4 * k + 1] = __fadd_rn(v[4 * k + 1], rv[k].y);
+        v[4 * k + 2] = __fadd_rn(v[4 * k + 2], rv[k].z);
+        v[4 * k + 3] = __fadd_rn(v[4 * k + 3], rv[k].w);
       }
-      named_bar_sync(bar_id, 128);
     }
+    if (t == 0) bulk_wait_group_read<1>();
+    named_bar_sync(bar_id, 128);  // staging buffer free
     float* myrow = sb + r * 32;
 #pragma unroll
-    for (int c4 = 0; c4 < 8; ++c4) {
-      float4* slot = reinterpret_cast<float4*>(myrow + ((c4 ^ (r & 7)) << 2));
-      float4 o = make_float4(v[c4 * 4], v[c4 * 4 + 1], v[c4 * 4 + 2], v[c4 * 4 + 3]);
-      if (e.residual) {
-        const float4 rv4 = *slot;
-        o.x = __fadd_rn(o.x, rv4.x);
-        o.y = __fadd_rn(o.y, rv4.y);
-        o.z = __fadd_rn(o.z, rv4.z);
-        o.w = __fadd_rn(o.w, rv4.w);
-      }
-      *slot = o;
-    }
+    for (int c4 = 0; c4 < 8; ++c4)
+      *reinterpret_cast<float4*>(myrow + ((c4 ^ (r & 7)) << 2)) =
+          make_float4(v[c4 * 4], v[c4 * 4 + 1], v[c4 * 4 + 2], v[c4 * 4 + 3]);
     fence_proxy_async_smem();
     named_bar_sync(bar_id, 128);
     if (t == 0) {
@@ -1320,7 +1312,7 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
   CUtensorMap mo = ma;
   const float* obase = epi.out + epi.col_off;
   if (!epi.partials && (N % 4) == 0 && (epi.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(obase) & 15) == 0 &&
-      (!epi.residual || (epi.ldr % 4) == 0)) {
+      (!epi.residual || ((epi.ldr % 4) == 0 && (reinterpret_cast<uintptr_t>(epi.residual) & 15) == 0))) {
     const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)epi.ldo * 4};
     const uint32_t box[2] = {32, BM};
@@ -1378,7 +1370,7 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
     mo = ma;
     const float* obase = epi.out + epi.col_off;
     if ((g.m % 4) == 0 && (epi.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(obase) & 15) == 0 &&
-        (!epi.residual || (epi.ldr % 4) == 0)) {
+        (!epi.residual || ((epi.ldr % 4) == 0 && (reinterpret_cast<uintptr_t>(epi.residual) & 15) == 0))) {
       const uint64_t dims[4] = {(uint64_t)g.m, (uint64_t)g.ow, (uint64_t)g.oh, (uint64_t)g.n};
       const uint64_t strides[3] = {(uint64_t)epi.ldo * 4, (uint64_t)epi.ldo * g.ow * 4,
                                    (uint64_t)epi.ldo * g.ow * g.oh * 4};
@@ -1440,7 +1432,7 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
       mo = ma;
       const float* obase = epi.out + epi.col_off;
       if ((g.m % 4) == 0 && (epi.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(obase) & 15) == 0 &&
-          (!epi.residual || (epi.ldr % 4) == 0)) {
+          (!epi.residual || ((epi.ldr % 4) == 0 && (reinterpret_cast<uintptr_t>(epi.residual) & 15) == 0))) {
         const uint64_t dims[4] = {(uint64_t)g.m, (uint64_t)g.ow, (uint64_t)g.oh, (uint64_t)g.n};
         const uint64_t strides[3] = {(uint64_t)epi.ldo * 4, (uint64_t)epi.ldo * g.ow * 4,
                                      (uint64_t)epi.ldo * g.ow * g.oh * 4};
@@ -1504,7 +1496,7 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
   CUtensorMap mo = ma;
   const float* obase = epi.out + epi.col_off;
   if ((g.m % 4) == 0 && (epi.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(obase) & 15) == 0 &&
-      (!epi.residual || (epi.ldr % 4) == 0)) {
+      (!epi.residual || ((epi.ldr % 4) == 0 && (reinterpret_cast<uintptr_t>(epi.residual) & 15) == 0))) {
     const uint64_t dims[4] = {(uint64_t)g.m, (uint64_t)g.ow, (uint64_t)g.oh, (uint64_t)g.n};
     const uint64_t strides[3] = {(uint64_t)epi.ldo * 4, (uint64_t)epi.ldo * g.ow * 4,
                                  (uint64_t)epi.ldo * g.ow * g.oh * 4};
