@@ -489,13 +489,52 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1u;
+        const float* gate = A_MODE == 0 ? args.epi.a_gate : nullptr;
+        // image of this tile's first row and that row's place in it (rows
+        // are consecutive pixels, so a row's image is img0 + the number of
+        // image boundaries crossed, at most one when an image has >= 128 rows)
+        const int64_t row0 = (int64_t)(tile / n_tiles) * BM;
+        const int ghw = args.epi.a_gate_rows;
+        const int64_t img0 = gate ? row0 / ghw : 0;
+        const int r0 = gate ? (int)(row0 - img0 * ghw) : 0;
+        // Chunk i = t + 64 j is row (t >> 3) + 8 j, channel quad (t & 7) ^ ((t >> 3) & 7):
+        // the same quad for all of this thread's chunks, so with >= 128-row
+        // images only two gate values (this image's, the next one's) occur.
+        // They do not depend on the stage's data: load them before its wait.
+        float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), gb = ga;
+        if (gate && ghw >= BM) {
+          const int ch = kb * BK + (((t & 7) ^ ((t >> 3) & 7)) << 2);
+          if (ch < args.K) {
+            const int64_t img_last = (args.M - 1) / ghw;
+            ga = __ldg(reinterpret_cast<const float4*>(gate + img0 * (int64_t)args.K + ch));
+            gb = __ldg(reinterpret_cast<const float4*>(gate + min(img0 + 1, img_last) * (int64_t)args.K + ch));
+          }
+        }
         if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
         float4* a = reinterpret_cast<float4*>(smem + s * SM::STAGE);
         float4* lo = reinterpret_cast<float4*>(smem + s * SM::STAGE + SM::A_BYTES + SM::B_BYTES);
         const int n4 = A_MODE == 2 ? (BM + args.kw - 1) * (BK / 4) : A_TILE_BYTES / 16;
 #pragma unroll 4
         for (int i = t; i < n4; i += 64) {
-          const float4 v = a[i];
+          float4 v = a[i];
+          if (gate) {
+            // logical (row, channel quad) of swizzled 16-byte chunk i
+            const int row = i >> 3, c4 = (i & 7) ^ (row & 7);
+            const int ch = kb * BK + c4 * 4;
+            if (row0 + row < args.M && ch < args.K) {
+              float4 g4;
+              if (ghw >= BM) {
+                g4 = r0 + row >= ghw ? gb : ga;
+              } else {
+                const int64_t img = img0 + (r0 + row) / ghw;
+                g4 = __ldg(reinterpret_cast<const float4*>(gate + img * (int64_t)args.K + ch));
+              }
+              v.x = __fmul_rn(v.x, g4.x);
+              v.y = __fmul_rn(v.y, g4.y);
+              v.z = __fmul_rn(v.z, g4.z);
+              v.w = __fmul_rn(v.w, g4.w);
+            }
+          }
           float4 h;
           h.x = tf32_rna(v.x);
           h.y = tf32_rna(v.y);

@@ -51,6 +51,11 @@ struct GemmEpilogue {
   // nearest-upsample residual: output rows are pixels of an (n, oh, ow) map;
   // the residual is an (n, rh, rw) map. rh == 0 disables the remap.
   int oh = 0, ow = 0, rh = 0, rw = 0;
+  // Per-image channel gate on A (SE block: the 1x1 conv reads x * g with g
+  // [images, K] broadcast over each image's a_gate_rows pixels), applied as A
+  // is rounded on chip, so x * g is never written.  Rows-mode GEMM only.
+  const float* a_gate = nullptr;
+  int a_gate_rows = 0;
   // Row-argmax epilogue (CTC head): instead of storing D, each output tile
   // writes per row (max, argmax bits, sum exp(l - max)) of its columns to
   // partials[n_tile * M + row] (float4); nothing is written to `out`.

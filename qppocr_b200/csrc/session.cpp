@@ -311,6 +311,20 @@ const float* Session::dweight(const std::string& name, const std::string& varian
         for (int64_t mo = 0; mo < m; ++mo)
           for (int64_t ch = 0; ch < c; ++ch)
             v[(ky * nf + kx * m + mo) * c + ch] = src[((mo * c + ch) * kh + ky) * kw + kx];
+  } else if (base_variant.size() == 3 && base_variant.compare(0, 2, "pk") == 0) {
+    // pkP: 1x1 conv [M, C] as the block diagonal of P copies, [P*M][P*C]:
+    // P consecutive pixels share one row of P*C inputs and P*M outputs.
+    const int64_t pk = base_variant[2] - '0';
+    const int64_t m = h->shape[0], c = h->shape[1];
+    v.assign(pk * m * pk * c, 0.f);
+    for (int64_t q = 0; q < pk; ++q)
+      for (int64_t mo = 0; mo < m; ++mo)
+        for (int64_t ch = 0; ch < c; ++ch) v[(q * m + mo) * (pk * c) + q * c + ch] = src[mo * c + ch];
+  } else if (base_variant.size() == 4 && base_variant.compare(0, 3, "dup") == 0) {
+    // dupP: a vector repeated P times (bias of a pkP GEMM)
+    const int64_t pk = base_variant[3] - '0';
+    v.reserve(src.size() * pk);
+    for (int64_t q = 0; q < pk; ++q) v.insert(v.end(), src.begin(), src.end());
   } else if (base_variant == "nk") {
     const int64_t k = h->shape[0], n = h->shape[1];
     v.resize(k * n);
@@ -1194,6 +1208,8 @@ class Planner {
     } else if (pw1) {
       Val x = as_nhwc(x0, nm);
       const float* xp = out_ptr(x);
+      auto gi = gated_.find(n.in[0]);
+      const float* gate = gi != gated_.end() ? optr(gi->second.g) : nullptr;
       const bool split = math == QPC_MATH_3XTF32;
       const float* wb = S.dweight(n.in[1], split ? "raw.hi" : "raw.rn");
       const float* wl = split ? S.dweight(n.in[1], "raw.lo") : nullptr;
@@ -1210,11 +1226,41 @@ class Planner {
         e.oh = (int)oh;
         e.ow = (int)ow;
       }
+      if (gate) {
+        e.a_gate = gate;
+        e.a_gate_rows = (int)(H * W);
+      }
       const int64_t rows = N * H * W;
       const double bytes = 4.0 * rows * C + out_bytes + 4.0 * M * C + res_bytes;
-      step("gemm_tc", nm, bytes, flops, [=](cudaStream_t s) {
-        return launch_gemm_tc(xp, rows, (int)C, (int)C, wb, wl, (int)M, e, math, err, s);
-      });
+      // Narrow K (8 or 16 channels, a quarter / half of the 32-float k-block):
+      // P = 32 / C consecutive pixels share one GEMM row against the block
+      // diagonal of P filter copies, so no k-block is half padding and each
+      // tile carries P times the pixels.  Rows are contiguous, so the input,
+      // output and a plain residual are the same memory viewed [rows/P, P*C].
+      const int64_t pk = (C == 8 || C == 16) ? 32 / C : 1;
+      if (pk > 1 && !gate && (rows % pk) == 0 && M * pk <= 128 && ldo == M && res_h == 0 && (M % 4) == 0) {
+        const std::string pv = "pk" + std::to_string(pk);
+        const float* pwb = S.dweight(n.in[1], pv + (split ? ".hi" : ".rn"));
+        const float* pwl = split ? S.dweight(n.in[1], pv + ".lo") : nullptr;
+        GemmEpilogue ep = e;
+        ep.bias = has_bias ? S.dweight(n.in[2], "dup" + std::to_string(pk)) : nullptr;
+        ep.ldo = (int)(M * pk);
+        ep.ldr = (int)(M * pk);
+        const int64_t prow = rows / pk;
+        const int pc = (int)(C * pk), pm = (int)(M * pk);
+        step("gemm_tc", nm, bytes, flops, [=](cudaStream_t s) {
+          return launch_gemm_tc(xp, prow, pc, pc, pwb, pwl, pm, ep, math, err, s);
+        });
+      } else {
+        step("gemm_tc", nm, bytes, flops, [=](cudaStream_t s) {
+          return launch_gemm_tc(xp, rows, (int)C, (int)C, wb, wl, (int)M, e, math, err, s);
+        });
+      }
+      if (gate) {
+        unref(gi->second.x);
+        unref(gi->second.g);
+        gated_.erase(gi);
+      }
       unref(x);
     } else if (kxk_tc) {
       Val x = as_nhwc(x0, nm);
@@ -1435,7 +1481,55 @@ class Planner {
     define(n.out[0], y);
   }
 
+  // SE gate: Mul(x [N,C,H,W], g [N,C,1,1]) whose only consumer is a 1x1
+  // stride-1 unpadded Conv reading it as its input is not materialised; the
+  // conv's GEMM multiplies A by g as it rounds A on chip (same f32 products).
+  struct Gated {
+    Val x, g;
+  };
+  std::map<std::string, Gated> gated_;
+
+  bool try_gate(const Node& n) {
+    const std::string& out = n.out[0];
+    for (auto& go : S.graph_outputs())
+      if (go == out) return false;
+    auto cit = consumers_.find(out);
+    if (cit == consumers_.end() || cit->second.size() != 1) return false;
+    const Node& c = S.nodes()[cit->second[0]];
+    if (c.op != "Conv" || c.in.empty() || c.in[0] != out || c.has_in(4)) return false;
+    for (size_t k = 1; k < c.in.size(); ++k)
+      if (c.in[k] == out) return false;
+    Val a = operand(n.in[0]), b = operand(n.in[1]);
+    if (a.is_const || b.is_const || a.shape.size() != 4 || b.shape.size() != 4) return false;
+    const bool a_is_x = b.shape[2] == 1 && b.shape[3] == 1;
+    const Val& x = a_is_x ? a : b;
+    const Val& g = a_is_x ? b : a;
+    const int64_t N = x.shape[0], C = x.shape[1], H = x.shape[2], W = x.shape[3];
+    if (g.shape != std::vector<int64_t>{N, C, 1, 1} || !is_rowmajor(g) || (g.off % 4) || (C % 4) || C == 8 ||
+        C == 16 || H * W < 2)
+      return false;
+    const HostTensor* w = S.weight(c.in[1]);
+    if (!w || w->shape.size() != 4 || w->shape[1] != C || w->shape[2] != 1 || w->shape[3] != 1 ||
+        c.geti("group", 1) != 1)
+      return false;
+    auto st = c.getints("strides");
+    if (st.size() == 2 && (st[0] != 1 || st[1] != 1)) return false;
+    int64_t ph, pw, peh, pew;
+    resolve_pads(c, H, W, 1, 1, 1, 1, &ph, &pw, &peh, &pew);
+    if (ph || pw || peh || pew) return false;
+    Gated gt;
+    gt.x = as_nhwc(x, n.name);
+    gt.g = g;
+    A.retain(g.buf);
+    Val y = gt.x;  // what the conv reads as its input; the gate rides along
+    A.retain(y.buf);
+    define(out, y);
+    gated_[out] = gt;
+    return true;
+  }
+
   void plan_binary(const Node& n) {
+    if (n.op == "Mul" && try_gate(n)) return;
     Val a = operand(n.in[0]);
     Val b = operand(n.in[1]);
     int op = 0;

@@ -1,4 +1,5 @@
-"""k x k stride-1 convolutions on the tensor-core implicit GEMM, one Conv node
+"""k x k stride-1 convolutions on the tensor-core implicit GEMM (and narrow 1x1
+convs on the row-packed GEMM), one Conv node
 per graph, against the oracle's conv (qppocr-kernels conv.rs im2col + panel
 GEMM), metric max|d|/max|ref| (reference tests/kernels.rs:51-77).
 
@@ -33,6 +34,11 @@ CASES = [
     (1, 24, 32, (3, 1), 8, 100, None, False), # halo, one tap per kernel row
     (1, 48, 136, 3, 10, 96, None, False),    # above the halo N limit: tile path
     (2, 96, 24, 3, 30, 30, None, False),     # tile path, narrow rows
+    # 1x1 with 8 / 16 input channels: P = 32 / C pixels packed per GEMM row
+    (1, 16, 32, 1, 20, 30, "relu", False),   # P = 2
+    (1, 16, 16, 1, 10, 12, "relu", True),    # P = 2 with a residual
+    (2, 8, 24, 1, 10, 12, None, False),      # P = 4
+    (2, 8, 24, 1, 9, 11, None, False),       # 198 pixels, not a multiple of 4: unpacked
 ]
 
 
@@ -84,3 +90,23 @@ def test_conv_upsampled_residual(cuda_ctx, case, math):
     got = s.run({"x": x, "z": z})[0]
     err = np.abs(got.astype(np.float64) - ref).max() / max(np.abs(ref).max(), 1e-6)
     assert err < TOL[math], err
+
+
+@pytest.mark.parametrize("math", ["tf32", "3xtf32"])
+def test_se_gate_fused_into_pointwise(cuda_ctx, math):
+    """SE block (GAP -> 1x1 -> relu -> 1x1 -> HardSigmoid -> Mul) feeding a
+    1x1 conv: the gate multiply runs inside the conv's GEMM as A is rounded,
+    so the plan has no separate elementwise Mul; results match the oracle."""
+    b = nets.Builder(17, "se")
+    y = b.se("x", 64)
+    y = b.conv(y, 64, 96, 1, bias=True, bn=False, act="hswish")
+    g, wts = b.graph(["x"], [y], [[1, 64, 0, 0]])
+    g = q.optimize(g, wts)
+    x = np.random.Generator(np.random.PCG64(5)).uniform(-1, 1, (3, 64, 10, 14)).astype(np.float32)
+    ref = orc.run_graph(g, wts, {"x": x})[0]
+    s = cuda_ctx.create_session(g, wts, role="other", math=math)
+    got = s.run({"x": x})[0]
+    err = np.abs(got.astype(np.float64) - ref).max() / max(np.abs(ref).max(), 1e-6)
+    assert err < TOL[math], err
+    kinds = [p[0] for p in s.profile({"x": x}, iters=1)]
+    assert "binary" not in kinds and "gemm_tc" in kinds, kinds
