@@ -105,7 +105,7 @@ bool conv_fold_ok(const ConvGeom& g);
 // (gemm.rs:75-128 implicit-GEMM k order).
 cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const float* bias,
                                const float* residual, float* y, const ConvGeom& g, int group,
-                               const ActParams& act, cudaStream_t st);
+                               const ActParams& act, cudaStream_t st, unsigned int* err = nullptr);
 
 // ---- det / rec pre and post (prepost.cu), bit-exact with the reference's
 // host code.  Images are n x h x w x 3 uint8 (HWC), masks n x h x w uint8.

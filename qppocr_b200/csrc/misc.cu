@@ -145,114 +145,166 @@ __global__ void __launch_bounds__(256) conv_small_c_kernel(
   }
 }
 
-// Stem specialisation (C = 3, 3x3, stride 2, NCHW input, NHWC output): a
-// block makes an 8 x 64 output tile; its 3 x 17 x 129 input window is staged
-// in shared memory with coalesced row loads (zeros outside the image), and
-// each thread makes 2 horizontally adjacent pixels, so every broadcast weight
-// read feeds 2 FMAs.  Per element the chain is the generic kernel's: acc = 0,
-// fma over k = (ch, ky, kx) ascending, then + bias, act, + residual.
+// Stem specialisation (C = 3, 3x3, stride 2, NCHW input, NHWC output).  A
+// persistent block walks 8 x 64 output tiles.  Each tile's input window
+// (3 planes x 17 rows x 129 columns, its first column rounded down to a
+// 16-byte boundary, hence 132) arrives by one 4-D TMA load (zeros outside
+// the image = the zero padding) into one of two shared-memory buffers, the
+// next tile's load overlapping this tile's arithmetic.  Thread (row tr, lane
+// tc) makes pixels tc and tc + 32 of its row: each broadcast weight read
+// feeds 2 FMAs and a warp writes 32 consecutive pixels.  Per element the
+// chain is the generic kernel's: acc = 0, fma over k = (ch, ky, kx)
+// ascending, then + bias, act, + residual.
+constexpr int STEM_TH = 8, STEM_TW = 64, STEM_IR = 2 * STEM_TH + 1, STEM_IC = 132;
+constexpr int STEM_BOX_BYTES = 3 * STEM_IR * STEM_IC * 4;           // 26,928 bytes per load
+constexpr int STEM_BUF = ((STEM_BOX_BYTES + 1023) / 1024) * 1024;   // buffer stride, 1024-aligned
+
 template <int M>
 __global__ void __launch_bounds__(256) conv_stem3s2_kernel(
-    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
-    const float* __restrict__ residual, float* __restrict__ y, int N, int H, int W, int OH, int OW,
-    int PH, int PW, ActParams act) {
-  constexpr int TH = 8, TW = 64, IR = 2 * TH + 1, IC = 2 * TW + 1, ICP = IC + 3;
+    const __grid_constant__ CUtensorMap tmX, const float* __restrict__ w, const float* __restrict__ bias,
+    const float* __restrict__ residual, float* __restrict__ y, int N, int OH, int OW, int PH, int PW,
+    ActParams act, unsigned int* err) {
+  extern __shared__ __align__(1024) uint8_t stem_raw[];
+  float* xs0 = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(stem_raw) + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(16) float wsm[27 * M];
-  __shared__ float xs[3][IR][ICP];
-  for (int i = threadIdx.x; i < 27 * M; i += 256) {
+  __shared__ __align__(8) uint64_t full[2];
+  const int tid = threadIdx.x;
+  for (int i = tid; i < 27 * M; i += 256) {
     const int k = i / M, m = i % M;
     wsm[i] = w[m * 27 + k];
   }
-  const int tiles_x = (OW + TW - 1) / TW, tiles_y = (OH + TH - 1) / TH;
-  const int64_t tiles = (int64_t)N * tiles_y * tiles_x;
-  const int tr = threadIdx.x >> 5, tc = threadIdx.x & 31;
-  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-    const int bx = (int)(tile % tiles_x);
-    const int64_t rr = tile / tiles_x;
-    const int by = (int)(rr % tiles_y);
-    const int n = (int)(rr / tiles_y);
-    const int oy0 = by * TH, ox0 = bx * TW;
-    const int iy0 = oy0 * 2 - PH, ix0 = ox0 * 2 - PW;
-    __syncthreads();  // previous tile consumed (and weights staged)
-    for (int i = threadIdx.x; i < 3 * IR * IC; i += 256) {
-      const int col = i % IC;
-      const int row = (i / IC) % IR;
-      const int ch = i / (IC * IR);
-      const int iy = iy0 + row, ix = ix0 + col;
-      float v = 0.f;
-      if (iy >= 0 && iy < H && ix >= 0 && ix < W) v = __ldg(x + (((int64_t)n * 3 + ch) * H + iy) * W + ix);
-      xs[ch][row][col] = v;
-    }
-    __syncthreads();
-    float a0[M], a1[M];
+  if (tid == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    fence_barrier_init();
+    prefetch_tensormap(&tmX);
+  }
+  __syncthreads();
+  const int tiles_x = (OW + STEM_TW - 1) / STEM_TW, tiles_y = (OH + STEM_TH - 1) / STEM_TH;
+  const int total = N * tiles_y * tiles_x;
+  auto coords = [&](int tile, int& n, int& oy0, int& ox0) {
+    const int bx = tile % tiles_x;
+    const int r = tile / tiles_x;
+    oy0 = (r % tiles_y) * STEM_TH;
+    n = r / tiles_y;
+    ox0 = bx * STEM_TW;
+  };
+  auto issue = [&](int tile, int buf) {
+    int n, oy0, ox0;
+    coords(tile, n, oy0, ox0);
+    const int ix0 = 2 * ox0 - PW;
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&full[buf], STEM_BOX_BYTES);
+    tma_load_4d(reinterpret_cast<uint8_t*>(xs0) + buf * STEM_BUF, &tmX, &full[buf], ix0 & ~3, 2 * oy0 - PH, 0, n);
+  };
+  if (tid == 0 && (int)blockIdx.x < total) issue(blockIdx.x, 0);
+  const int tr = tid >> 5, tc = tid & 31;
+  uint32_t it = 0;
+  for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+    const int buf = it & 1;
+    if (tid == 0 && tile + (int)gridDim.x < total) issue(tile + gridDim.x, buf ^ 1);
+    int n, oy0, ox0;
+    coords(tile, n, oy0, ox0);
+    const int d = (2 * ox0 - PW) - ((2 * ox0 - PW) & ~3);  // column offset of the window in the box
+    const bool ok = mbar_wait(&full[buf], (it >> 1) & 1u, err);
+    if (ok) {
+      const float* xs = xs0 + buf * (STEM_BUF / 4);
+      float a0[M], a1[M];
 #pragma unroll
-    for (int i = 0; i < M; ++i) a0[i] = a1[i] = 0.f;
+      for (int i = 0; i < M; ++i) a0[i] = a1[i] = 0.f;
 #pragma unroll
-    for (int ch = 0; ch < 3; ++ch)
+      for (int ch = 0; ch < 3; ++ch)
 #pragma unroll
-      for (int ky = 0; ky < 3; ++ky)
+        for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
-        for (int kx = 0; kx < 3; ++kx) {
-          const int k = (ch * 3 + ky) * 3 + kx;
-          const float v0 = xs[ch][2 * tr + ky][4 * tc + kx];
-          const float v1 = xs[ch][2 * tr + ky][4 * tc + 2 + kx];
-          const float4* wk = reinterpret_cast<const float4*>(wsm + k * M);
+          for (int kx = 0; kx < 3; ++kx) {
+            const int k = (ch * 3 + ky) * 3 + kx;
+            const float* row = xs + (ch * STEM_IR + 2 * tr + ky) * STEM_IC + d + kx;
+            const float v0 = row[2 * tc], v1 = row[2 * tc + 64];
+            const float4* wk = reinterpret_cast<const float4*>(wsm + k * M);
 #pragma unroll
-          for (int i4 = 0; i4 < M / 4; ++i4) {
-            const float4 wv = wk[i4];
-            a0[4 * i4] = __fmaf_rn(wv.x, v0, a0[4 * i4]);
-            a0[4 * i4 + 1] = __fmaf_rn(wv.y, v0, a0[4 * i4 + 1]);
-            a0[4 * i4 + 2] = __fmaf_rn(wv.z, v0, a0[4 * i4 + 2]);
-            a0[4 * i4 + 3] = __fmaf_rn(wv.w, v0, a0[4 * i4 + 3]);
-            a1[4 * i4] = __fmaf_rn(wv.x, v1, a1[4 * i4]);
-            a1[4 * i4 + 1] = __fmaf_rn(wv.y, v1, a1[4 * i4 + 1]);
-            a1[4 * i4 + 2] = __fmaf_rn(wv.z, v1, a1[4 * i4 + 2]);
-            a1[4 * i4 + 3] = __fmaf_rn(wv.w, v1, a1[4 * i4 + 3]);
+            for (int i4 = 0; i4 < M / 4; ++i4) {
+              const float4 wv = wk[i4];
+              a0[4 * i4] = __fmaf_rn(wv.x, v0, a0[4 * i4]);
+              a0[4 * i4 + 1] = __fmaf_rn(wv.y, v0, a0[4 * i4 + 1]);
+              a0[4 * i4 + 2] = __fmaf_rn(wv.z, v0, a0[4 * i4 + 2]);
+              a0[4 * i4 + 3] = __fmaf_rn(wv.w, v0, a0[4 * i4 + 3]);
+              a1[4 * i4] = __fmaf_rn(wv.x, v1, a1[4 * i4]);
+              a1[4 * i4 + 1] = __fmaf_rn(wv.y, v1, a1[4 * i4 + 1]);
+              a1[4 * i4 + 2] = __fmaf_rn(wv.z, v1, a1[4 * i4 + 2]);
+              a1[4 * i4 + 3] = __fmaf_rn(wv.w, v1, a1[4 * i4 + 3]);
+            }
           }
-        }
-    const int oy = oy0 + tr;
+      const int oy = oy0 + tr;
 #pragma unroll
-    for (int px = 0; px < 2; ++px) {
-      const int ox = ox0 + 2 * tc + px;
-      if (oy >= OH || ox >= OW) continue;
-      const int64_t t = ((int64_t)n * OH + oy) * OW + ox;
-      float o[M];
+      for (int px = 0; px < 2; ++px) {
+        const int ox = ox0 + tc + 32 * px;
+        if (oy >= OH || ox >= OW) continue;
+        const int64_t t = ((int64_t)n * OH + oy) * OW + ox;
+        float o[M];
 #pragma unroll
-      for (int i = 0; i < M; ++i) o[i] = px ? a1[i] : a0[i];
-      if (bias)
+        for (int i = 0; i < M; ++i) o[i] = px ? a1[i] : a0[i];
+        if (bias)
 #pragma unroll
-        for (int i = 0; i < M; ++i) o[i] = __fadd_rn(o[i], __ldg(bias + i));
-      apply_act_n(o, act);
-      if (residual)
+          for (int i = 0; i < M; ++i) o[i] = __fadd_rn(o[i], __ldg(bias + i));
+        apply_act_n(o, act);
+        if (residual)
 #pragma unroll
-        for (int i = 0; i < M; ++i) o[i] = __fadd_rn(o[i], __ldg(residual + t * M + i));
-      float4* yo = reinterpret_cast<float4*>(y + t * M);
+          for (int i = 0; i < M; ++i) o[i] = __fadd_rn(o[i], __ldg(residual + t * M + i));
+        float4* yo = reinterpret_cast<float4*>(y + t * M);
 #pragma unroll
-      for (int i4 = 0; i4 < M / 4; ++i4)
-        yo[i4] = make_float4(o[4 * i4], o[4 * i4 + 1], o[4 * i4 + 2], o[4 * i4 + 3]);
+        for (int i4 = 0; i4 < M / 4; ++i4)
+          yo[i4] = make_float4(o[4 * i4], o[4 * i4 + 1], o[4 * i4 + 2], o[4 * i4 + 3]);
+      }
+    }
+    // buffer `buf` is refilled by the issue at the top of the next iteration;
+    // a timed-out wait anywhere stops the whole block, after its loads land
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) {
+        mbar_wait(&full[buf], (it >> 1) & 1u, nullptr);
+        if (tile + (int)gridDim.x < total) mbar_wait(&full[buf ^ 1], ((it + 1) >> 1) & 1u, nullptr);
+      }
+      __syncthreads();
+      break;
     }
   }
 }
 
 cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const float* bias,
                                const float* residual, float* y, const ConvGeom& g, int group,
-                               const ActParams& act, cudaStream_t st) {
+                               const ActParams& act, cudaStream_t st, unsigned int* err) {
   const int mg = g.m / group;
   const int64_t pix = (int64_t)g.n * g.oh * g.ow;
-  if (group == 1 && x_nchw && g.c == 3 && g.kh == 3 && g.kw == 3 && g.sh == 2 && g.sw == 2 &&
-      (g.m == 8 || g.m == 16 || g.m == 32)) {
-    const int64_t tiles = (int64_t)g.n * ((g.oh + 7) / 8) * ((g.ow + 63) / 64);
-    const int grid = (int)(tiles < 148 * 8 ? tiles : 148 * 8);
-#define QPC_STEM(M_)                                                                              \
-  if (g.m == M_) {                                                                                \
-    conv_stem3s2_kernel<M_><<<grid, 256, 0, st>>>(x, w, bias, residual, y, g.n, g.h, g.w, g.oh,   \
-                                                  g.ow, g.ph, g.pw, act);                          \
-    return cudaGetLastError();                                                                    \
+  if (group == 1 && x_nchw && err && g.c == 3 && g.kh == 3 && g.kw == 3 && g.sh == 2 && g.sw == 2 &&
+      (g.m == 8 || g.m == 16 || g.m == 32) && (g.w % 4) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    CUtensorMap map;
+    const uint64_t dims[4] = {(uint64_t)g.w, (uint64_t)g.h, 3, (uint64_t)g.n};
+    const uint64_t strides[3] = {(uint64_t)g.w * 4, (uint64_t)g.w * g.h * 4, (uint64_t)g.w * g.h * 3 * 4};
+    const uint32_t box[4] = {STEM_IC, STEM_IR, 3, 1};
+    if (make_tensor_map(&map, x, 4, dims, strides, box, false)) {
+      const int smem = 2 * STEM_BUF + 1024;
+      const int64_t tiles = (int64_t)g.n * ((g.oh + STEM_TH - 1) / STEM_TH) * ((g.ow + STEM_TW - 1) / STEM_TW);
+#define QPC_STEM(M_)                                                                                    \
+  if (g.m == M_) {                                                                                      \
+    auto kern = conv_stem3s2_kernel<M_>;                                                                \
+    static int per_sm = 0;                                                                              \
+    if (!per_sm) {                                                                                      \
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                    \
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem) != cudaSuccess ||     \
+          per_sm < 1)                                                                                   \
+        per_sm = 1;                                                                                     \
+    }                                                                                                   \
+    const int64_t cap = 148LL * per_sm;                                                                 \
+    kern<<<(int)(tiles < cap ? tiles : cap), 256, smem, st>>>(map, w, bias, residual, y, g.n, g.oh, g.ow, \
+                                                              g.ph, g.pw, act, err);                    \
+    return cudaGetLastError();                                                                          \
   }
-    QPC_STEM(8)
-    QPC_STEM(16)
-    QPC_STEM(32)
+      QPC_STEM(8)
+      QPC_STEM(16)
+      QPC_STEM(32)
 #undef QPC_STEM
+    }
   }
   if (group == 1 && g.c <= 4 && (g.m == 8 || g.m == 16 || g.m == 32)) {
     const size_t smem = (size_t)g.c * g.kh * g.kw * g.m * sizeof(float);

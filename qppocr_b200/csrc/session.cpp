@@ -1294,7 +1294,7 @@ class Planner {
       const double bytes = 4.0 * N * H * W * C + out_bytes + (has_res ? out_bytes : 0);
       const int grp = (int)group;
       step("conv_direct", nm, bytes, flops, [=](cudaStream_t s) {
-        return launch_conv_direct(xp, nchw_in ? 1 : 0, wr, bias, rp, yp, g, grp, act, s);
+        return launch_conv_direct(xp, nchw_in ? 1 : 0, wr, bias, rp, yp, g, grp, act, s, err);
       });
       unref(x);
     }
