@@ -484,9 +484,160 @@ __global__ void __launch_bounds__(SLOTS * M) convt2x2_wide_kernel(
   }
 }
 
+// The same arithmetic with the input chunks arriving by TMA (the input as a
+// [pixels, C] matrix, PIX rows per load) into a 2-stage shared-memory ring,
+// so the next chunk's load overlaps this chunk's FMAs, and two pixels per
+// iteration for more independent chains.  Waits are bounded (error word).
+template <int C, int M, int SLOTS, int PIX>
+__global__ void __launch_bounds__(SLOTS * M) convt2x2_tma_kernel(
+    const __grid_constant__ CUtensorMap tmX, const float* __restrict__ wt, const float* __restrict__ bn_a,
+    const float* __restrict__ bn_b, float* __restrict__ y, int N, int H, int W, ActParams act,
+    unsigned int* err) {
+  static_assert(C % 4 == 0 && M % 4 == 0 && (PIX * C * 4) % 1024 == 0, "vector widths / buffer alignment");
+  constexpr int G = M / 4;  // float4 groups per tap
+  constexpr uint32_t BYTES = PIX * C * 4;
+  extern __shared__ __align__(1024) uint8_t ct_raw[];
+  float* xs0 = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(ct_raw) + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full[2];
+  const int tid = threadIdx.x;
+  const int j = tid % M, slot = tid / M;
+  const int t = j / G, m0 = 4 * (j % G);
+  float w[C][4];
+#pragma unroll
+  for (int c = 0; c < C; ++c)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[c][i] = __ldg(wt + (c * M + m0 + i) * 4 + t);
+  float4 ba = make_float4(1.f, 1.f, 1.f, 1.f), bb = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (bn_a) {
+    ba = __ldg(reinterpret_cast<const float4*>(bn_a + m0));
+    bb = __ldg(reinterpret_cast<const float4*>(bn_b + m0));
+  }
+  if (tid == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    fence_barrier_init();
+    prefetch_tensormap(&tmX);
+  }
+  __syncthreads();
+  const int OW = 2 * W;
+  const int64_t total = (int64_t)N * H * W;
+  const int chunks = (int)((total + PIX - 1) / PIX);
+  auto issue = [&](int chunk, int buf) {
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&full[buf], BYTES);
+    tma_load_2d(reinterpret_cast<uint8_t*>(xs0) + buf * BYTES, &tmX, &full[buf], 0, chunk * PIX);
+  };
+  if (tid == 0 && (int)blockIdx.x < chunks) issue(blockIdx.x, 0);
+  uint32_t it = 0;
+  for (int chunk = blockIdx.x; chunk < chunks; chunk += gridDim.x, ++it) {
+    const int buf = it & 1;
+    if (tid == 0 && chunk + (int)gridDim.x < chunks) issue(chunk + gridDim.x, buf ^ 1);
+    const bool ok = mbar_wait(&full[buf], (it >> 1) & 1u, err);
+    if (ok) {
+      const float* xs = xs0 + buf * (PIX * C);
+      const int64_t p0 = (int64_t)chunk * PIX;
+      const int np = (int)(total - p0 < PIX ? total - p0 : PIX);
+      // slot `slot` takes the contiguous run [slot * RUN, slot * RUN + RUN) of
+      // the chunk, two adjacent pixels per step; its coordinates are found
+      // once per run and then stepped
+      constexpr int RUN = PIX / SLOTS;
+      const int kb = slot * RUN;
+      const uint32_t pp = (uint32_t)(p0 + kb);
+      const uint32_t rr = pp / (uint32_t)W;
+      int ix = (int)(pp - rr * (uint32_t)W);
+      const uint32_t nn = rr / (uint32_t)H;
+      int iy = (int)(rr - nn * (uint32_t)H);
+      int n = (int)nn;
+      for (int k = kb; k < kb + RUN && k < np; k += 2) {
+        const bool two = k + 1 < np;
+        float a[2][4];
+#pragma unroll
+        for (int u = 0; u < 2; ++u)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a[u][i] = 0.f;
+        const float4* xp0 = reinterpret_cast<const float4*>(xs + k * C);
+        const float4* xp1 = reinterpret_cast<const float4*>(xs + (two ? k + 1 : k) * C);
+#pragma unroll
+        for (int c4 = 0; c4 < C / 4; ++c4) {
+          const float4 v0 = xp0[c4], v1 = xp1[c4];
+          const float x0[4] = {v0.x, v0.y, v0.z, v0.w}, x1[4] = {v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) {
+            const int c = 4 * c4 + qq;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              a[0][i] = __fmaf_rn(x0[qq], w[c][i], a[0][i]);
+              a[1][i] = __fmaf_rn(x1[qq], w[c][i], a[1][i]);
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          if (u == 1 && !two) break;
+          float o[4] = {a[u][0], a[u][1], a[u][2], a[u][3]};
+          if (bn_a) {
+            o[0] = __fmaf_rn(o[0], ba.x, bb.x);
+            o[1] = __fmaf_rn(o[1], ba.y, bb.y);
+            o[2] = __fmaf_rn(o[2], ba.z, bb.z);
+            o[3] = __fmaf_rn(o[3], ba.w, bb.w);
+          }
+          apply_act_n(o, act);
+          const int oy = 2 * iy + (t >> 1), ox = 2 * ix + (t & 1);
+          *reinterpret_cast<float4*>(y + (((int64_t)n * 2 * H + oy) * OW + ox) * M + m0) =
+              make_float4(o[0], o[1], o[2], o[3]);
+          // next input pixel
+          if (++ix == W) {
+            ix = 0;
+            if (++iy == H) {
+              iy = 0;
+              ++n;
+            }
+          }
+        }
+      }
+    }
+    // buffer `buf` is refilled by the issue at the top of the next iteration;
+    // a timed-out wait stops the whole block after its loads have landed
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) {
+        mbar_wait(&full[buf], (it >> 1) & 1u, nullptr);
+        if (chunk + (int)gridDim.x < chunks) mbar_wait(&full[buf ^ 1], ((it + 1) >> 1) & 1u, nullptr);
+      }
+      __syncthreads();
+      break;
+    }
+  }
+}
+
 cudaError_t launch_convt2x2(const float* x, const float* wt, const float* bn_a, const float* bn_b,
                             float* y, int n, int h, int w, int c, int m, const ActParams& act,
-                            cudaStream_t st) {
+                            cudaStream_t st, unsigned int* err) {
+  if (c == 24 && m == 24 && err && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(y) & 15) == 0 && (!bn_a || (reinterpret_cast<uintptr_t>(bn_a) & 15) == 0) &&
+      (!bn_b || (reinterpret_cast<uintptr_t>(bn_b) & 15) == 0)) {
+    constexpr int SLOTS = 8, PIX = 256;
+    CUtensorMap map;
+    const int64_t pixels = (int64_t)n * h * w;
+    const uint64_t dims[2] = {24, (uint64_t)pixels};
+    const uint64_t strides[1] = {24 * 4};
+    const uint32_t box[2] = {24, PIX};
+    if (make_tensor_map(&map, x, 2, dims, strides, box, false)) {
+      auto kern = convt2x2_tma_kernel<24, 24, SLOTS, PIX>;
+      const int smem = 2 * PIX * 24 * 4 + 1024;
+      static int per_sm = 0;
+      if (!per_sm) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, SLOTS * 24, smem) != cudaSuccess ||
+            per_sm < 1)
+          per_sm = 1;
+      }
+      const int64_t chunks = (pixels + PIX - 1) / PIX;
+      const int64_t cap = 148LL * per_sm;
+      kern<<<(int)(chunks < cap ? chunks : cap), SLOTS * 24, smem, st>>>(map, wt, bn_a, bn_b, y, n, h, w, act,
+                                                                         err);
+      return cudaGetLastError();
+    }
+  }
   if (c == 24 && m == 24) {
     constexpr int SLOTS = 8, PIX = 256;
     const int64_t chunks = ((int64_t)n * h * w + PIX - 1) / PIX;

@@ -25,7 +25,7 @@ struct BmmDims {
 
 cudaError_t launch_convt2x2(const float* x, const float* wt, const float* bn_a, const float* bn_b,
                             float* y, int n, int h, int w, int c, int m, const ActParams& act,
-                            cudaStream_t st);
+                            cudaStream_t st, unsigned int* err = nullptr);
 cudaError_t launch_gap_nhwc(const float* x, float* y, int n, int hw, int c, cudaStream_t st);
 cudaError_t launch_pool2d_nhwc(const float* x, float* y, int n, int h, int w, int c, int oh, int ow,
                                int kh, int kw, int sh, int sw, int ph, int pw, int is_max,

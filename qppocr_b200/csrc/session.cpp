@@ -1341,8 +1341,9 @@ class Planner {
     const float* wp = S.dweight(n.in[1], "raw");
     const ActParams act = act_of(n);
     const double bytes = 4.0 * (N * H * W * C + N * 4 * H * W * M);
+    unsigned int* err = device_state(S.device()).err_word;
     step("convt2x2", n.name, bytes, 2.0 * N * 4 * H * W * M * C, [=](cudaStream_t s) {
-      return launch_convt2x2(xp, wp, bn_a, bn_b, yp, (int)N, (int)H, (int)W, (int)C, (int)M, act, s);
+      return launch_convt2x2(xp, wp, bn_a, bn_b, yp, (int)N, (int)H, (int)W, (int)C, (int)M, act, s, err);
     });
     unref(x);
     define(n.out[0], y);
