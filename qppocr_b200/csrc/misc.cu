@@ -722,30 +722,37 @@ cudaError_t launch_pool2d_nhwc(const float* x, float* y, int n, int h, int w, in
 // resize.rs:8-57 nearest: iy = min((int)((float)oy * H / oh), H - 1).  Writes
 // into a channel slice [c_off, c_off + C) of an output with ldc channels, so
 // the FPN concat needs no separate copy.
-__global__ void resize_nearest_nhwc_kernel(const float* __restrict__ x, float* __restrict__ y, int N,
-                                           int H, int W, int C, int OH, int OW, int ldc, int c_off) {
+// One output row per blockIdx.y (n * OH + oy), (ox, channel quad) along x:
+// the source row is found once per block, the source column once per thread,
+// all in 32-bit arithmetic.  Source index (int)((float)o * in / out), clamped
+// (resize.rs:43-50).
+__global__ void __launch_bounds__(256) resize_nearest_nhwc_kernel(const float* __restrict__ x,
+                                                                  float* __restrict__ y, int N, int H, int W,
+                                                                  int C, int OH, int OW, int ldc, int c_off) {
   const int C4 = C >> 2;
-  GRID_LOOP(t, (int64_t)N * OH * OW * C4) {
-    const int c4 = (int)(t % C4);
-    int64_t r = t / C4;
-    const int ox = (int)(r % OW);
-    r /= OW;
-    const int oy = (int)(r % OH);
-    const int n = (int)(r / OH);
+  for (int row = blockIdx.y; row < N * OH; row += gridDim.y) {  // row = n * OH + oy
+    const int oy = row % OH, n = row / OH;
     int iy = (int)__fdiv_rn(__fmul_rn((float)oy, (float)H), (float)OH);
-    int ix = (int)__fdiv_rn(__fmul_rn((float)ox, (float)W), (float)OW);
     iy = iy < H - 1 ? iy : H - 1;
-    ix = ix < W - 1 ? ix : W - 1;
-    const float4 v = __ldg(reinterpret_cast<const float4*>(x + (((int64_t)n * H + iy) * W + ix) * C) + c4);
-    *reinterpret_cast<float4*>(y + (((int64_t)n * OH + oy) * OW + ox) * ldc + c_off + c4 * 4) = v;
+    const float4* src = reinterpret_cast<const float4*>(x + ((int64_t)n * H + iy) * W * C);
+    float* dst = y + (int64_t)row * OW * ldc + c_off;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < OW * C4; i += gridDim.x * blockDim.x) {
+      const int ox = i / C4, c4 = i - ox * C4;
+      int ix = (int)__fdiv_rn(__fmul_rn((float)ox, (float)W), (float)OW);
+      ix = ix < W - 1 ? ix : W - 1;
+      *reinterpret_cast<float4*>(dst + (int64_t)ox * ldc + c4 * 4) = __ldg(src + (int64_t)ix * C4 + c4);
+    }
   }
 }
 
 cudaError_t launch_resize_nearest_nhwc(const float* x, float* y, int n, int h, int w, int c, int oh,
                                        int ow, int ldc, int c_off, cudaStream_t st) {
   if ((c & 3) || (ldc & 3) || (c_off & 3)) return cudaErrorInvalidValue;
-  resize_nearest_nhwc_kernel<<<grid_for((int64_t)n * oh * ow * (c / 4)), 256, 0, st>>>(
-      x, y, n, h, w, c, oh, ow, ldc, c_off);
+  if ((int64_t)n * oh >= (1LL << 31) || (int64_t)ow * (c / 4) >= (1LL << 31)) return cudaErrorInvalidValue;
+  const int per_row = ow * (c / 4);
+  const int rows = n * oh;
+  dim3 grid((per_row + 255) / 256, rows < 65535 ? rows : 65535);
+  resize_nearest_nhwc_kernel<<<grid, 256, 0, st>>>(x, y, n, h, w, c, oh, ow, ldc, c_off);
   return cudaGetLastError();
 }
 
