@@ -295,13 +295,13 @@ __device__ __forceinline__ void argmax_tile(const GemmArgs& args, int64_t orow, 
 
 // Warp roles: w0 TMA producer, w1 MMA issuer, w2-3 convert A, then 4-warp
 // epilogue groups that take tiles round-robin (their serial TMEM -> smem ->
-// TMA-store chains overlap).  TF32 runs 4 groups for N tiles <= 64 columns,
+// TMA-store chains overlap).  TF32 runs 4 groups for 32-column N tiles,
 // where a tile carries little work and the chain's latency sets the pace, and
 // 2 otherwise; 3xTF32 keeps one group, whose registers hold the promoted
 // accumulator.
 template <int BN, bool SPLIT>
 struct Roles {
-  static constexpr int EPI_GROUPS = SPLIT ? 1 : (BN <= 64 ? 4 : 2);
+  static constexpr int EPI_GROUPS = SPLIT ? 1 : (BN <= 32 ? 4 : 2);
   static constexpr int THREADS = 128 + 128 * EPI_GROUPS;
 };
 // TMEM accumulators: 8 for 32-column tiles, 4 up to 128 columns, 2 otherwise
@@ -342,6 +342,9 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
                    const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmOut,
                    const GemmArgs args) {
   using SM = Smem<BN, SPLIT, A_MODE>;
+  // A_MODE 3: rows mode (0) with the per-image channel gate applied to A
+  constexpr int AM = A_MODE == 3 ? 0 : A_MODE;
+  constexpr bool GATED = A_MODE == 3;
   constexpr int NBUF = Accs<BN, SPLIT>::NBUF;
   constexpr int NGRP = Roles<BN, SPLIT>::EPI_GROUPS;
   constexpr uint32_t TMEM_COLS = (NBUF * BN < 32) ? 32 : NBUF * BN;
@@ -391,8 +394,8 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
-      const uint32_t a_bytes = A_MODE == 2 ? (uint32_t)(BM + args.kw - 1) * BK * 4 : A_TILE_BYTES;
-      const uint32_t b_bytes = (A_MODE == 2 ? args.kw : 1) * SM::B_TILE;
+      const uint32_t a_bytes = AM == 2 ? (uint32_t)(BM + args.kw - 1) * BK * 4 : A_TILE_BYTES;
+      const uint32_t b_bytes = (AM == 2 ? args.kw : 1) * SM::B_TILE;
       const uint32_t bytes = SPLIT ? (a_bytes + 2 * b_bytes) : (a_bytes + b_bytes);
       uint32_t it = 0;
       bool ok = true;
@@ -404,11 +407,11 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
           if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.err)) { ok = false; break; }
           uint8_t* st = smem + s * SM::STAGE;
           mbar_arrive_expect_tx(&full_bar[s], bytes);
-          if (A_MODE == 0) {
+          if (AM == 0) {
             tma_load_2d(st, &tmA, &full_bar[s], kb * BK, tc.m_blk * BM);
             tma_load_2d(st + SM::A_BYTES, &tmB, &full_bar[s], kb * BK, tc.n0);
             if (SPLIT) tma_load_2d(st + 2 * SM::A_BYTES + SM::B_BYTES, &tmBlo, &full_bar[s], kb * BK, tc.n0);
-          } else if (A_MODE == 2) {
+          } else if (AM == 2) {
             // halo row of input row oy + ky - ph, columns ox0 - pw .. ox0 - pw + 128 + kw - 2
             const int ky = kb / args.cblocks, cb = kb % args.cblocks;
             tma_load_4d(st, &tmA, &full_bar[s], cb * BK, tc.ox0 - args.pw, tc.oy0 + ky - args.ph, tc.img);
@@ -450,8 +453,8 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
           const uint32_t b_addr = a_addr + SM::A_BYTES;
           const uint32_t alo_addr = b_addr + SM::B_BYTES;
           const uint32_t blo_addr = alo_addr + SM::A_BYTES;
-          // A_MODE 2: tap kx of this kernel row is the halo shifted by kx rows
-          const int ntap = A_MODE == 2 ? args.kw : 1;
+          // AM 2: tap kx of this kernel row is the halo shifted by kx rows
+          const int ntap = AM == 2 ? args.kw : 1;
           for (int kx = 0; kx < ntap; ++kx) {
             const uint32_t a_off = (uint32_t)kx * 128u, b_off = (uint32_t)kx * SM::B_TILE;
 #pragma unroll
@@ -489,7 +492,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1u;
-        const float* gate = A_MODE == 0 ? args.epi.a_gate : nullptr;
+        const float* gate = GATED ? args.epi.a_gate : nullptr;
         // image of this tile's first row and that row's place in it (rows
         // are consecutive pixels, so a row's image is img0 + the number of
         // image boundaries crossed, at most one when an image has >= 128 rows)
@@ -502,7 +505,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
         // images only two gate values (this image's, the next one's) occur.
         // They do not depend on the stage's data: load them before its wait.
         float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), gb = ga;
-        if (gate && ghw >= BM) {
+        if (GATED && gate && ghw >= BM) {
           const int ch = kb * BK + (((t & 7) ^ ((t >> 3) & 7)) << 2);
           if (ch < args.K) {
             const int64_t img_last = (args.M - 1) / ghw;
@@ -513,11 +516,11 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
         if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
         float4* a = reinterpret_cast<float4*>(smem + s * SM::STAGE);
         float4* lo = reinterpret_cast<float4*>(smem + s * SM::STAGE + SM::A_BYTES + SM::B_BYTES);
-        const int n4 = A_MODE == 2 ? (BM + args.kw - 1) * (BK / 4) : A_TILE_BYTES / 16;
+        const int n4 = AM == 2 ? (BM + args.kw - 1) * (BK / 4) : A_TILE_BYTES / 16;
 #pragma unroll 4
         for (int i = t; i < n4; i += 64) {
           float4 v = a[i];
-          if (gate) {
+          if (GATED && gate) {
             // logical (row, channel quad) of swizzled 16-byte chunk i
             const int row = i >> 3, c4 = (i & 7) ^ (row & 7);
             const int ch = kb * BK + c4 * 4;
@@ -570,7 +573,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
     for (int tile = blockIdx.x + grp * gridDim.x; tile < total_tiles && ok; tile += NGRP * gridDim.x) {
       const TileCoord tc = tile_coord(args, tile, n_tiles, BN);
       int64_t orow = -1, rrow = -1;
-      if (A_MODE == 0) {
+      if (AM == 0) {
         const int64_t m = (int64_t)tc.m_blk * BM + r;
         if (m < args.M) orow = m;
       } else {
@@ -608,7 +611,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
             }
           });
         } else if (args.tma_store) {
-          store_tile<BN, A_MODE>(args, &tmOut, my_stage, s_rrow[grp], 1 + grp, chunk_ctr, tc.m_blk, tc.n0, tc.img,
+          store_tile<BN, AM>(args, &tmOut, my_stage, s_rrow[grp], 1 + grp, chunk_ctr, tc.m_blk, tc.n0, tc.img,
                                  tc.oy0, tc.ox0, r, gt, [&](int c, float (&v)[32]) {
                                    uint32_t a[16], b[16];
                                    tmem_ld16_nowait(lane_base + buf * BN + c, a);
@@ -665,7 +668,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
                 for (int j = 0; j < 32; ++j) v[j] = accr[(cb + j) % (SPLIT ? BN : 1)];
           });
         } else if (args.tma_store) {
-          store_tile<BN, A_MODE>(args, &tmOut, my_stage, s_rrow[grp], 1 + grp, chunk_ctr, tc.m_blk, tc.n0, tc.img,
+          store_tile<BN, AM>(args, &tmOut, my_stage, s_rrow[grp], 1 + grp, chunk_ctr, tc.m_blk, tc.n0, tc.img,
                                  tc.oy0, tc.ox0, r, gt, [&](int c, float (&v)[32]) {
 #pragma unroll
                                    for (int cb = 0; cb < BN; cb += 32)
@@ -1358,6 +1361,7 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
     args.tma_store = make_map(&mo, obase, 2, dims, strides, box) ? 1 : 0;
   }
   const int grid_m = (int)((M + BM - 1) / BM);
+  if (epi.a_gate) return dispatch<3>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
   return dispatch<0>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
 }
 
