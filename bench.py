@@ -155,12 +155,12 @@ def barrier(world):
 # or per line (rec), measured by ncu on the full-size bench workload (det
 # batch 64, rec batch 256; profiles/det_b64_launch_list.md).  The roofline's
 # `traffic` is this times the batch, for the dominant family.
-DET_TRAFFIC_PER_IMAGE = {"gemm_tc": 10497110, "conv_tc": 12623699, "dwconv": 15400158,
-                         "convt2x2": 26141910, "conv_direct": 25001176, "resize": 5674939,
-                         "binary": 2067942, "gap": 1383408}
-REC_TRAFFIC_PER_LINE = {"gemm_tc": 116109, "dwconv": 277567, "head_gemm": 54866, "bmm_small": 58286,
-                        "layernorm": 19268, "softmax": 57083, "conv_direct": 212710, "pool2d": 232163,
-                        "head_combine": 94134, "binary": 23152, "copy": 19274}
+DET_TRAFFIC_PER_IMAGE = {"gemm_tc": 10491990, "conv_tc": 12609374, "dwconv": 15406045,
+                         "convt2x2": 26149256, "conv_direct": 25452224, "resize": 5645492,
+                         "gap": 1383436, "det_preprocess": 3216060}
+REC_TRAFFIC_PER_LINE = {"gemm_tc": 115978, "dwconv": 278276, "head_gemm": 54866, "bmm_small": 58288,
+                        "layernorm": 19268, "softmax": 51302, "conv_direct": 207445, "pool2d": 232145,
+                        "head_combine": 94134, "binary": 23150, "copy": 19274}
 TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, profiles/det_b64_launch_list.md, scaled by batch"
 
 
