@@ -488,29 +488,30 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
     const int t = threadIdx.x - 64;
     uint32_t it = 0;
     bool ok = true;
+    const float* gate = GATED ? args.epi.a_gate : nullptr;
+    const int ghw = GATED ? args.epi.a_gate_rows : 1;
+    const int64_t img_last = GATED ? (args.M - 1) / ghw : 0;
     for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      // image of this tile's first row and that row's place in it (rows are
+      // consecutive pixels, so a row's image is img0 + the number of image
+      // boundaries crossed, at most one when an image has >= 128 rows)
+      const int64_t row0 = (int64_t)(tile / n_tiles) * BM;
+      const int64_t img0 = GATED ? row0 / ghw : 0;
+      const int r0 = GATED ? (int)(row0 - img0 * ghw) : 0;
+      const int64_t img1 = GATED ? min(img0 + 1, img_last) : 0;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1u;
-        const float* gate = GATED ? args.epi.a_gate : nullptr;
-        // image of this tile's first row and that row's place in it (rows
-        // are consecutive pixels, so a row's image is img0 + the number of
-        // image boundaries crossed, at most one when an image has >= 128 rows)
-        const int64_t row0 = (int64_t)(tile / n_tiles) * BM;
-        const int ghw = args.epi.a_gate_rows;
-        const int64_t img0 = gate ? row0 / ghw : 0;
-        const int r0 = gate ? (int)(row0 - img0 * ghw) : 0;
         // Chunk i = t + 64 j is row (t >> 3) + 8 j, channel quad (t & 7) ^ ((t >> 3) & 7):
         // the same quad for all of this thread's chunks, so with >= 128-row
         // images only two gate values (this image's, the next one's) occur.
         // They do not depend on the stage's data: load them before its wait.
         float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), gb = ga;
-        if (GATED && gate && ghw >= BM) {
+        if (GATED && ghw >= BM) {
           const int ch = kb * BK + (((t & 7) ^ ((t >> 3) & 7)) << 2);
           if (ch < args.K) {
-            const int64_t img_last = (args.M - 1) / ghw;
             ga = __ldg(reinterpret_cast<const float4*>(gate + img0 * (int64_t)args.K + ch));
-            gb = __ldg(reinterpret_cast<const float4*>(gate + min(img0 + 1, img_last) * (int64_t)args.K + ch));
+            gb = __ldg(reinterpret_cast<const float4*>(gate + img1 * (int64_t)args.K + ch));
           }
         }
         if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
@@ -520,7 +521,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
 #pragma unroll 4
         for (int i = t; i < n4; i += 64) {
           float4 v = a[i];
-          if (GATED && gate) {
+          if (GATED) {
             // logical (row, channel quad) of swizzled 16-byte chunk i
             const int row = i >> 3, c4 = (i & 7) ^ (row & 7);
             const int ch = kb * BK + c4 * 4;
