@@ -104,7 +104,14 @@ typedef struct {
  * the device exactly as the reference engine prepares the det input,
  * v = u8 * (1/255), (v - 0.5) * (1/0.5), HWC -> CHW (engine.rs:963-982), so
  * a run moves a quarter of the bytes across the host and PCIe. */
-enum qpc_dtype { QPC_F32 = 0, QPC_I64 = 1, QPC_U8_IMAGE = 2 };
+/* QPC_F32_DEVICE (run inputs only; no counterpart in the reference) is an
+ * f32 tensor already in this device's memory (`data` is a device pointer): the
+ * run copies it device-to-device on its own stream, so a caller that prepared
+ * the input on the GPU (qpc_op_rec_pack, qpc_op_det_preprocess) hands it over
+ * without a host round trip.  The data must be complete before the call (make
+ * the producing stream finish first) and stay unchanged until the run
+ * completes.  Same plans as QPC_F32. */
+enum qpc_dtype { QPC_F32 = 0, QPC_I64 = 1, QPC_U8_IMAGE = 2, QPC_F32_DEVICE = 3 };
 
 /* A host tensor (tensor.rs:28-40): initializers and run inputs. */
 typedef struct {
@@ -286,6 +293,15 @@ int qpc_op_resize_bilinear_rgb_u8(const uint8_t* src, int n, int sh, int sw, uin
  * v = u8 * (1/255), (v - 0.5) * (1/0.5) into planar n x 3 x dh x dw f32 -
  * the det session's input tensor. */
 int qpc_op_det_preprocess(const uint8_t* src, int n, int sh, int sw, float* dst, int dh, int dw, void* stream);
+
+/* Rec line pack (crates/qppocr-core/src/pipeline/crop.rs:153-185 pack_crop
+ * into the zeroed batch tensor of engine.rs:1425-1440): n uint8 crops (h[k] x
+ * w[k] x 3 at byte offset off[k] of `crops`) -> n x 3 x img_h x img_w f32;
+ * line k is resized to rw[k] x img_h (bilinear, as resize_bilinear_img), then
+ * v = u8 / 255, (v - 0.5) / 0.5; with pad[k] != 0 it is placed unresized,
+ * centred vertically.  Other positions are 0.  All arrays in device memory. */
+int qpc_op_rec_pack(const uint8_t* crops, const int64_t* off, const int* h, const int* w, const int* rw,
+                    const int* pad, int n, int img_h, int img_w, float* out, void* stream);
 
 /* DB post-processing mask (crates/qppocr-core/src/pipeline/geometry.rs:
  * 286-296 with qppocr-kernels resize.rs:213-245 dilate2x2_max): mask =

@@ -357,6 +357,17 @@ def det_normalize(img):
     return out
 
 
+def rec_pack_line(crop, rw, img_h, img_w, pad=False):
+    """crop.rs:153-185 pack_crop of one h x w x 3 uint8 crop into a zeroed
+    [3, img_h, img_w] float32 slot."""
+    crop = np.ascontiguousarray(crop, np.uint8)
+    h, w, _ = crop.shape
+    out = np.empty((3, img_h, img_w), np.float32)
+    lib().orc_rec_pack_line(_u8(crop), ctypes.c_int64(h), ctypes.c_int64(w), ctypes.c_int64(rw),
+                            ctypes.c_int(1 if pad else 0), ctypes.c_int64(img_h), ctypes.c_int64(img_w), _f(out))
+    return out
+
+
 def dilate2x2(mask):
     """resize.rs:213-245 on [n, h, w] uint8."""
     mask = np.ascontiguousarray(mask, np.uint8)

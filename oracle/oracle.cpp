@@ -874,6 +874,32 @@ void orc_resize_bilinear_rgb_u8(const uint8_t* src, int64_t n, int64_t sh, int64
   }, 16);
 }
 
+// crop.rs:153-185 pack_crop into a zeroed [3, img_h, img_w] slot: resize to
+// rw x img_h (resize_bilinear_rgb_u8), v = u8 / 255, (v - 0.5) / 0.5 for
+// columns < rw; or, pad_only, the crop centred vertically, columns <
+// min(w, img_w).
+void orc_rec_pack_line(const uint8_t* crop, int64_t h, int64_t w, int64_t rw, int pad, int64_t img_h,
+                       int64_t img_w, float* dst) {
+  const int64_t plane = img_h * img_w;
+  std::fill(dst, dst + 3 * plane, 0.0f);
+  auto put = [&](int64_t y, int64_t x, const uint8_t* px) {
+    for (int c = 0; c < 3; ++c) {
+      const float v = (float)px[c] / 255.0f;
+      dst[c * plane + y * img_w + x] = (v - 0.5f) / 0.5f;
+    }
+  };
+  if (pad) {
+    const int64_t y0 = (img_h - h) / 2, cols = std::min(w, img_w);
+    for (int64_t y = 0; y < h; ++y)
+      for (int64_t x = 0; x < cols; ++x) put(y + y0, x, crop + (y * w + x) * 3);
+    return;
+  }
+  std::vector<uint8_t> r((size_t)(img_h * rw * 3));
+  orc_resize_bilinear_rgb_u8(crop, 1, h, w, r.data(), img_h, rw);
+  for (int64_t y = 0; y < img_h; ++y)
+    for (int64_t x = 0; x < rw; ++x) put(y, x, r.data() + (y * rw + x) * 3);
+}
+
 // engine.rs:963-982 det input: v = u8 * (1/255), (v - 0.5) * (1/0.5), HWC ->
 // planar CHW.  n images of h x w x 3.
 void orc_det_normalize(const uint8_t* src, int64_t n, int64_t h, int64_t w, float* dst) {

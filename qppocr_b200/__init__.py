@@ -96,6 +96,7 @@ EXPORTED = (
     "qpc_session_destroy", "qpc_session_profile", "qpc_session_profile_step",
     "qpc_session_replay", "qpc_session_node_count", "qpc_session_node", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_ctc_head", "qpc_op_ctc_head_noalloc",
     "qpc_op_split_tf32", "qpc_op_resize_bilinear_rgb_u8", "qpc_op_det_preprocess", "qpc_op_db_mask",
+    "qpc_op_rec_pack",
     "qpc_kernel_error",
 )
 
@@ -148,6 +149,7 @@ def lib():
     L.qpc_op_resize_bilinear_rgb_u8.argtypes = [P, I, I, I, P, I, I, P]
     L.qpc_op_det_preprocess.argtypes = [P, I, I, I, P, I, I, P]
     L.qpc_op_db_mask.argtypes = [P, P, P, I, I, I, ctypes.c_float, I, P]
+    L.qpc_op_rec_pack.argtypes = [P, P, P, P, P, P, I, I, I, P, P]
     L.qpc_op_ctc_head.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P, ctypes.c_int,
                                   P, P]
     L.qpc_op_ctc_head_noalloc.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P,
@@ -215,7 +217,20 @@ def _attr(keep: _Keep, name: str, v) -> QpcAttr:
     return a
 
 
-def _tensor(keep: _Keep, name: str, arr: np.ndarray) -> QpcTensor:
+def _tensor(keep: _Keep, name: str, arr) -> QpcTensor:
+    if hasattr(arr, "is_cuda") and arr.is_cuda:
+        # f32 tensor already on the device (QPC_F32_DEVICE): copied on the GPU
+        import torch
+        assert arr.dtype == torch.float32 and arr.is_contiguous(), "contiguous f32 device tensor expected"
+        keep.add(arr)
+        shp = keep.add((ctypes.c_int64 * max(arr.dim(), 1))(*arr.shape))
+        t = QpcTensor()
+        t.name = keep.add(name.encode())
+        t.shape = shp
+        t.rank = arr.dim()
+        t.dtype = 3
+        t.data = arr.data_ptr()
+        return t
     if arr.dtype == np.int64 or arr.dtype == np.int32:
         arr = keep.add(np.ascontiguousarray(arr, np.int64))
         dt = 1
@@ -274,9 +289,10 @@ def _graph(keep: _Keep, g: Graph) -> QpcGraph:
 class DeferredRun:
     """A submitted run (DeferredRun, device.rs:105-108)."""
 
-    def __init__(self, session: "CudaSession", ticket: ctypes.c_void_p):
+    def __init__(self, session: "CudaSession", ticket: ctypes.c_void_p, keep=None):
         self._s = session
         self._t = ticket
+        self._keep = keep  # device inputs are read by the run's own copy: hold them until it completes
 
     def complete(self, timeout_ms: int = -1) -> List[np.ndarray]:
         L = lib()
@@ -304,6 +320,7 @@ class DeferredRun:
         if self._t:
             lib().qpc_ticket_release(self._t)
             self._t = None
+        self._keep = None
 
     def __del__(self):
         try:
@@ -334,7 +351,7 @@ class CudaSession:
         arr, n = self._inputs(keep, inputs)
         t = ctypes.c_void_p()
         _check(lib().qpc_run_async(self._h, arr, n, ctypes.byref(t)))
-        return DeferredRun(self, t)
+        return DeferredRun(self, t, keep)
 
     def caps(self) -> Dict[str, int]:
         c = QpcCaps()
@@ -531,6 +548,18 @@ def op_db_mask(pred=None, thresh: float = 0.3, dilate: bool = True, mask_in=None
     _check(lib().qpc_op_db_mask(_dptr(pred) if pred is not None else None,
                                 _dptr(mask_in) if mask_in is not None else None, _dptr(out), n, h, w,
                                 ctypes.c_float(thresh), 1 if dilate else 0, stream))
+    return out
+
+
+def op_rec_pack(crops, off, h, w, rw, pad, img_h: int, img_w: int, stream=None):
+    """Device rec line pack (crop.rs:153-185): crops = concatenated uint8 HWC
+    crops, off (int64) / h / w / rw / pad (int32) per line, all device tensors
+    -> [n, 3, img_h, img_w] f32."""
+    import torch
+    n = int(h.numel())
+    out = torch.empty((n, 3, img_h, img_w), dtype=torch.float32, device=crops.device)
+    _check(lib().qpc_op_rec_pack(_dptr(crops), _dptr(off), _dptr(h), _dptr(w), _dptr(rw), _dptr(pad), n, img_h,
+                                 img_w, _dptr(out), stream))
     return out
 
 

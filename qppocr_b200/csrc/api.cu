@@ -412,6 +412,18 @@ int qpc_op_det_preprocess(const uint8_t* src, int n, int sh, int sw, float* dst,
   });
 }
 
+int qpc_op_rec_pack(const uint8_t* crops, const int64_t* off, const int* h, const int* w, const int* rw,
+                    const int* pad, int n, int img_h, int img_w, float* out, void* stream) {
+  if (!crops || !off || !h || !w || !rw || !pad || !out || n < 0 || n > 65535 || img_h <= 0 || img_w <= 0) {
+    set_error("invalid argument");
+    return E_INVALID;
+  }
+  return guarded([&] {
+    QPC_CUDA_OR_THROW(launch_rec_pack(crops, off, h, w, rw, pad, n, img_h, img_w, out, (cudaStream_t)stream));
+    return (int)OK;
+  });
+}
+
 int qpc_op_db_mask(const float* pred, const uint8_t* mask_in, uint8_t* mask, int n, int h, int w, float thresh,
                    int dilate, void* stream) {
   if ((!pred && !mask_in) || !mask || n < 0 || h <= 0 || w <= 0) {

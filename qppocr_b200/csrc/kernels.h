@@ -116,6 +116,13 @@ cudaError_t launch_resize_bilinear_rgb_u8(const uint8_t* src, int n, int sh, int
 // (u8 / 255 - 0.5) * 2 into planar n x 3 x dh x dw f32.
 cudaError_t launch_det_preprocess(const uint8_t* src, int n, int sh, int sw, float* dst, int dh, int dw,
                                   cudaStream_t st);
+// Rec line pack (crop.rs:153-185 into engine.rs:1425-1440's zeroed batch): n
+// uint8 crops (h x w x 3 at byte offsets off) -> n x 3 x img_h x img_w f32,
+// line k resized to rws[k] x img_h (or centred unresized when pads[k]).
+// All arrays on the device.
+cudaError_t launch_rec_pack(const uint8_t* crops, const int64_t* off, const int* hs, const int* ws,
+                            const int* rws, const int* pads, int n, int img_h, int img_w, float* out,
+                            cudaStream_t st);
 // DB mask (geometry.rs:286-296): pred > thresh (or an existing u8 mask when
 // pred is null), then the 2x2 dilation when `dilate`.
 cudaError_t launch_db_mask(const float* pred, const uint8_t* mask_in, uint8_t* out, int n, int h, int w,

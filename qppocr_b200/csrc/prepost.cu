@@ -148,6 +148,58 @@ __global__ void __launch_bounds__(256) db_mask_kernel(const float* __restrict__ 
   }
 }
 
+// Rec line pack (crop.rs:153-185 pack_crop into the zeroed batch tensor of
+// engine.rs:1425-1440): line k (an h x w x 3 uint8 crop at byte offset
+// off[k]) becomes rows 0..img_h-1, columns 0..rw-1 of batch item k: bilinear
+// resize to rw x img_h, then v = u8 / 255, (v - 0.5) / 0.5; or, pad_only, the
+// crop itself centred vertically (columns < min(w, img_w)).  Everything else
+// is 0.  One block row (blockIdx.y) per line.
+__global__ void __launch_bounds__(256) rec_pack_kernel(const uint8_t* __restrict__ crops,
+                                                       const int64_t* __restrict__ off, const int* __restrict__ hs,
+                                                       const int* __restrict__ ws, const int* __restrict__ rws,
+                                                       const int* __restrict__ pads, float* __restrict__ out,
+                                                       int img_h, int img_w) {
+  const int k = blockIdx.y;
+  const int h = hs[k], w = ws[k], rw = rws[k], pad = pads[k];
+  const uint8_t* src = crops + off[k];
+  const int64_t plane = (int64_t)img_h * img_w;
+  float* dst = out + (int64_t)k * 3 * plane;
+  ResizeMap m;
+  m.sw = w;
+  m.sh = h;
+  m.dw = rw;
+  m.dh = img_h;
+  m.sx = __fdiv_rn((float)w, (float)rw);
+  m.sy = __fdiv_rn((float)h, (float)img_h);
+  const int y0 = (img_h - h) / 2, cols = min(w, img_w);
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < img_h * img_w; i += gridDim.x * blockDim.x) {
+    const int y = i / img_w, x = i - y * img_w;
+    float o[3] = {0.f, 0.f, 0.f};
+    bool have = false;
+    uint8_t px[3];
+    if (pad) {
+      if (y >= y0 && y < y0 + h && x < cols) {
+        const uint8_t* p = src + ((int64_t)(y - y0) * w + x) * 3;
+        px[0] = p[0];
+        px[1] = p[1];
+        px[2] = p[2];
+        have = true;
+      }
+    } else if (x < rw) {
+      resized_rgb(src, m, 0, x, y, px);
+      have = true;
+    }
+    if (have)
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        const float v = __fdiv_rn((float)px[c], 255.0f);
+        o[c] = __fdiv_rn(__fsub_rn(v, 0.5f), 0.5f);
+      }
+#pragma unroll
+    for (int c = 0; c < 3; ++c) dst[c * plane + i] = o[c];
+  }
+}
+
 int grid_of(int64_t items) {
   const int64_t blocks = (items + 255) / 256;
   const int64_t cap = 148LL * 16;
@@ -182,6 +234,17 @@ cudaError_t launch_det_preprocess(const uint8_t* src, int n, int sh, int sw, flo
   if (n == 0) return cudaSuccess;
   det_preprocess_kernel<<<grid_of((int64_t)n * dh * dw), 256, 0, st>>>(
       src, dst, n, make_map(sh, sw, dh, dw), (sh == dh && sw == dw) ? 1 : 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rec_pack(const uint8_t* crops, const int64_t* off, const int* hs, const int* ws,
+                            const int* rws, const int* pads, int n, int img_h, int img_w, float* out,
+                            cudaStream_t st) {
+  if (n < 0 || img_h <= 0 || img_w <= 0 || n > 65535) return cudaErrorInvalidValue;
+  if (n == 0) return cudaSuccess;
+  const int per = img_h * img_w;
+  dim3 grid((per + 255) / 256, n);
+  rec_pack_kernel<<<grid, 256, 0, st>>>(crops, off, hs, ws, rws, pads, out, img_h, img_w);
   return cudaGetLastError();
 }
 

@@ -788,12 +788,12 @@ class Planner {
       for (int k = 0; k < n_inputs; ++k)
         if (gi == inputs[k].name) t = &inputs[k];
       if (!t) throw GraphError{"missing graph input " + gi};
-      if (t->dtype != QPC_F32 && t->dtype != QPC_U8_IMAGE)
+      if (t->dtype != QPC_F32 && t->dtype != QPC_F32_DEVICE && t->dtype != QPC_U8_IMAGE)
         throw GraphError{"graph input " + gi + " must be f32 (or a u8 image batch)"};
       Val v;
       PlanInstance::IO io;
       io.name = gi;
-      io.dtype = t->dtype;
+      io.dtype = t->dtype == QPC_F32_DEVICE ? QPC_F32 : t->dtype;  // host or device f32: same plan
       if (t->dtype == QPC_U8_IMAGE) {
         // n x h x w x 3 u8 images for an [n, 3, h, w] f32 input: staged as
         // bytes, normalised on the device as the reference engine does
@@ -2122,7 +2122,7 @@ class Planner {
 static std::string shape_key(const qpc_tensor* in, int n) {
   std::ostringstream o;
   for (int k = 0; k < n; ++k) {
-    o << (in[k].name ? in[k].name : "") << ":d" << in[k].dtype << ":";
+    o << (in[k].name ? in[k].name : "") << ":d" << (in[k].dtype == QPC_F32_DEVICE ? QPC_F32 : in[k].dtype) << ":";
     for (int d = 0; d < in[k].rank; ++d) o << in[k].shape[d] << "x";
     o << ";";
   }
@@ -2223,8 +2223,12 @@ PlanInstance* Session::launch(const qpc_tensor* inputs, int n) {
       const qpc_tensor* t = nullptr;
       for (int k = 0; k < n; ++k)
         if (io.name == inputs[k].name) t = &inputs[k];
-      if (t->dtype != io.dtype) throw GraphError{"input " + io.name + ": dtype differs from the plan's"};
-      QPC_CUDA_OR_THROW(staged_h2d(io.dev, io.host, t->data, io.bytes, p->stream));
+      const int dt = t->dtype == QPC_F32_DEVICE ? QPC_F32 : t->dtype;
+      if (dt != io.dtype) throw GraphError{"input " + io.name + ": dtype differs from the plan's"};
+      if (t->dtype == QPC_F32_DEVICE)
+        QPC_CUDA_OR_THROW(cudaMemcpyAsync(io.dev, t->data, io.bytes, cudaMemcpyDeviceToDevice, p->stream));
+      else
+        QPC_CUDA_OR_THROW(staged_h2d(io.dev, io.host, t->data, io.bytes, p->stream));
     }
     QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[1], p->stream));
     if (p->exec) {

@@ -1,0 +1,194 @@
+"""Recognition stage around a rec session: the reference engine's line
+grouping, batch packing, pipelined submission and CTC decoding, with the
+packing on the device.
+
+  * lines sorted by width ratio, stably (engine.rs:1162-1163), ratio = w / h
+    (crop.rs:136-145 batch_ratio);
+  * consecutive lines grouped while their raw widths (img_h * ratio,
+    truncated) stay within one width grain of the group's first line, at most
+    `per_batch` lines (engine.rs:1238-1286, the default relative-span rule;
+    the grain and per_batch default to the session's bucket_grain and
+    rec_chunk, device.rs:139-163);
+  * batch width = img_h * max(rec_min_width / img_h, max ratio), truncated,
+    rounded up to the grain (engine.rs:1416-1423);
+  * each line resized to ceil(img_h * w / h) x img_h (at most the batch width)
+    and normalised (v / 255 - 0.5) / 0.5 into a zeroed batch
+    (crop.rs:153-185, engine.rs:1425-1440) - on the device, by
+    qpc_op_rec_pack;
+  * batch k + 1 packed and submitted while batch k runs (run_deferred,
+    engine.rs:1409-1450), the packed batch handed over as a device tensor;
+  * greedy CTC decoding of the (value, index) pairs of the argmax exit
+    (rec.rs:82-120) or of full probabilities (rec.rs:34-79).
+"""
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from . import op_rec_pack
+
+F32 = np.float32
+
+
+def crop_pads(h: int, img_h: int, pad_min_h: float) -> bool:
+    """crop.rs:129-131: a crop close to img_h is centred, not resized."""
+    return pad_min_h > 0.0 and 0 < h <= img_h and h >= pad_min_h * img_h
+
+
+def batch_ratio(h: int, w: int, img_h: int, pad_min_h: float = 0.0) -> np.float32:
+    """crop.rs:136-145 (f32)."""
+    if h <= 0:
+        return F32(1.0)
+    if crop_pads(h, img_h, pad_min_h):
+        return F32(w) / F32(img_h)
+    return F32(w) / F32(h)
+
+
+def raw_width(img_h: int, ratio) -> int:
+    """engine.rs:1228: (img_h as f32 * r) as i32."""
+    return int(F32(img_h) * F32(ratio))
+
+
+def group_lines(ratios_sorted: Sequence, img_h: int, grain: int, per_batch: int) -> List[Tuple[int, int]]:
+    """engine.rs:1238-1286 (relative span when grain > 1, else fixed chunks):
+    [begin, end) ranges over the ratio-sorted lines."""
+    n = len(ratios_sorted)
+    out = []
+    beg = 0
+    while beg < n:
+        end = beg + 1
+        if grain > 1:
+            w0 = raw_width(img_h, ratios_sorted[beg])
+            while end < n and end - beg < per_batch and raw_width(img_h, ratios_sorted[end]) - w0 <= grain:
+                end += 1
+        else:
+            end = min(beg + per_batch, n)
+        out.append((beg, end))
+        beg = end
+    return out
+
+
+def batch_width(ratios: Sequence, img_h: int, min_width: int, grain: int) -> int:
+    """engine.rs:1416-1423."""
+    m = F32(min_width) / F32(img_h)
+    for r in ratios:
+        m = max(m, F32(r))
+    w = int(F32(img_h) * m)
+    if grain > 1:
+        w = (w + grain - 1) // grain * grain
+    return w
+
+
+def resized_width(h: int, w: int, img_h: int, img_w: int) -> int:
+    """crop.rs:171-173: ceil(img_h * (w / h)), clamped to [1, img_w]."""
+    ratio = F32(w) / F32(h)
+    rw = int(np.ceil(F32(img_h) * ratio))
+    return max(min(rw, img_w), 1)
+
+
+def ctc_decode_pairs(pairs, charset: Optional[Sequence[str]] = None):
+    """rec.rs:82-120: pairs [T, 2] = (value, index as f32 bits).  A step emits
+    when its index is not 0 (blank) and differs from the previous step's;
+    conf = f64 mean of the emitted steps' values.  Returns (indices or text,
+    conf)."""
+    pairs = np.asarray(pairs, np.float32).reshape(-1, 2)
+    idx = pairs[:, 1].copy().view(np.uint32).astype(np.int64)
+    vals = pairs[:, 0]
+    out, conf_sum, conf_n, prev = [], 0.0, 0, -1
+    for t in range(pairs.shape[0]):
+        b = int(idx[t])
+        if b != 0 and b != prev:
+            if charset is None or b < len(charset):
+                out.append(b)
+            conf_sum += float(vals[t])
+            conf_n += 1
+        prev = b
+    conf = np.float32(conf_sum / conf_n) if conf_n else np.float32(0.0)
+    if charset is not None:
+        return "".join(charset[i] for i in out), conf
+    return out, conf
+
+
+def ctc_decode_probs(probs, charset: Optional[Sequence[str]] = None):
+    """rec.rs:34-79 on one line's [T, C] probabilities (first strict max)."""
+    probs = np.asarray(probs, np.float32)
+    best = np.argmax(probs, axis=1)  # numpy: first maximum, as the reference's strict '>'
+    pairs = np.empty((probs.shape[0], 2), np.float32)
+    pairs[:, 0] = probs[np.arange(probs.shape[0]), best]
+    pairs[:, 1] = best.astype(np.uint32).view(np.float32)
+    return ctc_decode_pairs(pairs, charset)
+
+
+class RecStage:
+    """Lines (uint8 h x w x 3 crops) -> (text or indices, confidence), through
+    a rec session created by CudaContext.create_session(role="rec")."""
+
+    def __init__(self, session, img_h: int = 48, min_width: int = 16, pad_min_h: float = 0.0,
+                 grain: Optional[int] = None, per_batch: Optional[int] = None, charset=None, device: int = 0):
+        self.s = session
+        self.img_h = img_h
+        self.min_width = min_width
+        self.pad_min_h = pad_min_h
+        self.grain = session.bucket_grain() if grain is None else grain
+        self.per_batch = session.rec_chunk() if per_batch is None else per_batch
+        self.charset = charset
+        self.pairs = session.rec_argmax_pairs()
+        self.device = device
+        self.batches = 0
+
+    def plan(self, shapes: Sequence[Tuple[int, int]]):
+        """Order, batches and per-line widths for crops of these (h, w)."""
+        ratios = [batch_ratio(h, w, self.img_h, self.pad_min_h) for h, w in shapes]
+        order = sorted(range(len(shapes)), key=lambda i: ratios[i])  # stable, as sort_by
+        groups = group_lines([ratios[i] for i in order], self.img_h, self.grain, self.per_batch)
+        out = []
+        for beg, end in groups:
+            ids = order[beg:end]
+            img_w = batch_width([ratios[i] for i in ids], self.img_h, self.min_width, self.grain)
+            out.append((ids, img_w))
+        return out
+
+    def run(self, crops: Sequence[np.ndarray]):
+        import torch
+
+        shapes = [(int(c.shape[0]), int(c.shape[1])) for c in crops]
+        batches = self.plan(shapes)
+        dev = torch.device("cuda", self.device)
+        # all crops uploaded once, back to back
+        sizes = [c.size for c in crops]
+        offs = np.zeros(len(crops), np.int64)
+        if len(crops) > 1:
+            offs[1:] = np.cumsum(sizes)[:-1]
+        host = np.empty(max(int(sum(sizes)), 1), np.uint8)
+        for i, c in enumerate(crops):
+            host[offs[i]:offs[i] + sizes[i]] = np.ascontiguousarray(c, np.uint8).reshape(-1)
+        blob = torch.from_numpy(host).pin_memory().to(dev, non_blocking=True)
+        results: List = [None] * len(crops)
+
+        def submit(ids, img_w):
+            pads = [crop_pads(shapes[i][0], self.img_h, self.pad_min_h) for i in ids]
+            rws = [min(shapes[i][1], img_w) if p else resized_width(shapes[i][0], shapes[i][1], self.img_h, img_w)
+                   for i, p in zip(ids, pads)]
+            meta = np.array([[shapes[i][0], shapes[i][1], rw, int(p)] for i, rw, p in zip(ids, rws, pads)], np.int32)
+            m = torch.from_numpy(np.ascontiguousarray(meta.T)).to(dev)
+            o = torch.from_numpy(offs[list(ids)]).to(dev)
+            x = op_rec_pack(blob, o, m[0].contiguous(), m[1].contiguous(), m[2].contiguous(), m[3].contiguous(),
+                            self.img_h, img_w)
+            torch.cuda.current_stream(dev).synchronize()  # packed before the session's stream copies it
+            self.batches += 1
+            return self.s.run_deferred({"x": x})
+
+        pending = None
+        for ids, img_w in batches:
+            d = submit(ids, img_w)
+            if pending is not None:
+                self._finish(*pending, results)
+            pending = (d, ids)
+        if pending is not None:
+            self._finish(*pending, results)
+        return results
+
+    def _finish(self, d, ids, results):
+        out = d.complete()[0]
+        for k, i in enumerate(ids):
+            results[i] = ctc_decode_pairs(out[k], self.charset) if self.pairs else ctc_decode_probs(out[k],
+                                                                                                    self.charset)

@@ -1,0 +1,52 @@
+"""Host logic of the recognition stage (engine.rs:1160-1500, crop.rs:129-185,
+rec.rs:34-120) on hand-worked cases and against the oracle's CTC decoder."""
+import numpy as np
+
+import oracle as orc
+from qppocr_b200 import rec_pipeline as rp
+
+
+def test_group_lines_relative_span():
+    # raw widths at img_h 48: 48, 96, 120, 192, 480 (grain 64)
+    ratios = [np.float32(r) for r in (1.0, 2.0, 2.5, 4.0, 10.0)]
+    assert rp.group_lines(ratios, 48, 64, 256) == [(0, 2), (2, 3), (3, 4), (4, 5)]
+    # per_batch caps a group
+    assert rp.group_lines([np.float32(1.0)] * 5, 48, 64, 2) == [(0, 2), (2, 4), (4, 5)]
+    # grain <= 1: fixed chunks
+    assert rp.group_lines(ratios, 48, 1, 2) == [(0, 2), (2, 4), (4, 5)]
+
+
+def test_batch_width_and_resized_width():
+    assert rp.batch_width([np.float32(1.0), np.float32(2.0)], 48, 16, 64) == 128  # 96 -> 128
+    assert rp.batch_width([np.float32(0.2)], 48, 16, 64) == 64                    # min width 16 -> 64
+    assert rp.batch_width([np.float32(2.0)], 48, 16, 1) == 96                     # no rounding
+    assert rp.resized_width(32, 100, 48, 512) == 150                               # ceil(48 * 3.125)
+    assert rp.resized_width(32, 100, 48, 128) == 128                               # clamped to the batch
+    assert rp.resized_width(1000, 1, 48, 128) == 1                                 # at least 1
+
+
+def test_batch_ratio_and_pads():
+    assert rp.batch_ratio(32, 96, 48) == np.float32(3.0)
+    assert not rp.crop_pads(40, 48, 0.0)          # default pad_min_h = 0: never pad-only
+    assert rp.crop_pads(40, 48, 0.8)
+    assert rp.batch_ratio(40, 96, 48, 0.8) == np.float32(2.0)  # w / img_h when pad-only
+
+
+def test_ctc_decode_pairs_matches_oracle():
+    rng = np.random.Generator(np.random.PCG64(2))
+    for _ in range(20):
+        t, c = 40, 30
+        logits = rng.standard_normal((t, c)).astype(np.float32) * 3
+        logits[rng.uniform(size=t) < 0.4, 0] += 6  # plenty of blanks
+        p = np.exp(logits - logits.max(1, keepdims=True)).astype(np.float32)
+        p /= p.sum(1, keepdims=True)
+        pairs = orc.argmax_pairs(p)
+        got_i, got_c = rp.ctc_decode_pairs(pairs)
+        ref_i, ref_c = orc.ctc_decode(p)
+        assert got_i == ref_i and got_c == ref_c
+        assert rp.ctc_decode_probs(p) == (ref_i, ref_c)
+    # charset: indices past it are skipped in the text but count for conf
+    pairs = np.array([[0.9, 0], [0.8, 2], [0.7, 5], [0.6, 1]], np.float32)
+    pairs[:, 1] = pairs[:, 1].astype(np.uint32).view(np.float32)
+    text, conf = rp.ctc_decode_pairs(pairs, charset=["_", "a", "b"])
+    assert text == "ba" and conf == np.float32((0.8 + 0.7 + 0.6) / 3)
