@@ -397,13 +397,30 @@ def main():
         rms = max_over_ranks(rs.replay({"x": xr}, args.steps), world)
         rprof = rs.profile({"x": xr}, iters=2)
         re2e = max_over_ranks(e2e_seconds(rs, {"x": xr}, args.steps, world), world)
+        # the recognition stage around the session (grouping by width, device
+        # line pack, two batches in flight, CTC decode) on variable-size crops
+        from qppocr_b200.rec_pipeline import RecStage
+
+        crng = np.random.Generator(np.random.PCG64(40 + rank))
+        crops = [crng.integers(0, 256, (int(crng.integers(24, 65)), int(crng.integers(32, 401)), 3),
+                               dtype=np.uint8) for _ in range(1024)]
+        stage = RecStage(rs)
+        stage.run(crops)  # plans for every batch width
+        barrier(world)
+        t0 = time.perf_counter()
+        stage.run(crops)
+        st_s = max_over_ranks(time.perf_counter() - t0, world)
         rec = {"metric": "rec_lines_per_s", "value": round(world * args.rec_batch / (rms / 1000.0), 1),
                "unit": "lines/s", "ms_per_step": round(rms, 3), "batch": args.rec_batch,
                "roofline": roofline(rprof, hbm, tf, REC_TRAFFIC_PER_LINE, args.rec_batch),
                "e2e": {"value": round(world * args.rec_batch / re2e, 1), "unit": "lines/s",
                        "h2d_bytes_per_step": int(xr.nbytes),
                        "d2h_bytes_per_step": int(args.rec_batch * 40 * 2 * 4), "timing": E2E_TIMING},
-               "gpu_launches": len(rprof) * args.steps}
+               "gpu_launches": len(rprof) * args.steps,
+               "stage": {"value": round(world * len(crops) / st_s, 1), "unit": "lines/s", "lines": len(crops),
+                         "crops": "uint8, h 24-64, w 32-400 (seeded)",
+                         "timing": "wall clock of RecStage.run: width grouping, crop upload, device line pack, "
+                                   "two batches in flight, CTC decode of the argmax pairs"}}
         rs.close()
 
     cpu = None
