@@ -318,13 +318,15 @@ cudaError_t launch_dwconv_nhwc(const float* x, const float* wt, const float* bia
     // per geometry, the configuration measured fastest on the det backbone
     if (g.kh == 3 && g.sh == 1)
       e = c32 ? run_dw_tile<3, 1, 32, 32, 8, 2>(x, wt, bias, residual, y, g, act, err, st)
-              : run_dw_tile<3, 1, 16, 32, 8, 2>(x, wt, bias, residual, y, g, act, err, st);
+              : run_dw_tile<3, 1, 16, 32, 16, 2>(x, wt, bias, residual, y, g, act, err, st);
     else if (g.kh == 3 && g.sh == 2)
       e = c32 ? run_dw_tile<3, 2, 32, 16, 8, 1>(x, wt, bias, residual, y, g, act, err, st)
               : run_dw_tile<3, 2, 16, 16, 8, 1>(x, wt, bias, residual, y, g, act, err, st);
+    else if (g.kh == 5 && g.sh == 1 && c32)
+      e = g.ow <= 32 ? run_dw_tile<5, 1, 32, 10, 16, 2>(x, wt, bias, residual, y, g, act, err, st)
+                     : run_dw_tile<5, 1, 32, 20, 8, 2>(x, wt, bias, residual, y, g, act, err, st);
     else if (g.kh == 5 && g.sh == 1)
-      e = c32 ? run_dw_tile<5, 1, 32, 32, 8, 1>(x, wt, bias, residual, y, g, act, err, st)
-              : run_dw_tile<5, 1, 16, 32, 8, 1>(x, wt, bias, residual, y, g, act, err, st);
+      e = run_dw_tile<5, 1, 16, 32, 8, 1>(x, wt, bias, residual, y, g, act, err, st);
     else if (g.kh == 5 && g.sh == 2)
       e = c32 ? run_dw_tile<5, 2, 32, 16, 8, 1>(x, wt, bias, residual, y, g, act, err, st)
               : run_dw_tile<5, 2, 16, 16, 8, 1>(x, wt, bias, residual, y, g, act, err, st);

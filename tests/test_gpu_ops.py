@@ -42,6 +42,8 @@ def dev(a):
     (1, 23, 50, 64, 5, (2, 2), None, True),
     (3, 8, 33, 16, 5, (1, 1), "sigmoid", False),
     (1, 3, 2, 32, 3, (1, 1), "hswish", True),
+    (1, 30, 30, 64, 5, (1, 1), "hswish", True),    # 5x5, narrow map: 10 x 16 tiles
+    (1, 50, 70, 16, 3, (1, 1), "relu", False),     # 16 channels: 32 x 16 tiles
 ])
 def test_dwconv_bit_exact(cuda_ctx, n, h, w, c, k, s, act, res):
     import torch
