@@ -3,9 +3,11 @@ convs on the row-packed GEMM), one Conv node
 per graph, against the oracle's conv (qppocr-kernels conv.rs im2col + panel
 GEMM), metric max|d|/max|ref| (reference tests/kernels.rs:51-77).
 
-The cases cover the three implicit-GEMM tilings: in TF32, output rows >= 64
-wide with at most 64 output channels and a filter that fits in shared memory
-take the row-band tiling (4 output rows per tile, resident filter); other
+The cases cover the implicit-GEMM tilings: in TF32, kernels at most 3 wide
+with at most 32 output channels take the kx-folded band (the kw taps stacked
+in N), output rows >= 64 wide with at most 64 output channels and a filter
+that fits in shared memory the row-band tiling (4 output rows per tile,
+resident filter); other
 rows >= 64 wide take the halo-row tiling (one 128-pixel row per tile, kernel
 taps as shifted views of one staged halo row); narrower rows the 2-D
 pixel-tile tiling.  Edges cover
@@ -25,7 +27,9 @@ TOL = {"tf32": 1e-3, "3xtf32": 1e-5}
 
 # (batch, cin, cout, k, h, w, act, residual)
 CASES = [
-    (2, 96, 24, 3, 40, 240, None, False),    # band (tf32) / halo, DBFPN-like, 2 row tiles (128 + 112)
+    (2, 96, 24, 3, 40, 240, None, False),    # kx-folded band (tf32) / halo, DBFPN-like, 2 x-tiles
+    (1, 48, 16, 3, 7, 200, "relu", False),   # kx-folded, M = 16, ragged channel block, 7 rows
+    (1, 24, 24, 3, 20, 64, None, True),      # kx-folded with a residual
     (1, 64, 64, 3, 17, 128, "relu", True),   # halo (filter too big for band), relu + residual
     (1, 32, 32, 3, 13, 150, "relu", True),   # band, 13 rows = 3 full bands + 1, relu + residual
     (1, 20, 40, 3, 9, 200, None, False),     # band N=40 (64-col tile), ragged channel block (20 of 32)
