@@ -302,6 +302,48 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def gemm_sweep(args):
+    """Config 2: X [M, K] U[-1, 1] x W [K, N] + bias + hardswish through
+    qpc_op_gemm, inputs resident, CUDA events over 20 launches after warm-up;
+    one markdown row per (M, K, N, math)."""
+    import numpy as np
+    import torch
+
+    import qppocr_b200 as q
+    from qppocr_b200 import nets
+
+    hbm, tf, _ = peaks()
+    tf32_peak = tf / 2  # dense TF32 is half the dense bf16 rate
+    print("| M | K | N | math | us | GB/s | TFLOP/s | HBM frac | TF32 frac |")
+    print("|---:|---:|---:|---|---:|---:|---:|---:|---:|")
+    for m in nets.GEMM_SWEEP_M:
+        for k, n in nets.GEMM_SWEEP_KN:
+            x, w, b = nets.gemm_case(m, k, n)
+            xd = torch.from_numpy(x).cuda()
+            wd = torch.from_numpy(np.ascontiguousarray(w.T)).cuda()  # [N, K]
+            bd = torch.from_numpy(np.concatenate([b, np.zeros(16, np.float32)])).cuda()
+            yd = torch.empty((m, n), dtype=torch.float32, device="cuda")
+            for math in ("tf32", "3xtf32"):
+                if math == "tf32":
+                    wh, wl = q.op_split_tf32(wd)[0], None
+                else:
+                    wh, wl = q.op_split_tf32(wd)
+                for _ in range(3):
+                    q.op_gemm(xd, wh, w_lo=wl, bias=bd, act="hswish", math=math, out=yd)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(20):
+                    q.op_gemm(xd, wh, w_lo=wl, bias=bd, act="hswish", math=math, out=yd)
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) / 20 * 1e3
+                by = 4.0 * (m * k + m * n + k * n)
+                fl = 2.0 * m * k * n
+                print(f"| {m} | {k} | {n} | {math} | {us:.1f} | {by / us / 1e3:.0f} | {fl / us / 1e6:.1f} | "
+                      f"{by / us / 1e3 / hbm:.2f} | {fl / us / 1e6 / tf32_peak:.2f} |", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -313,6 +355,8 @@ def main():
     ap.add_argument("--math", default="tf32", choices=["tf32", "3xtf32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-rec", action="store_true")
+    ap.add_argument("--gemm-sweep", action="store_true",
+                    help="config 2: time the pointwise GEMM over its M x (K, N) grid and print a table")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -320,6 +364,9 @@ def main():
         # (no process group: the reference arm has no collective)
         world = int(os.environ.get("WORLD_SIZE", "1"))
         run_reference(args, world, int(os.environ.get("RANK", "0")))
+        return
+    if args.gemm_sweep:
+        gemm_sweep(args)
         return
     world, rank, local = dist_init()
 
