@@ -82,7 +82,9 @@ class Pool {
 
  private:
   Pool() {
+    // the host's cores shared by the processes of this node (one per GPU)
     int n = (int)std::thread::hardware_concurrency();
+    if (const char* lw = std::getenv("LOCAL_WORLD_SIZE")) n /= std::max(1, std::atoi(lw));
     if (const char* env = std::getenv("QPPOCR_CUDA_COPY_THREADS")) n = std::atoi(env) + 1;
     n = std::max(1, std::min(n, 16)) - 1;  // the caller is the n-th copier
     for (int i = 0; i < n; ++i) workers_.emplace_back([this] { loop(); });
