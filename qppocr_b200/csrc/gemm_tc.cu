@@ -118,9 +118,10 @@ struct RowMap {
 template <int A_MODE>
 __device__ __forceinline__ RowMap row_map(const GemmArgs& args, int m_blk, int img, int oy0, int ox0,
                                           int r) {
+  // Row counts are below 2^31 (GemmArgs::M is an int): 32-bit index math.
   RowMap m{-1, -1};
   if (A_MODE == 0) {
-    const int64_t row = (int64_t)m_blk * BM + r;
+    const int row = m_blk * BM + r;
     if (row < args.M) m.orow = row;
   } else {
     const int oy = oy0 + r / args.tw, ox = ox0 + r % args.tw;
@@ -130,14 +131,16 @@ __device__ __forceinline__ RowMap row_map(const GemmArgs& args, int m_blk, int i
   const GemmEpilogue& e = args.epi;
   if (m.orow >= 0 && e.residual && e.rh > 0) {
     // nearest resize source row, resize.rs:43-50: (int)((float)o * in / out)
-    const int x = (int)(m.orow % e.ow);
-    const int y = (int)((m.orow / e.ow) % e.oh);
-    const int64_t nn = m.orow / ((int64_t)e.ow * e.oh);
+    const unsigned o = (unsigned)m.orow;
+    const unsigned yx = o / (unsigned)e.ow;
+    const int x = (int)(o - yx * (unsigned)e.ow);
+    const unsigned nn = yx / (unsigned)e.oh;
+    const int y = (int)(yx - nn * (unsigned)e.oh);
     int iy = (int)__fdiv_rn(__fmul_rn((float)y, (float)e.rh), (float)e.oh);
     int ix = (int)__fdiv_rn(__fmul_rn((float)x, (float)e.rw), (float)e.ow);
     iy = iy < e.rh - 1 ? iy : e.rh - 1;
     ix = ix < e.rw - 1 ? ix : e.rw - 1;
-    m.rrow = (nn * e.rh + iy) * e.rw + ix;
+    m.rrow = ((int64_t)nn * e.rh + iy) * e.rw + ix;
   }
   return m;
 }
@@ -293,16 +296,90 @@ __device__ __forceinline__ void argmax_tile(const GemmArgs& args, int64_t orow, 
   if (orow >= 0) e.partials[(int64_t)n_blk * args.M + orow] = make_float4(m, __uint_as_float((unsigned)mi), s, 0.f);
 }
 
+// ConvT pair epilogue for one tile (A_MODE 4, launch_convt_pair): row r is
+// input pixel `orow` of the first ConvT and its 128 columns are that layer's
+// outputs for the sub-pixels s = 2 dy + dx, 32 columns each.  Per sub-pixel:
+// BN (fma(acc, scale, shift)), act1, then the second ConvT's four outputs
+// sum_m z[m] * w2[m][ey][ex] (m ascending, fma from 0; padding columns carry
+// zero weights) and act2.  The pixel's 4 x 4 output block leaves as four
+// 16-byte row segments (a warp's 32 pixels write 512 contiguous bytes per
+// output row).  `cs` is the shared-memory copy of scale, shift and w2.
+template <class Consts, class Fetch>
+__device__ __forceinline__ void pair_tile(const GemmArgs& args, int64_t orow, const Consts& pc,
+                                          Fetch&& fetch) {
+  const GemmEpilogue& e = args.epi;
+  const int64_t ow = 4 * (int64_t)e.pair_w;
+  float* dst = nullptr;
+  if (orow >= 0) {
+    const int64_t hw = (int64_t)e.pair_h * e.pair_w;
+    const int64_t img = orow / hw;
+    const int rem = (int)(orow - img * hw);
+    const int y = rem / e.pair_w, x = rem - y * e.pair_w;
+    dst = e.out + ((img * 4 * e.pair_h + 4 * y) * ow + 4 * x);
+  }
+#pragma unroll
+  for (int dy = 0; dy < 2; ++dy) {
+    float o[8];  // output rows 4y + 2 dy + ey, columns 4x + 2 dx + ex: [ey][2 dx + ex]
+#pragma unroll
+    for (int dx = 0; dx < 2; ++dx) {
+      const int s = 2 * dy + dx;
+      float v[32];
+      fetch(32 * s, v);  // warp-collective
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __fmaf_rn(v[j], pc.scale[32 * s + j], pc.shift[32 * s + j]);
+      apply_act_n(v, e.act);
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+      for (int m = 0; m < 32; ++m) {
+        a0 = __fmaf_rn(v[m], pc.w2[m][0], a0);
+        a1 = __fmaf_rn(v[m], pc.w2[m][1], a1);
+        a2 = __fmaf_rn(v[m], pc.w2[m][2], a2);
+        a3 = __fmaf_rn(v[m], pc.w2[m][3], a3);
+      }
+      o[2 * dx] = a0;
+      o[2 * dx + 1] = a1;
+      o[4 + 2 * dx] = a2;
+      o[4 + 2 * dx + 1] = a3;
+    }
+    apply_act_n(o, e.pair_act);
+    if (dst) {
+      *reinterpret_cast<float4*>(dst + (2 * dy) * ow) = make_float4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<float4*>(dst + (2 * dy + 1) * ow) = make_float4(o[4], o[5], o[6], o[7]);
+    }
+  }
+}
+
 // Warp roles: w0 TMA producer, w1 MMA issuer, w2-3 convert A, then 4-warp
 // epilogue groups that take tiles round-robin (their serial TMEM -> smem ->
 // TMA-store chains overlap).  TF32 runs 4 groups for 32-column N tiles,
 // where a tile carries little work and the chain's latency sets the pace, and
 // 2 otherwise; 3xTF32 keeps one group, whose registers hold the promoted
 // accumulator.
-template <int BN, bool SPLIT>
+// The ConvT pair mode (A_MODE 4) runs 4 groups: its epilogue is arithmetic
+// (a second layer per row), and it stages no output in shared memory.
+template <int BN, bool SPLIT, int A_MODE = 0>
 struct Roles {
-  static constexpr int EPI_GROUPS = SPLIT ? 1 : (BN <= 32 ? 4 : 2);
+  static constexpr int EPI_GROUPS = SPLIT ? 1 : ((BN <= 32 || A_MODE == 4) ? 4 : 2);
   static constexpr int THREADS = 128 + 128 * EPI_GROUPS;
+  static constexpr int STAGING = A_MODE == 4 ? 0 : EPI_GROUPS * 2 * OUT_STAGE_BYTES;
+};
+
+// Per-mode constants passed by value in the kernel parameters (constant
+// bank), so an unrolled epilogue reads them as instruction operands.
+struct NoConsts {
+  int unused;
+};
+struct PairConsts {
+  float scale[128], shift[128];  // first ConvT's BN per column, zero on padding
+  float w2[32][4];               // second ConvT [m][2 ey + ex], zero rows past M
+};
+template <int A_MODE>
+struct ModeConsts {
+  using type = NoConsts;
+};
+template <>
+struct ModeConsts<4> {
+  using type = PairConsts;
 };
 // TMEM accumulators: 8 for 32-column tiles, 4 up to 128 columns, 2 otherwise
 // (the MMA runs ahead of the epilogue groups by NBUF - groups tiles);
@@ -337,16 +414,18 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmArgs& a, int tile, int
 // the MMAs run ahead across tile boundaries while the epilogue warps drain the
 // previous tile from the other TMEM accumulator.
 template <int BN, int STAGES, bool SPLIT, int A_MODE>
-__global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
+__global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmBlo, const __grid_constant__ CUtensorMap tmOut,
-                   const GemmArgs args) {
+                   const GemmArgs args, const __grid_constant__ typename ModeConsts<A_MODE>::type mc) {
   using SM = Smem<BN, SPLIT, A_MODE>;
-  // A_MODE 3: rows mode (0) with the per-image channel gate applied to A
-  constexpr int AM = A_MODE == 3 ? 0 : A_MODE;
+  // A_MODE 3: rows mode (0) with the per-image channel gate applied to A;
+  // A_MODE 4: rows mode with the ConvT pair epilogue (pair_tile)
+  constexpr int AM = (A_MODE == 3 || A_MODE == 4) ? 0 : A_MODE;
   constexpr bool GATED = A_MODE == 3;
+  constexpr bool PAIR = A_MODE == 4;
   constexpr int NBUF = Accs<BN, SPLIT>::NBUF;
-  constexpr int NGRP = Roles<BN, SPLIT>::EPI_GROUPS;
+  constexpr int NGRP = Roles<BN, SPLIT, A_MODE>::EPI_GROUPS;
   constexpr uint32_t TMEM_COLS = (NBUF * BN < 32) ? 32 : NBUF * BN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -571,59 +650,52 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
     uint32_t acc_i = grp, chunk_ctr = 0;
     bool ok = true;
     float accr[SPLIT ? BN : 1];
+    bool first_tile = true;
     for (int tile = blockIdx.x + grp * gridDim.x; tile < total_tiles && ok; tile += NGRP * gridDim.x) {
       const TileCoord tc = tile_coord(args, tile, n_tiles, BN);
-      int64_t orow = -1, rrow = -1;
-      if (AM == 0) {
-        const int64_t m = (int64_t)tc.m_blk * BM + r;
-        if (m < args.M) orow = m;
-      } else {
-        const int oy = tc.oy0 + r / args.tw, ox = tc.ox0 + r % args.tw;
-        if (oy < args.oh && ox < args.ow) orow = ((int64_t)tc.img * args.oh + oy) * args.ow + ox;
-      }
-      if (orow >= 0) {
-        rrow = orow;
-        if (e.residual && e.rh > 0) {
-          // nearest resize source row, resize.rs:43-50: (int)((float)o * in / out)
-          const int x = (int)(orow % e.ow);
-          const int y = (int)((orow / e.ow) % e.oh);
-          const int64_t nn = orow / ((int64_t)e.ow * e.oh);
-          int iy = (int)__fdiv_rn(__fmul_rn((float)y, (float)e.rh), (float)e.oh);
-          int ix = (int)__fdiv_rn(__fmul_rn((float)x, (float)e.rw), (float)e.ow);
-          iy = iy < e.rh - 1 ? iy : e.rh - 1;
-          ix = ix < e.rw - 1 ? ix : e.rw - 1;
-          rrow = (nn * e.rh + iy) * e.rw + ix;
+      const RowMap rm = row_map<AM>(args, tc.m_blk, tc.img, tc.oy0, tc.ox0, r);
+      const int64_t orow = rm.orow, rrow = rm.orow >= 0 ? rm.rrow : -1;
+      if (!SPLIT && NGRP <= 2 && e.residual) {
+        // Residual lines of this group's next tile (and, first, of this one)
+        // into L2 while the MMAs run, so the per-chunk loads hit L2.
+        auto prefetch = [&](const TileCoord& pc, int64_t prow) {
+          if (prow < 0) return;
+          const float* rp = e.residual + prow * e.ldr + pc.n0;
+#pragma unroll
+          for (int c = 0; c < BN; c += 32)
+            if (pc.n0 + c < args.N) prefetch_l2(rp + c);
+        };
+        if (first_tile) prefetch(tc, rrow);
+        const int nt = tile + NGRP * gridDim.x;
+        if (nt < total_tiles) {
+          const TileCoord nc = tile_coord(args, nt, n_tiles, BN);
+          const RowMap nm = row_map<AM>(args, nc.m_blk, nc.img, nc.oy0, nc.ox0, r);
+          prefetch(nc, nm.orow >= 0 ? nm.rrow : -1);
         }
+        first_tile = false;
       }
       if (!SPLIT) {
         const uint32_t buf = acc_i % NBUF;
         if (!mbar_wait(&acc_full[buf], (acc_i / NBUF) & 1u, args.err)) { ok = false; break; }
         tc_fence_after();
-        if (e.partials) {
-          argmax_tile<BN>(args, orow, tc.n0, tc.n0 / BN, [&](int c, float (&v)[32]) {
-            uint32_t a[16], b[16];
-            tmem_ld16_nowait(lane_base + buf * BN + c, a);
-            tmem_ld16_nowait(lane_base + buf * BN + c + 16, b);
-            tmem_ld_wait();
+        auto fetch = [&](int c, float (&v)[32]) {
+          uint32_t a[16], b[16];
+          tmem_ld16_nowait(lane_base + buf * BN + c, a);
+          tmem_ld16_nowait(lane_base + buf * BN + c + 16, b);
+          tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              v[j] = __uint_as_float(a[j]);
-              v[16 + j] = __uint_as_float(b[j]);
-            }
-          });
+          for (int j = 0; j < 16; ++j) {
+            v[j] = __uint_as_float(a[j]);
+            v[16 + j] = __uint_as_float(b[j]);
+          }
+        };
+        if constexpr (PAIR) {
+          pair_tile(args, orow, mc, fetch);
+        } else if (e.partials) {
+          argmax_tile<BN>(args, orow, tc.n0, tc.n0 / BN, fetch);
         } else if (args.tma_store) {
           store_tile<BN, AM>(args, &tmOut, my_stage, s_rrow[grp], 1 + grp, chunk_ctr, tc.m_blk, tc.n0, tc.img,
-                                 tc.oy0, tc.ox0, r, gt, [&](int c, float (&v)[32]) {
-                                   uint32_t a[16], b[16];
-                                   tmem_ld16_nowait(lane_base + buf * BN + c, a);
-                                   tmem_ld16_nowait(lane_base + buf * BN + c + 16, b);
-                                   tmem_ld_wait();
-#pragma unroll
-                                   for (int j = 0; j < 16; ++j) {
-                                     v[j] = __uint_as_float(a[j]);
-                                     v[16 + j] = __uint_as_float(b[j]);
-                                   }
-                                 });
+                             tc.oy0, tc.ox0, r, gt, fetch);
         } else {
 #pragma unroll 1
           for (int c = 0; c < BN; c += 16) {
@@ -660,23 +732,20 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT>::THREADS, 1)
           ++acc_i;
         }
         if (!ok) break;
-        if (e.partials) {
-          argmax_tile<BN>(args, orow, tc.n0, tc.n0 / BN, [&](int c, float (&v)[32]) {
+        auto fetch = [&](int c, float (&v)[32]) {
 #pragma unroll
-            for (int cb = 0; cb < BN; cb += 32)
-              if (cb == c)
+          for (int cb = 0; cb < BN; cb += 32)
+            if (cb == c)
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = accr[(cb + j) % (SPLIT ? BN : 1)];
-          });
+              for (int j = 0; j < 32; ++j) v[j] = accr[(cb + j) % (SPLIT ? BN : 1)];
+        };
+        if constexpr (PAIR) {
+          pair_tile(args, orow, mc, fetch);
+        } else if (e.partials) {
+          argmax_tile<BN>(args, orow, tc.n0, tc.n0 / BN, fetch);
         } else if (args.tma_store) {
           store_tile<BN, AM>(args, &tmOut, my_stage, s_rrow[grp], 1 + grp, chunk_ctr, tc.m_blk, tc.n0, tc.img,
-                                 tc.oy0, tc.ox0, r, gt, [&](int c, float (&v)[32]) {
-#pragma unroll
-                                   for (int cb = 0; cb < BN; cb += 32)
-                                     if (cb == c)
-#pragma unroll
-                                       for (int j = 0; j < 32; ++j) v[j] = accr[(cb + j) % (SPLIT ? BN : 1)];
-                                 });
+                             tc.oy0, tc.ox0, r, gt, fetch);
         } else {
 #pragma unroll
           for (int c = 0; c < BN; c += 16) {
@@ -1180,7 +1249,7 @@ int sm_count() {
 // most 8.  An instantiation with room for fewer than 2 stages is not built.
 template <int BN, bool SPLIT, int A_MODE>
 constexpr int stages_raw() {
-  return (224 * 1024 - Roles<BN, SPLIT>::EPI_GROUPS * 2 * OUT_STAGE_BYTES - 1024) / Smem<BN, SPLIT, A_MODE>::STAGE;
+  return (224 * 1024 - Roles<BN, SPLIT, A_MODE>::STAGING - 1024) / Smem<BN, SPLIT, A_MODE>::STAGE;
 }
 template <int BN, bool SPLIT, int A_MODE>
 constexpr int stages_for() {
@@ -1189,13 +1258,14 @@ constexpr int stages_for() {
 
 template <int BN, bool SPLIT, int A_MODE>
 cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& blo,
-                       const CUtensorMap& out, const GemmArgs& args, int tiles, cudaStream_t st) {
+                       const CUtensorMap& out, const GemmArgs& args, int tiles, cudaStream_t st,
+                       const typename ModeConsts<A_MODE>::type& mc = {}) {
   if constexpr (stages_raw<BN, SPLIT, A_MODE>() < 2) {
     return cudaErrorInvalidValue;
   } else {
   constexpr int STAGES = stages_for<BN, SPLIT, A_MODE>();
   auto kern = gemm_tc_kernel<BN, STAGES, SPLIT, A_MODE>;
-  const int smem = STAGES * Smem<BN, SPLIT, A_MODE>::STAGE + Roles<BN, SPLIT>::EPI_GROUPS * 2 * OUT_STAGE_BYTES + 1024;
+  const int smem = STAGES * Smem<BN, SPLIT, A_MODE>::STAGE + Roles<BN, SPLIT, A_MODE>::STAGING + 1024;
   static bool attr_set = false;  // per instantiation
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1203,7 +1273,7 @@ cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
     attr_set = true;
   }
   const int grid = tiles < sm_count() ? tiles : sm_count();
-  kern<<<grid, Roles<BN, SPLIT>::THREADS, smem, st>>>(a, b, blo, out, args);
+  kern<<<grid, Roles<BN, SPLIT, A_MODE>::THREADS, smem, st>>>(a, b, blo, out, args, mc);
   return cudaGetLastError();
   }
 }
@@ -1364,6 +1434,55 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
   const int grid_m = (int)((M + BM - 1) / BM);
   if (epi.a_gate) return dispatch<3>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
   return dispatch<0>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
+}
+
+cudaError_t launch_convt_pair(const float* x, int n, int h, int w, int c, const float* b1,
+                              const float* b1_lo, const float* consts, const ActParams& act1,
+                              const ActParams& act2, float* out, int math, unsigned int* err,
+                              cudaStream_t st) {
+  const int64_t M = (int64_t)n * h * w;
+  if (M <= 0) return cudaSuccess;
+  auto misaligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; };
+  if (c <= 0 || (c & 3) || M > (int64_t)0x7fffffff || !consts || !err || misaligned(x) || misaligned(b1) ||
+      misaligned(out))
+    return cudaErrorInvalidValue;
+  PairConsts pc;
+  std::memcpy(pc.scale, consts, sizeof(pc.scale));
+  std::memcpy(pc.shift, consts + 128, sizeof(pc.shift));
+  std::memcpy(pc.w2, consts + 256, sizeof(pc.w2));
+  const bool split = math == MATH_3XTF32;
+  if (split && (!b1_lo || misaligned(b1_lo))) return cudaErrorInvalidValue;
+  CUtensorMap ma, mb, mblo;
+  {
+    const uint64_t dims[2] = {(uint64_t)c, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)c * 4};
+    const uint32_t box[2] = {BK, BM};
+    if (!make_map(&ma, x, 2, dims, strides, box)) return cudaErrorInvalidValue;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)c, 128};
+    const uint64_t strides[1] = {(uint64_t)c * 4};
+    const uint32_t box[2] = {BK, 128};
+    if (!make_map(&mb, b1, 2, dims, strides, box)) return cudaErrorInvalidValue;
+    if (split && !make_map(&mblo, b1_lo, 2, dims, strides, box)) return cudaErrorInvalidValue;
+    if (!split) mblo = mb;
+  }
+  GemmArgs args{};
+  args.M = (int)M;
+  args.N = 128;
+  args.K = c;
+  args.nkb = (c + BK - 1) / BK;
+  args.err = err;
+  args.tma_store = 0;
+  args.epi.out = out;
+  args.epi.act = act1;
+  args.epi.pair_h = h;
+  args.epi.pair_w = w;
+  args.epi.pair_act = act2;
+  const int grid_m = (int)((M + BM - 1) / BM);
+  args.m_tiles = grid_m;
+  return split ? run_kernel<128, true, 4>(ma, mb, mblo, ma, args, grid_m, st, pc)
+               : run_kernel<128, false, 4>(ma, mb, mblo, ma, args, grid_m, st, pc);
 }
 
 cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, const float* wk_lo,

@@ -60,6 +60,10 @@ struct GemmEpilogue {
   // writes per row (max, argmax bits, sum exp(l - max)) of its columns to
   // partials[n_tile * M + row] (float4); nothing is written to `out`.
   float4* partials = nullptr;
+  // ConvT pair epilogue (two 2x2 stride-2 ConvTranspose layers, the second
+  // to one channel; launch_convt_pair): set by that launcher only.
+  int pair_h = 0, pair_w = 0;  // input map of the first ConvT
+  ActParams pair_act{};        // activation after the second ConvT
 };
 
 enum MathMode : int { MATH_TF32 = 0, MATH_3XTF32 = 1 };
@@ -93,6 +97,24 @@ cudaError_t launch_argmax_combine(const float4* partials, int n_tiles, int64_t M
 cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, const float* wk_lo,
                            const GemmEpilogue& epi, int math, unsigned int* err,
                            cudaStream_t st, const float* wk_fold = nullptr);
+
+// Two 2x2 stride-2 ConvTranspose layers back to back, the second to one
+// channel (DB head: ConvT -> BN -> act1 -> ConvT -> act2; executor.rs:654-731,
+// conv.rs:730-838), as one tcgen05 GEMM of the first layer whose epilogue
+// finishes the second, so the 2x-upsampled intermediate is never written.
+//   x     n x h x w x c NHWC, c % 4 == 0
+//   b1    [128][c]: row 32 (2 dy + dx) + m = W1[c][m][dy][dx] for m < m1
+//         (m1 <= 32; other rows zero), tf32-rounded (b1_lo: 3xTF32 residue)
+//   consts  scale[128], shift[128] (BN of the first layer, y = fma(acc,
+//         scale, shift), zero on padding columns), w2[32][4] = W2[m][0][ey][ex]
+//         (zero rows past m1); 384 floats in HOST memory, passed to the kernel
+//         by value
+//   out   n x 4h x 4w (one channel): out[4y + 2dy + ey][4x + 2dx + ex] =
+//         act2(sum_m act1(fma(acc[32 s + m], scale, shift)) * w2[m][2 ey + ex])
+cudaError_t launch_convt_pair(const float* x, int n, int h, int w, int c, const float* b1,
+                              const float* b1_lo, const float* consts, const ActParams& act1,
+                              const ActParams& act2, float* out, int math, unsigned int* err,
+                              cudaStream_t st);
 
 // Whether the tap-folded TF32 kernel takes this conv (kw <= 3, M <= 32,
 // output rows >= 48 wide, stride 1, filter within the shared-memory budget).

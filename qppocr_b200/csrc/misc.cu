@@ -722,25 +722,39 @@ cudaError_t launch_pool2d_nhwc(const float* x, float* y, int n, int h, int w, in
 // resize.rs:8-57 nearest: iy = min((int)((float)oy * H / oh), H - 1).  Writes
 // into a channel slice [c_off, c_off + C) of an output with ldc channels, so
 // the FPN concat needs no separate copy.
-// One output row per blockIdx.y (n * OH + oy), (ox, channel quad) along x:
-// the source row is found once per block, the source column once per thread,
-// all in 32-bit arithmetic.  Source index (int)((float)o * in / out), clamped
-// (resize.rs:43-50).
+// Threads take one (ox, channel quad) column of the output, its source
+// column found once; blockIdx.y takes RESIZE_ROWS consecutive output rows
+// (n * OH + oy), whose loads are all issued before their stores so several
+// are in flight per thread.  Source index (int)((float)o * in / out),
+// clamped (resize.rs:43-50), in 32-bit arithmetic.
+constexpr int RESIZE_ROWS = 8;
 __global__ void __launch_bounds__(256) resize_nearest_nhwc_kernel(const float* __restrict__ x,
                                                                   float* __restrict__ y, int N, int H, int W,
                                                                   int C, int OH, int OW, int ldc, int c_off) {
   const int C4 = C >> 2;
-  for (int row = blockIdx.y; row < N * OH; row += gridDim.y) {  // row = n * OH + oy
-    const int oy = row % OH, n = row / OH;
-    int iy = (int)__fdiv_rn(__fmul_rn((float)oy, (float)H), (float)OH);
-    iy = iy < H - 1 ? iy : H - 1;
-    const float4* src = reinterpret_cast<const float4*>(x + ((int64_t)n * H + iy) * W * C);
-    float* dst = y + (int64_t)row * OW * ldc + c_off;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < OW * C4; i += gridDim.x * blockDim.x) {
-      const int ox = i / C4, c4 = i - ox * C4;
-      int ix = (int)__fdiv_rn(__fmul_rn((float)ox, (float)W), (float)OW);
-      ix = ix < W - 1 ? ix : W - 1;
-      *reinterpret_cast<float4*>(dst + (int64_t)ox * ldc + c4 * 4) = __ldg(src + (int64_t)ix * C4 + c4);
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= OW * C4) return;
+  const int ox = i / C4, c4 = i - ox * C4;
+  int ix = (int)__fdiv_rn(__fmul_rn((float)ox, (float)W), (float)OW);
+  ix = ix < W - 1 ? ix : W - 1;
+  const int rows = N * OH;
+  for (int row0 = blockIdx.y * RESIZE_ROWS; row0 < rows; row0 += gridDim.y * RESIZE_ROWS) {
+    float4 v[RESIZE_ROWS];
+#pragma unroll
+    for (int k = 0; k < RESIZE_ROWS; ++k) {
+      const int row = row0 + k;
+      if (row < rows) {
+        const int n = row / OH, oy = row - n * OH;
+        int iy = (int)__fdiv_rn(__fmul_rn((float)oy, (float)H), (float)OH);
+        iy = iy < H - 1 ? iy : H - 1;
+        v[k] = __ldg(reinterpret_cast<const float4*>(x + (((int64_t)n * H + iy) * W + ix) * C) + c4);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < RESIZE_ROWS; ++k) {
+      const int row = row0 + k;
+      if (row < rows)
+        *reinterpret_cast<float4*>(y + ((int64_t)row * OW + ox) * ldc + c_off + c4 * 4) = v[k];
     }
   }
 }
@@ -748,10 +762,12 @@ __global__ void __launch_bounds__(256) resize_nearest_nhwc_kernel(const float* _
 cudaError_t launch_resize_nearest_nhwc(const float* x, float* y, int n, int h, int w, int c, int oh,
                                        int ow, int ldc, int c_off, cudaStream_t st) {
   if ((c & 3) || (ldc & 3) || (c_off & 3)) return cudaErrorInvalidValue;
-  if ((int64_t)n * oh >= (1LL << 31) || (int64_t)ow * (c / 4) >= (1LL << 31)) return cudaErrorInvalidValue;
+  if ((int64_t)n * oh + RESIZE_ROWS >= (1LL << 31) || (int64_t)ow * (c / 4) >= (1LL << 31))
+    return cudaErrorInvalidValue;
+  if (n <= 0 || oh <= 0 || ow <= 0 || c <= 0) return cudaSuccess;
   const int per_row = ow * (c / 4);
-  const int rows = n * oh;
-  dim3 grid((per_row + 255) / 256, rows < 65535 ? rows : 65535);
+  const int row_groups = (n * oh + RESIZE_ROWS - 1) / RESIZE_ROWS;
+  dim3 grid((per_row + 255) / 256, row_groups < 65535 ? row_groups : 65535);
   resize_nearest_nhwc_kernel<<<grid, 256, 0, st>>>(x, y, n, h, w, c, oh, ow, ldc, c_off);
   return cudaGetLastError();
 }

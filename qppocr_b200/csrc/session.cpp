@@ -142,7 +142,7 @@ static const std::set<std::string>& supported_ops() {
       "Transpose", "Reshape", "Squeeze", "Unsqueeze", "Flatten", "ReduceMean", "MatMul",
       "Identity", "Dropout", "Gather", "Shape", "Cast",
       // internal (produced by Session::fuse)
-      "QpcLinear", "QpcConvT", "QpcLayerNorm", "QpcCtcHead"};
+      "QpcLinear", "QpcConvT", "QpcConvTPair", "QpcLayerNorm", "QpcCtcHead"};
   return ops;
 }
 
@@ -495,6 +495,47 @@ void Session::fuse() {
         }
       }
     }
+  }
+
+  // ConvT pair: a QpcConvT to M <= 32 channels whose only consumer is a
+  // QpcConvT to one channel (the DB head's two upsampling steps) becomes one
+  // QpcConvTPair (in = x, w1, BN scale / bias / mean / var or "", w2; the
+  // second layer's activation as qpc_act2...), planned as one tensor-core
+  // GEMM whose epilogue applies the second layer.
+  for (size_t i = 0; i < N.size(); ++i) {
+    if (!alive[i] || N[i].op != "QpcConvT") continue;
+    const std::string o = N[i].out[0];
+    if (gouts.count(o)) continue;
+    auto cs = consumers(o);
+    if (cs.size() != 1 || N[cs[0]].op != "QpcConvT" || N[cs[0]].in.size() != 2 || N[cs[0]].in[0] != o)
+      continue;
+    const Node& second = N[cs[0]];
+    const HostTensor* w1 = weight(N[i].in[1]);
+    const HostTensor* w2 = weight(second.in[1]);
+    if (!w1 || !w2 || w1->shape.size() != 4 || w2->shape.size() != 4 || w1->dtype != QPC_F32 ||
+        w2->dtype != QPC_F32)
+      continue;
+    if (w1->shape[1] > 32 || w1->shape[0] % 4 != 0 || w2->shape[0] != w1->shape[1] || w2->shape[1] != 1 ||
+        w2->shape[2] != 2 || w2->shape[3] != 2)
+      continue;
+    auto s2 = second.getints("strides");
+    if (!(s2.empty() || (s2.size() == 2 && s2[0] == 2 && s2[1] == 2))) continue;
+    bool padded = false;
+    for (auto pd : second.getints("pads")) padded = padded || pd != 0;
+    if (padded) continue;
+    Node p = N[i];
+    p.op = "QpcConvTPair";
+    p.in.resize(6, "");
+    p.in.push_back(second.in[1]);
+    p.seti("qpc_act2", second.geti("qpc_act", 0));
+    p.setf("qpc_alpha2", second.getf("qpc_alpha", 1.0f / 6.0f));
+    p.setf("qpc_beta2", second.getf("qpc_beta", 0.5f));
+    p.setf("qpc_c12", second.getf("qpc_c1", 1.4142135f));
+    p.setf("qpc_c22", second.getf("qpc_c2", 1.0f));
+    p.setf("qpc_c32", second.getf("qpc_c3", 0.5f));
+    p.out = second.out;
+    alive[i] = false;
+    N[cs[0]] = p;
   }
 
   // Residual absorption: P -> Add(P.out, R) (fuse_conv_residual semantics,
@@ -885,6 +926,7 @@ class Planner {
     const Node& n = S.nodes()[p->second];
     if (n.op == "Conv") return S.weight(n.in[1])->shape[0];
     if (n.op == "QpcConvT" || n.op == "ConvTranspose") return S.weight(n.in[1])->shape[1];
+    if (n.op == "QpcConvTPair") return S.weight(n.in[6])->shape[1];
     if (n.op == "Concat") {
       int64_t t = 0;
       for (auto& x : n.in) {
@@ -1055,6 +1097,7 @@ class Planner {
     const std::string& op = n.op;
     if (op == "Conv") return plan_conv(n);
     if (op == "QpcConvT" || op == "ConvTranspose") return plan_convt(n);
+    if (op == "QpcConvTPair") return plan_convt_pair(n);
     if (op == "QpcLinear") return plan_linear(n, false);
     if (op == "QpcCtcHead") return plan_linear(n, true);
     if (op == "QpcLayerNorm") return plan_layernorm(n);
@@ -1344,6 +1387,82 @@ class Planner {
     unsigned int* err = device_state(S.device()).err_word;
     step("convt2x2", n.name, bytes, 2.0 * N * 4 * H * W * M * C, [=](cudaStream_t s) {
       return launch_convt2x2(xp, wp, bn_a, bn_b, yp, (int)N, (int)H, (int)W, (int)C, (int)M, act, s, err);
+    });
+    unref(x);
+    define(n.out[0], y);
+  }
+
+  // ConvT pair (QpcConvTPair, fused at load): the first layer's 2x2 taps as
+  // the [128][C] B operand of one GEMM (row 32 (2 dy + dx) + m), its BN as
+  // per-column scale / shift, and the second layer's [m][ey][ex] filter; see
+  // launch_convt_pair.
+  void plan_convt_pair(const Node& n) {
+    const Val& x0 = get(n.in[0]);
+    const HostTensor* w1 = S.weight(n.in[1]);
+    const HostTensor* w2 = S.weight(n.in[6]);
+    if (!w1 || w1->shape.size() != 4 || w1->shape[2] != 2 || w1->shape[3] != 2)
+      throw GraphError{"ConvTranspose: only 2x2 s2 p0"};
+    auto st = n.getints("strides");
+    if (!(st.empty() || (st.size() == 2 && st[0] == 2 && st[1] == 2)))
+      throw GraphError{"ConvTranspose: stride must be 2"};
+    for (auto p : n.getints("pads"))
+      if (p) throw GraphError{"ConvTranspose: pads must be 0"};
+    const int64_t N = x0.shape[0], C = x0.shape[1], H = x0.shape[2], W = x0.shape[3];
+    if (w1->shape[0] != C) throw GraphError{"ConvTranspose: weight C_in mismatch"};
+    const int64_t M = w1->shape[1];
+    // B operand [128][C]: column block s = 2 dy + dx, row m < M
+    std::vector<float> b1(128 * C, 0.f);
+    for (int64_t s = 0; s < 4; ++s)
+      for (int64_t m = 0; m < M; ++m)
+        for (int64_t c = 0; c < C; ++c) b1[(32 * s + m) * C + c] = w1->f[((c * M + m) * 2 + s / 2) * 2 + s % 2];
+    const bool split = S.math() == MATH_3XTF32;
+    std::vector<float> hi(b1.size()), lo(b1.size());
+    for (size_t k = 0; k < b1.size(); ++k) {
+      hi[k] = tf32_rn_host(b1[k]);
+      lo[k] = tf32_rn_host(b1[k] - hi[k]);
+    }
+    // scale[128], shift[128], w2[32][4]; BN as plan_convt folds it (shape.rs:700-733)
+    std::vector<float> cs(384, 0.f);
+    for (int64_t m = 0; m < M; ++m) {
+      float a = 1.f, b = 0.f;
+      if (n.has_in(2)) {
+        const float eps = n.getf("qpc_eps", 1e-5f);
+        const HostTensor* sc = S.weight(n.in[2]);
+        const HostTensor* bi = S.weight(n.in[3]);
+        const HostTensor* me = S.weight(n.in[4]);
+        const HostTensor* va = S.weight(n.in[5]);
+        a = sc->f[m] / std::sqrt(va->f[m] + eps);
+        b = std::fma(-me->f[m], a, bi->f[m]);
+      }
+      for (int64_t s = 0; s < 4; ++s) {
+        cs[32 * s + m] = a;
+        cs[128 + 32 * s + m] = b;
+      }
+      for (int e = 0; e < 4; ++e) cs[256 + 4 * m + e] = w2->f[m * 4 + e];
+    }
+    const float* b1p = upload_temp(hi);
+    const float* b1lo = split ? upload_temp(lo) : nullptr;
+    Val x = as_nhwc(x0, n.name);
+    Val y = new_val({N, 1, 4 * H, 4 * W}, true);
+    const float* xp = out_ptr(x);
+    float* yp = out_ptr(y);
+    if ((reinterpret_cast<uintptr_t>(xp) | reinterpret_cast<uintptr_t>(yp)) & 15)
+      throw GraphError{"internal: unaligned ConvT pair buffers"};
+    const ActParams act1 = act_of(n);
+    ActParams act2{};
+    act2.kind = (int)n.geti("qpc_act2", 0);
+    act2.alpha = n.getf("qpc_alpha2", 1.0f / 6.0f);
+    act2.beta = n.getf("qpc_beta2", 0.5f);
+    act2.c1 = n.getf("qpc_c12", 1.4142135f);
+    act2.c2 = n.getf("qpc_c22", 1.0f);
+    act2.c3 = n.getf("qpc_c32", 0.5f);
+    const double bytes = 4.0 * (N * H * W * C + N * 16 * H * W);
+    const double flops = 2.0 * N * H * W * (4 * M * C + 16 * M);
+    unsigned int* err = device_state(S.device()).err_word;
+    const int math = S.math();
+    step("convt_pair", n.name, bytes, flops, [=](cudaStream_t s) {
+      return launch_convt_pair(xp, (int)N, (int)H, (int)W, (int)C, b1p, b1lo, cs.data(), act1, act2, yp, math,
+                               err, s);
     });
     unref(x);
     define(n.out[0], y);

@@ -114,3 +114,43 @@ def test_se_gate_fused_into_pointwise(cuda_ctx, math):
     assert err < TOL[math], err
     kinds = [p[0] for p in s.profile({"x": x}, iters=1)]
     assert "binary" not in kinds and "gemm_tc" in kinds, kinds
+
+
+# (batch, cin, mid, h, w, bn, act1, act2)
+PAIR_CASES = [
+    (2, 24, 24, 12, 40, True, "Relu", "Sigmoid"),   # DB head tail, rows span images
+    (1, 8, 7, 5, 9, False, None, None),            # no BN, no activations, mid < 32, 45 pixels
+    (3, 36, 32, 3, 50, True, "Sigmoid", None),     # K = 36: two k-blocks, 32 mid channels
+]
+
+
+@pytest.mark.parametrize("math", ["tf32", "3xtf32"])
+@pytest.mark.parametrize("case", PAIR_CASES)
+def test_convt_pair_fused(cuda_ctx, math, case):
+    """ConvT(C -> M) [+ BN] [+ act] -> ConvT(M -> 1) [-> act]: one tensor-core
+    GEMM of the first layer whose epilogue applies the second, so the plan has
+    no convt2x2 step; the 4x-upsampled output matches the oracle's two
+    ConvTranspose layers (conv.rs:730-838)."""
+    n, c, m, h, w, use_bn, act1, act2 = case
+    b = nets.Builder(23, "ctp")
+    w1 = b.const(b.normal((c, m, 2, 2), np.sqrt(2.0 / (c * 4))), "ct_w")
+    y = b.node("ConvTranspose", ["x", w1], {"kernel_shape": [2, 2], "strides": [2, 2]})
+    if use_bn:
+        y = b.bn(y, m)
+    if act1:
+        y = b.node(act1, [y])
+    w2 = b.const(b.normal((m, 1, 2, 2), np.sqrt(2.0 / (m * 4))), "ct_w")
+    y = b.node("ConvTranspose", [y, w2], {"kernel_shape": [2, 2], "strides": [2, 2]})
+    if act2:
+        y = b.node(act2, [y])
+    g, wts = b.graph(["x"], [y], [[1, c, 0, 0]])
+    g = q.optimize(g, wts)
+    x = np.random.Generator(np.random.PCG64(11)).uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    ref = orc.run_graph(g, wts, {"x": x})[0]
+    s = cuda_ctx.create_session(g, wts, role="other", math=math)
+    got = s.run({"x": x})[0]
+    assert got.shape == (n, 1, 4 * h, 4 * w)
+    err = np.abs(got.astype(np.float64) - ref).max() / max(np.abs(ref).max(), 1e-6)
+    assert err < TOL[math], err
+    kinds = [p[0] for p in s.profile({"x": x}, iters=1)]
+    assert "convt_pair" in kinds and "convt2x2" not in kinds, kinds

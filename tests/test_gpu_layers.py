@@ -60,7 +60,7 @@ def per_node(ctx, builder, x, math, role, **kw):
 def test_det_per_node(cuda_ctx, math):
     fused, errs = per_node(cuda_ctx, nets.build_det, nets.det_input(2, 128, 160), math, "det")
     ops = [f[0] for f in fused]
-    assert "QpcConvT" in ops and ops.count("Conv") >= 40
+    assert "QpcConvTPair" in ops and ops.count("Conv") >= 40
     worst = max(errs.items(), key=lambda kv: kv[1][1])
     assert worst[1][1] < TOL[math], worst
 
