@@ -181,6 +181,14 @@ int qpc_ticket_output(const qpc_ticket* ticket, int index, const float** data,
  * DeviceSession::run returns (device.rs:130); a binding may instead copy
  * from qpc_ticket_output's pointer itself. */
 int qpc_ticket_output_copy(const qpc_ticket* ticket, int index, float* dst, int64_t count);
+
+/* Pinned (page-locked) host memory for run inputs (extension; the reference's
+ * host tensors are plain Vec<f32>).  A run input whose bytes lie wholly in one
+ * such block is copied to the device by DMA straight from it, with no staging
+ * copy; the caller keeps it unchanged until the ticket completes.  Outputs are
+ * always delivered in pinned memory (qpc_ticket_output). */
+int qpc_host_alloc(int64_t bytes, void** ptr);
+int qpc_host_free(void* ptr);
 int qpc_ticket_release(qpc_ticket* ticket);
 
 /* DeviceSession::run (device.rs:130): run_async + complete(no bound). */

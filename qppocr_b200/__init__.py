@@ -93,6 +93,7 @@ EXPORTED = (
     "qpc_last_error", "qpc_device_count", "qpc_device_info", "qpc_session_create",
     "qpc_session_caps", "qpc_run_async", "qpc_complete", "qpc_ticket_output_count",
     "qpc_ticket_output", "qpc_ticket_output_copy", "qpc_ticket_release", "qpc_run", "qpc_ticket_device_ms",
+    "qpc_host_alloc", "qpc_host_free",
     "qpc_session_destroy", "qpc_session_profile", "qpc_session_profile_step",
     "qpc_session_replay", "qpc_session_node_count", "qpc_session_node", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_ctc_head", "qpc_op_ctc_head_noalloc",
     "qpc_op_split_tf32", "qpc_op_resize_bilinear_rgb_u8", "qpc_op_det_preprocess", "qpc_op_db_mask",
@@ -125,6 +126,8 @@ def lib():
                                     ctypes.POINTER(ctypes.POINTER(ctypes.c_int64)),
                                     ctypes.POINTER(ctypes.c_int)]
     L.qpc_ticket_output_copy.argtypes = [P, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64]
+    L.qpc_host_alloc.argtypes = [ctypes.c_int64, ctypes.POINTER(P)]
+    L.qpc_host_free.argtypes = [P]
     L.qpc_ticket_release.argtypes = [P]
     L.qpc_ticket_device_ms.argtypes = [P, ctypes.POINTER(ctypes.c_float)]
     L.qpc_session_destroy.argtypes = [P]
@@ -285,6 +288,47 @@ def _graph(keep: _Keep, g: Graph) -> QpcGraph:
     return qg
 
 
+# ------------------------------------------------------------------ pinned host memory
+class _PinnedBlock:
+    """Owner of one qpc_host_alloc block (freed with the last array on it)."""
+
+    def __init__(self, nbytes: int):
+        p = ctypes.c_void_p()
+        _check(lib().qpc_host_alloc(nbytes, ctypes.byref(p)))
+        self.ptr = p.value
+
+    def __del__(self):
+        try:
+            if self.ptr:
+                lib().qpc_host_free(ctypes.c_void_p(self.ptr))
+                self.ptr = None
+        except Exception:
+            pass
+
+
+def host_empty(shape, dtype=np.float32) -> np.ndarray:
+    """An uninitialised array in pinned host memory.  Passed as a run input,
+    it is copied to the device by DMA straight from this memory (no staging
+    copy); keep it unchanged until the run completes."""
+    dt = np.dtype(dtype)
+    shape = tuple(int(d) for d in shape)
+    nbytes = int(np.prod(shape, dtype=np.int64)) * dt.itemsize
+    blk = _PinnedBlock(max(nbytes, 1))
+    buf = (ctypes.c_char * max(nbytes, 1)).from_address(blk.ptr)
+    buf._owner = blk  # the ctypes buffer keeps the block alive, the array keeps the buffer
+    return np.frombuffer(buf, dtype=dt, count=int(np.prod(shape, dtype=np.int64))).reshape(shape)
+
+
+def _pinned_view(data, shape, cnt: int, owner) -> np.ndarray:
+    """Read-only array over a run's pinned output buffer; holds `owner` (the
+    DeferredRun, whose ticket keeps the buffer) alive."""
+    buf = (ctypes.c_float * max(cnt, 1)).from_address(ctypes.addressof(data.contents))
+    buf._owner = owner
+    a = np.frombuffer(buf, dtype=np.float32, count=cnt).reshape(shape)
+    a.flags.writeable = False
+    return a
+
+
 # ------------------------------------------------------------------ device seam
 class DeferredRun:
     """A submitted run (DeferredRun, device.rs:105-108)."""
@@ -294,7 +338,11 @@ class DeferredRun:
         self._t = ticket
         self._keep = keep  # device inputs are read by the run's own copy: hold them until it completes
 
-    def complete(self, timeout_ms: int = -1) -> List[np.ndarray]:
+    def complete(self, timeout_ms: int = -1, copy: bool = True) -> List[np.ndarray]:
+        """Wait for the run and return its outputs.  copy=True: fresh arrays
+        (the ticket is released).  copy=False: read-only views of the run's
+        pinned output buffers, no host copy; the ticket (and its plan
+        instance) stays held until every view has been dropped."""
         L = lib()
         _check(L.qpc_complete(self._t, timeout_ms))
         n = ctypes.c_int(0)
@@ -307,13 +355,17 @@ class DeferredRun:
             _check(L.qpc_ticket_output(self._t, k, ctypes.byref(data), ctypes.byref(shp), ctypes.byref(rank)))
             shape = tuple(shp[i] for i in range(rank.value))
             cnt = int(np.prod(shape)) if shape else 1
-            out = np.empty(shape, np.float32)
-            _check(L.qpc_ticket_output_copy(self._t, k, out.ctypes.data, cnt))
+            if copy:
+                out = np.empty(shape, np.float32)
+                _check(L.qpc_ticket_output_copy(self._t, k, out.ctypes.data, cnt))
+            else:
+                out = _pinned_view(data, shape, cnt, self)
             outs.append(out)
         ms = ctypes.c_float(0)
         _check(L.qpc_ticket_device_ms(self._t, ctypes.byref(ms)))
         self.device_ms = ms.value
-        self.release()
+        if copy:
+            self.release()
         return outs
 
     def release(self):

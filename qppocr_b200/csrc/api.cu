@@ -218,6 +218,29 @@ int qpc_ticket_device_ms(const qpc_ticket* t, float* ms) {
   return OK;
 }
 
+int qpc_host_alloc(int64_t bytes, void** ptr) {
+  if (!ptr || bytes < 0) {
+    set_error("invalid argument");
+    return E_INVALID;
+  }
+  void* p = pinned_alloc((size_t)bytes);
+  if (!p) {
+    set_error("pinned host allocation of " + std::to_string(bytes) + " bytes failed");
+    return E_OOM;
+  }
+  *ptr = p;
+  return OK;
+}
+
+int qpc_host_free(void* ptr) {
+  if (!ptr) return OK;
+  if (!pinned_free(ptr)) {
+    set_error("not a qpc_host_alloc block");
+    return E_INVALID;
+  }
+  return OK;
+}
+
 int qpc_ticket_release(qpc_ticket* t) {
   if (!t) return E_INVALID;
   if (t->plan && !t->completed) {

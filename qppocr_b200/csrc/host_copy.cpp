@@ -8,6 +8,7 @@
 #include <cstring>
 #include <deque>
 #include <functional>
+#include <map>
 #include <memory>
 #include <mutex>
 #include <thread>
@@ -123,6 +124,44 @@ std::shared_ptr<Batch> make_batch(void* dst, const void* src, size_t bytes) {
 }  // namespace
 
 int host_copy_threads() { return Pool::get().threads(); }
+
+namespace {
+std::mutex g_pin_mu;
+std::map<uintptr_t, size_t>& pinned_blocks() {  // base -> bytes
+  static std::map<uintptr_t, size_t> m;
+  return m;
+}
+}  // namespace
+
+void* pinned_alloc(size_t bytes) {
+  void* p = nullptr;
+  if (cudaHostAlloc(&p, bytes ? bytes : 1, cudaHostAllocPortable) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(g_pin_mu);
+  pinned_blocks()[reinterpret_cast<uintptr_t>(p)] = bytes;
+  return p;
+}
+
+bool pinned_free(void* p) {
+  {
+    std::lock_guard<std::mutex> lk(g_pin_mu);
+    auto& m = pinned_blocks();
+    auto it = m.find(reinterpret_cast<uintptr_t>(p));
+    if (it == m.end()) return false;
+    m.erase(it);
+  }
+  cudaFreeHost(p);
+  return true;
+}
+
+bool pinned_contains(const void* p, size_t bytes) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  std::lock_guard<std::mutex> lk(g_pin_mu);
+  auto& m = pinned_blocks();
+  auto it = m.upper_bound(a);  // first block starting after a
+  if (it == m.begin()) return false;
+  --it;
+  return a >= it->first && a - it->first <= it->second && bytes <= it->second - (a - it->first);
+}
 
 void parallel_copy(void* dst, const void* src, size_t bytes) {
   if (bytes < kSerialBelow || Pool::get().threads() == 0) {

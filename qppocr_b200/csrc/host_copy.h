@@ -31,4 +31,11 @@ cudaError_t staged_h2d(void* dev, void* pinned, const void* src, size_t bytes, c
 // Worker threads used (excluding the calling thread).
 int host_copy_threads();
 
+// Pinned host allocations made through the library (qpc_host_alloc).  A run
+// input that lies wholly inside one is copied to the device by DMA straight
+// from the caller's memory, with no staging copy.
+void* pinned_alloc(size_t bytes);
+bool pinned_free(void* p);
+bool pinned_contains(const void* p, size_t bytes);
+
 }  // namespace qpc

@@ -2346,6 +2346,8 @@ PlanInstance* Session::launch(const qpc_tensor* inputs, int n) {
       if (dt != io.dtype) throw GraphError{"input " + io.name + ": dtype differs from the plan's"};
       if (t->dtype == QPC_F32_DEVICE)
         QPC_CUDA_OR_THROW(cudaMemcpyAsync(io.dev, t->data, io.bytes, cudaMemcpyDeviceToDevice, p->stream));
+      else if (pinned_contains(t->data, io.bytes))  // caller's pinned buffer: DMA, no staging
+        QPC_CUDA_OR_THROW(cudaMemcpyAsync(io.dev, t->data, io.bytes, cudaMemcpyHostToDevice, p->stream));
       else
         QPC_CUDA_OR_THROW(staged_h2d(io.dev, io.host, t->data, io.bytes, p->stream));
     }

@@ -80,3 +80,33 @@ def test_session_u8_image_input(cuda_ctx):
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
     d = s.run_deferred({"x": img})
     assert np.array_equal(d.complete()[0].view(np.uint32), ref.view(np.uint32))
+
+
+def test_pinned_inputs_and_output_views(cuda_ctx):
+    """Inputs in library-pinned host memory (qpc_host_alloc) go to the device by
+    DMA straight from the caller's buffer; complete(copy=False) returns
+    read-only views of the run's pinned outputs.  Both give the bytes of the
+    staged / copied path; the plan instance held by the views is reused once
+    they are dropped."""
+    from qppocr_b200 import nets
+    g, w = nets.build_det()
+    g = q.optimize(g, w)
+    s = cuda_ctx.create_session(g, w, role="det", math="3xtf32")
+    img = rsz_src(sw=128, sh=96, n=2, salt=9)
+    ref = s.run({"x": img})[0]
+    pin = q.host_empty(img.shape, np.uint8)
+    pin[...] = img
+    a = s.run_deferred({"x": pin})
+    b = s.run_deferred({"x": pin})
+    va = a.complete(copy=False)[0]
+    vb = b.complete(copy=False)[0]
+    assert not va.flags.writeable
+    assert np.array_equal(va.view(np.uint32), ref.view(np.uint32))
+    assert np.array_equal(vb.view(np.uint32), ref.view(np.uint32))
+    del va, vb, a, b
+    x = orc.det_normalize(img)
+    xf = q.host_empty(x.shape, np.float32)
+    xf[...] = x
+    for _ in range(3):
+        got = s.run({"x": xf})[0]
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
