@@ -54,7 +54,10 @@ constexpr int OUT_STAGE_BYTES = BM * 32 * 4;  // one 128 x 32 fp32 output chunk 
 struct GemmArgs {
   int M, N, K;          // M = output rows (pixels/tokens), N = output channels
   unsigned int* err;    // device error word for bounded-wait timeouts
-  int nkb;              // number of 32-wide k-blocks
+  int nkb;              // number of k-blocks
+  int bkw;              // k-block width in floats: 32, or 24 (rows modes, K % 24 == 0 but K % 32 != 0:
+                        // the boxes end at the tensor's edge instead of overrunning it; the
+                        // 128-byte stage rows keep their layout, and 3 of 4 k-steps are issued)
   int m_tiles;          // output row tiles (128 rows each)
   int tma_store;        // 1: output tiles leave through smem staging + TMA store
   GemmEpilogue epi;
@@ -473,8 +476,9 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
-      const uint32_t a_bytes = AM == 2 ? (uint32_t)(BM + args.kw - 1) * BK * 4 : A_TILE_BYTES;
-      const uint32_t b_bytes = (AM == 2 ? args.kw : 1) * SM::B_TILE;
+      const uint32_t a_bytes = AM == 2 ? (uint32_t)(BM + args.kw - 1) * BK * 4
+                                       : (AM == 0 ? (uint32_t)(BM * args.bkw * 4) : A_TILE_BYTES);
+      const uint32_t b_bytes = AM == 2 ? args.kw * SM::B_TILE : (AM == 0 ? (uint32_t)(BN * args.bkw * 4) : SM::B_TILE);
       const uint32_t bytes = SPLIT ? (a_bytes + 2 * b_bytes) : (a_bytes + b_bytes);
       uint32_t it = 0;
       bool ok = true;
@@ -487,9 +491,9 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
           uint8_t* st = smem + s * SM::STAGE;
           mbar_arrive_expect_tx(&full_bar[s], bytes);
           if (AM == 0) {
-            tma_load_2d(st, &tmA, &full_bar[s], kb * BK, tc.m_blk * BM);
-            tma_load_2d(st + SM::A_BYTES, &tmB, &full_bar[s], kb * BK, tc.n0);
-            if (SPLIT) tma_load_2d(st + 2 * SM::A_BYTES + SM::B_BYTES, &tmBlo, &full_bar[s], kb * BK, tc.n0);
+            tma_load_2d(st, &tmA, &full_bar[s], kb * args.bkw, tc.m_blk * BM);
+            tma_load_2d(st + SM::A_BYTES, &tmB, &full_bar[s], kb * args.bkw, tc.n0);
+            if (SPLIT) tma_load_2d(st + 2 * SM::A_BYTES + SM::B_BYTES, &tmBlo, &full_bar[s], kb * args.bkw, tc.n0);
           } else if (AM == 2) {
             // halo row of input row oy + ky - ph, columns ox0 - pw .. ox0 - pw + 128 + kw - 2
             const int ky = kb / args.cblocks, cb = kb % args.cblocks;
@@ -518,15 +522,19 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
         for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
           const bool first = SPLIT ? (kb % CH) == 0 : kb == 0;
           const uint32_t buf = acc_i % NBUF;
-          if (first && acc_i >= (uint32_t)NBUF &&
-              !mbar_wait(&acc_empty[buf], ((acc_i / NBUF) - 1) & 1u, args.err)) {
-            ok = false;
-            break;
+          if (first && acc_i >= (uint32_t)NBUF) {
+            if (!mbar_wait(&acc_empty[buf], ((acc_i / NBUF) - 1) & 1u, args.err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();  // the epilogue's TMEM reads of this accumulator come first
           }
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
+          // Operand stages need no tcgen05 fence: the mbarrier wait orders the
+          // TMA writes and the converters' (proxy-fenced) writes before the MMAs,
+          // and a fence per stage would stall this thread on the MMAs in flight.
           if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
-          tc_fence_after();
           const uint32_t d_tmem = tmem_d + buf * BN;
           const uint32_t a_addr = smem_u32(smem + s * SM::STAGE);
           const uint32_t b_addr = a_addr + SM::A_BYTES;
@@ -534,10 +542,12 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
           const uint32_t blo_addr = alo_addr + SM::A_BYTES;
           // AM 2: tap kx of this kernel row is the halo shifted by kx rows
           const int ntap = AM == 2 ? args.kw : 1;
+          const int ksteps = AM == 0 ? args.bkw / 8 : BK / 8;
           for (int kx = 0; kx < ntap; ++kx) {
             const uint32_t a_off = (uint32_t)kx * 128u, b_off = (uint32_t)kx * SM::B_TILE;
 #pragma unroll
             for (int ks = 0; ks < BK / 8; ++ks) {
+              if (ks >= ksteps) break;
               const uint32_t acc = (!first || kx > 0 || ks > 0) ? 1u : 0u;
               const uint64_t ad = sw128_kmajor_desc(a_addr + a_off + ks * 32);
               const uint64_t bd = sw128_kmajor_desc(b_addr + b_off + ks * 32);
@@ -587,7 +597,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
         // They do not depend on the stage's data: load them before its wait.
         float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), gb = ga;
         if (GATED && ghw >= BM) {
-          const int ch = kb * BK + (((t & 7) ^ ((t >> 3) & 7)) << 2);
+          const int ch = kb * args.bkw + (((t & 7) ^ ((t >> 3) & 7)) << 2);
           if (ch < args.K) {
             ga = __ldg(reinterpret_cast<const float4*>(gate + img0 * (int64_t)args.K + ch));
             gb = __ldg(reinterpret_cast<const float4*>(gate + img1 * (int64_t)args.K + ch));
@@ -603,7 +613,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
           if (GATED) {
             // logical (row, channel quad) of swizzled 16-byte chunk i
             const int row = i >> 3, c4 = (i & 7) ^ (row & 7);
-            const int ch = kb * BK + c4 * 4;
+            const int ch = kb * args.bkw + c4 * 4;
             if (row0 + row < args.M && ch < args.K) {
               float4 g4;
               if (ghw >= BM) {
@@ -866,14 +876,16 @@ __global__ void __launch_bounds__(256, 1)
         const TileCoord tc = tile_coord(args, tile, 1, BN);
         const int rows = min(RB, args.oh - tc.oy0);
         const uint32_t buf = acc_i & 1u;
-        if (acc_i >= 2 && !mbar_wait(&acc_empty[buf], ((acc_i >> 1) - 1) & 1u, args.err)) break;
+        if (acc_i >= 2) {
+          if (!mbar_wait(&acc_empty[buf], ((acc_i >> 1) - 1) & 1u, args.err)) break;
+          tc_fence_after();  // the epilogue's TMEM reads of this accumulator come first
+        }
         const uint32_t d_base = tmem_d + buf * (RB * BN);
         for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
           const int j = kb / cblocks, cb = kb % cblocks;
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
-          tc_fence_after();
           const uint32_t a_addr = smem_u32(ring + s * HALO_BYTES);
           for (int ky = 0; ky < kh; ++ky) {
             const int i = j - ky;  // output row of this tile fed by kernel row ky
@@ -1069,14 +1081,16 @@ __global__ void __launch_bounds__(256, 1)
         const TileCoord tc = tile_coord(args, tile, 1, 32);
         const int rows = min(rb, args.oh - tc.oy0);
         const uint32_t buf = acc_i & 1u;
-        if (acc_i >= 2 && !mbar_wait(&acc_empty[buf], ((acc_i >> 1) - 1) & 1u, args.err)) break;
+        if (acc_i >= 2) {
+          if (!mbar_wait(&acc_empty[buf], ((acc_i >> 1) - 1) & 1u, args.err)) break;
+          tc_fence_after();  // the epilogue's TMEM reads of this accumulator come first
+        }
         const uint32_t d_base = tmem_d + buf * (uint32_t)(rb * nf);
         for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
           const int j = kb / cblocks, cb = kb % cblocks;
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
-          tc_fence_after();
           const uint32_t a_addr = smem_u32(ring + s * A_TILE_BYTES);
           for (int ky = 0; ky < kh; ++ky) {
             const int i = j - ky;  // output row of this tile fed by kernel row ky
@@ -1334,6 +1348,12 @@ int fold_smem(const ConvGeom& g, int* w_bytes_out) {
   return w_bytes + FOLD_STAGES * A_TILE_BYTES + exch + 2 * OUT_STAGE_BYTES + 1024;
 }
 
+// k-block width of a rows-mode GEMM: 32 floats (one 128-byte swizzle row),
+// or 24 when K is a multiple of 24 but not of 32, so that every TMA box ends
+// at the tensor's edge (a box overrunning the inner dimension was measured
+// several times slower in the kernel's ring).
+int k_block_width(int K) { return (K % 32 != 0 && K % 24 == 0) ? 24 : BK; }
+
 // Output tile width: the smallest N tile that covers N with the least padding
 // (3xTF32 keeps its promoted accumulator in registers: at most 128 columns).
 int pick_bn(int n, bool split) {
@@ -1400,17 +1420,18 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
   const bool split = math == MATH_3XTF32;
   if (split && !b_lo) return cudaErrorInvalidValue;
   const int bn = pick_bn(N, split);
+  const int bkw = k_block_width(K);
   CUtensorMap ma, mb, mblo;
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)lda * 4};
-    const uint32_t box[2] = {BK, BM};
+    const uint32_t box[2] = {(uint32_t)bkw, BM};
     if (!make_map(&ma, a, 2, dims, strides, box)) return cudaErrorInvalidValue;
   }
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t strides[1] = {(uint64_t)K * 4};
-    const uint32_t box[2] = {BK, (uint32_t)bn};
+    const uint32_t box[2] = {(uint32_t)bkw, (uint32_t)bn};
     if (!make_map(&mb, b, 2, dims, strides, box)) return cudaErrorInvalidValue;
     if (split && !make_map(&mblo, b_lo, 2, dims, strides, box)) return cudaErrorInvalidValue;
     if (!split) mblo = mb;
@@ -1419,7 +1440,8 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
   args.M = (int)M;
   args.N = N;
   args.K = K;
-  args.nkb = (K + BK - 1) / BK;
+  args.bkw = bkw;
+  args.nkb = (K + bkw - 1) / bkw;
   args.epi = epi;
   args.err = err;
   CUtensorMap mo = ma;
@@ -1452,17 +1474,18 @@ cudaError_t launch_convt_pair(const float* x, int n, int h, int w, int c, const 
   std::memcpy(pc.w2, consts + 256, sizeof(pc.w2));
   const bool split = math == MATH_3XTF32;
   if (split && (!b1_lo || misaligned(b1_lo))) return cudaErrorInvalidValue;
+  const int bkw = k_block_width(c);
   CUtensorMap ma, mb, mblo;
   {
     const uint64_t dims[2] = {(uint64_t)c, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)c * 4};
-    const uint32_t box[2] = {BK, BM};
+    const uint32_t box[2] = {(uint32_t)bkw, BM};
     if (!make_map(&ma, x, 2, dims, strides, box)) return cudaErrorInvalidValue;
   }
   {
     const uint64_t dims[2] = {(uint64_t)c, 128};
     const uint64_t strides[1] = {(uint64_t)c * 4};
-    const uint32_t box[2] = {BK, 128};
+    const uint32_t box[2] = {(uint32_t)bkw, 128};
     if (!make_map(&mb, b1, 2, dims, strides, box)) return cudaErrorInvalidValue;
     if (split && !make_map(&mblo, b1_lo, 2, dims, strides, box)) return cudaErrorInvalidValue;
     if (!split) mblo = mb;
@@ -1471,7 +1494,8 @@ cudaError_t launch_convt_pair(const float* x, int n, int h, int w, int c, const 
   args.M = (int)M;
   args.N = 128;
   args.K = c;
-  args.nkb = (c + BK - 1) / BK;
+  args.bkw = bkw;
+  args.nkb = (c + bkw - 1) / bkw;
   args.err = err;
   args.tma_store = 0;
   args.epi.out = out;

@@ -124,10 +124,13 @@ bool conv_fold_ok(const ConvGeom& g);
 // (C % 4 != 0 stems, strided kxk).  Input is NCHW when x_nchw != 0 (graph
 // input), NHWC otherwise.  w is the ONNX layout [M][C/group][kh][kw].
 // Accumulation order: ch -> ky -> kx ascending, fma from 0, bias after
-// (gemm.rs:75-128 implicit-GEMM k order).
+// (gemm.rs:75-128 implicit-GEMM k order).  w_host / bias_host: host copies
+// of w and bias (the 3 -> 8/16/32 stride-2 stem specialisation takes its
+// filter by value from them; without them the generic kernel runs).
 cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const float* bias,
                                const float* residual, float* y, const ConvGeom& g, int group,
-                               const ActParams& act, cudaStream_t st, unsigned int* err = nullptr);
+                               const ActParams& act, cudaStream_t st, unsigned int* err = nullptr,
+                               const float* w_host = nullptr, const float* bias_host = nullptr);
 
 // ---- det / rec pre and post (prepost.cu), bit-exact with the reference's
 // host code.  Images are n x h x w x 3 uint8 (HWC), masks n x h x w uint8.

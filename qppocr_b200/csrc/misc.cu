@@ -159,20 +159,23 @@ constexpr int STEM_TH = 8, STEM_TW = 64, STEM_IR = 2 * STEM_TH + 1, STEM_IC = 13
 constexpr int STEM_BOX_BYTES = 3 * STEM_IR * STEM_IC * 4;           // 26,928 bytes per load
 constexpr int STEM_BUF = ((STEM_BOX_BYTES + 1023) / 1024) * 1024;   // buffer stride, 1024-aligned
 
+// Filter and bias by value in the kernel parameters: the unrolled FMA chain
+// reads them as constant-bank operands (no shared-memory weight loads).
+template <int M>
+struct StemConsts {
+  float w[27][M];  // [(ch * 3 + ky) * 3 + kx][m]
+  float b[M];      // zeros when the conv has no bias
+};
+
 template <int M>
 __global__ void __launch_bounds__(256) conv_stem3s2_kernel(
-    const __grid_constant__ CUtensorMap tmX, const float* __restrict__ w, const float* __restrict__ bias,
+    const __grid_constant__ CUtensorMap tmX, const __grid_constant__ StemConsts<M> sc, int has_bias,
     const float* __restrict__ residual, float* __restrict__ y, int N, int OH, int OW, int PH, int PW,
     ActParams act, unsigned int* err) {
   extern __shared__ __align__(1024) uint8_t stem_raw[];
   float* xs0 = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(stem_raw) + 1023) & ~(uintptr_t)1023);
-  __shared__ __align__(16) float wsm[27 * M];
   __shared__ __align__(8) uint64_t full[2];
   const int tid = threadIdx.x;
-  for (int i = tid; i < 27 * M; i += 256) {
-    const int k = i / M, m = i % M;
-    wsm[i] = w[m * 27 + k];
-  }
   if (tid == 0) {
     mbar_init(&full[0], 1);
     mbar_init(&full[1], 1);
@@ -221,18 +224,10 @@ __global__ void __launch_bounds__(256) conv_stem3s2_kernel(
             const int k = (ch * 3 + ky) * 3 + kx;
             const float* row = xs + (ch * STEM_IR + 2 * tr + ky) * STEM_IC + d + kx;
             const float v0 = row[2 * tc], v1 = row[2 * tc + 64];
-            const float4* wk = reinterpret_cast<const float4*>(wsm + k * M);
 #pragma unroll
-            for (int i4 = 0; i4 < M / 4; ++i4) {
-              const float4 wv = wk[i4];
-              a0[4 * i4] = __fmaf_rn(wv.x, v0, a0[4 * i4]);
-              a0[4 * i4 + 1] = __fmaf_rn(wv.y, v0, a0[4 * i4 + 1]);
-              a0[4 * i4 + 2] = __fmaf_rn(wv.z, v0, a0[4 * i4 + 2]);
-              a0[4 * i4 + 3] = __fmaf_rn(wv.w, v0, a0[4 * i4 + 3]);
-              a1[4 * i4] = __fmaf_rn(wv.x, v1, a1[4 * i4]);
-              a1[4 * i4 + 1] = __fmaf_rn(wv.y, v1, a1[4 * i4 + 1]);
-              a1[4 * i4 + 2] = __fmaf_rn(wv.z, v1, a1[4 * i4 + 2]);
-              a1[4 * i4 + 3] = __fmaf_rn(wv.w, v1, a1[4 * i4 + 3]);
+            for (int i = 0; i < M; ++i) {
+              a0[i] = __fmaf_rn(sc.w[k][i], v0, a0[i]);
+              a1[i] = __fmaf_rn(sc.w[k][i], v1, a1[i]);
             }
           }
       const int oy = oy0 + tr;
@@ -244,9 +239,9 @@ __global__ void __launch_bounds__(256) conv_stem3s2_kernel(
         float o[M];
 #pragma unroll
         for (int i = 0; i < M; ++i) o[i] = px ? a1[i] : a0[i];
-        if (bias)
+        if (has_bias)
 #pragma unroll
-          for (int i = 0; i < M; ++i) o[i] = __fadd_rn(o[i], __ldg(bias + i));
+          for (int i = 0; i < M; ++i) o[i] = __fadd_rn(o[i], sc.b[i]);
         apply_act_n(o, act);
         if (residual)
 #pragma unroll
@@ -272,10 +267,12 @@ __global__ void __launch_bounds__(256) conv_stem3s2_kernel(
 
 cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const float* bias,
                                const float* residual, float* y, const ConvGeom& g, int group,
-                               const ActParams& act, cudaStream_t st, unsigned int* err) {
+                               const ActParams& act, cudaStream_t st, unsigned int* err, const float* w_host,
+                               const float* bias_host) {
   const int mg = g.m / group;
   const int64_t pix = (int64_t)g.n * g.oh * g.ow;
-  if (group == 1 && x_nchw && err && g.c == 3 && g.kh == 3 && g.kw == 3 && g.sh == 2 && g.sw == 2 &&
+  if (group == 1 && x_nchw && err && w_host && (!bias || bias_host) && g.c == 3 && g.kh == 3 && g.kw == 3 &&
+      g.sh == 2 && g.sw == 2 &&
       (g.m == 8 || g.m == 16 || g.m == 32) && (g.w % 4) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     CUtensorMap map;
@@ -287,6 +284,10 @@ cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const
       const int64_t tiles = (int64_t)g.n * ((g.oh + STEM_TH - 1) / STEM_TH) * ((g.ow + STEM_TW - 1) / STEM_TW);
 #define QPC_STEM(M_)                                                                                    \
   if (g.m == M_) {                                                                                      \
+    StemConsts<M_> sc;                                                                                  \
+    for (int k = 0; k < 27; ++k)                                                                        \
+      for (int m = 0; m < M_; ++m) sc.w[k][m] = w_host[m * 27 + k];                                     \
+    for (int m = 0; m < M_; ++m) sc.b[m] = bias ? bias_host[m] : 0.0f;                                  \
     auto kern = conv_stem3s2_kernel<M_>;                                                                \
     static int per_sm = 0;                                                                              \
     if (!per_sm) {                                                                                      \
@@ -296,8 +297,8 @@ cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const
         per_sm = 1;                                                                                     \
     }                                                                                                   \
     const int64_t cap = 148LL * per_sm;                                                                 \
-    kern<<<(int)(tiles < cap ? tiles : cap), 256, smem, st>>>(map, w, bias, residual, y, g.n, g.oh, g.ow, \
-                                                              g.ph, g.pw, act, err);                    \
+    kern<<<(int)(tiles < cap ? tiles : cap), 256, smem, st>>>(map, sc, bias ? 1 : 0, residual, y, g.n,  \
+                                                              g.oh, g.ow, g.ph, g.pw, act, err);        \
     return cudaGetLastError();                                                                          \
   }
       QPC_STEM(8)

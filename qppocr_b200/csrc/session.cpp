@@ -1336,8 +1336,13 @@ class Planner {
       const float* wr = S.dweight(n.in[1], "raw");
       const double bytes = 4.0 * N * H * W * C + out_bytes + (has_res ? out_bytes : 0);
       const int grp = (int)group;
+      // host copies (kernel-parameter filters); the session owns the weights
+      const HostTensor* wh = S.weight(n.in[1]);
+      const HostTensor* bh = has_bias ? S.weight(n.in[2]) : nullptr;
+      const float* w_host = (wh && wh->dtype == QPC_F32) ? wh->f.data() : nullptr;
+      const float* b_host = (bh && bh->dtype == QPC_F32) ? bh->f.data() : nullptr;
       step("conv_direct", nm, bytes, flops, [=](cudaStream_t s) {
-        return launch_conv_direct(xp, nchw_in ? 1 : 0, wr, bias, rp, yp, g, grp, act, s, err);
+        return launch_conv_direct(xp, nchw_in ? 1 : 0, wr, bias, rp, yp, g, grp, act, s, err, w_host, b_host);
       });
       unref(x);
     }
