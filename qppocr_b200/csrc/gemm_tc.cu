@@ -299,17 +299,17 @@ __device__ __forceinline__ void argmax_tile(const GemmArgs& args, int64_t orow, 
   if (orow >= 0) e.partials[(int64_t)n_blk * args.M + orow] = make_float4(m, __uint_as_float((unsigned)mi), s, 0.f);
 }
 
-// ConvT pair epilogue for one tile (A_MODE 4, launch_convt_pair): row r is
-// input pixel `orow` of the first ConvT and its 128 columns are that layer's
-// outputs for the sub-pixels s = 2 dy + dx, 32 columns each.  Per sub-pixel:
-// BN (fma(acc, scale, shift)), act1, then the second ConvT's four outputs
-// sum_m z[m] * w2[m][ey][ex] (m ascending, fma from 0; padding columns carry
-// zero weights) and act2.  The pixel's 4 x 4 output block leaves as four
-// 16-byte row segments (a warp's 32 pixels write 512 contiguous bytes per
-// output row).  `cs` is the shared-memory copy of scale, shift and w2.
-template <class Consts, class Fetch>
-__device__ __forceinline__ void pair_tile(const GemmArgs& args, int64_t orow, const Consts& pc,
-                                          Fetch&& fetch) {
+// ConvT pair epilogue for one tile (A_MODE 4: up to 32 channels between the
+// layers, A_MODE 5: up to 24; launch_convt_pair): row r is input pixel
+// `orow` of the first ConvT and its 128 columns are that layer's outputs for
+// the sub-pixels s = 2 dy + dx, 32 columns each.  Per sub-pixel: + BN shift
+// (the scale is folded into the filter), act1, then the second ConvT's four
+// outputs sum_m z[m] * w2[m][ey][ex] (m ascending, fma from 0) and act2.
+// The pixel's 4 x 4 output block leaves as four 16-byte row segments (a
+// warp's 32 pixels write 512 contiguous bytes per output row).  `pc` (shift,
+// w2) sits in the kernel parameters.
+template <int PM, class Consts, class Fetch>
+__device__ __forceinline__ void pair_tile(const GemmArgs& args, int64_t orow, const Consts& pc, Fetch&& fetch) {
   const GemmEpilogue& e = args.epi;
   const int64_t ow = 4 * (int64_t)e.pair_w;
   float* dst = nullptr;
@@ -329,11 +329,11 @@ __device__ __forceinline__ void pair_tile(const GemmArgs& args, int64_t orow, co
       float v[32];
       fetch(32 * s, v);  // warp-collective
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = __fmaf_rn(v[j], pc.scale[32 * s + j], pc.shift[32 * s + j]);
+      for (int j = 0; j < PM; ++j) v[j] = __fadd_rn(v[j], pc.shift[32 * s + j]);
       apply_act_n(v, e.act);
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
-      for (int m = 0; m < 32; ++m) {
+      for (int m = 0; m < PM; ++m) {
         a0 = __fmaf_rn(v[m], pc.w2[m][0], a0);
         a1 = __fmaf_rn(v[m], pc.w2[m][1], a1);
         a2 = __fmaf_rn(v[m], pc.w2[m][2], a2);
@@ -362,9 +362,9 @@ __device__ __forceinline__ void pair_tile(const GemmArgs& args, int64_t orow, co
 // (a second layer per row), and it stages no output in shared memory.
 template <int BN, bool SPLIT, int A_MODE = 0>
 struct Roles {
-  static constexpr int EPI_GROUPS = SPLIT ? 1 : ((BN <= 32 || A_MODE == 4) ? 4 : 2);
+  static constexpr int EPI_GROUPS = SPLIT ? 1 : ((BN <= 32 || A_MODE >= 4) ? 4 : 2);
   static constexpr int THREADS = 128 + 128 * EPI_GROUPS;
-  static constexpr int STAGING = A_MODE == 4 ? 0 : EPI_GROUPS * 2 * OUT_STAGE_BYTES;
+  static constexpr int STAGING = A_MODE >= 4 ? 0 : EPI_GROUPS * 2 * OUT_STAGE_BYTES;
 };
 
 // Per-mode constants passed by value in the kernel parameters (constant
@@ -373,8 +373,8 @@ struct NoConsts {
   int unused;
 };
 struct PairConsts {
-  float scale[128], shift[128];  // first ConvT's BN per column, zero on padding
-  float w2[32][4];               // second ConvT [m][2 ey + ex], zero rows past M
+  float shift[128];  // first ConvT's BN shift per column (its scale is folded into B), zero on padding
+  float w2[32][4];   // second ConvT [m][2 ey + ex], zero rows past M
 };
 template <int A_MODE>
 struct ModeConsts {
@@ -382,6 +382,10 @@ struct ModeConsts {
 };
 template <>
 struct ModeConsts<4> {
+  using type = PairConsts;
+};
+template <>
+struct ModeConsts<5> {
   using type = PairConsts;
 };
 // TMEM accumulators: 8 for 32-column tiles, 4 up to 128 columns, 2 otherwise
@@ -424,9 +428,10 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
   using SM = Smem<BN, SPLIT, A_MODE>;
   // A_MODE 3: rows mode (0) with the per-image channel gate applied to A;
   // A_MODE 4: rows mode with the ConvT pair epilogue (pair_tile)
-  constexpr int AM = (A_MODE == 3 || A_MODE == 4) ? 0 : A_MODE;
+  constexpr int AM = (A_MODE == 3 || A_MODE >= 4) ? 0 : A_MODE;
   constexpr bool GATED = A_MODE == 3;
-  constexpr bool PAIR = A_MODE == 4;
+  constexpr bool PAIR = A_MODE >= 4;
+  constexpr int PAIR_M = A_MODE == 5 ? 24 : 32;
   constexpr int NBUF = Accs<BN, SPLIT>::NBUF;
   constexpr int NGRP = Roles<BN, SPLIT, A_MODE>::EPI_GROUPS;
   constexpr uint32_t TMEM_COLS = (NBUF * BN < 32) ? 32 : NBUF * BN;
@@ -700,7 +705,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
           }
         };
         if constexpr (PAIR) {
-          pair_tile(args, orow, mc, fetch);
+          pair_tile<PAIR_M>(args, orow, mc, fetch);
         } else if (e.partials) {
           argmax_tile<BN>(args, orow, tc.n0, tc.n0 / BN, fetch);
         } else if (args.tma_store) {
@@ -750,7 +755,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
               for (int j = 0; j < 32; ++j) v[j] = accr[(cb + j) % (SPLIT ? BN : 1)];
         };
         if constexpr (PAIR) {
-          pair_tile(args, orow, mc, fetch);
+          pair_tile<PAIR_M>(args, orow, mc, fetch);
         } else if (e.partials) {
           argmax_tile<BN>(args, orow, tc.n0, tc.n0 / BN, fetch);
         } else if (args.tma_store) {
@@ -1458,10 +1463,11 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
   return dispatch<0>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
 }
 
-cudaError_t launch_convt_pair(const float* x, int n, int h, int w, int c, const float* b1,
+cudaError_t launch_convt_pair(const float* x, int n, int h, int w, int c, int m1, const float* b1,
                               const float* b1_lo, const float* consts, const ActParams& act1,
                               const ActParams& act2, float* out, int math, unsigned int* err,
                               cudaStream_t st) {
+  if (m1 <= 0 || m1 > 32) return cudaErrorInvalidValue;
   const int64_t M = (int64_t)n * h * w;
   if (M <= 0) return cudaSuccess;
   auto misaligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; };
@@ -1469,9 +1475,8 @@ cudaError_t launch_convt_pair(const float* x, int n, int h, int w, int c, const 
       misaligned(out))
     return cudaErrorInvalidValue;
   PairConsts pc;
-  std::memcpy(pc.scale, consts, sizeof(pc.scale));
-  std::memcpy(pc.shift, consts + 128, sizeof(pc.shift));
-  std::memcpy(pc.w2, consts + 256, sizeof(pc.w2));
+  std::memcpy(pc.shift, consts, sizeof(pc.shift));
+  std::memcpy(pc.w2, consts + 128, sizeof(pc.w2));
   const bool split = math == MATH_3XTF32;
   if (split && (!b1_lo || misaligned(b1_lo))) return cudaErrorInvalidValue;
   const int bkw = k_block_width(c);
@@ -1505,6 +1510,9 @@ cudaError_t launch_convt_pair(const float* x, int n, int h, int w, int c, const 
   args.epi.pair_act = act2;
   const int grid_m = (int)((M + BM - 1) / BM);
   args.m_tiles = grid_m;
+  if (m1 <= 24)
+    return split ? run_kernel<128, true, 5>(ma, mb, mblo, ma, args, grid_m, st, pc)
+                 : run_kernel<128, false, 5>(ma, mb, mblo, ma, args, grid_m, st, pc);
   return split ? run_kernel<128, true, 4>(ma, mb, mblo, ma, args, grid_m, st, pc)
                : run_kernel<128, false, 4>(ma, mb, mblo, ma, args, grid_m, st, pc);
 }

@@ -102,16 +102,16 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
 // channel (DB head: ConvT -> BN -> act1 -> ConvT -> act2; executor.rs:654-731,
 // conv.rs:730-838), as one tcgen05 GEMM of the first layer whose epilogue
 // finishes the second, so the 2x-upsampled intermediate is never written.
-//   x     n x h x w x c NHWC, c % 4 == 0
-//   b1    [128][c]: row 32 (2 dy + dx) + m = W1[c][m][dy][dx] for m < m1
-//         (m1 <= 32; other rows zero), tf32-rounded (b1_lo: 3xTF32 residue)
-//   consts  scale[128], shift[128] (BN of the first layer, y = fma(acc,
-//         scale, shift), zero on padding columns), w2[32][4] = W2[m][0][ey][ex]
-//         (zero rows past m1); 384 floats in HOST memory, passed to the kernel
-//         by value
+//   x     n x h x w x c NHWC, c % 4 == 0; m1 (<= 32) channels between the layers
+//   b1    [128][c]: row 32 (2 dy + dx) + m = W1[c][m][dy][dx] * scale[m] for
+//         m < m1 (the first layer's BN scale folded in; other rows zero),
+//         tf32-rounded (b1_lo: 3xTF32 residue)
+//   consts  shift[128] (BN shift of the first layer per column, zero on
+//         padding columns), w2[32][4] = W2[m][0][ey][ex] (zero rows past m1);
+//         256 floats in HOST memory, passed to the kernel by value
 //   out   n x 4h x 4w (one channel): out[4y + 2dy + ey][4x + 2dx + ex] =
-//         act2(sum_m act1(fma(acc[32 s + m], scale, shift)) * w2[m][2 ey + ex])
-cudaError_t launch_convt_pair(const float* x, int n, int h, int w, int c, const float* b1,
+//         act2(sum_m act1(acc[32 s + m] + shift) * w2[m][2 ey + ex])
+cudaError_t launch_convt_pair(const float* x, int n, int h, int w, int c, int m1, const float* b1,
                               const float* b1_lo, const float* consts, const ActParams& act1,
                               const ActParams& act2, float* out, int math, unsigned int* err,
                               cudaStream_t st);

@@ -1415,35 +1415,38 @@ class Planner {
     const int64_t N = x0.shape[0], C = x0.shape[1], H = x0.shape[2], W = x0.shape[3];
     if (w1->shape[0] != C) throw GraphError{"ConvTranspose: weight C_in mismatch"};
     const int64_t M = w1->shape[1];
+    // BN of the first layer as plan_convt computes it (shape.rs:700-733):
+    // y = acc * a + b; the scale a goes into the filter, the shift b into
+    // the epilogue.
+    std::vector<float> bn_a(M, 1.f), bn_b(M, 0.f);
+    if (n.has_in(2)) {
+      const float eps = n.getf("qpc_eps", 1e-5f);
+      const HostTensor* sc = S.weight(n.in[2]);
+      const HostTensor* bi = S.weight(n.in[3]);
+      const HostTensor* me = S.weight(n.in[4]);
+      const HostTensor* va = S.weight(n.in[5]);
+      for (int64_t m = 0; m < M; ++m) {
+        bn_a[m] = sc->f[m] / std::sqrt(va->f[m] + eps);
+        bn_b[m] = std::fma(-me->f[m], bn_a[m], bi->f[m]);
+      }
+    }
     // B operand [128][C]: column block s = 2 dy + dx, row m < M
     std::vector<float> b1(128 * C, 0.f);
     for (int64_t s = 0; s < 4; ++s)
       for (int64_t m = 0; m < M; ++m)
-        for (int64_t c = 0; c < C; ++c) b1[(32 * s + m) * C + c] = w1->f[((c * M + m) * 2 + s / 2) * 2 + s % 2];
+        for (int64_t c = 0; c < C; ++c)
+          b1[(32 * s + m) * C + c] = w1->f[((c * M + m) * 2 + s / 2) * 2 + s % 2] * bn_a[m];
     const bool split = S.math() == MATH_3XTF32;
     std::vector<float> hi(b1.size()), lo(b1.size());
     for (size_t k = 0; k < b1.size(); ++k) {
       hi[k] = tf32_rn_host(b1[k]);
       lo[k] = tf32_rn_host(b1[k] - hi[k]);
     }
-    // scale[128], shift[128], w2[32][4]; BN as plan_convt folds it (shape.rs:700-733)
-    std::vector<float> cs(384, 0.f);
+    // shift[128], w2[32][4]
+    std::vector<float> cs(256, 0.f);
     for (int64_t m = 0; m < M; ++m) {
-      float a = 1.f, b = 0.f;
-      if (n.has_in(2)) {
-        const float eps = n.getf("qpc_eps", 1e-5f);
-        const HostTensor* sc = S.weight(n.in[2]);
-        const HostTensor* bi = S.weight(n.in[3]);
-        const HostTensor* me = S.weight(n.in[4]);
-        const HostTensor* va = S.weight(n.in[5]);
-        a = sc->f[m] / std::sqrt(va->f[m] + eps);
-        b = std::fma(-me->f[m], a, bi->f[m]);
-      }
-      for (int64_t s = 0; s < 4; ++s) {
-        cs[32 * s + m] = a;
-        cs[128 + 32 * s + m] = b;
-      }
-      for (int e = 0; e < 4; ++e) cs[256 + 4 * m + e] = w2->f[m * 4 + e];
+      for (int64_t s = 0; s < 4; ++s) cs[32 * s + m] = bn_b[m];
+      for (int e = 0; e < 4; ++e) cs[128 + 4 * m + e] = w2->f[m * 4 + e];
     }
     const float* b1p = upload_temp(hi);
     const float* b1lo = split ? upload_temp(lo) : nullptr;
@@ -1466,8 +1469,8 @@ class Planner {
     unsigned int* err = device_state(S.device()).err_word;
     const int math = S.math();
     step("convt_pair", n.name, bytes, flops, [=](cudaStream_t s) {
-      return launch_convt_pair(xp, (int)N, (int)H, (int)W, (int)C, b1p, b1lo, cs.data(), act1, act2, yp, math,
-                               err, s);
+      return launch_convt_pair(xp, (int)N, (int)H, (int)W, (int)C, (int)M, b1p, b1lo, cs.data(), act1, act2, yp,
+                               math, err, s);
     });
     unref(x);
     define(n.out[0], y);
