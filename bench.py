@@ -155,12 +155,11 @@ def barrier(world):
 # or per line (rec), measured by ncu on the full-size bench workload (det
 # batch 64, rec batch 256; profiles/det_b64_launch_list.md).  The roofline's
 # `traffic` is this times the batch, for the dominant family.
-DET_TRAFFIC_PER_IMAGE = {"gemm_tc": 10491990, "conv_tc": 12609374, "dwconv": 15406045,
-                         "convt2x2": 26149256, "conv_direct": 25452224, "resize": 5645492,
-                         "gap": 1383436, "det_preprocess": 3216060}
-REC_TRAFFIC_PER_LINE = {"gemm_tc": 115978, "dwconv": 278276, "head_gemm": 54866, "bmm_small": 58288,
-                        "layernorm": 19268, "softmax": 51302, "conv_direct": 207445, "pool2d": 232145,
-                        "head_combine": 94134, "binary": 23150, "copy": 19274}
+DET_TRAFFIC_PER_IMAGE = {"gemm_tc": 10566357, "dwconv": 15433708, "conv_tc": 12610016, "conv_direct": 25488540,
+                         "resize": 5656441, "convt_pair": 8569284, "gap": 1383448, "det_preprocess": 3216060}
+REC_TRAFFIC_PER_LINE = {"gemm_tc": 116037, "dwconv": 276898, "head_gemm": 54868, "bmm_small": 58286,
+                        "layernorm": 19268, "softmax": 57812, "pool2d": 232776, "head_combine": 94134,
+                        "conv_direct": 209837, "binary": 23147, "copy": 19274}
 TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, profiles/det_b64_launch_list.md, scaled by batch"
 
 
