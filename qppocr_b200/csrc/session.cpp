@@ -206,6 +206,7 @@ Session::~Session() {
   for (auto& kv : plans_)
     for (auto& p : kv.second)
       if (p->stream) cudaStreamSynchronize(p->stream);
+  if (compute_done_) cudaEventDestroy(compute_done_);
 }
 
 void Session::validate_ops() const {
@@ -2359,13 +2360,19 @@ PlanInstance* Session::launch(const qpc_tensor* inputs, int n) {
       else
         QPC_CUDA_OR_THROW(staged_h2d(io.dev, io.host, t->data, io.bytes, p->stream));
     }
-    QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[1], p->stream));
-    if (p->exec) {
-      QPC_CUDA_OR_THROW(cudaGraphLaunch(p->exec, p->stream));
-    } else {
-      for (size_t k = 0; k < p->steps.size(); ++k) QPC_CUDA_OR_THROW(p->steps[k](p->stream));
+    {
+      std::lock_guard<std::mutex> lk(launch_mu_);
+      if (!compute_done_) QPC_CUDA_OR_THROW(cudaEventCreateWithFlags(&compute_done_, cudaEventDisableTiming));
+      QPC_CUDA_OR_THROW(cudaStreamWaitEvent(p->stream, compute_done_, 0));  // the previous run's graph first
+      QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[1], p->stream));
+      if (p->exec) {
+        QPC_CUDA_OR_THROW(cudaGraphLaunch(p->exec, p->stream));
+      } else {
+        for (size_t k = 0; k < p->steps.size(); ++k) QPC_CUDA_OR_THROW(p->steps[k](p->stream));
+      }
+      QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[2], p->stream));
+      QPC_CUDA_OR_THROW(cudaEventRecord(compute_done_, p->stream));
     }
-    QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[2], p->stream));
     for (auto& io : p->outs)
       QPC_CUDA_OR_THROW(cudaMemcpyAsync(io.host, io.dev, io.count * sizeof(float), cudaMemcpyDeviceToHost, p->stream));
     QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[3], p->stream));

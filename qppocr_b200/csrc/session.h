@@ -125,6 +125,12 @@ class Session {
   std::unordered_map<std::string, HostTensor> weights_;
   std::unordered_map<std::string, std::unique_ptr<DevBuf>> dev_cache_;
   std::mutex mu_;
+  // Runs of this session execute their graphs one after another: each
+  // graph waits for the previous run's graph (compute_done_), so two runs in
+  // flight overlap one's copies with the other's compute instead of sharing
+  // the SMs and finishing together.
+  std::mutex launch_mu_;
+  cudaEvent_t compute_done_ = nullptr;
   std::map<std::string, std::vector<std::unique_ptr<PlanInstance>>> plans_;
   uint64_t tick_ = 0;
   std::vector<StepInfo> prof_;
