@@ -593,40 +593,71 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
       const int64_t img0 = GATED ? row0 / ghw : 0;
       const int r0 = GATED ? (int)(row0 - img0 * ghw) : 0;
       const int64_t img1 = GATED ? min(img0 + 1, img_last) : 0;
+      // Chunk i = t + 64 j is row (t >> 3) + 8 j, channel quad (t & 7) ^ ((t >> 3) & 7):
+      // the same quad for all of this thread's chunks, so with >= 128-row
+      // images only two gate values (this image's, the next one's) occur,
+      // the next one's from tile row rsw on.  They do not depend on the
+      // stage's data: each stage's pair is loaded one stage ahead.
+      const int quad = ((t & 7) ^ ((t >> 3) & 7)) << 2;
+      const int rsw = GATED ? ghw - r0 : 0;
+      auto gate_pair = [&](int kb, float4& ga, float4& gb) {
+        ga = make_float4(0.f, 0.f, 0.f, 0.f);
+        gb = ga;
+        const int ch = kb * args.bkw + quad;
+        if (ch < args.K) {
+          ga = __ldg(reinterpret_cast<const float4*>(gate + img0 * (int64_t)args.K + ch));
+          gb = __ldg(reinterpret_cast<const float4*>(gate + img1 * (int64_t)args.K + ch));
+        }
+      };
+      float4 ga_next = make_float4(0.f, 0.f, 0.f, 0.f), gb_next = ga_next;
+      if (GATED && ghw >= BM) gate_pair(0, ga_next, gb_next);
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1u;
-        // Chunk i = t + 64 j is row (t >> 3) + 8 j, channel quad (t & 7) ^ ((t >> 3) & 7):
-        // the same quad for all of this thread's chunks, so with >= 128-row
-        // images only two gate values (this image's, the next one's) occur.
-        // They do not depend on the stage's data: load them before its wait.
-        float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), gb = ga;
-        if (GATED && ghw >= BM) {
-          const int ch = kb * args.bkw + (((t & 7) ^ ((t >> 3) & 7)) << 2);
-          if (ch < args.K) {
-            ga = __ldg(reinterpret_cast<const float4*>(gate + img0 * (int64_t)args.K + ch));
-            gb = __ldg(reinterpret_cast<const float4*>(gate + img1 * (int64_t)args.K + ch));
-          }
-        }
+        const float4 ga = ga_next, gb = gb_next;
+        if (GATED && ghw >= BM && kb + 1 < nkb) gate_pair(kb + 1, ga_next, gb_next);
         if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
         float4* a = reinterpret_cast<float4*>(smem + s * SM::STAGE);
         float4* lo = reinterpret_cast<float4*>(smem + s * SM::STAGE + SM::A_BYTES + SM::B_BYTES);
         const int n4 = AM == 2 ? (BM + args.kw - 1) * (BK / 4) : A_TILE_BYTES / 16;
+        if (GATED && ghw >= BM) {
+          // rows past M and channels past K hold TMA zero fill (or, past a
+          // 24-wide k-block, bytes no MMA reads): no bounds checks needed
+#pragma unroll 4
+          for (int i = t; i < n4; i += 64) {
+            float4 v = a[i];
+            const float4 g4 = (i >> 3) >= rsw ? gb : ga;
+            v.x = __fmul_rn(v.x, g4.x);
+            v.y = __fmul_rn(v.y, g4.y);
+            v.z = __fmul_rn(v.z, g4.z);
+            v.w = __fmul_rn(v.w, g4.w);
+            float4 h;
+            h.x = tf32_rna(v.x);
+            h.y = tf32_rna(v.y);
+            h.z = tf32_rna(v.z);
+            h.w = tf32_rna(v.w);
+            a[i] = h;
+            if (SPLIT) {
+              float4 l;
+              l.x = tf32_rna(__fsub_rn(v.x, h.x));
+              l.y = tf32_rna(__fsub_rn(v.y, h.y));
+              l.z = tf32_rna(__fsub_rn(v.z, h.z));
+              l.w = tf32_rna(__fsub_rn(v.w, h.w));
+              lo[i] = l;
+            }
+          }
+        } else {
 #pragma unroll 4
         for (int i = t; i < n4; i += 64) {
           float4 v = a[i];
           if (GATED) {
-            // logical (row, channel quad) of swizzled 16-byte chunk i
+            // logical (row, channel quad) of swizzled 16-byte chunk i; images
+            // of fewer than 128 rows: the row's own image's gate
             const int row = i >> 3, c4 = (i & 7) ^ (row & 7);
             const int ch = kb * args.bkw + c4 * 4;
             if (row0 + row < args.M && ch < args.K) {
-              float4 g4;
-              if (ghw >= BM) {
-                g4 = r0 + row >= ghw ? gb : ga;
-              } else {
-                const int64_t img = img0 + (r0 + row) / ghw;
-                g4 = __ldg(reinterpret_cast<const float4*>(gate + img * (int64_t)args.K + ch));
-              }
+              const int64_t img = img0 + (r0 + row) / ghw;
+              const float4 g4 = __ldg(reinterpret_cast<const float4*>(gate + img * (int64_t)args.K + ch));
               v.x = __fmul_rn(v.x, g4.x);
               v.y = __fmul_rn(v.y, g4.y);
               v.z = __fmul_rn(v.z, g4.z);
@@ -647,6 +678,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
             l.w = tf32_rna(__fsub_rn(v.w, h.w));
             lo[i] = l;
           }
+        }
         }
         fence_proxy_async_smem();
         mbar_arrive(&conv_bar[s]);
