@@ -1029,6 +1029,23 @@ __global__ void __launch_bounds__(256, 1)
 // slices are added in fp32 (slice 0, then 1, then 2) in the epilogue.
 // The filter stays in shared memory ([kh][cblocks] tiles of NF rows).
 // Warps: w0 TMA, w1 MMA, w2-3 tf32 rounding of A, w4-7 epilogue.
+// MMAs of one staged input row for kernel rows LO..HI (3-row kernels), as one
+// straight-line run: a runtime loop around MMA issue, closed by a commit,
+// was measured to slow every MMA in it several-fold.
+template <int LO, int HI>
+__device__ __forceinline__ void fold_issue(uint32_t d_base, int j, uint32_t nf, uint32_t a_addr, uint32_t w_addr,
+                                           int cblocks, int cb, uint32_t idesc) {
+#pragma unroll
+  for (int ky = LO; ky <= HI; ++ky) {
+    const uint32_t d = d_base + (uint32_t)(j - ky) * nf;
+    const uint32_t b_addr = w_addr + (uint32_t)(ky * cblocks + cb) * nf * 128u;
+#pragma unroll
+    for (int ks = 0; ks < BK / 8; ++ks)
+      mma_tf32(d, sw128_kmajor_desc(a_addr + ks * 32), sw128_kmajor_desc(b_addr + ks * 32), idesc,
+               (ky | cb | ks) ? 1u : 0u);
+  }
+}
+
 template <int STAGES>
 __global__ void __launch_bounds__(256, 1)
     conv_fold_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
@@ -1129,6 +1146,19 @@ __global__ void __launch_bounds__(256, 1)
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
           const uint32_t a_addr = smem_u32(ring + s * A_TILE_BYTES);
+          if (kh == 3) {
+            // kernel rows ky with output row j - ky inside the tile: lo..hi
+            const int lo = max(0, j - (rows - 1)), hi = min(2, j);
+            switch (lo * 4 + hi) {
+              case 0: fold_issue<0, 0>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
+              case 1: fold_issue<0, 1>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
+              case 2: fold_issue<0, 2>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
+              case 5: fold_issue<1, 1>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
+              case 6: fold_issue<1, 2>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
+              case 10: fold_issue<2, 2>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
+              default: break;  // lo > hi: no output row of this tile uses input row j
+            }
+          } else
           for (int ky = 0; ky < kh; ++ky) {
             const int i = j - ky;  // output row of this tile fed by kernel row ky
             if (i < 0 || i >= rows) continue;
