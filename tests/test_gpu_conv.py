@@ -96,8 +96,9 @@ def test_conv_upsampled_residual(cuda_ctx, case, math):
     assert err < TOL[math], err
 
 
+@pytest.mark.parametrize("hw", [(10, 14), (5, 6), (16, 16)])  # tiles crossing images; images < 128 px; aligned
 @pytest.mark.parametrize("math", ["tf32", "3xtf32"])
-def test_se_gate_fused_into_pointwise(cuda_ctx, math):
+def test_se_gate_fused_into_pointwise(cuda_ctx, math, hw):
     """SE block (GAP -> 1x1 -> relu -> 1x1 -> HardSigmoid -> Mul) feeding a
     1x1 conv: the gate multiply runs inside the conv's GEMM as A is rounded,
     so the plan has no separate elementwise Mul; results match the oracle."""
@@ -106,7 +107,7 @@ def test_se_gate_fused_into_pointwise(cuda_ctx, math):
     y = b.conv(y, 64, 96, 1, bias=True, bn=False, act="hswish")
     g, wts = b.graph(["x"], [y], [[1, 64, 0, 0]])
     g = q.optimize(g, wts)
-    x = np.random.Generator(np.random.PCG64(5)).uniform(-1, 1, (3, 64, 10, 14)).astype(np.float32)
+    x = np.random.Generator(np.random.PCG64(5)).uniform(-1, 1, (3, 64) + hw).astype(np.float32)
     ref = orc.run_graph(g, wts, {"x": x})[0]
     s = cuda_ctx.create_session(g, wts, role="other", math=math)
     got = s.run({"x": x})[0]

@@ -80,7 +80,9 @@ def test_dwconv_bit_exact(cuda_ctx, n, h, w, c, k, s, act, res):
 
 @pytest.mark.parametrize("m,k,n", [(6400, 16, 32), (6400, 64, 128), (25600, 128, 256),
                                    (6400, 256, 512), (6400, 512, 512), (1000, 120, 360),
-                                   (77, 36, 24), (300, 480, 120), (129, 120, 18709)])
+                                   (77, 36, 24), (300, 480, 120), (129, 120, 18709),
+                                   # 24-wide k-blocks (K % 24 == 0, K % 32 != 0), ragged rows
+                                   (3000, 24, 96), (1001, 48, 64), (517, 240, 120), (260, 72, 300)])
 @pytest.mark.parametrize("math", ["tf32", "3xtf32"])
 def test_gemm_parity(cuda_ctx, m, k, n, math):
     import torch
