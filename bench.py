@@ -470,7 +470,7 @@ def main():
         crng = np.random.Generator(np.random.PCG64(40 + rank))
         crops = [crng.integers(0, 256, (int(crng.integers(24, 65)), int(crng.integers(32, 401)), 3),
                                dtype=np.uint8) for _ in range(1024)]
-        stage = RecStage(rs)
+        stage = RecStage(rs, device=local)
         stage.run(crops)  # plans for every batch width
         barrier(world)
         t0 = time.perf_counter()

@@ -387,6 +387,7 @@ class CudaSession:
     def __init__(self, handle: ctypes.c_void_p, input_names: List[str]):
         self._h = handle
         self.input_names = input_names
+        self.device = 0
 
     def _inputs(self, keep, inputs):
         if isinstance(inputs, dict):
@@ -507,7 +508,9 @@ class CudaContext:
         h = ctypes.c_void_p()
         _check(lib().qpc_session_create(self.index, ctypes.byref(qg), wt, nw, ROLE[role], ctypes.byref(opts),
                                         ctypes.byref(h)))
-        return CudaSession(h, list(graph.inputs))
+        sess = CudaSession(h, list(graph.inputs))
+        sess.device = self.index  # the GPU the session's buffers and streams live on
+        return sess
 
 
 # ------------------------------------------------------------------ operator entry points
@@ -610,8 +613,11 @@ def op_rec_pack(crops, off, h, w, rw, pad, img_h: int, img_w: int, stream=None):
     import torch
     n = int(h.numel())
     out = torch.empty((n, 3, img_h, img_w), dtype=torch.float32, device=crops.device)
-    _check(lib().qpc_op_rec_pack(_dptr(crops), _dptr(off), _dptr(h), _dptr(w), _dptr(rw), _dptr(pad), n, img_h,
-                                 img_w, _dptr(out), stream))
+    # on the tensors' own GPU and its current torch stream, whatever the caller's current device
+    with torch.cuda.device(crops.device):
+        st = stream if stream is not None else torch.cuda.current_stream(crops.device).cuda_stream
+        _check(lib().qpc_op_rec_pack(_dptr(crops), _dptr(off), _dptr(h), _dptr(w), _dptr(rw), _dptr(pad), n, img_h,
+                                     img_w, _dptr(out), st))
     return out
 
 

@@ -123,7 +123,8 @@ class RecStage:
     a rec session created by CudaContext.create_session(role="rec")."""
 
     def __init__(self, session, img_h: int = 48, min_width: int = 16, pad_min_h: float = 0.0,
-                 grain: Optional[int] = None, per_batch: Optional[int] = None, charset=None, device: int = 0):
+                 grain: Optional[int] = None, per_batch: Optional[int] = None, charset=None,
+                 device: Optional[int] = None):
         self.s = session
         self.img_h = img_h
         self.min_width = min_width
@@ -132,7 +133,8 @@ class RecStage:
         self.per_batch = session.rec_chunk() if per_batch is None else per_batch
         self.charset = charset
         self.pairs = session.rec_argmax_pairs()
-        self.device = device
+        # device tensors (crops, packed batches) live on the session's own GPU
+        self.device = getattr(session, "device", 0) if device is None else device
         self.batches = 0
 
     def plan(self, shapes: Sequence[Tuple[int, int]]):

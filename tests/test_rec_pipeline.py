@@ -50,3 +50,29 @@ def test_ctc_decode_pairs_matches_oracle():
     pairs[:, 1] = pairs[:, 1].astype(np.uint32).view(np.float32)
     text, conf = rp.ctc_decode_pairs(pairs, charset=["_", "a", "b"])
     assert text == "ba" and conf == np.float32((0.8 + 0.7 + 0.6) / 3)
+
+
+class _FakeRecSession:
+    """Capability queries only (DeviceSession caps, device.rs:134-163)."""
+
+    def __init__(self, device):
+        self.device = device
+
+    def bucket_grain(self):
+        return 64
+
+    def rec_chunk(self):
+        return 256
+
+    def rec_argmax_pairs(self):
+        return True
+
+
+def test_rec_stage_uses_the_sessions_gpu():
+    """The stage's device tensors (crops, packed batches) live on the GPU of
+    the session they feed, so a rank driving GPU 1 never hands it GPU-0
+    memory; an explicit device still wins."""
+    from qppocr_b200.rec_pipeline import RecStage
+
+    assert RecStage(_FakeRecSession(1)).device == 1
+    assert RecStage(_FakeRecSession(3), device=2).device == 2
