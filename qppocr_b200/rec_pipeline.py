@@ -108,6 +108,29 @@ def ctc_decode_pairs(pairs, charset: Optional[Sequence[str]] = None):
     return out, conf
 
 
+def ctc_decode_pairs_batch(pairs, charset: Optional[Sequence[str]] = None):
+    """ctc_decode_pairs over a batch [B, T, 2] with array operations.  The
+    confidence sum runs left to right in f64 (cumsum), as the per-line loop
+    does, so the results are identical."""
+    pairs = np.asarray(pairs, np.float32)
+    b, t = pairs.shape[0], pairs.shape[1]
+    idx = np.ascontiguousarray(pairs[:, :, 1]).view(np.uint32).astype(np.int64)
+    vals = pairs[:, :, 0].astype(np.float64)
+    prev = np.empty_like(idx)
+    prev[:, 0] = -1
+    prev[:, 1:] = idx[:, :-1]
+    emit = (idx != 0) & (idx != prev)
+    cnt = emit.sum(axis=1)
+    sums = np.cumsum(np.where(emit, vals, 0.0), axis=1)[:, -1] if t else np.zeros(b)
+    keep = emit if charset is None else emit & (idx < len(charset))
+    out = []
+    for k in range(b):
+        conf = np.float32(sums[k] / cnt[k]) if cnt[k] else np.float32(0.0)
+        ids = idx[k][keep[k]].tolist()
+        out.append(("".join(charset[i] for i in ids) if charset is not None else ids, conf))
+    return out
+
+
 def ctc_decode_probs(probs, charset: Optional[Sequence[str]] = None):
     """rec.rs:34-79 on one line's [T, C] probabilities (first strict max)."""
     probs = np.asarray(probs, np.float32)
@@ -191,6 +214,9 @@ class RecStage:
 
     def _finish(self, d, ids, results):
         out = d.complete()[0]
-        for k, i in enumerate(ids):
-            results[i] = ctc_decode_pairs(out[k], self.charset) if self.pairs else ctc_decode_probs(out[k],
-                                                                                                    self.charset)
+        if self.pairs:
+            for i, r in zip(ids, ctc_decode_pairs_batch(out[:len(ids)], self.charset)):
+                results[i] = r
+        else:
+            for k, i in enumerate(ids):
+                results[i] = ctc_decode_probs(out[k], self.charset)

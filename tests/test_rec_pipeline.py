@@ -76,3 +76,24 @@ def test_rec_stage_uses_the_sessions_gpu():
 
     assert RecStage(_FakeRecSession(1)).device == 1
     assert RecStage(_FakeRecSession(3), device=2).device == 2
+
+
+def test_batch_decode_matches_per_line():
+    """The array form of the pairs decode gives the per-line loop's indices,
+    text and f64-mean confidence exactly (rec.rs:82-120), blanks, repeats,
+    out-of-charset indices and all-blank lines included."""
+    from qppocr_b200.rec_pipeline import ctc_decode_pairs, ctc_decode_pairs_batch
+
+    rng = np.random.Generator(np.random.PCG64(12))
+    b, t = 37, 40
+    pairs = np.empty((b, t, 2), np.float32)
+    pairs[:, :, 0] = rng.uniform(1e-6, 1.0, (b, t)).astype(np.float32)
+    idx = rng.integers(0, 6, (b, t)).astype(np.uint32)
+    idx[3] = 0  # an all-blank line
+    pairs[:, :, 1] = idx.view(np.float32)
+    charset = ["_", "a", "b", "c", "d"]  # index 5 is outside the charset
+    for cs in (None, charset):
+        got = ctc_decode_pairs_batch(pairs, cs)
+        for k in range(b):
+            ref = ctc_decode_pairs(pairs[k], cs)
+            assert got[k][0] == ref[0] and got[k][1] == ref[1] and type(got[k][1]) == type(ref[1])
