@@ -52,6 +52,10 @@ struct ActParams {
   int kind;
   float alpha, beta;      // HardSigmoid alpha / beta
   float c1, c2, c3;       // GELU constants
+  // depthwise conv only: round the final output to tf32 (nearest), set when
+  // every consumer is a TF32 GEMM that rounds its A operand the same way, so
+  // the GEMM can skip that pass and the results do not change
+  int round_tf32;
 };
 
 // exp1: the reference's polynomial exp (activation.rs:28-47): clamp to

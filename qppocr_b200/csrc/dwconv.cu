@@ -76,6 +76,7 @@ __global__ void __launch_bounds__(256) dwconv_nhwc_kernel(
         o.z = __fadd_rn(o.z, rr.z);
         o.w = __fadd_rn(o.w, rr.w);
       }
+      if (act.round_tf32) o = make_float4(tf32_rna(o.x), tf32_rna(o.y), tf32_rna(o.z), tf32_rna(o.w));
       reinterpret_cast<float4*>(y)[oidx] = o;
     }
   }
@@ -106,7 +107,7 @@ __global__ void __launch_bounds__(256) dwconv_nhwc_generic(
       }
     float o = apply_act(__fadd_rn(acc, bias ? __ldg(bias + c) : 0.f), act);
     if (residual) o = __fadd_rn(o, __ldg(residual + t));
-    y[t] = o;
+    y[t] = act.round_tf32 ? tf32_rna(o) : o;
   }
 }
 
@@ -248,6 +249,7 @@ __global__ void __launch_bounds__(256, MINB) dwconv_tile_kernel(
             v.z = __fadd_rn(v.z, rr.z);
             v.w = __fadd_rn(v.w, rr.w);
           }
+          if (act.round_tf32) v = make_float4(tf32_rna(v.x), tf32_rna(v.y), tf32_rna(v.z), tf32_rna(v.w));
           *reinterpret_cast<float4*>(y + oidx) = v;
         }
       }

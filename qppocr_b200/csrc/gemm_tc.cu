@@ -619,7 +619,10 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
         if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
         float4* a = reinterpret_cast<float4*>(smem + s * SM::STAGE);
         float4* lo = reinterpret_cast<float4*>(smem + s * SM::STAGE + SM::A_BYTES + SM::B_BYTES);
-        const int n4 = AM == 2 ? (BM + args.kw - 1) * (BK / 4) : A_TILE_BYTES / 16;
+        // (A rounded by its producer: nothing to do but hand the stage on)
+        const int n4 = (AM == 0 && !GATED && !SPLIT && args.epi.a_rounded)
+                           ? 0
+                           : (AM == 2 ? (BM + args.kw - 1) * (BK / 4) : A_TILE_BYTES / 16);
         if (GATED && ghw >= BM) {
           // rows past M and channels past K hold TMA zero fill (or, past a
           // 24-wide k-block, bytes no MMA reads): no bounds checks needed

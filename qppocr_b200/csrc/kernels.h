@@ -60,6 +60,9 @@ struct GemmEpilogue {
   // writes per row (max, argmax bits, sum exp(l - max)) of its columns to
   // partials[n_tile * M + row] (float4); nothing is written to `out`.
   float4* partials = nullptr;
+  // A already rounded to tf32 by its producer (a depthwise conv with
+  // ActParams::round_tf32): TF32 rows-mode GEMMs skip the rounding pass.
+  int a_rounded = 0;
   // ConvT pair epilogue (two 2x2 stride-2 ConvTranspose layers, the second
   // to one channel; launch_convt_pair): set by that launcher only.
   int pair_h = 0, pair_w = 0;  // input map of the first ConvT

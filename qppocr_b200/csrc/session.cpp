@@ -944,6 +944,33 @@ class Planner {
     return -1;
   }
 
+  // Whether every consumer of `o` is a TF32 pointwise conv that reads it as
+  // its GEMM A operand (input 0 only), so `o` may be stored tf32-rounded: the
+  // GEMM would round it to the same values.
+  std::set<std::string> tf32_rounded_;
+  bool feeds_only_tf32_pointwise(const std::string& o) {
+    if (S.math() != QPC_MATH_TF32) return false;
+    for (auto& go : S.graph_outputs())
+      if (go == o) return false;
+    auto cit = consumers_.find(o);
+    if (cit == consumers_.end() || cit->second.empty()) return false;
+    for (int ci : cit->second) {
+      const Node& c = S.nodes()[ci];
+      if (c.op != "Conv" || c.in.size() < 2 || c.in[0] != o) return false;
+      for (size_t k = 1; k < c.in.size(); ++k)
+        if (c.in[k] == o) return false;
+      const HostTensor* w = S.weight(c.in[1]);
+      if (!w || w->shape.size() != 4 || w->shape[2] != 1 || w->shape[3] != 1 || (w->shape[1] % 4) != 0)
+        return false;
+      if (c.geti("group", 1) != 1) return false;
+      for (auto v : c.getints("strides"))
+        if (v != 1) return false;
+      for (auto v : c.getints("pads"))
+        if (v != 0) return false;
+    }
+    return true;
+  }
+
   // If `o` (4-D, NHWC-produced) feeds only a channel Concat, return the view of
   // its slice in the Concat's buffer (allocated now, at the first part, so no
   // buffer that is live in between can alias it).
@@ -1246,8 +1273,13 @@ class Planner {
       const float* xp = out_ptr(x);
       const float* wt = S.dweight(n.in[1], "dw");
       const double bytes = 4.0 * N * H * W * C + out_bytes + (has_res ? out_bytes : 0);
+      ActParams dact = act;
+      if (feeds_only_tf32_pointwise(n.out[0])) {
+        dact.round_tf32 = 1;
+        tf32_rounded_.insert(n.out[0]);
+      }
       step("dwconv", nm, bytes, flops,
-           [=](cudaStream_t s) { return launch_dwconv_nhwc(xp, wt, bias, rp, yp, g, act, s, err); });
+           [=](cudaStream_t s) { return launch_dwconv_nhwc(xp, wt, bias, rp, yp, g, dact, s, err); });
       unref(x);
     } else if (pw1) {
       Val x = as_nhwc(x0, nm);
@@ -1273,6 +1305,8 @@ class Planner {
       if (gate) {
         e.a_gate = gate;
         e.a_gate_rows = (int)(H * W);
+      } else if (tf32_rounded_.count(n.in[0])) {
+        e.a_rounded = 1;
       }
       const int64_t rows = N * H * W;
       const double bytes = 4.0 * rows * C + out_bytes + 4.0 * M * C + res_bytes;
