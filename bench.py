@@ -155,11 +155,11 @@ def barrier(world):
 # or per line (rec), measured by ncu on the full-size bench workload (det
 # batch 64, rec batch 256; profiles/det_b64_launch_list.md).  The roofline's
 # `traffic` is this times the batch, for the dominant family.
-DET_TRAFFIC_PER_IMAGE = {"gemm_tc": 10566357, "dwconv": 15433708, "conv_tc": 12610016, "conv_direct": 25488540,
-                         "resize": 5656441, "convt_pair": 8569284, "gap": 1383448, "det_preprocess": 3216060}
-REC_TRAFFIC_PER_LINE = {"gemm_tc": 116037, "dwconv": 276898, "head_gemm": 54868, "bmm_small": 58286,
-                        "layernorm": 19268, "softmax": 57812, "pool2d": 232776, "head_combine": 94134,
-                        "conv_direct": 209837, "binary": 23147, "copy": 19274}
+DET_TRAFFIC_PER_IMAGE = {"gemm_tc": 10579557, "dwconv": 15433143, "conv_tc": 12606576, "conv_direct": 25509848,
+                         "resize": 5653212, "convt_pair": 8577152, "gap": 1383226, "det_preprocess": 3216060}
+REC_TRAFFIC_PER_LINE = {"gemm_tc": 115481, "dwconv": 276782, "head_gemm": 54870, "bmm_small": 58308,
+                        "layernorm": 19268, "softmax": 51293, "pool2d": 231737, "head_combine": 94134,
+                        "conv_direct": 209899, "binary": 23149, "copy": 19274}
 TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, profiles/det_b64_launch_list.md, scaled by batch"
 
 
