@@ -462,7 +462,9 @@ def main():
         rprof = rs.profile({"x": xr}, iters=2)
         xr_pin = q.host_empty(xr.shape, np.float32)
         xr_pin[...] = xr
-        re2e = max_over_ranks(e2e_seconds(rs, {"x": xr_pin}, args.steps, world), world)
+        # a rec step is ~1.7 ms: time at least 50 of them so host jitter averages out
+        rec_e2e_steps = max(args.steps, 50)
+        re2e = max_over_ranks(e2e_seconds(rs, {"x": xr_pin}, rec_e2e_steps, world), world)
         # the recognition stage around the session (grouping by width, device
         # line pack, two batches in flight, CTC decode) on variable-size crops
         from qppocr_b200.rec_pipeline import RecStage
@@ -481,7 +483,8 @@ def main():
                "roofline": roofline(rprof, hbm, tf, REC_TRAFFIC_PER_LINE, args.rec_batch),
                "e2e": {"value": round(world * args.rec_batch / re2e, 1), "unit": "lines/s",
                        "h2d_bytes_per_step": int(xr.nbytes),
-                       "d2h_bytes_per_step": int(args.rec_batch * 40 * 2 * 4), "timing": E2E_TIMING},
+                       "d2h_bytes_per_step": int(args.rec_batch * 40 * 2 * 4), "timing": E2E_TIMING,
+                       "steps": rec_e2e_steps},
                "gpu_launches": len(rprof) * args.steps,
                "stage": {"value": round(world * len(crops) / st_s, 1), "unit": "lines/s", "lines": len(crops),
                          "crops": "uint8, h 24-64, w 32-400 (seeded)",
