@@ -152,15 +152,15 @@ def barrier(world):
 
 
 # DRAM bytes (read + write) per launch of each kernel family, per image (det)
-# or per line (rec), measured by ncu on the full-size bench workload (det
-# batch 64, rec batch 256; profiles/det_b64_launch_list.md).  The roofline's
-# `traffic` is this times the batch, for the dominant family.
+# or per line (rec), from ncu dram__bytes_read.sum + dram__bytes_write.sum
+# captures.  The roofline's `traffic` is this times the batch, for the
+# dominant family.
 DET_TRAFFIC_PER_IMAGE = {"gemm_tc": 10579557, "dwconv": 15433143, "conv_tc": 12606576, "conv_direct": 25509848,
                          "resize": 5653212, "convt_pair": 8577152, "gap": 1383226, "det_preprocess": 3216060}
 REC_TRAFFIC_PER_LINE = {"gemm_tc": 115481, "dwconv": 276782, "head_gemm": 54870, "bmm_small": 58308,
                         "layernorm": 19268, "softmax": 51293, "pool2d": 231737, "head_combine": 94134,
                         "conv_direct": 209899, "binary": 23149, "copy": 19274}
-TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, profiles/det_b64_launch_list.md, scaled by batch"
+TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, per image (line), scaled by batch"
 
 
 def roofline(profile, hbm, tf, traffic_per_unit=None, units=1):
@@ -362,6 +362,7 @@ def main():
     ap.add_argument("--math", default="tf32", choices=["tf32", "3xtf32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-rec", action="store_true")
+    ap.add_argument("--no-3x", action="store_true", help="skip the 3xTF32 det line")
     ap.add_argument("--gemm-sweep", action="store_true",
                     help="config 2: time the pointwise GEMM over its M x (K, N) grid and print a table")
     args = ap.parse_args()
@@ -417,6 +418,20 @@ def main():
     ms_max = max_over_ranks(ms, world)
     value = world * B / (ms_max / 1000.0)
 
+    # the fp32-exact mode (3xTF32: meets 1e-5 end to end) on the same batch
+    det_3x = None
+    if args.math == "tf32" and not args.no_3x:
+        d3 = ctx.create_session(g, w, role="det", math="3xtf32")
+        d3.run({"x": x})
+        for _ in range(args.warmup):
+            d3.replay({"x": x}, 1)
+        barrier(world)
+        ms3 = max_over_ranks(d3.replay({"x": x}, args.steps), world)
+        d3.close()
+        det_3x = {"value": round(world * B / (ms3 / 1000.0), 2), "unit": "img/s", "ms_per_step": round(ms3, 3),
+                  "math": "3xtf32", "tolerance": "max|d|/max|ref| < 1e-5 end to end vs the oracle",
+                  "timing": "as value: CUDA-graph replays, inputs resident, CUDA events, max over ranks"}
+
     prof = det.profile({"x": x}, iters=2)
     launches = len(prof)
     rl = roofline(prof, hbm, tf, DET_TRAFFIC_PER_IMAGE, B)
@@ -433,8 +448,9 @@ def main():
     e2e_s = max_over_ranks(e2e_seconds(det, {"x": img_pin}, args.steps, world), world)
     e2e = {"value": round(world * B / e2e_s, 2), "unit": "img/s",
            "h2d_bytes_per_step": int(img.nbytes), "d2h_bytes_per_step": int(B * DET_HW * DET_HW * 4),
-           "input": "u8 HWC images in pinned host memory, normalised on the device in the plan "
-                    "(engine.rs:963-982)",
+           "input": "u8 HWC images in pinned host memory, normalised on the device in the plan as the "
+                    "engine does, (v/255 - 0.5)/0.5 (engine.rs:963-982); config 3's ImageNet mean/std is the "
+                    "same per-channel affine map with other constants, at the same cost",
            "timing": E2E_TIMING}
     e2e_p = max_over_ranks(e2e_seconds(det, {"x": img}, args.steps, world, copy=True), world)
     e2e_pageable = {"value": round(world * B / e2e_p, 2), "unit": "img/s", "h2d_bytes_per_step": int(img.nbytes),
@@ -503,12 +519,16 @@ def main():
             "metric": "det_img_per_s (DB det 3x960x960) + rec_lines_per_s",
             "value": round(value, 2), "unit": "img/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": args.math, "data": "synthetic",
             "config": {"workload": f"config 3: DB det (PP-LCNet x1.0 13-block, DBFPN 96, DB head), "
                                    f"batch {B} x 3x{DET_HW}x{DET_HW} per GPU",
                        "math": args.math, "global_batch": world * B,
                        "parallelism": f"dp{world} (replicas, image shards)",
                        "l2": "inputs 708 MB/step > 126 MB L2, no flush"},
+            "tolerance": ("per fused node max|d|/max|ref| < 1e-3 vs the oracle (teacher forced); end to end "
+                          "< 1e-2 (random-init nets amplify TF32 rounding)" if args.math == "tf32" else
+                          "max|d|/max|ref| < 1e-5 end to end vs the oracle"),
+            "det_3xtf32": det_3x,
             "roofline": rl, "cpu_baseline": cpu, "e2e": e2e, "e2e_pageable": e2e_pageable, "e2e_f32_input": e2e_f32, "clocks": clk,
             "gpu_launches": launches * args.steps, "rec": rec,
         }

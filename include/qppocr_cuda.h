@@ -9,7 +9,7 @@
  *   trait DeviceSession  (crates/qppocr-core/src/device.rs:125-176)
  *   trait DeferredRun    (crates/qppocr-core/src/device.rs:105-108)
  * A thin Rust FFI crate (qppocr-cuda) binds these symbols and implements the
- * traits; the bindings are listed in INTEGRATION.md.
+ * traits.
  *
  * Conventions: every function returns int status (QPC_OK == 0).  On failure,
  * qpc_last_error() returns a thread-local message naming the node, op or CUDA
@@ -273,10 +273,12 @@ int qpc_op_ctc_head(const float* x, int64_t rows, int k, const float* w, const f
  * loop that must not call the CUDA allocator once running).  Same arguments
  * and result as qpc_op_ctc_head; the partials live in a fixed array compiled
  * into this library (32 MiB per device, held until process exit).
- * Limits: rows * ceil(n / 128) <= 2^21, else QPC_ERR_INVALID.  All calls on a
- * device share that array: calls whose kernels overlap on the GPU race.  The
- * first call on a device looks up the array's address (cudaGetSymbolAddress);
- * make it before any stream capture. */
+ * Limit: rows x (column tiles of n) <= 2^21 entries, else QPC_ERR_INVALID;
+ * rows * ceil(n / 128) <= 2^21 is sufficient.  All calls on a device share
+ * that array: calls whose kernels overlap on the GPU race.  A pipeline wait
+ * that runs out is kept (in a fixed word, not allocated) until
+ * qpc_kernel_error reads it.  The first call on a device looks up the
+ * array's address (cudaGetSymbolAddress); make it before any stream capture. */
 int qpc_op_ctc_head_noalloc(const float* x, int64_t rows, int k, const float* w, const float* w_lo,
                             int n, const float* bias, int math, float* pairs, void* stream);
 
@@ -320,9 +322,30 @@ int qpc_op_rec_pack(const uint8_t* crops, const int64_t* off, const int* h, cons
 int qpc_op_db_mask(const float* pred, const uint8_t* mask_in, uint8_t* mask, int n, int h, int w, float thresh,
                    int dilate, void* stream);
 
-/* Device fault / timeout flag raised by kernels with bounded waits on the
- * current device since the last call (0 = none); clears it. */
+/* Device fault / timeout flags raised by kernels with bounded waits on
+ * `device` since the last call (0 = none; 1 = a pipeline wait ran out, 2 = a
+ * kernel saw an impossible shape), including the faults kept by
+ * qpc_op_ctc_head_noalloc; clears them.  Session runs read them after every
+ * run and fail with QPC_ERR_DEVICE. */
 int qpc_kernel_error(int device, unsigned int* flags);
+
+/* ------------------------------------------------ failure-path self-tests
+ * Host-driven checks of the error paths that need no real fault (the
+ * reference's failure handling: no silent fallback, bounded device waits,
+ * crates/qppocr-core/src/device.rs:88-94, vulkan/session.rs:306-312). */
+
+/* Launch one CTA that waits, with the bounded wait of the pipelined kernels
+ * and a limit of limit_us microseconds (1 .. 1e6), on an mbarrier nothing
+ * arrives on, and wait for it to return.  path 0 reports into the device's
+ * fault word, path 1 into the word of qpc_op_ctc_head_noalloc (as its kernels
+ * would after a timed-out wait).  Either way qpc_kernel_error(device) then
+ * returns flag 1 and the device stays usable. */
+int qpc_selftest_wait_timeout(int device, int path, int limit_us);
+
+/* Make the nth device allocation of the library from now on (1 = the next
+ * one; 0 cancels) fail as if the device were out of memory: the call that
+ * makes it returns QPC_ERR_OOM and leaves no state behind. */
+int qpc_inject_alloc_failure(int nth);
 
 #ifdef __cplusplus
 }

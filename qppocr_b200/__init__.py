@@ -51,6 +51,10 @@ class TimeoutError_(DeviceError):
     pass
 
 
+class OutOfMemoryError(DeviceError):
+    """A device or pinned-host allocation failed (QPC_ERR_OOM)."""
+
+
 # ------------------------------------------------------------------ C structs
 class QpcAttr(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char_p), ("kind", ctypes.c_int), ("f", ctypes.c_float),
@@ -98,7 +102,7 @@ EXPORTED = (
     "qpc_session_replay", "qpc_session_node_count", "qpc_session_node", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_ctc_head", "qpc_op_ctc_head_noalloc",
     "qpc_op_split_tf32", "qpc_op_resize_bilinear_rgb_u8", "qpc_op_det_preprocess", "qpc_op_db_mask",
     "qpc_op_rec_pack",
-    "qpc_kernel_error",
+    "qpc_kernel_error", "qpc_selftest_wait_timeout", "qpc_inject_alloc_failure",
 )
 
 _lib = None
@@ -158,6 +162,8 @@ def lib():
     L.qpc_op_ctc_head_noalloc.argtypes = [P, ctypes.c_int64, ctypes.c_int, P, P, ctypes.c_int, P,
                                           ctypes.c_int, P, P]
     L.qpc_kernel_error.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]
+    L.qpc_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.qpc_inject_alloc_failure.argtypes = [ctypes.c_int]
     _lib = L
     return L
 
@@ -170,7 +176,9 @@ def _check(rc: int):
         raise GraphError(msg)
     if rc == QPC_ERR_TIMEOUT:
         raise TimeoutError_(msg)
-    if rc in (QPC_ERR_DEVICE, QPC_ERR_OOM):
+    if rc == QPC_ERR_OOM:
+        raise OutOfMemoryError(msg)
+    if rc == QPC_ERR_DEVICE:
         raise DeviceError(msg)
     raise QppocrError(f"status {rc}: {msg}")
 
@@ -625,3 +633,17 @@ def kernel_error(device: int = 0) -> int:
     f = ctypes.c_uint(0)
     _check(lib().qpc_kernel_error(device, ctypes.byref(f)))
     return f.value
+
+
+def selftest_wait_timeout(device: int = 0, path: str = "device", limit_us: int = 2000) -> None:
+    """Run the bounded-wait self-test kernel: a wait on an mbarrier nothing
+    arrives on runs out after limit_us and reports into the device's fault
+    word (path "device") or the allocation-free CTC head's (path "noalloc");
+    read the flag with kernel_error(device)."""
+    _check(lib().qpc_selftest_wait_timeout(device, {"device": 0, "noalloc": 1}[path], limit_us))
+
+
+def inject_alloc_failure(nth: int = 1) -> None:
+    """Make the nth device allocation of the library from now on fail as if
+    the device were out of memory (0 cancels)."""
+    _check(lib().qpc_inject_alloc_failure(nth))

@@ -24,6 +24,9 @@ int guarded(F&& f) {
   } catch (DeviceError& e) {
     set_error("device: " + e.msg);
     return E_DEVICE;
+  } catch (OomError& e) {
+    set_error("out of memory: " + e.msg);
+    return E_OOM;
   } catch (std::bad_alloc&) {
     set_error("host allocation failed");
     return E_OOM;
@@ -386,7 +389,13 @@ int qpc_op_ctc_head(const float* x, int64_t rows, int k, const float* w, const f
     cudaStream_t st = (cudaStream_t)stream;
     const int ntiles = gemm_tc_col_tiles(n, math);
     void* part = nullptr;
-    QPC_CUDA_OR_THROW(cudaMallocAsync(&part, (size_t)ntiles * rows * sizeof(float4), st));
+    if (alloc_failure_due()) throw OomError{"cudaMallocAsync(ctc head partials): out of memory (injected)"};
+    cudaError_t ae = cudaMallocAsync(&part, (size_t)ntiles * rows * sizeof(float4), st);
+    if (ae == cudaErrorMemoryAllocation) {
+      cudaGetLastError();
+      throw OomError{"cudaMallocAsync(ctc head partials): out of memory"};
+    }
+    QPC_CUDA_OR_THROW(ae);
     GemmEpilogue e;
     e.bias = bias;
     e.partials = static_cast<float4*>(part);
@@ -457,6 +466,33 @@ int qpc_op_db_mask(const float* pred, const uint8_t* mask_in, uint8_t* mask, int
     QPC_CUDA_OR_THROW(launch_db_mask(pred, mask_in, mask, n, h, w, thresh, dilate, (cudaStream_t)stream));
     return (int)OK;
   });
+}
+
+int qpc_selftest_wait_timeout(int device, int path, int limit_us) {
+  if (path < 0 || path > 1 || limit_us < 1 || limit_us > 1000000) {
+    set_error("invalid argument (path 0 or 1, limit_us in [1, 1e6])");
+    return E_INVALID;
+  }
+  return guarded([&] {
+    DeviceState& ds = device_state(device);
+    cudaStream_t st = nullptr;
+    QPC_CUDA_OR_THROW(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    const uint64_t ns = (uint64_t)limit_us * 1000ull;
+    cudaError_t e = path == 0 ? launch_wait_selftest(ds.err_word, ns, st) : noalloc_head_selftest(ns, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaStreamDestroy(st);
+    QPC_CUDA_OR_THROW(e);
+    return (int)OK;
+  });
+}
+
+int qpc_inject_alloc_failure(int nth) {
+  if (nth < 0) {
+    set_error("invalid argument");
+    return E_INVALID;
+  }
+  inject_alloc_failure(nth);
+  return OK;
 }
 
 int qpc_kernel_error(int device, unsigned int* flags) {

@@ -198,19 +198,23 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // false when the time limit passes (raising the error flag) or when another
 // CTA has already raised it (so a broken launch drains in one timeout, not
 // one per CTA).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, unsigned int* err,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 127u) == 0) {
       if (err && *reinterpret_cast<volatile unsigned int*>(err)) return false;
-      if (global_timer_ns() - t0 > kWaitNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         if (err) atomicOr(err, (unsigned)KERR_MBAR_TIMEOUT);
         return false;
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
+  return mbar_wait_for(bar, parity, err, kWaitNs);
 }
 
 // TMA tiled loads (no multicast).  Coordinates are element indices, innermost first.

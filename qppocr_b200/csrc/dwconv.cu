@@ -280,21 +280,11 @@ cudaError_t run_dw_tile(const float* x, const float* wt, const float* bias, cons
   if (!make_tensor_map(&map, x, 4, dims, strides, box, false)) return cudaErrorNotSupported;
   const int smem = T::SMEM;
   auto kern = dwconv_tile_kernel<K, S, CC, TW, TH, MINB>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  cudaError_t ae = ensure_dyn_smem((const void*)kern, smem);
+  if (ae != cudaSuccess) return ae;
   const int64_t tiles = (int64_t)(g.c / CC) * g.n * ((g.oh + TH - 1) / TH) * ((g.ow + TW - 1) / TW);
-  static int per_sm = 0;
-  if (!per_sm && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem) != cudaSuccess ||
-                  per_sm < 1))
-    per_sm = 1;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t cap = (int64_t)sms * per_sm;
+  const int per_sm = blocks_per_sm((const void*)kern, 256, smem);
+  const int64_t cap = (int64_t)current_sm_count() * per_sm;
   const int grid = (int)(tiles < cap ? tiles : cap);
   kern<<<grid, 256, smem, st>>>(map, wt, bias, residual, y, g.n, g.c, g.oh, g.ow, g.ph, g.pw, act, err);
   return cudaGetLastError();

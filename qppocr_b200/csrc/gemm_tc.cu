@@ -1317,15 +1317,7 @@ bool make_tensor_map(CUtensorMap* map, const void* base, int rank, const uint64_
 
 namespace {
 
-int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-  }
-  return n;
-}
+int sm_count() { return current_sm_count(); }
 
 // Ring depth: as many stages as fit next to the output staging buffers and
 // the 1 KB alignment slack in 224 KB of dynamic shared memory (the 227 KB
@@ -1350,12 +1342,7 @@ cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
   constexpr int STAGES = stages_for<BN, SPLIT, A_MODE>();
   auto kern = gemm_tc_kernel<BN, STAGES, SPLIT, A_MODE>;
   const int smem = STAGES * Smem<BN, SPLIT, A_MODE>::STAGE + Roles<BN, SPLIT, A_MODE>::STAGING + 1024;
-  static bool attr_set = false;  // per instantiation
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  if (cudaError_t e = ensure_dyn_smem((const void*)kern, smem); e != cudaSuccess) return e;
   const int grid = tiles < sm_count() ? tiles : sm_count();
   kern<<<grid, Roles<BN, SPLIT, A_MODE>::THREADS, smem, st>>>(a, b, blo, out, args, mc);
   return cudaGetLastError();
@@ -1395,12 +1382,7 @@ cudaError_t run_band(const CUtensorMap& a, const CUtensorMap& w, const CUtensorM
   auto kern = conv_band_kernel<BN, BAND_STAGES, BAND_RB>;
   const int smem = w_bytes + BAND_STAGES * HALO_BYTES + 2 * OUT_STAGE_BYTES + 1024;
   if (w_bytes > BAND_W_MAX) return cudaErrorInvalidValue;
-  static int attr_set = 0;  // per instantiation: the largest size set so far
-  if (smem > attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr_set = smem;
-  }
+  if (cudaError_t e = ensure_dyn_smem((const void*)kern, smem); e != cudaSuccess) return e;
   const int grid = args.m_tiles < sm_count() ? args.m_tiles : sm_count();
   kern<<<grid, 256, smem, st>>>(a, w, out, args, w_bytes);
   return cudaGetLastError();
@@ -1638,12 +1620,7 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
       args.tma_store = make_map(&mo, obase, 4, dims, strides, box) ? 1 : 0;
     }
     auto kern = conv_fold_kernel<FOLD_STAGES>;
-    static int attr_set = 0;
-    if (smem > attr_set) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return e;
-      attr_set = smem;
-    }
+    if (cudaError_t e = ensure_dyn_smem((const void*)kern, smem); e != cudaSuccess) return e;
     const int grid = args.m_tiles < sm_count() ? args.m_tiles : sm_count();
     kern<<<grid, 256, smem, st>>>(ma, mw, mo, args, w_bytes, nf, rb);
     return cudaGetLastError();

@@ -10,8 +10,16 @@
 //
 // Properties a caller must know:
 //  * The array holds at most kMaxPartials float4 (32 MiB) per device.  Every
-//    GPU that loads the library holds it until the process exits.  Calls with
-//    rows * ceil(n / 128) > kMaxPartials are rejected with QPC_ERR_INVALID.
+//    GPU that loads the library holds it until the process exits.  A call
+//    needs rows x (column tiles of n) entries, and is rejected with
+//    QPC_ERR_INVALID above kMaxPartials.  A column tile is 32 to 256 classes
+//    wide, never narrower than min(n, 128) classes, so
+//    rows * ceil(n / 128) <= kMaxPartials is a sufficient (not the exact)
+//    condition for acceptance.
+//  * A bounded wait that runs out inside the kernels is kept in a second
+//    fixed word per device until qpc_kernel_error (or the next session run on
+//    that device) reads and clears it, so the calls report faults like every
+//    other entry point; a call itself returns as soon as it is queued.
 //  * All calls share the one array (per device) and it keeps the last call's
 //    contents.  Two calls whose kernels overlap on the GPU (different streams,
 //    or different host threads) race on it: serialise them.
@@ -31,12 +39,22 @@ constexpr int64_t kMaxPartials = int64_t(1) << 21;  // float4 entries = 32 MiB
 // Device-side storage.  In host code these names are host-side stand-ins, not
 // device addresses: only the pointers from cudaGetSymbolAddress go to kernels.
 static __device__ __align__(256) float4 g_head_partials[kMaxPartials];
-static __device__ __align__(256) unsigned int g_head_err;
+// err[0]: the word this call's kernels report into (cleared at the start of
+// each call, since the kernels stop early while it is set); err[1]: the
+// faults of every call since the last read, kept until the host reads them.
+static __device__ __align__(256) unsigned int g_head_err[2];
 
 struct DevicePtrs {
   float4* partials = nullptr;
   unsigned int* err = nullptr;
 };
+
+// Folds this call's fault word into the kept one and clears it.
+__global__ void keep_fault_kernel(unsigned int* err) {
+  const unsigned v = err[0];
+  if (v) atomicOr(&err[1], v);
+  err[0] = 0;
+}
 
 std::mutex g_mu;
 constexpr int kMaxDevices = 64;
@@ -81,7 +99,8 @@ extern "C" int qpc_op_ctc_head_noalloc(const float* x, int64_t rows, int k, cons
   if (rows == 0) return QPC_OK;
   const int ntiles = qpc::gemm_tc_col_tiles(n, math);
   if ((int64_t)ntiles * rows > kMaxPartials) {
-    qpc::set_error("ctc head (no-alloc): rows * ceil(n / 128) = " + std::to_string((int64_t)ntiles * rows) +
+    qpc::set_error("ctc head (no-alloc): rows * column tiles = " + std::to_string(rows) + " * " +
+                   std::to_string(ntiles) + " = " + std::to_string((int64_t)ntiles * rows) +
                    " exceeds the fixed scratch of " + std::to_string(kMaxPartials) + " entries");
     return QPC_ERR_INVALID;
   }
@@ -94,8 +113,9 @@ extern "C" int qpc_op_ctc_head_noalloc(const float* x, int64_t rows, int k, cons
   DevicePtrs p;
   if (!device_ptrs(dev, &p)) return QPC_ERR_DEVICE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The error word must start each call at zero; the partials are fully
-  // rewritten by the GEMM before the combine reads them.
+  // The call's own fault word must start at zero (its kernels stop early
+  // while it is set); the partials are fully rewritten by the GEMM before the
+  // combine reads them.  The fold afterwards keeps any fault for the host.
   e = cudaMemsetAsync(p.err, 0, sizeof(unsigned int), st);
   qpc::GemmEpilogue epi;
   epi.bias = bias;
@@ -103,9 +123,52 @@ extern "C" int qpc_op_ctc_head_noalloc(const float* x, int64_t rows, int k, cons
   epi.ldo = n;
   if (e == cudaSuccess) e = qpc::launch_gemm_tc(x, rows, k, k, w, w_lo, n, epi, math, p.err, st);
   if (e == cudaSuccess) e = qpc::launch_argmax_combine(p.partials, ntiles, rows, pairs, st);
+  if (e == cudaSuccess) {
+    keep_fault_kernel<<<1, 1, 0, st>>>(p.err);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) {
     qpc::set_error(std::string("device: ctc head (no-alloc) launch: ") + cudaGetErrorString(e));
     return QPC_ERR_DEVICE;
   }
   return QPC_OK;
 }
+
+namespace qpc {
+
+// Faults kept by the allocation-free CTC head on `dev` since the last read
+// (0 if it never ran there); reads and clears them.  The device is current
+// (take_kernel_error sets it).
+// The failure path of a call whose bounded wait runs out, without the GEMM:
+// the self-test wait kernel reports into this call's word, then the fold
+// keeps it, as after a real timeout.
+cudaError_t noalloc_head_selftest(uint64_t limit_ns, cudaStream_t st) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  DevicePtrs p;
+  if (!device_ptrs(dev, &p)) return cudaErrorInvalidSymbol;
+  e = cudaMemsetAsync(p.err, 0, sizeof(unsigned int), st);
+  if (e == cudaSuccess) e = launch_wait_selftest(p.err, limit_ns, st);
+  if (e == cudaSuccess) {
+    keep_fault_kernel<<<1, 1, 0, st>>>(p.err);
+    e = cudaGetLastError();
+  }
+  return e;
+}
+
+unsigned int take_noalloc_head_error(int dev) {
+  unsigned int* err = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (dev >= 0 && dev < kMaxDevices) err = g_ptrs[dev].err;
+  }
+  if (!err) return 0;
+  unsigned int v = 0;
+  QPC_CUDA_OR_THROW(cudaMemcpy(&v, err + 1, sizeof(v), cudaMemcpyDeviceToHost));
+  if (v) QPC_CUDA_OR_THROW(cudaMemset(err + 1, 0, sizeof(v)));
+  return v;
+}
+
+}  // namespace qpc

@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include "common.cuh"
+#include "runtime.h"
 
 namespace qpc {
 
@@ -26,6 +27,13 @@ struct ConvGeom {
 // swizzle (tensor-core operands) instead of the plain row layout.
 bool make_tensor_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                      const uint64_t* strides, const uint32_t* box, bool swizzle128);
+
+// Failure-path self-test: one CTA initialises an mbarrier that nothing ever
+// arrives on and waits for it with the bounded wait every pipelined kernel
+// uses (mbar_wait_for), here with a limit of limit_ns.  The wait runs out,
+// raises KERR_MBAR_TIMEOUT in `err` and the kernel returns: the context stays
+// usable and the host reads the flag like any kernel fault.
+cudaError_t launch_wait_selftest(unsigned int* err, uint64_t limit_ns, cudaStream_t st);
 
 // Depthwise conv (group == C, one filter per channel), NHWC in/out.
 // wt is tap-major [kh*kw][C].  out = act(sum_taps + bias) (+ residual).

@@ -15,6 +15,22 @@ static int grid_for(int64_t threads, int block = 256) {
 #define GRID_LOOP(i, total) \
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (total); i += (int64_t)gridDim.x * blockDim.x)
 
+// ------------------------------------------------------------ self-test
+__global__ void wait_selftest_kernel(unsigned int* err, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    // nothing arrives: phase 0 never completes, so the bounded wait runs out
+    mbar_wait_for(&bar, 0, err, limit_ns);
+  }
+}
+
+cudaError_t launch_wait_selftest(unsigned int* err, uint64_t limit_ns, cudaStream_t st) {
+  wait_selftest_kernel<<<1, 32, 0, st>>>(err, limit_ns);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------ direct conv
 // Implicit-GEMM per-element semantics of conv.rs:553-637 / gemm.rs:75-128 and
 // 523-589: k order ch -> ky -> kx; acc from 0 then + bias, except M%4 tail rows
@@ -289,14 +305,9 @@ cudaError_t launch_conv_direct(const float* x, int x_nchw, const float* w, const
       for (int m = 0; m < M_; ++m) sc.w[k][m] = w_host[m * 27 + k];                                     \
     for (int m = 0; m < M_; ++m) sc.b[m] = bias ? bias_host[m] : 0.0f;                                  \
     auto kern = conv_stem3s2_kernel<M_>;                                                                \
-    static int per_sm = 0;                                                                              \
-    if (!per_sm) {                                                                                      \
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                    \
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem) != cudaSuccess ||     \
-          per_sm < 1)                                                                                   \
-        per_sm = 1;                                                                                     \
-    }                                                                                                   \
-    const int64_t cap = 148LL * per_sm;                                                                 \
+    if (cudaError_t ae = ensure_dyn_smem((const void*)kern, smem); ae != cudaSuccess) return ae;        \
+    const int per_sm = blocks_per_sm((const void*)kern, 256, smem);                                     \
+    const int64_t cap = (int64_t)current_sm_count() * per_sm;                                           \
     kern<<<(int)(tiles < cap ? tiles : cap), 256, smem, st>>>(map, sc, bias ? 1 : 0, residual, y, g.n,  \
                                                               g.oh, g.ow, g.ph, g.pw, act, err);        \
     return cudaGetLastError();                                                                          \
@@ -625,15 +636,10 @@ cudaError_t launch_convt2x2(const float* x, const float* wt, const float* bn_a, 
     if (make_tensor_map(&map, x, 2, dims, strides, box, false)) {
       auto kern = convt2x2_tma_kernel<24, 24, SLOTS, PIX>;
       const int smem = 2 * PIX * 24 * 4 + 1024;
-      static int per_sm = 0;
-      if (!per_sm) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, SLOTS * 24, smem) != cudaSuccess ||
-            per_sm < 1)
-          per_sm = 1;
-      }
+      if (cudaError_t ae = ensure_dyn_smem((const void*)kern, smem); ae != cudaSuccess) return ae;
+      const int per_sm = blocks_per_sm((const void*)kern, SLOTS * 24, smem);
       const int64_t chunks = (pixels + PIX - 1) / PIX;
-      const int64_t cap = 148LL * per_sm;
+      const int64_t cap = (int64_t)current_sm_count() * per_sm;
       kern<<<(int)(chunks < cap ? chunks : cap), SLOTS * 24, smem, st>>>(map, wt, bn_a, bn_b, y, n, h, w, act,
                                                                          err);
       return cudaGetLastError();

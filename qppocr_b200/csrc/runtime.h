@@ -23,6 +23,10 @@ struct GraphError {
 struct DeviceError {
   std::string msg;
 };
+// A device allocation that failed for lack of memory (QPC_ERR_OOM).
+struct OomError {
+  std::string msg;
+};
 
 #define QPC_CUDA_OR_THROW(expr)                                                           \
   do {                                                                                    \
@@ -38,8 +42,34 @@ struct DeviceState {
 };
 DeviceState& device_state(int device);  // sets the device current; throws DeviceError
 
-// Reads and clears the device error word (after the caller synchronised).
+// Reads and clears the device error word (after the caller synchronised),
+// ORed with the word of the allocation-free CTC head on that device.
 unsigned int take_kernel_error(int device);
+
+// Reads and clears the error word of the allocation-free CTC head on the
+// current device (head_noalloc.cu); 0 when it was never called there.
+unsigned int take_noalloc_head_error(int device);
+// Runs the bounded-wait self-test into the allocation-free head's own fault
+// word and keeps the fault there, as a timed-out call would (current device).
+cudaError_t noalloc_head_selftest(uint64_t limit_ns, cudaStream_t st);
+
+// Launch configuration, per device.  cudaFuncSetAttribute applies to the
+// current device only, so the dynamic shared-memory opt-in of a kernel is
+// recorded per (device, kernel) - the largest size set so far - under a
+// mutex; a process with sessions on several GPUs sets it on each.
+cudaError_t ensure_dyn_smem(const void* func, int bytes);
+// SM count of the current device.
+int current_sm_count();
+// Resident blocks per SM of `func` at (threads, smem) on the current device
+// (at least 1), after ensure_dyn_smem(func, smem).
+int blocks_per_sm(const void* func, int threads, int smem);
+
+// Test hook: when > 0, the n-th device allocation made by the library from
+// now on (DevBuf, plan arenas, the stream-ordered scratch of the operator
+// entry points) fails as if the device were out of memory, once.
+void inject_alloc_failure(int nth);
+// True when an injected failure is due for this allocation (consumes it).
+bool alloc_failure_due();
 
 // Owning device allocation.
 struct DevBuf {

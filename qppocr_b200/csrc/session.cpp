@@ -25,6 +25,7 @@
 #include <set>
 #include <sstream>
 #include <thread>
+#include <tuple>
 
 #include "kernels.h"
 #include "misc.h"
@@ -36,13 +37,27 @@ static thread_local std::string g_err;
 void set_error(const std::string& m) { g_err = m; }
 const std::string& last_error() { return g_err; }
 
+static std::atomic<int> g_alloc_fail_countdown{0};
+void inject_alloc_failure(int nth) { g_alloc_fail_countdown.store(nth > 0 ? nth : 0); }
+bool alloc_failure_due() {
+  int v = g_alloc_fail_countdown.load();
+  while (v > 0) {
+    if (g_alloc_fail_countdown.compare_exchange_weak(v, v - 1)) return v == 1;
+  }
+  return false;
+}
+
 DevBuf::DevBuf(size_t n) : bytes(n) {
   if (n) {
+    if (alloc_failure_due())
+      throw OomError{"cudaMalloc(" + std::to_string(n) + " bytes): out of memory (injected)"};
     cudaError_t e = cudaMalloc(&ptr, n);
     if (e != cudaSuccess) {
       ptr = nullptr;
       cudaGetLastError();
-      throw DeviceError{"cudaMalloc(" + std::to_string(n) + " bytes): " + cudaGetErrorString(e)};
+      const std::string m = "cudaMalloc(" + std::to_string(n) + " bytes): " + cudaGetErrorString(e);
+      if (e == cudaErrorMemoryAllocation) throw OomError{m};
+      throw DeviceError{m};
     }
   }
 }
@@ -70,7 +85,62 @@ unsigned int take_kernel_error(int d) {
   unsigned int v = 0;
   QPC_CUDA_OR_THROW(cudaMemcpy(&v, s.err_word, sizeof(v), cudaMemcpyDeviceToHost));
   if (v) QPC_CUDA_OR_THROW(cudaMemset(s.err_word, 0, sizeof(v)));
-  return v;
+  return v | take_noalloc_head_error(d);
+}
+
+// ---- per-device launch configuration
+namespace {
+std::mutex g_launch_mu;
+std::map<std::pair<int, const void*>, int> g_dyn_smem;           // (device, kernel) -> bytes set
+std::map<std::tuple<int, const void*, int, int>, int> g_occupancy;  // (device, kernel, threads, smem)
+std::map<int, int> g_sms;
+int current_dev() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+}  // namespace
+
+cudaError_t ensure_dyn_smem(const void* func, int bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  const int d = current_dev();
+  std::lock_guard<std::mutex> lk(g_launch_mu);
+  int& set = g_dyn_smem[{d, func}];
+  if (bytes > set) {
+    cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    set = bytes;
+  }
+  return cudaSuccess;
+}
+
+int current_sm_count() {
+  const int d = current_dev();
+  std::lock_guard<std::mutex> lk(g_launch_mu);
+  auto it = g_sms.find(d);
+  if (it != g_sms.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = 148;
+  }
+  g_sms[d] = n;
+  return n;
+}
+
+int blocks_per_sm(const void* func, int threads, int smem) {
+  const int d = current_dev();
+  std::lock_guard<std::mutex> lk(g_launch_mu);
+  auto key = std::make_tuple(d, func, threads, smem);
+  auto it = g_occupancy.find(key);
+  if (it != g_occupancy.end()) return it->second;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, func, threads, smem) != cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  g_occupancy[key] = per_sm;
+  return per_sm;
 }
 
 // ================================================================ IR
@@ -805,6 +875,21 @@ void resolve_pads(const Node& n, int64_t h, int64_t w, int64_t kh, int64_t kw, i
   }
 }
 
+// The pointwise tensor-core path of plan_conv: a 1x1, stride-1, unpadded,
+// ungrouped conv over a C % 4 == 0 input (rows = pixels, one tcgen05 GEMM),
+// given the conv's input height and width.
+bool takes_pointwise_gemm(const Node& n, const HostTensor& w, int64_t H, int64_t W) {
+  if (w.shape.size() != 4) return false;
+  const int64_t cg = w.shape[1], kh = w.shape[2], kw = w.shape[3];
+  const int64_t group = n.geti("group", 1);
+  auto st = n.getints("strides");
+  const int64_t sh = st.size() == 2 ? st[0] : 1, sw = st.size() == 2 ? st[1] : 1;
+  int64_t ph, pw, peh, pew;
+  resolve_pads(n, H, W, kh, kw, sh, sw, &ph, &pw, &peh, &pew);
+  return group == 1 && kh == 1 && kw == 1 && sh == 1 && sw == 1 && ph == 0 && pw == 0 && peh == 0 &&
+         pew == 0 && (cg % 4) == 0;
+}
+
 }  // namespace
 
 class Planner {
@@ -944,11 +1029,13 @@ class Planner {
     return -1;
   }
 
-  // Whether every consumer of `o` is a TF32 pointwise conv that reads it as
-  // its GEMM A operand (input 0 only), so `o` may be stored tf32-rounded: the
-  // GEMM would round it to the same values.
+  // Whether every consumer of `o` (an NCHW-shaped value of spatial size H x W)
+  // is a TF32 conv that takes the pointwise GEMM path (the same predicate
+  // plan_conv uses) and reads `o` as its A operand (input 0 only), so `o` may
+  // be stored tf32-rounded: the GEMM would round it to the same values.
+  // plan_conv checks, when it plans each such consumer, that it took that path.
   std::set<std::string> tf32_rounded_;
-  bool feeds_only_tf32_pointwise(const std::string& o) {
+  bool feeds_only_tf32_pointwise(const std::string& o, int64_t H, int64_t W) {
     if (S.math() != QPC_MATH_TF32) return false;
     for (auto& go : S.graph_outputs())
       if (go == o) return false;
@@ -960,13 +1047,7 @@ class Planner {
       for (size_t k = 1; k < c.in.size(); ++k)
         if (c.in[k] == o) return false;
       const HostTensor* w = S.weight(c.in[1]);
-      if (!w || w->shape.size() != 4 || w->shape[2] != 1 || w->shape[3] != 1 || (w->shape[1] % 4) != 0)
-        return false;
-      if (c.geti("group", 1) != 1) return false;
-      for (auto v : c.getints("strides"))
-        if (v != 1) return false;
-      for (auto v : c.getints("pads"))
-        if (v != 0) return false;
+      if (!w || !takes_pointwise_gemm(c, *w, H, W)) return false;
     }
     return true;
   }
@@ -1216,8 +1297,9 @@ class Planner {
     ConvGeom g{(int)N, (int)H, (int)W, (int)C, (int)oh, (int)ow, (int)M, (int)kh, (int)kw,
                (int)sh, (int)sw, (int)ph, (int)pw};
     const bool dw = group > 1 && cg == 1 && M == C;
-    const bool pw1 = group == 1 && kh == 1 && kw == 1 && sh == 1 && sw == 1 && ph == 0 && pw == 0 &&
-                     peh == 0 && pew == 0 && (C % 4) == 0;
+    const bool pw1 = takes_pointwise_gemm(n, *w, H, W);
+    if (tf32_rounded_.count(n.in[0]) && !pw1)
+      throw GraphError{"internal: " + n.name + " reads a tf32-rounded value but is not a pointwise GEMM"};
     const bool kxk_tc = group == 1 && sh == 1 && sw == 1 && (C % 4) == 0 && !pw1 && kh * kw > 1;
     const int math = S.math();
     const double flops = 2.0 * N * oh * ow * M * cg * kh * kw;
@@ -1274,7 +1356,7 @@ class Planner {
       const float* wt = S.dweight(n.in[1], "dw");
       const double bytes = 4.0 * N * H * W * C + out_bytes + (has_res ? out_bytes : 0);
       ActParams dact = act;
-      if (feeds_only_tf32_pointwise(n.out[0])) {
+      if (feeds_only_tf32_pointwise(n.out[0], oh, ow)) {
         dact.round_tf32 = 1;
         tf32_rounded_.insert(n.out[0]);
       }

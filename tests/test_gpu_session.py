@@ -50,6 +50,33 @@ def test_block_config1(cuda_ctx, math):
     assert np.array_equal(got, got2)
 
 
+def test_block_tf32_producer_rounding_is_invisible(cuda_ctx):
+    """In TF32 the session stores the depthwise output tf32-rounded because
+    its only consumer is a pointwise GEMM that rounds its A operand the same
+    way.  The session's block output must equal, bit for bit, the two
+    operator entry points chained without that rounding (dwconv in fp32, then
+    the TF32 GEMM that rounds on chip)."""
+    import torch
+    g, w = load(nets.build_block)
+    dwn, pwn = g.nodes[0], g.nodes[3]
+    assert dwn.attrs["group"] == 64 and pwn.op_type == "Conv"
+    x = nets.block_input(0, (2, 64, 96, 80))
+    s = cuda_ctx.create_session(g, w, role="other", math="tf32")
+    got = s.run({"x": x})[0]
+    wd = w[dwn.inputs[1]]                      # [64, 1, 3, 3]
+    tap = np.ascontiguousarray(wd.reshape(64, 9).T)
+    xd = torch.from_numpy(np.ascontiguousarray(np.transpose(x, (0, 2, 3, 1)))).cuda()
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    y1 = q.op_dwconv_nhwc(xd, dev(tap), 3, 3, (1, 1), (1, 1, 1, 1), bias=dev(w[dwn.inputs[2]]), act="hswish")
+    wp = w[pwn.inputs[1]].reshape(128, 64)
+    hi, _ = q.op_split_tf32(dev(wp))
+    bp = np.concatenate([w[pwn.inputs[2]], np.zeros(16, np.float32)])
+    y2 = q.op_gemm(y1.reshape(-1, 64), hi, bias=dev(bp), act="hswish", math="tf32")
+    torch.cuda.synchronize()
+    ref = np.transpose(y2.cpu().numpy().reshape(2, 96, 80, 128), (0, 3, 1, 2))
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
 @pytest.mark.parametrize("math", ["tf32", "3xtf32"])
 def test_gemm_graph_config2(cuda_ctx, math):
     g, w = load(nets.build_gemm, k=128, n=256)
