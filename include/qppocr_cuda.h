@@ -140,9 +140,12 @@ typedef struct {
 
 typedef struct qpc_session qpc_session;
 
-/* DeviceContext::create_session (device.rs:88-101): weights are copied to the
- * device once and owned by the session.  Unsupported ops fail here, naming the
- * node (QPC_ERR_GRAPH).  opts may be NULL (defaults). */
+/* DeviceContext::create_session (device.rs:88-101): the session takes a host
+ * copy of the weights and owns them; each is uploaded to the device once, in
+ * the layout its kernel wants, when the first run that needs it builds its
+ * plan (so a device out-of-memory surfaces at that run as QPC_ERR_OOM).
+ * Unsupported ops fail here, naming the node (QPC_ERR_GRAPH).  opts may be
+ * NULL (defaults). */
 int qpc_session_create(int device, const qpc_graph* graph, const qpc_tensor* weights,
                        int n_weights, int role, const qpc_session_options* opts,
                        qpc_session** out);

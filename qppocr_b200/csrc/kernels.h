@@ -127,6 +127,19 @@ cudaError_t launch_convt_pair(const float* x, int n, int h, int w, int c, int m1
                               const ActParams& act2, float* out, int math, unsigned int* err,
                               cudaStream_t st);
 
+// Fused depthwise-separable block (dwpw.cu): a depthwise conv `g` (group ==
+// C, k = 3 or 5, equal strides 1 or 2, C == 16 or C % 32 == 0) whose output
+// feeds only a TF32 pointwise conv to n_out (<= 256) channels, in one tcgen05
+// kernel: y = epi(pw_w * round_tf32(act(dw(x) + dw_bias))).  dw_w is
+// tap-major [k*k][C]; pw_w is [n_out][C], tf32-rounded; epi supplies the
+// pointwise bias, activation and output (no residual).  The depthwise part
+// is bit-identical to launch_dwconv_nhwc and the pointwise part to
+// launch_gemm_tc on its (rounded) output.
+bool dwpw_ok(const ConvGeom& g, int n_out);
+cudaError_t launch_dwpw(const float* x, const ConvGeom& g, const float* dw_w, const float* dw_bias,
+                        const ActParams& dw_act, const float* pw_w, int n_out, const GemmEpilogue& epi,
+                        unsigned int* err, cudaStream_t st);
+
 // Whether the tap-folded TF32 kernel takes this conv (kw <= 3, M <= 32,
 // output rows >= 48 wide, stride 1, filter within the shared-memory budget).
 bool conv_fold_ok(const ConvGeom& g);

@@ -20,6 +20,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <numeric>
 #include <set>
@@ -1029,6 +1030,75 @@ class Planner {
     return -1;
   }
 
+  // A depthwise conv planned together with its pointwise consumer
+  // (launch_dwpw): the consumer's input name -> the depthwise conv's operands.
+  struct FusedDw {
+    Val x;  // NHWC input, held until the consumer is planned
+    ConvGeom g;
+    const float* w = nullptr;
+    const float* bias = nullptr;
+    ActParams act{};
+    std::string name;
+  };
+  std::map<std::string, FusedDw> fused_dw_;
+
+  // Whether depthwise conv `n` (geometry g) runs fused into its consumer: TF32
+  // math (the fused A operand is the tf32-rounded depthwise output), its
+  // output is no graph output and feeds exactly one Conv, as input 0 only,
+  // which takes the pointwise GEMM path without residual or channel gate,
+  // and launch_dwpw supports the shapes.  QPPOCR_CUDA_FUSE_DWPW=0 turns the
+  // fusion off (both paths give identical results).
+  bool dw_fusable(const Node& n, const ConvGeom& g) {
+    if (S.math() != QPC_MATH_TF32) return false;
+    static const bool enabled = [] {
+      const char* v = std::getenv("QPPOCR_CUDA_FUSE_DWPW");
+      return !(v && std::string(v) == "0");
+    }();
+    if (!enabled) return false;
+    const std::string& o = n.out[0];
+    for (auto& go : S.graph_outputs())
+      if (go == o) return false;
+    auto cit = consumers_.find(o);
+    if (cit == consumers_.end() || cit->second.size() != 1) return false;
+    const Node& c = S.nodes()[cit->second[0]];
+    if (c.op != "Conv" || c.in.size() < 2 || c.in[0] != o || c.has_in(3) || c.geti("qpc_res_up", 0)) return false;
+    for (size_t k = 1; k < c.in.size(); ++k)
+      if (c.in[k] == o) return false;
+    const HostTensor* w = S.weight(c.in[1]);
+    if (!w || !takes_pointwise_gemm(c, *w, g.oh, g.ow)) return false;
+    if (c.has_in(2) && !S.weight(c.in[2])) return false;
+    return dwpw_ok(g, (int)w->shape[0]);
+  }
+
+  // The pointwise conv `n` whose input is the fused depthwise conv `f`.
+  void plan_dwpw(const Node& n, const FusedDw& f) {
+    const HostTensor* w = S.weight(n.in[1]);
+    const int64_t M = w->shape[0];
+    const ConvGeom g = f.g;
+    const std::vector<int64_t> oshape = {g.n, M, g.oh, g.ow};
+    Val y = new_val(oshape, true);
+    float* yp = out_ptr(y);
+    const float* xp = out_ptr(f.x);
+    const float* wb = S.dweight(n.in[1], "raw.rn");
+    GemmEpilogue e;
+    e.bias = n.has_in(2) ? S.dweight(n.in[2], "raw") : nullptr;
+    e.out = yp;
+    e.ldo = (int)M;
+    e.ldr = (int)M;
+    e.act = act_of(n);
+    unsigned int* err = device_state(S.device()).err_word;
+    const double pix = (double)g.n * g.oh * g.ow;
+    const double bytes = 4.0 * g.n * g.h * g.w * g.c + 4.0 * pix * M + 4.0 * g.c * (M + g.kh * g.kw);
+    const double flops = 2.0 * pix * g.c * (g.kh * g.kw + M);
+    const float* dww = f.w;
+    const float* dwb = f.bias;
+    const ActParams dwa = f.act;
+    step("dwpw", f.name + "+" + n.name, bytes, flops, [=](cudaStream_t s) {
+      return launch_dwpw(xp, g, dww, dwb, dwa, wb, (int)M, e, err, s);
+    });
+    define(n.out[0], y);
+  }
+
   // Whether every consumer of `o` (an NCHW-shaped value of spatial size H x W)
   // is a TF32 conv that takes the pointwise GEMM path (the same predicate
   // plan_conv uses) and reads `o` as its A operand (input 0 only), so `o` may
@@ -1277,6 +1347,13 @@ class Planner {
   //   kxk s1 g1, C % 4 == 0              -> tcgen05 implicit GEMM (4-D TMA)
   //   anything else                      -> direct SIMT conv
   void plan_conv(const Node& n) {
+    auto fit = fused_dw_.find(n.in[0]);
+    if (fit != fused_dw_.end()) {
+      plan_dwpw(n, fit->second);
+      unref(fit->second.x);
+      fused_dw_.erase(fit);
+      return;
+    }
     const Val& x0 = get(n.in[0]);
     const HostTensor* w = S.weight(n.in[1]);
     if (x0.shape.size() != 4 || w->shape.size() != 4) throw GraphError{"only 2-D convolutions"};
@@ -1304,6 +1381,19 @@ class Planner {
     const int math = S.math();
     const double flops = 2.0 * N * oh * ow * M * cg * kh * kw;
     const double out_bytes = 4.0 * N * oh * ow * M;
+    if (dw && !n.has_in(3) && dw_fusable(n, g)) {
+      // planned with its pointwise consumer as one kernel (plan_dwpw); the
+      // depthwise output is never materialised
+      FusedDw f;
+      f.x = as_nhwc(x0, n.name);
+      f.g = g;
+      f.w = S.dweight(n.in[1], "dw");
+      f.bias = bias;
+      f.act = act;
+      f.name = n.name;
+      fused_dw_[n.out[0]] = f;
+      return;
+    }
 
     // Residual: plain tensor, or (qpc_res_up) the pre-upsample map of a
     // nearest resize to the output size, read through the epilogue's remap

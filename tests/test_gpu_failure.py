@@ -6,8 +6,9 @@ crates/qppocr-gpu/src/vulkan/session.rs:306-312).
 * A wait that nothing completes runs out after a 2 ms limit, raises the
   timeout flag in the device's fault word and returns; the context stays
   usable and the next session run is correct.
-* A forced device allocation failure makes session creation (or the CTC
-  head's scratch allocation) fail with QPC_ERR_OOM and leaves nothing behind.
+* A forced device allocation failure makes the run that uploads weights and
+  builds the plan (or the CTC head's scratch allocation) fail with
+  QPC_ERR_OOM and leaves nothing behind.
 * Sessions on two devices in one process (when two are visible) each set
   their kernels' shared-memory limits on their own device.
 """
@@ -45,31 +46,17 @@ def test_bounded_wait_runs_out_and_context_survives(cuda_ctx):
     s.close()
 
 
-def test_forced_allocation_failure_in_session_create(cuda_ctx):
-    g, w = _block()
-    q.inject_alloc_failure(1)
-    with pytest.raises(q.OutOfMemoryError, match="injected"):
-        cuda_ctx.create_session(g, w)
-    # a failure deep inside the weight upload
-    q.inject_alloc_failure(3)
-    with pytest.raises(q.OutOfMemoryError):
-        cuda_ctx.create_session(g, w)
-    q.inject_alloc_failure(0)
-    s = cuda_ctx.create_session(g, w, math="3xtf32")
-    x = nets.block_input(0, (1, 64, 32, 32))
-    assert rel(s.run({"x": x})[0], orc.run_graph(g, w, {"x": x})[0]) < 1e-5
-    s.close()
-
-
 def test_forced_allocation_failure_in_first_run(cuda_ctx):
-    """The plan (arena) is built on the first run of a shape: a failed
-    allocation there fails that run only."""
+    """Weights go to the device, and the plan's arena is allocated, when a
+    shape is first run: a failed allocation there fails that run only, at the
+    first allocation or deep inside the upload, and the next run is correct."""
     g, w = _block()
     s = cuda_ctx.create_session(g, w, math="3xtf32")
     x = nets.block_input(0, (1, 64, 32, 32))
-    q.inject_alloc_failure(1)
-    with pytest.raises(q.OutOfMemoryError):
-        s.run({"x": x})
+    for nth in (1, 3):
+        q.inject_alloc_failure(nth)
+        with pytest.raises(q.OutOfMemoryError, match="injected"):
+            s.run({"x": x})
     q.inject_alloc_failure(0)
     assert rel(s.run({"x": x})[0], orc.run_graph(g, w, {"x": x})[0]) < 1e-5
     s.close()
