@@ -325,6 +325,46 @@ int qpc_op_rec_pack(const uint8_t* crops, const int64_t* off, const int* h, cons
 int qpc_op_db_mask(const float* pred, const uint8_t* mask_in, uint8_t* mask, int n, int h, int w, float thresh,
                    int dilate, void* stream);
 
+/* box_score_fast (crates/qppocr-core/src/pipeline/geometry.rs:221-269) on
+ * the device: for box k, the mean (f64 sum in the reference's order, rounded
+ * to f32) of pred over the quadrilateral boxes[8k .. 8k+7] ((x, y) corners in
+ * pred's coordinates) of image img[k] by the scan-line even-odd fill; 0 for
+ * an empty box.  pred: n x h x w probabilities; boxes, img, scores device
+ * arrays.  The DB post's score filter without copying the map to the host. */
+int qpc_op_box_score(const float* pred, int h, int w, const float* boxes, const int* img, int n_boxes,
+                     float* scores, void* stream);
+
+/* Host helper for qpc_op_crop_text_boxes: the size of crop_text_box's output
+ * for each box (crates/qppocr-core/src/pipeline/crop.rs:9-15): cw = max(1,
+ * max(|p0 p1|, |p2 p3|) truncated), ch likewise from |p0 p3|, |p1 p2| (f32
+ * hypot); rotated[k] = ch / cw >= 1.5 (the crop is then ch wide, cw high).
+ * pts: host array [n][4][2]. */
+int qpc_crop_size(const float* pts, int n, int* cw, int* ch, int* rotated);
+
+/* crop_text_box (crop.rs:8-127) on the device: box k of image img[k] (n_images
+ * images of h x w x 3 uint8, device) -> cw[k] x ch[k] x 3 bytes at out +
+ * off[k], the f64 homography solve, f64 inverse mapping and edge-replicated
+ * bilinear sampling of the reference, bit for bit; tall crops rotated
+ * clockwise.  pts, img, cw, ch, off: device arrays; max_pixels: the largest
+ * cw * ch. */
+int qpc_op_crop_text_boxes(const uint8_t* images, int n_images, int h, int w, const float* pts, const int* img,
+                           const int* cw, const int* ch, const int64_t* off, int n_boxes, int max_pixels,
+                           uint8_t* out, void* stream);
+
+/* Line pack on the device (pack_crop, crop.rs:153-185, into the zeroed batch
+ * of engine.rs:1425-1440): line k is the view of an h[k] x w[k] window,
+ * starting at column x0[k], of a crop whose rows are stride[k] pixels, at
+ * byte offset off[k] of crops; flip[k] != 0 rotates the view 180 degrees (a
+ * line the classifier flagged, engine.rs:1402-1407; flip may be NULL).  The
+ * view is resized to rw[k] x img_h (bilinear, as resize_bilinear_img) and
+ * normalised (v/255 - 0.5)/0.5, or with pad[k] != 0 placed unresized and
+ * centred vertically, into slot k of out (n x 3 x img_h x img_w f32).  The
+ * cls batch is this with cls_view's centred window (crop.rs:193-218) and
+ * pad 0; the rec batch with the whole crop.  All arrays on the device. */
+int qpc_op_line_pack(const uint8_t* crops, const int64_t* off, const int* stride, const int* x0, const int* h,
+                     const int* w, const int* rw, const int* pad, const int* flip, int n, int img_h, int img_w,
+                     float* out, void* stream);
+
 /* Device fault / timeout flags raised by kernels with bounded waits on
  * `device` since the last call (0 = none; 1 = a pipeline wait ran out, 2 = a
  * kernel saw an impossible shape), including the faults kept by

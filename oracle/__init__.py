@@ -387,6 +387,51 @@ def db_mask(pred, thresh, dilate=True):
     return out
 
 
+def box_scores(pred, boxes, img=None):
+    """geometry.rs:221-269 box_score_fast for each box: pred [n, h, w] f32,
+    boxes [k, 4, 2] (x, y) corners in pred coordinates, img [k] image index."""
+    pred = _c(pred)
+    n, h, w = pred.shape
+    boxes = np.ascontiguousarray(boxes, np.float32).reshape(-1, 8)
+    k = boxes.shape[0]
+    img = np.zeros(k, np.int32) if img is None else np.ascontiguousarray(img, np.int32)
+    out = np.empty(k, np.float32)
+    lib().orc_box_scores(_f(pred), ctypes.c_int64(h), ctypes.c_int64(w), _f(boxes),
+                         img.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), ctypes.c_int64(k), _f(out))
+    return out
+
+
+def crop_size(pts):
+    """crop.rs:8-20: (cw, ch, rotated) of crop_text_box for corners pts [4, 2]."""
+    pts = np.ascontiguousarray(pts, np.float32).reshape(8)
+    cw, ch, rot = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    lib().orc_crop_size(_f(pts), ctypes.byref(cw), ctypes.byref(ch), ctypes.byref(rot))
+    return cw.value, ch.value, bool(rot.value)
+
+
+def crop_text_box(src, pts):
+    """crop.rs:8-127 on one h x w x 3 uint8 image: the perspective crop of the
+    quadrilateral pts [4, 2] (ch x cw x 3, or cw x ch x 3 when rotated)."""
+    src = np.ascontiguousarray(src, np.uint8)
+    h, w, _ = src.shape
+    cw, ch, rot = crop_size(pts)
+    out = np.empty((cw, ch, 3) if rot else (ch, cw, 3), np.uint8)
+    pts = np.ascontiguousarray(pts, np.float32).reshape(8)
+    lib().orc_crop_text_box(_u8(src), ctypes.c_int(h), ctypes.c_int(w), _f(pts), _u8(out))
+    return out
+
+
+def cls_pack_line(crop, cls_h, cls_w):
+    """crop.rs:193-218 cls_view then pack_crop (resize) into a zeroed
+    [3, cls_h, cls_w] float32 slot."""
+    crop = np.ascontiguousarray(crop, np.uint8)
+    h, w, _ = crop.shape
+    out = np.empty((3, cls_h, cls_w), np.float32)
+    lib().orc_cls_pack_line(_u8(crop), ctypes.c_int64(h), ctypes.c_int64(w), ctypes.c_int64(cls_h),
+                            ctypes.c_int64(cls_w), _f(out))
+    return out
+
+
 def ctc_decode(probs, charset=None):
     """rec.rs:34-79 greedy CTC over one line's [T, C] probabilities: per step
     the first strict maximum; emit when best != 0 and best != previous; conf =

@@ -949,4 +949,167 @@ void orc_db_mask(const float* pred, int64_t n, int64_t h, int64_t w, float thres
   else std::memcpy(out, m.data(), m.size());
 }
 
+// geometry.rs:221-269 box_score_fast: mean of pred over the quadrilateral
+// bpts (x, y pairs) by scan-line even-odd fill (sample at y + 0.5, columns
+// ceil(xa - 0.5) .. floor(xb - 0.5)), clipped to the box's integer bounds,
+// summed in f64 in row order, left to right.
+float orc_box_score_one(const float* pred, int hh, int ww, const float* bpts) {
+  float fxmin = 3.40282347e38f, fxmax = -3.40282347e38f, fymin = 3.40282347e38f, fymax = -3.40282347e38f;
+  for (int i = 0; i < 4; ++i) {
+    fxmin = std::fmin(fxmin, bpts[2 * i]);
+    fxmax = std::fmax(fxmax, bpts[2 * i]);
+    fymin = std::fmin(fymin, bpts[2 * i + 1]);
+    fymax = std::fmax(fymax, bpts[2 * i + 1]);
+  }
+  auto to_i32 = [](float v) -> int {  // Rust `as i32`: saturating, NaN -> 0
+    if (v != v) return 0;
+    if (v >= 2147483647.0f) return 2147483647;
+    if (v <= -2147483648.0f) return (int)-2147483648LL;
+    return (int)v;
+  };
+  auto clampi = [](int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); };
+  const int xmin = clampi(to_i32(std::floor(fxmin)), 0, ww - 1);
+  const int xmax = clampi(to_i32(std::ceil(fxmax)), 0, ww - 1);
+  const int ymin = clampi(to_i32(std::floor(fymin)), 0, hh - 1);
+  const int ymax = clampi(to_i32(std::ceil(fymax)), 0, hh - 1);
+  double sum = 0.0;
+  int64_t count = 0;
+  for (int y = ymin; y <= ymax; ++y) {
+    const float sy = (float)y + 0.5f;
+    float xs[8];
+    int nx = 0;
+    for (int i = 0; i < 4; ++i) {
+      const float ax = bpts[2 * i], ay = bpts[2 * i + 1];
+      const float bx = bpts[2 * ((i + 1) % 4)], by = bpts[2 * ((i + 1) % 4) + 1];
+      if ((ay <= sy && by > sy) || (by <= sy && ay > sy)) {
+        const float t = (sy - ay) / (by - ay);
+        xs[nx++] = ax + t * (bx - ax);
+      }
+    }
+    std::sort(xs, xs + nx);
+    for (int i = 0; i + 1 < nx; i += 2) {
+      const int xa = to_i32(std::ceil(xs[i] - 0.5f));
+      const int xb = to_i32(std::floor(xs[i + 1] - 0.5f));
+      for (int x = xa; x <= xb; ++x) {
+        if (x < xmin || x > xmax) continue;
+        sum += (double)pred[(int64_t)y * ww + x];
+        ++count;
+      }
+    }
+  }
+  if (count == 0) return 0.0f;
+  return (float)(sum / (double)count);
+}
+
+void orc_box_scores(const float* pred, int64_t hh, int64_t ww, const float* boxes, const int* img, int64_t n,
+                    float* out) {
+  for (int64_t k = 0; k < n; ++k)
+    out[k] = orc_box_score_one(pred + (int64_t)img[k] * hh * ww, (int)hh, (int)ww, boxes + 8 * k);
+}
+
+// crop.rs:8-127 crop_text_box size: cw = max(1, max(|p0 p1|, |p2 p3|) as i32),
+// ch = max(1, max(|p0 p3|, |p1 p2|) as i32) with f32 hypot; rotated when
+// ch / cw >= 1.5 (the output is then ch wide and cw high).
+void orc_crop_size(const float* pts, int* cw, int* ch, int* rotated) {
+  auto d = [&](int a, int b) { return std::hypot(pts[2 * a] - pts[2 * b], pts[2 * a + 1] - pts[2 * b + 1]); };
+  const float w1 = d(0, 1), w2 = d(2, 3), h1 = d(0, 3), h2 = d(1, 2);
+  const float mw = std::fmax(w1, w2), mh = std::fmax(h1, h2);
+  *cw = std::max(1, (int)mw);
+  *ch = std::max(1, (int)mh);
+  *rotated = ((float)*ch / (float)*cw >= 1.5f) ? 1 : 0;
+}
+
+// crop.rs:8-127 crop_text_box: homography dst corners (0,0),(cw,0),(cw,ch),
+// (0,ch) -> pts by f64 Gauss-Jordan with partial pivoting on the 8 x 9
+// system; per output pixel the source point in f64, bilinear with the edge
+// replicated (first term two multiplies, then fused multiply-adds), u8 by
+// (v + 0.5) clamped and truncated; tall crops rotated clockwise.
+// src: h x w x 3 uint8; out: cw * ch * 3 bytes.
+void orc_crop_text_box(const uint8_t* src, int h, int w, const float* pts, uint8_t* out) {
+  int cw, ch, rot;
+  orc_crop_size(pts, &cw, &ch, &rot);
+  double a[8][9];
+  for (int i = 0; i < 4; ++i) {
+    const double dx = (i == 1 || i == 2) ? (double)cw : 0.0;
+    const double dy = i >= 2 ? (double)ch : 0.0;
+    const double sx = (double)pts[2 * i], sy = (double)pts[2 * i + 1];
+    const double r0[9] = {dx, dy, 1.0, 0.0, 0.0, 0.0, -dx * sx, -dy * sx, sx};
+    const double r1[9] = {0.0, 0.0, 0.0, dx, dy, 1.0, -dx * sy, -dy * sy, sy};
+    for (int c = 0; c < 9; ++c) {
+      a[2 * i][c] = r0[c];
+      a[2 * i + 1][c] = r1[c];
+    }
+  }
+  for (int col = 0; col < 8; ++col) {
+    int piv = col;
+    for (int r = col + 1; r < 8; ++r)
+      if (std::fabs(a[r][col]) > std::fabs(a[piv][col])) piv = r;
+    if (piv != col)
+      for (int c = 0; c < 9; ++c) std::swap(a[col][c], a[piv][c]);
+    const double dd = a[col][col];
+    if (std::fabs(dd) < 1e-12) continue;
+    for (int c = col; c < 9; ++c) a[col][c] /= dd;
+    for (int r = 0; r < 8; ++r) {
+      if (r == col) continue;
+      const double f = a[r][col];
+      if (f == 0.0) continue;
+      for (int c = col; c < 9; ++c) a[r][c] -= f * a[col][c];
+    }
+  }
+  double hm[9];
+  for (int i = 0; i < 8; ++i) hm[i] = a[i][8];
+  hm[8] = 1.0;
+  auto to_i32 = [](double v) -> int {
+    if (v != v) return 0;
+    if (v >= 2147483647.0) return 2147483647;
+    if (v <= -2147483648.0) return (int)-2147483648LL;
+    return (int)v;
+  };
+  for (int y = 0; y < ch; ++y)
+    for (int x = 0; x < cw; ++x) {
+      const double xf = (double)x, yf = (double)y;
+      const double den = hm[6] * xf + hm[7] * yf + hm[8];
+      const double sx = (hm[0] * xf + hm[1] * yf + hm[2]) / den;
+      const double sy = (hm[3] * xf + hm[4] * yf + hm[5]) / den;
+      int ix = to_i32(std::floor(sx));
+      int iy = to_i32(std::floor(sy));
+      const float fx = (float)(sx - (double)ix);
+      const float fy = (float)(sy - (double)iy);
+      ix = std::min(std::max(ix, 0), w - 1);
+      iy = std::min(std::max(iy, 0), h - 1);
+      const int ix1 = std::min(ix + 1, w - 1), iy1 = std::min(iy + 1, h - 1);
+      const uint8_t* r0 = src + (int64_t)iy * w * 3;
+      const uint8_t* r1 = src + (int64_t)iy1 * w * 3;
+      const int64_t o = rot ? ((int64_t)x * ch + (ch - 1 - y)) * 3 : ((int64_t)y * cw + x) * 3;
+      for (int c = 0; c < 3; ++c) {
+        const float v00 = r0[ix * 3 + c], v01 = r0[ix1 * 3 + c], v10 = r1[ix * 3 + c], v11 = r1[ix1 * 3 + c];
+        float t = v00 * (1.0f - fx) * (1.0f - fy);
+        t = std::fma(v01 * fx, 1.0f - fy, t);
+        t = std::fma(v10 * (1.0f - fx), fy, t);
+        const float v = std::fma(v11 * fx, fy, t);
+        out[o + c] = (uint8_t)std::min(std::max(v + 0.5f, 0.0f), 255.0f);
+      }
+    }
+}
+
+// crop.rs:193-218 cls_view then crop.rs:153-185 pack_crop (resize, never
+// pad_only) into a zeroed [3, cls_h, cls_w] slot: crops wider than
+// h * cls_w / cls_h (i64) are cut to that many centred columns first.
+void orc_cls_pack_line(const uint8_t* crop, int64_t h, int64_t w, int64_t cls_h, int64_t cls_w, float* dst) {
+  int64_t x0 = 0, ww = w;
+  if (h > 0 && w > 0) {
+    const int64_t max_w = h * cls_w / cls_h;
+    if (w > max_w) {
+      ww = std::max<int64_t>(1, max_w);
+      x0 = (w - ww) / 2;
+    }
+  }
+  std::vector<uint8_t> view((size_t)(h * ww * 3));
+  for (int64_t y = 0; y < h; ++y) std::memcpy(&view[y * ww * 3], crop + (y * w + x0) * 3, ww * 3);
+  const float ratio = (float)ww / (float)h;
+  int64_t rw = (int64_t)std::ceil((float)cls_h * ratio);
+  rw = std::max<int64_t>(std::min(rw, cls_w), 1);
+  orc_rec_pack_line(view.data(), h, ww, rw, 0, cls_h, cls_w, dst);
+}
+
 }  // extern "C"

@@ -103,6 +103,7 @@ EXPORTED = (
     "qpc_op_split_tf32", "qpc_op_resize_bilinear_rgb_u8", "qpc_op_det_preprocess", "qpc_op_db_mask",
     "qpc_op_rec_pack",
     "qpc_kernel_error", "qpc_selftest_wait_timeout", "qpc_inject_alloc_failure",
+    "qpc_op_box_score", "qpc_crop_size", "qpc_op_crop_text_boxes", "qpc_op_line_pack",
 )
 
 _lib = None
@@ -164,6 +165,10 @@ def lib():
     L.qpc_kernel_error.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]
     L.qpc_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int]
     L.qpc_inject_alloc_failure.argtypes = [ctypes.c_int]
+    L.qpc_op_box_score.argtypes = [P, I, I, P, P, I, P, P]
+    L.qpc_crop_size.argtypes = [P, I, P, P, P]
+    L.qpc_op_crop_text_boxes.argtypes = [P, I, I, I, P, P, P, P, P, I, I, P, P]
+    L.qpc_op_line_pack.argtypes = [P, P, P, P, P, P, P, P, P, I, I, I, P, P]
     _lib = L
     return L
 
@@ -647,3 +652,83 @@ def inject_alloc_failure(nth: int = 1) -> None:
     """Make the nth device allocation of the library from now on fail as if
     the device were out of memory (0 cancels)."""
     _check(lib().qpc_inject_alloc_failure(nth))
+
+
+def _stream_of(t, stream):
+    import torch
+    return stream if stream is not None else torch.cuda.current_stream(t.device).cuda_stream
+
+
+def op_box_score(pred, boxes, img, stream=None):
+    """box_score_fast (geometry.rs:221-269) on the device: pred [n, h, w] f32,
+    boxes [k, 4, 2] f32 corners, img [k] int32 image index (device tensors)
+    -> scores [k] f32."""
+    import torch
+    n, h, w = pred.shape
+    k = int(img.numel())
+    out = torch.empty(k, dtype=torch.float32, device=pred.device)
+    with torch.cuda.device(pred.device):
+        _check(lib().qpc_op_box_score(_dptr(pred), h, w, _dptr(boxes.contiguous()), _dptr(img), k, _dptr(out),
+                                      _stream_of(pred, stream)))
+    return out
+
+
+def crop_size(pts):
+    """Host helper: (cw, ch, rotated) int32 arrays of crop_text_box's output
+    for boxes pts [k, 4, 2] (crop.rs:9-15)."""
+    pts = np.ascontiguousarray(pts, np.float32).reshape(-1, 8)
+    k = pts.shape[0]
+    cw, ch, rot = (np.empty(k, np.int32) for _ in range(3))
+    _check(lib().qpc_crop_size(pts.ctypes.data, k, cw.ctypes.data, ch.ctypes.data, rot.ctypes.data))
+    return cw, ch, rot
+
+
+def op_crop_text_boxes(images, pts, img, stream=None):
+    """crop_text_box (crop.rs:8-127) for every box on the device.  images:
+    [n, h, w, 3] uint8 device tensor; pts [k, 4, 2] f32 and img [k] int32 host
+    arrays.  Returns (crops: one uint8 device buffer, off int64 [k], cw, ch,
+    rotated int32 [k]); crop k is (cw x ch x 3 if rotated else ch x cw x 3)
+    bytes at off[k]."""
+    import torch
+    n, h, w, _ = images.shape
+    pts = np.ascontiguousarray(pts, np.float32).reshape(-1, 8)
+    k = pts.shape[0]
+    cw, ch, rot = crop_size(pts)
+    sizes = cw.astype(np.int64) * ch * 3
+    off = np.zeros(k, np.int64)
+    if k:
+        off[1:] = np.cumsum(sizes)[:-1]
+    total = int(sizes.sum()) if k else 0
+    dev = images.device
+    out = torch.empty(max(total, 16), dtype=torch.uint8, device=dev)
+    if k:
+        tp = torch.from_numpy(pts).to(dev)
+        ti = torch.from_numpy(np.ascontiguousarray(img, np.int32)).to(dev)
+        tcw, tch = torch.from_numpy(cw).to(dev), torch.from_numpy(ch).to(dev)
+        toff = torch.from_numpy(off).to(dev)
+        with torch.cuda.device(dev):
+            _check(lib().qpc_op_crop_text_boxes(_dptr(images), n, h, w, _dptr(tp), _dptr(ti), _dptr(tcw), _dptr(tch),
+                                                _dptr(toff), k, int((cw.astype(np.int64) * ch).max()), _dptr(out),
+                                                _stream_of(images, stream)))
+    return out, off, cw, ch, rot
+
+
+def op_line_pack(crops, off, stride, x0, h, w, rw, pad, img_h, img_w, flip=None, stream=None):
+    """Line pack (crop.rs:153-185, cls_view windows crop.rs:193-218) on the
+    device.  crops: uint8 device buffer; the per-line arrays are host numpy
+    arrays (copied to the device here).  Returns [n, 3, img_h, img_w] f32."""
+    import torch
+    n = len(h)
+    dev = crops.device
+    out = torch.empty((n, 3, img_h, img_w), dtype=torch.float32, device=dev)
+    if n == 0:
+        return out
+    i32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int32)).to(dev)
+    toff = torch.from_numpy(np.ascontiguousarray(off, np.int64)).to(dev)
+    arrs = [i32(a) for a in (stride, x0, h, w, rw, pad)]
+    tflip = i32(flip) if flip is not None else None
+    with torch.cuda.device(dev):
+        _check(lib().qpc_op_line_pack(_dptr(crops), _dptr(toff), *[_dptr(a) for a in arrs],
+                                      _dptr(tflip) if tflip is not None else None, n, img_h, img_w, _dptr(out),
+                                      _stream_of(crops, stream)))
+    return out

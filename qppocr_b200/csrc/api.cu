@@ -1,7 +1,9 @@
 // extern "C" entry points of libqppocr_cuda.so (declared in
 // include/qppocr_cuda.h).  Each converts exceptions into a status code plus
 // a thread-local message.
+#include <algorithm>
 #include <chrono>
+#include <cmath>
 #include <cstring>
 #include <thread>
 
@@ -464,6 +466,68 @@ int qpc_op_db_mask(const float* pred, const uint8_t* mask_in, uint8_t* mask, int
   }
   return guarded([&] {
     QPC_CUDA_OR_THROW(launch_db_mask(pred, mask_in, mask, n, h, w, thresh, dilate, (cudaStream_t)stream));
+    return (int)OK;
+  });
+}
+
+int qpc_op_box_score(const float* pred, int h, int w, const float* boxes, const int* img, int n_boxes,
+                     float* scores, void* stream) {
+  if (!pred || (n_boxes && (!boxes || !img || !scores)) || n_boxes < 0 || h <= 0 || w <= 0) {
+    set_error("invalid argument");
+    return E_INVALID;
+  }
+  return guarded([&] {
+    QPC_CUDA_OR_THROW(launch_box_score(pred, h, w, boxes, img, n_boxes, scores, (cudaStream_t)stream));
+    return (int)OK;
+  });
+}
+
+int qpc_crop_size(const float* pts, int n, int* cw, int* ch, int* rotated) {
+  if ((n && (!pts || !cw || !ch || !rotated)) || n < 0) {
+    set_error("invalid argument");
+    return E_INVALID;
+  }
+  for (int k = 0; k < n; ++k) {
+    const float* p = pts + 8 * (int64_t)k;
+    auto d = [&](int a, int b) { return std::hypot(p[2 * a] - p[2 * b], p[2 * a + 1] - p[2 * b + 1]); };
+    const float mw = std::fmax(d(0, 1), d(2, 3)), mh = std::fmax(d(0, 3), d(1, 2));
+    if (!(mw < 2147483647.0f) || !(mh < 2147483647.0f)) {
+      set_error("box " + std::to_string(k) + ": corners are not finite or too far apart");
+      return E_INVALID;
+    }
+    cw[k] = std::max(1, (int)mw);
+    ch[k] = std::max(1, (int)mh);
+    rotated[k] = ((float)ch[k] / (float)cw[k] >= 1.5f) ? 1 : 0;
+  }
+  return OK;
+}
+
+int qpc_op_crop_text_boxes(const uint8_t* images, int n_images, int h, int w, const float* pts, const int* img,
+                           const int* cw, const int* ch, const int64_t* off, int n_boxes, int max_pixels,
+                           uint8_t* out, void* stream) {
+  if (!images || n_images <= 0 || h <= 0 || w <= 0 || n_boxes < 0 || n_boxes > 65535 ||
+      (n_boxes && (!pts || !img || !cw || !ch || !off || !out || max_pixels <= 0))) {
+    set_error("invalid argument");
+    return E_INVALID;
+  }
+  return guarded([&] {
+    QPC_CUDA_OR_THROW(launch_crop_boxes(images, h, w, pts, img, cw, ch, off, n_boxes, max_pixels, out,
+                                        (cudaStream_t)stream));
+    return (int)OK;
+  });
+}
+
+int qpc_op_line_pack(const uint8_t* crops, const int64_t* off, const int* stride, const int* x0, const int* h,
+                     const int* w, const int* rw, const int* pad, const int* flip, int n, int img_h, int img_w,
+                     float* out, void* stream) {
+  if (n < 0 || n > 65535 || img_h <= 0 || img_w <= 0 ||
+      (n && (!crops || !off || !stride || !x0 || !h || !w || !rw || !pad || !out))) {
+    set_error("invalid argument");
+    return E_INVALID;
+  }
+  return guarded([&] {
+    LinePack lp{off, stride, x0, h, w, rw, pad, flip};
+    QPC_CUDA_OR_THROW(launch_line_pack(crops, lp, n, img_h, img_w, out, (cudaStream_t)stream));
     return (int)OK;
   });
 }

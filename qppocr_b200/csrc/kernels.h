@@ -177,4 +177,34 @@ cudaError_t launch_rec_pack(const uint8_t* crops, const int64_t* off, const int*
 cudaError_t launch_db_mask(const float* pred, const uint8_t* mask_in, uint8_t* out, int n, int h, int w,
                            float thresh, int dilate, cudaStream_t st);
 
+// ---- text boxes and line preparation (crop.cu), bit-exact with the
+// reference's host code.
+// box_score_fast (geometry.rs:221-269) per box: pred is n x h x w, boxes
+// [n_boxes][4][2] (x, y) in pred coordinates, img[k] the box's image.
+cudaError_t launch_box_score(const float* pred, int h, int w, const float* boxes, const int* img, int n,
+                             float* out, cudaStream_t st);
+// crop_text_box (crop.rs:8-127) per box from n images of h x w x 3 uint8:
+// box k (corners pts[8k..8k+7]) of image img[k] -> cw[k] x ch[k] x 3 bytes at
+// out + off[k] (rotated clockwise, ch x cw, when ch / cw >= 1.5); max_pixels
+// is the largest cw * ch (sizes the grid).
+cudaError_t launch_crop_boxes(const uint8_t* imgs, int h, int w, const float* pts, const int* img, const int* cw,
+                              const int* ch, const int64_t* off, int n, int max_pixels, uint8_t* out,
+                              cudaStream_t st);
+// Per-line views for launch_line_pack (device arrays, one entry per line).
+struct LinePack {
+  const int64_t* off;  // byte offset of the line's crop
+  const int* stride;   // pixels per crop row
+  const int* x0;       // first column of the view in the crop
+  const int* h;        // view rows
+  const int* w;        // view columns
+  const int* rw;       // resized width (ignored when pad)
+  const int* pad;      // 1: unresized, centred vertically (pack_crop's pad_only)
+  const int* flip;     // 1: view rotated 180 degrees; null: none
+};
+// pack_crop (crop.rs:153-185) of each line's view into a zeroed
+// [3, img_h, img_w] slot of out (n slots): the rec batch and, with cls_view
+// windows (crop.rs:193-218), the cls batch.
+cudaError_t launch_line_pack(const uint8_t* crops, const LinePack& lp, int n, int img_h, int img_w, float* out,
+                             cudaStream_t st);
+
 }  // namespace qpc

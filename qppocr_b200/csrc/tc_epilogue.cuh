@@ -114,14 +114,15 @@ __device__ __forceinline__ void load_residual(const GemmArgs& args, int64_t rrow
                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-template <int BN, int A_MODE, class Fetch>
+// RES = false: the caller never passes a residual (saves its registers).
+template <int BN, int A_MODE, bool RES = true, class Fetch>
 __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorMap* tm_out,
                                            uint8_t* stage, int64_t* s_rrow, int bar_id,
                                            uint32_t& chunk_ctr, int m_blk, int n0, int img, int oy0,
                                            int ox0, int r, int t, Fetch&& fetch) {
   (void)s_rrow;
   const GemmEpilogue& e = args.epi;
-  const int64_t rrow = e.residual ? residual_row<A_MODE>(args, m_blk, img, oy0, ox0, r) : -1;
+  const int64_t rrow = (RES && e.residual) ? residual_row<A_MODE>(args, m_blk, img, oy0, ox0, r) : -1;
 #pragma unroll 1
   for (int cc = 0; cc < BN; cc += 32) {
     if (n0 + cc >= args.N) break;
@@ -130,7 +131,9 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
     // loads, TMEM fetch, bias, activation, residual add), so it overlaps the
     // wait for the store issued from this buffer two chunks ago.
     float4 rv[8];
-    if (e.residual) load_residual(args, rrow, n0 + cc, rv);
+    if constexpr (RES) {
+      if (e.residual) load_residual(args, rrow, n0 + cc, rv);
+    }
     float v[32];
     fetch(cc, v);
     if (e.bias) {
@@ -148,13 +151,14 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
       }
     }
     apply_act_n(v, e.act);
-    if (e.residual) {
+    if (RES && e.residual) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        v[4 * k] = __fadd_rn(v[4 * k], rv[k].x);
-        v[4 * k + 1] = __fadd_rn(v[4 * k + 1], rv[k].y);
-        v[4 * k + 2] = __fadd_rn(v[4 * k + 2], rv[k].z);
-        v[4 * k + 3] = __fadd_rn(v[4 * k + 3], rv[k].w);
+        const float4 q = rv[k];
+        v[4 * k] = __fadd_rn(v[4 * k], q.x);
+        v[4 * k + 1] = __fadd_rn(v[4 * k + 1], q.y);
+        v[4 * k + 2] = __fadd_rn(v[4 * k + 2], q.z);
+        v[4 * k + 3] = __fadd_rn(v[4 * k + 3], q.w);
       }
     }
     if (t == 0) bulk_wait_group_read<1>();

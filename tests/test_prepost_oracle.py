@@ -55,3 +55,23 @@ def test_ctc_decode_greedy():
     # ties keep the lowest index
     idx, _ = orc.ctc_decode(np.array([[0.2, 0.4, 0.4]], np.float32))
     assert idx == [1]
+
+
+def test_crop_size_host_helper_matches_oracle():
+    """qpc_crop_size (host code in the library) against the oracle's
+    restatement of crop.rs:9-15, including tall boxes that rotate."""
+    import qppocr_b200 as q
+    rng = np.random.Generator(np.random.PCG64(12))
+    pts = []
+    for _ in range(200):
+        cx, cy = rng.uniform(0, 500, 2)
+        w, h = rng.uniform(1, 300), rng.uniform(1, 300)
+        a = rng.uniform(-0.6, 0.6)
+        c, s = np.cos(a), np.sin(a)
+        corners = np.array([[-w, -h], [w, -h], [w, h], [-w, h]]) / 2
+        pts.append(corners @ np.array([[c, s], [-s, c]]) + [cx, cy])
+    pts = np.array(pts, np.float32)
+    cw, ch, rot = q.crop_size(pts)
+    for k in range(len(pts)):
+        assert (cw[k], ch[k], bool(rot[k])) == orc.crop_size(pts[k])
+    assert rot.any() and not rot.all()
