@@ -225,6 +225,46 @@ def e2e_seconds(sess, feeds, steps, world, copy=False):
     return (time.perf_counter() - t0) / steps
 
 
+def det_e2e(ctx, g, w, det, x, args, world, rank, B):
+    """Det e2e lines: the headline through a det session with the DB mask
+    exit (u8 mask to the host, map kept on the device), then the same with
+    the f32 map returned, from pageable arrays, and from the f32 input."""
+    import numpy as np
+
+    import qppocr_b200 as q
+
+    img = np.random.Generator(np.random.PCG64(30 + rank)).integers(0, 256, (B, DET_HW, DET_HW, 3),
+                                                                   dtype=np.uint8)
+    img_pin = q.host_empty(img.shape, np.uint8)  # a loader decoding into pinned batch buffers
+    img_pin[...] = img
+    detm = ctx.create_session(g, w, role="det", math=args.math, det_mask_exit=True)
+    e2e_s = max_over_ranks(e2e_seconds(detm, {"x": img_pin}, args.steps, world), world)
+    e2e = {"value": round(world * B / e2e_s, 2), "unit": "img/s",
+           "h2d_bytes_per_step": int(img.nbytes), "d2h_bytes_per_step": int(B * DET_HW * DET_HW),
+           "input": "u8 HWC images in pinned host memory, normalised on the device in the plan as the "
+                    "engine does, (v/255 - 0.5)/0.5 (engine.rs:963-982); config 3's ImageNet mean/std is the "
+                    "same per-channel affine map with other constants, at the same cost",
+           "output": "u8 DB mask (pred > 0.3, 2x2 dilated) to the host; the f32 probability map stays on the "
+                     "device",
+           "timing": E2E_TIMING}
+    detm.close()
+    e2e_s_map = max_over_ranks(e2e_seconds(det, {"x": img_pin}, args.steps, world), world)
+    e2e_map = {"value": round(world * B / e2e_s_map, 2), "unit": "img/s", "h2d_bytes_per_step": int(img.nbytes),
+               "d2h_bytes_per_step": int(B * DET_HW * DET_HW * 4),
+               "input": "as e2e", "output": "the f32 probability map to the host"}
+    e2e_p = max_over_ranks(e2e_seconds(det, {"x": img}, args.steps, world, copy=True), world)
+    e2e_pageable = {"value": round(world * B / e2e_p, 2), "unit": "img/s", "h2d_bytes_per_step": int(img.nbytes),
+                    "d2h_bytes_per_step": int(B * DET_HW * DET_HW * 4),
+                    "input": "u8 HWC images in pageable numpy memory", "timing": E2E_PAGEABLE_TIMING}
+    x_pin = q.host_empty(x.shape, np.float32)
+    x_pin[...] = x
+    e2e_f = max_over_ranks(e2e_seconds(det, {"x": x_pin}, args.steps, world), world)
+    e2e_f32 = {"value": round(world * B / e2e_f, 2), "unit": "img/s", "h2d_bytes_per_step": int(x.nbytes),
+               "d2h_bytes_per_step": int(B * DET_HW * DET_HW * 4),
+               "input": "f32 NCHW network input in pinned host memory"}
+    return e2e, e2e_map, e2e_pageable, e2e_f32
+
+
 def cpu_baseline_det(seconds_budget=20.0):
     """The reference CPU path (oracle restatement, all host threads) on a
     bounded sample: whole 960x960 images, one at a time."""
@@ -309,6 +349,67 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+PIPE_IMAGES = 4096   # config 5: 4096 images of 960 x 960, 16 boxes each, sharded by image
+PIPE_BATCH = 64      # images per pipeline step on one GPU
+PIPE_BOXES = 16
+
+
+def pipeline_bench(ctx, args, world, rank, local):
+    """Config 5: this rank's contiguous share of the images through
+    det (mask exit) -> box scores -> crops -> cls -> rec
+    (qppocr_b200/pipeline.py), PIPE_BATCH images per step; each step uploads
+    its u8 images from pinned host memory and ends with the decoded lines on
+    the host.  Wall clock over all steps after one warm-up step, max over
+    ranks."""
+    import numpy as np
+    import torch
+
+    import qppocr_b200 as q
+    from qppocr_b200 import nets
+    from qppocr_b200.pipeline import OcrPipeline, synthetic_boxes
+    from qppocr_b200.shard import shard_bounds
+
+    i0, i1 = shard_bounds(args.pipeline_images, world, rank)
+    n_img = i1 - i0
+    gd, wd = nets.build_det()
+    gd = q.optimize(gd, wd)
+    gc, wc = nets.build_cls()
+    gc = q.optimize(gc, wc)
+    gr, wr = nets.build_rec()
+    gr = q.optimize(gr, wr)
+    det = ctx.create_session(gd, wd, role="det", math=args.math, det_mask_exit=True)
+    cls = ctx.create_session(gc, wc, role="cls", math=args.math)
+    rec = ctx.create_session(gr, wr, role="rec", math=args.math)
+    # one cls run per step over all its lines (the engine's QPPOCR_CLS_BATCH
+    # override; the batch size changes no result, engine.rs:1309-1312)
+    pipe = OcrPipeline(det, cls, rec, device=local, cls_batch=PIPE_BATCH * PIPE_BOXES)
+    dev = torch.device("cuda", local)
+    rng = np.random.Generator(np.random.PCG64(70 + rank))
+    host = torch.from_numpy(rng.integers(0, 256, (PIPE_BATCH, DET_HW, DET_HW, 3), dtype=np.uint8)).pin_memory()
+    boxes = synthetic_boxes(PIPE_BATCH, PIPE_BOXES, DET_HW, DET_HW, seed=80 + rank)
+    steps = (n_img + PIPE_BATCH - 1) // PIPE_BATCH
+    pipe.run(host.to(dev), boxes)  # warm-up: plans for every batch shape
+    barrier(world)
+    t0 = time.perf_counter()
+    lines = 0
+    for k in range(steps):
+        nb = min(PIPE_BATCH, n_img - k * PIPE_BATCH)
+        imgs = host[:nb].to(dev, non_blocking=True)
+        out = pipe.run(imgs, boxes[:nb])
+        lines += out["lines"]
+    dt = max_over_ranks(time.perf_counter() - t0, world)
+    for s_ in (det, cls, rec):
+        s_.close()
+    return {"metric": "pipeline images/s and lines/s (config 5)", "value": round(world * n_img / dt, 1),
+            "unit": "img/s", "lines_per_s": round(world * lines / dt, 1), "images": world * n_img,
+            "lines": world * lines, "boxes_per_image": PIPE_BOXES, "batch_images": PIPE_BATCH,
+            "h2d_bytes_per_image": DET_HW * DET_HW * 3, "d2h_bytes_per_image": DET_HW * DET_HW,
+            "timing": "wall clock over all steps, max over ranks: per step the H2D of the u8 images, det with "
+                      "the mask exit (u8 mask to the host), box scores on the kept map, crops, one cls run, "
+                      "rec runs of up to rec_chunk lines with the next packed while one runs, host CTC decode",
+            "sharding": f"{world} rank(s), contiguous image shares of {args.pipeline_images}"}
+
+
 def gemm_sweep(args):
     """Config 2: X [M, K] U[-1, 1] x W [K, N] + bias + hardswish through
     qpc_op_gemm, inputs resident, CUDA events over 20 launches after warm-up;
@@ -363,6 +464,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-rec", action="store_true")
     ap.add_argument("--no-3x", action="store_true", help="skip the 3xTF32 det line")
+    ap.add_argument("--no-pipeline", action="store_true", help="skip the config-5 det->cls->rec line")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the det e2e lines (device timing only)")
+    ap.add_argument("--pipeline-images", type=int, default=PIPE_IMAGES,
+                    help="config 5 images over all ranks (each rank takes its contiguous share)")
     ap.add_argument("--gemm-sweep", action="store_true",
                     help="config 2: time the pointwise GEMM over its M x (K, N) grid and print a table")
     args = ap.parse_args()
@@ -439,29 +544,15 @@ def main():
 
     # e2e through the public API: host inputs, H2D + compute + D2H every step.
     # Headline: u8 HWC images (what the reference engine's det stage starts
-    # from), normalised on the device as engine.rs:963-982 does on the host;
-    # beside it the same with the f32 network input tensor.
-    img = np.random.Generator(np.random.PCG64(30 + rank)).integers(0, 256, (B, DET_HW, DET_HW, 3),
-                                                                   dtype=np.uint8)
-    img_pin = q.host_empty(img.shape, np.uint8)  # a loader decoding into pinned batch buffers
-    img_pin[...] = img
-    e2e_s = max_over_ranks(e2e_seconds(det, {"x": img_pin}, args.steps, world), world)
-    e2e = {"value": round(world * B / e2e_s, 2), "unit": "img/s",
-           "h2d_bytes_per_step": int(img.nbytes), "d2h_bytes_per_step": int(B * DET_HW * DET_HW * 4),
-           "input": "u8 HWC images in pinned host memory, normalised on the device in the plan as the "
-                    "engine does, (v/255 - 0.5)/0.5 (engine.rs:963-982); config 3's ImageNet mean/std is the "
-                    "same per-channel affine map with other constants, at the same cost",
-           "timing": E2E_TIMING}
-    e2e_p = max_over_ranks(e2e_seconds(det, {"x": img}, args.steps, world, copy=True), world)
-    e2e_pageable = {"value": round(world * B / e2e_p, 2), "unit": "img/s", "h2d_bytes_per_step": int(img.nbytes),
-                    "d2h_bytes_per_step": int(B * DET_HW * DET_HW * 4),
-                    "input": "u8 HWC images in pageable numpy memory", "timing": E2E_PAGEABLE_TIMING}
-    x_pin = q.host_empty(x.shape, np.float32)
-    x_pin[...] = x
-    e2e_f = max_over_ranks(e2e_seconds(det, {"x": x_pin}, args.steps, world), world)
-    e2e_f32 = {"value": round(world * B / e2e_f, 2), "unit": "img/s", "h2d_bytes_per_step": int(x.nbytes),
-               "d2h_bytes_per_step": int(B * DET_HW * DET_HW * 4),
-               "input": "f32 NCHW network input in pinned host memory"}
+    # from), normalised on the device as engine.rs:963-982 does on the host,
+    # through a det session with the DB mask exit: the host receives the u8
+    # mask its connected components run on (geometry.rs:286-296), the
+    # probability map stays on the device for box scoring.  Beside it: the
+    # same returning the f32 probability map, from pageable arrays, and from
+    # the f32 network input.
+    e2e = e2e_map = e2e_pageable = e2e_f32 = None
+    if not args.no_e2e:
+        e2e, e2e_map, e2e_pageable, e2e_f32 = det_e2e(ctx, g, w, det, x, args, world, rank, B)
 
     # ---------------------------------------------------------------- rec
     rec = None
@@ -508,6 +599,11 @@ def main():
                                    "two batches in flight, CTC decode of the argmax pairs"}}
         rs.close()
 
+    # ---------------------------------------------------------------- pipeline
+    pipe = None
+    if not args.no_pipeline:
+        pipe = pipeline_bench(ctx, args, world, rank, local)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_det()
@@ -529,8 +625,9 @@ def main():
                           "< 1e-2 (random-init nets amplify TF32 rounding)" if args.math == "tf32" else
                           "max|d|/max|ref| < 1e-5 end to end vs the oracle"),
             "det_3xtf32": det_3x,
-            "roofline": rl, "cpu_baseline": cpu, "e2e": e2e, "e2e_pageable": e2e_pageable, "e2e_f32_input": e2e_f32, "clocks": clk,
-            "gpu_launches": launches * args.steps, "rec": rec,
+            "roofline": rl, "cpu_baseline": cpu, "e2e": e2e, "e2e_prob_map": e2e_map, "e2e_pageable": e2e_pageable,
+            "e2e_f32_input": e2e_f32, "clocks": clk,
+            "gpu_launches": launches * args.steps, "rec": rec, "pipeline": pipe,
         }
         print(json.dumps(line), flush=True)
     det.close()

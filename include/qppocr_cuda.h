@@ -111,7 +111,18 @@ typedef struct {
  * without a host round trip.  The data must be complete before the call (make
  * the producing stream finish first) and stay unchanged until the run
  * completes.  Same plans as QPC_F32. */
-enum qpc_dtype { QPC_F32 = 0, QPC_I64 = 1, QPC_U8_IMAGE = 2, QPC_F32_DEVICE = 3 };
+/* QPC_U8 (outputs only): a uint8 tensor, the det mask exit's mask.
+ * QPC_U8_IMAGE_DEVICE (run inputs only): a QPC_U8_IMAGE batch already in this
+ * device's memory (same rules as QPC_F32_DEVICE), e.g. images a pipeline also
+ * crops text lines from on the device. */
+enum qpc_dtype {
+  QPC_F32 = 0,
+  QPC_I64 = 1,
+  QPC_U8_IMAGE = 2,
+  QPC_F32_DEVICE = 3,
+  QPC_U8 = 4,
+  QPC_U8_IMAGE_DEVICE = 5
+};
 
 /* A host tensor (tensor.rs:28-40): initializers and run inputs. */
 typedef struct {
@@ -136,6 +147,13 @@ typedef struct {
                                 -1 = role default (on for REC) */
   int64_t plan_budget_bytes; /* per-shape plan cache byte budget; 0 = default (8 GiB) */
   int use_cuda_graph;        /* 1 = one captured CUDA graph per shape (default), 0 = stream launches */
+  int det_mask_exit;         /* det (role DET, one [n,1,h,w] output): output 0 becomes the [n,h,w]
+                                QPC_U8 mask pred > mask_thresh, 2x2-dilated when mask_dilate
+                                (the DB post's first step, geometry.rs:286-296), and output 1 the
+                                probability map, kept in device memory (no host copy) for
+                                qpc_op_box_score; 0 = off */
+  float mask_thresh;         /* DB binarize threshold (PipelineConfig det_db_thresh; default 0.3) */
+  int mask_dilate;           /* 1 = 2x2 dilation (use_dilation) */
 } qpc_session_options;
 
 typedef struct qpc_session qpc_session;
@@ -178,8 +196,15 @@ int qpc_complete(qpc_ticket* ticket, int timeout_ms);
 int qpc_ticket_output_count(const qpc_ticket* ticket, int* count);
 int qpc_ticket_output(const qpc_ticket* ticket, int index, const float** data,
                       const int64_t** shape, int* rank);
+/* Type and place of output `index` of a completed ticket: *dtype a
+ * qpc_dtype (QPC_F32, or QPC_U8 for the det mask), *device_only 1 when the
+ * output stays in device memory (qpc_ticket_output then gives data NULL), and
+ * *device_data its device address, valid until qpc_ticket_release.  Any
+ * pointer may be NULL. */
+int qpc_ticket_output_info(const qpc_ticket* ticket, int index, int* dtype, int* device_only,
+                           const void** device_data);
 /* Copy output `index` of a completed ticket into the caller's buffer `dst`
- * (`count` floats, the output's element count) with the library's host copy
+ * (`count` elements of the output's dtype, its element count) with the library's host copy
  * threads.  This is the copy into the fresh host Tensor that
  * DeviceSession::run returns (device.rs:130); a binding may instead copy
  * from qpc_ticket_output's pointer itself. */

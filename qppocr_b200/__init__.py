@@ -30,6 +30,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libqppocr_cuda.so")
 
 QPC_OK, QPC_ERR_INVALID, QPC_ERR_GRAPH, QPC_ERR_DEVICE, QPC_ERR_TIMEOUT, QPC_ERR_OOM = range(6)
+QPC_U8 = 4  # qpc_dtype of u8 outputs (the det mask)
 ROLE = {"other": 0, "det": 1, "rec": 2, "cls": 3}
 MATH = {"tf32": 0, "3xtf32": 1}
 ACT = {None: 0, "none": 0, "relu": 1, "hswish": 2, "sigmoid": 3, "gelu": 4, "hsigmoid": 5, "swish": 6}
@@ -83,7 +84,8 @@ class QpcTensor(ctypes.Structure):
 
 class QpcOptions(ctypes.Structure):
     _fields_ = [("math", ctypes.c_int), ("argmax_exit", ctypes.c_int),
-                ("plan_budget_bytes", ctypes.c_int64), ("use_cuda_graph", ctypes.c_int)]
+                ("plan_budget_bytes", ctypes.c_int64), ("use_cuda_graph", ctypes.c_int),
+                ("det_mask_exit", ctypes.c_int), ("mask_thresh", ctypes.c_float), ("mask_dilate", ctypes.c_int)]
 
 
 class QpcCaps(ctypes.Structure):
@@ -96,7 +98,7 @@ class QpcCaps(ctypes.Structure):
 EXPORTED = (
     "qpc_last_error", "qpc_device_count", "qpc_device_info", "qpc_session_create",
     "qpc_session_caps", "qpc_run_async", "qpc_complete", "qpc_ticket_output_count",
-    "qpc_ticket_output", "qpc_ticket_output_copy", "qpc_ticket_release", "qpc_run", "qpc_ticket_device_ms",
+    "qpc_ticket_output", "qpc_ticket_output_copy", "qpc_ticket_output_info", "qpc_ticket_release", "qpc_run", "qpc_ticket_device_ms",
     "qpc_host_alloc", "qpc_host_free",
     "qpc_session_destroy", "qpc_session_profile", "qpc_session_profile_step",
     "qpc_session_replay", "qpc_session_node_count", "qpc_session_node", "qpc_op_dwconv_nhwc", "qpc_op_gemm", "qpc_op_ctc_head", "qpc_op_ctc_head_noalloc",
@@ -131,6 +133,8 @@ def lib():
                                     ctypes.POINTER(ctypes.POINTER(ctypes.c_int64)),
                                     ctypes.POINTER(ctypes.c_int)]
     L.qpc_ticket_output_copy.argtypes = [P, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64]
+    L.qpc_ticket_output_info.argtypes = [P, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
+                                         ctypes.POINTER(ctypes.c_void_p)]
     L.qpc_host_alloc.argtypes = [ctypes.c_int64, ctypes.POINTER(P)]
     L.qpc_host_free.argtypes = [P]
     L.qpc_ticket_release.argtypes = [P]
@@ -235,16 +239,17 @@ def _attr(keep: _Keep, name: str, v) -> QpcAttr:
 
 def _tensor(keep: _Keep, name: str, arr) -> QpcTensor:
     if hasattr(arr, "is_cuda") and arr.is_cuda:
-        # f32 tensor already on the device (QPC_F32_DEVICE): copied on the GPU
+        # tensor already on the device: f32 (QPC_F32_DEVICE) or a u8 n x h x w x
+        # 3 image batch (QPC_U8_IMAGE_DEVICE), copied on the GPU
         import torch
-        assert arr.dtype == torch.float32 and arr.is_contiguous(), "contiguous f32 device tensor expected"
+        assert arr.dtype in (torch.float32, torch.uint8) and arr.is_contiguous(), "contiguous device tensor expected"
         keep.add(arr)
         shp = keep.add((ctypes.c_int64 * max(arr.dim(), 1))(*arr.shape))
         t = QpcTensor()
         t.name = keep.add(name.encode())
         t.shape = shp
         t.rank = arr.dim()
-        t.dtype = 3
+        t.dtype = 3 if arr.dtype == torch.float32 else 5
         t.data = arr.data_ptr()
         return t
     if arr.dtype == np.int64 or arr.dtype == np.int32:
@@ -332,14 +337,37 @@ def host_empty(shape, dtype=np.float32) -> np.ndarray:
     return np.frombuffer(buf, dtype=dt, count=int(np.prod(shape, dtype=np.int64))).reshape(shape)
 
 
-def _pinned_view(data, shape, cnt: int, owner) -> np.ndarray:
+def _pinned_view(data, shape, cnt: int, owner, dtype=np.float32) -> np.ndarray:
     """Read-only array over a run's pinned output buffer; holds `owner` (the
     DeferredRun, whose ticket keeps the buffer) alive."""
-    buf = (ctypes.c_float * max(cnt, 1)).from_address(ctypes.addressof(data.contents))
+    dt = np.dtype(dtype)
+    buf = (ctypes.c_char * max(cnt * dt.itemsize, 1)).from_address(ctypes.addressof(data.contents))
     buf._owner = owner
-    a = np.frombuffer(buf, dtype=np.float32, count=cnt).reshape(shape)
+    a = np.frombuffer(buf, dtype=dt, count=cnt).reshape(shape)
     a.flags.writeable = False
     return a
+
+
+class DeviceOutput:
+    """An output a run keeps in device memory (the det mask exit's
+    probability map): shape, dtype and device address, valid while the
+    DeferredRun that produced it is alive.  `torch()` is a zero-copy view."""
+
+    def __init__(self, ptr: int, shape, dtype, owner, device: int):
+        self.ptr = ptr
+        self.shape = tuple(shape)
+        self.dtype = np.dtype(dtype)
+        self.device = device
+        self._owner = owner
+
+    @property
+    def __cuda_array_interface__(self):
+        return {"shape": self.shape, "typestr": self.dtype.str, "data": (self.ptr, False), "version": 3,
+                "strides": None}
+
+    def torch(self):
+        import torch
+        return torch.as_tensor(self, device=f"cuda:{self.device}")
 
 
 # ------------------------------------------------------------------ device seam
@@ -368,17 +396,23 @@ class DeferredRun:
             _check(L.qpc_ticket_output(self._t, k, ctypes.byref(data), ctypes.byref(shp), ctypes.byref(rank)))
             shape = tuple(shp[i] for i in range(rank.value))
             cnt = int(np.prod(shape)) if shape else 1
-            if copy:
-                out = np.empty(shape, np.float32)
+            dt, dev_only, dptr = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_void_p()
+            _check(L.qpc_ticket_output_info(self._t, k, ctypes.byref(dt), ctypes.byref(dev_only), ctypes.byref(dptr)))
+            np_dt = np.uint8 if dt.value == QPC_U8 else np.float32
+            if dev_only.value:
+                out = DeviceOutput(dptr.value, shape, np.float32, self, self._s.device)
+                self._device_outputs = True
+            elif copy:
+                out = np.empty(shape, np_dt)
                 _check(L.qpc_ticket_output_copy(self._t, k, out.ctypes.data, cnt))
             else:
-                out = _pinned_view(data, shape, cnt, self)
+                out = _pinned_view(data, shape, cnt, self, np_dt)
             outs.append(out)
         ms = ctypes.c_float(0)
         _check(L.qpc_ticket_device_ms(self._t, ctypes.byref(ms)))
         self.device_ms = ms.value
-        if copy:
-            self.release()
+        if copy and not getattr(self, "_device_outputs", False):
+            self.release()  # (a run with device outputs is released when dropped)
         return outs
 
     def release(self):
@@ -509,7 +543,8 @@ class CudaContext:
 
     def create_session(self, graph: Graph, initializers: Dict[str, np.ndarray], role: str = "other",
                        math: str = "tf32", argmax_exit: Optional[bool] = None,
-                       use_cuda_graph: bool = True, plan_budget_bytes: int = 0) -> CudaSession:
+                       use_cuda_graph: bool = True, plan_budget_bytes: int = 0, det_mask_exit: bool = False,
+                       mask_thresh: float = 0.3, mask_dilate: bool = True) -> CudaSession:
         keep = _Keep()
         qg = _graph(keep, graph)
         wt, nw = _tensors(keep, initializers)
@@ -518,6 +553,9 @@ class CudaContext:
         opts.argmax_exit = -1 if argmax_exit is None else int(bool(argmax_exit))
         opts.plan_budget_bytes = plan_budget_bytes
         opts.use_cuda_graph = 1 if use_cuda_graph else 0
+        opts.det_mask_exit = 1 if det_mask_exit else 0
+        opts.mask_thresh = mask_thresh
+        opts.mask_dilate = 1 if mask_dilate else 0
         h = ctypes.c_void_p()
         _check(lib().qpc_session_create(self.index, ctypes.byref(qg), wt, nw, ROLE[role], ctypes.byref(opts),
                                         ctypes.byref(h)))

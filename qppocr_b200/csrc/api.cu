@@ -208,12 +208,30 @@ int qpc_ticket_output_copy(const qpc_ticket* t, int index, float* dst, int64_t c
     return E_INVALID;
   }
   const auto& io = t->plan->outs[index];
+  if (io.device_only) {
+    set_error("output " + std::to_string(index) + " stays in device memory (qpc_ticket_output_info)");
+    return E_INVALID;
+  }
   if (count != io.count) {
     set_error("output " + std::to_string(index) + " has " + std::to_string(io.count) + " elements, not " +
               std::to_string(count));
     return E_INVALID;
   }
-  qpc::parallel_copy(dst, io.host, (size_t)count * sizeof(float));
+  qpc::parallel_copy(dst, io.host, io.bytes);
+  return OK;
+}
+
+int qpc_ticket_output_info(const qpc_ticket* t, int index, int* dtype, int* device_only,
+                           const void** device_data) {
+  if (!t || !t->plan || index < 0 || index >= (int)t->plan->outs.size()) return E_INVALID;
+  if (!t->completed) {
+    set_error("ticket not completed");
+    return E_INVALID;
+  }
+  const auto& io = t->plan->outs[index];
+  if (dtype) *dtype = io.dtype;
+  if (device_only) *device_only = io.device_only ? 1 : 0;
+  if (device_data) *device_data = io.dev;
   return OK;
 }
 

@@ -33,6 +33,12 @@
 
 namespace qpc {
 
+// The plan-level type of a run input: device-resident f32 / u8 images use
+// the same plans as their host forms (only the upload differs).
+static int base_dtype(int d) {
+  return d == QPC_F32_DEVICE ? QPC_F32 : (d == QPC_U8_IMAGE_DEVICE ? QPC_U8_IMAGE : d);
+}
+
 // ================================================================ runtime
 static thread_local std::string g_err;
 void set_error(const std::string& m) { g_err = m; }
@@ -224,7 +230,11 @@ Session::Session(int device, const qpc_graph* g, const qpc_tensor* w, int nw, in
   opts_.argmax_exit = -1;
   opts_.plan_budget_bytes = 0;
   opts_.use_cuda_graph = 1;
+  opts_.det_mask_exit = 0;
+  opts_.mask_thresh = 0.3f;
+  opts_.mask_dilate = 1;
   if (opts) opts_ = *opts;
+  if (opts_.det_mask_exit && role != QPC_ROLE_DET) throw GraphError{"det_mask_exit needs the det role"};
   if (opts_.plan_budget_bytes <= 0) opts_.plan_budget_bytes = (int64_t)8 << 30;
   argmax_exit_ = opts_.argmax_exit < 0 ? (role == QPC_ROLE_REC) : (opts_.argmax_exit != 0);
   device_state(device_);
@@ -916,13 +926,14 @@ class Planner {
       for (int k = 0; k < n_inputs; ++k)
         if (gi == inputs[k].name) t = &inputs[k];
       if (!t) throw GraphError{"missing graph input " + gi};
-      if (t->dtype != QPC_F32 && t->dtype != QPC_F32_DEVICE && t->dtype != QPC_U8_IMAGE)
+      if (t->dtype != QPC_F32 && t->dtype != QPC_F32_DEVICE && t->dtype != QPC_U8_IMAGE &&
+          t->dtype != QPC_U8_IMAGE_DEVICE)
         throw GraphError{"graph input " + gi + " must be f32 (or a u8 image batch)"};
       Val v;
       PlanInstance::IO io;
       io.name = gi;
-      io.dtype = t->dtype == QPC_F32_DEVICE ? QPC_F32 : t->dtype;  // host or device f32: same plan
-      if (t->dtype == QPC_U8_IMAGE) {
+      io.dtype = base_dtype(t->dtype);  // host or device data: same plan
+      if (io.dtype == QPC_U8_IMAGE) {
         // n x h x w x 3 u8 images for an [n, 3, h, w] f32 input: staged as
         // bytes, normalised on the device as the reference engine does
         if (t->rank != 4 || t->shape[3] != 3) throw GraphError{"u8 image input " + gi + " must be n x h x w x 3"};
@@ -985,8 +996,38 @@ class Planner {
       io.name = go;
       io.shape = o.shape;
       io.count = o.numel();
+      io.bytes = (size_t)io.count * sizeof(float);
+      io.dtype = QPC_F32;
       io.dev = A.ptr(o.buf) + o.off;
       P.outs.push_back(io);
+    }
+    if (S.det_mask_exit()) {
+      // DB mask exit (geometry.rs:286-296): the host receives the binarized,
+      // 2x2-dilated u8 mask its connected components run on (a quarter of
+      // the probability map's bytes); the map itself stays on the device
+      // (output 1, device only) for box scoring (qpc_op_box_score).
+      if (P.outs.size() != 1 || P.outs[0].shape.size() != 4 || P.outs[0].shape[1] != 1)
+        throw GraphError{"det mask exit needs one [n, 1, h, w] output"};
+      PlanInstance::IO& pred = P.outs[0];
+      const int64_t n = pred.shape[0], h = pred.shape[2], w = pred.shape[3];
+      PlanInstance::IO m;
+      m.name = pred.name + ".mask";
+      m.shape = {n, h, w};
+      m.count = n * h * w;
+      m.bytes = (size_t)m.count;
+      m.dtype = QPC_U8;
+      const int mb = A.alloc((m.count + 3) / 4, true);
+      m.dev = A.ptr(mb);
+      const float* pp = pred.dev;
+      uint8_t* mp = reinterpret_cast<uint8_t*>(m.dev);
+      const float th = S.mask_thresh();
+      const int dil = S.mask_dilate() ? 1 : 0;
+      step("db_mask", m.name, 4.0 * m.count + (double)m.count, 0, [=](cudaStream_t st) {
+        return launch_db_mask(pp, nullptr, mp, (int)n, (int)h, (int)w, th, dil, st);
+      });
+      pred.device_only = true;
+      pred.bytes = 0;
+      P.outs.insert(P.outs.begin(), m);
     }
     for (auto& b : A.bufs) {
       P.bytes += b.mem->bytes;
@@ -2456,7 +2497,7 @@ class Planner {
 static std::string shape_key(const qpc_tensor* in, int n) {
   std::ostringstream o;
   for (int k = 0; k < n; ++k) {
-    o << (in[k].name ? in[k].name : "") << ":d" << (in[k].dtype == QPC_F32_DEVICE ? QPC_F32 : in[k].dtype) << ":";
+    o << (in[k].name ? in[k].name : "") << ":d" << base_dtype(in[k].dtype) << ":";
     for (int d = 0; d < in[k].rank; ++d) o << in[k].shape[d] << "x";
     o << ";";
   }
@@ -2476,7 +2517,8 @@ std::unique_ptr<PlanInstance> Session::build(const qpc_tensor* inputs, int n, co
   for (auto& io : p->ins)
     QPC_CUDA_OR_THROW(cudaHostAlloc((void**)&io.host, std::max<size_t>(io.bytes, 4), cudaHostAllocDefault));
   for (auto& io : p->outs)
-    QPC_CUDA_OR_THROW(cudaHostAlloc((void**)&io.host, std::max<int64_t>(io.count, 1) * sizeof(float), cudaHostAllocDefault));
+    if (!io.device_only)
+      QPC_CUDA_OR_THROW(cudaHostAlloc((void**)&io.host, std::max<size_t>(io.bytes, 4), cudaHostAllocDefault));
   // Eager validation pass (sets kernel attributes, surfaces launch errors).
   for (size_t k = 0; k < p->steps.size(); ++k) {
     cudaError_t e = p->steps[k](p->stream);
@@ -2557,9 +2599,9 @@ PlanInstance* Session::launch(const qpc_tensor* inputs, int n) {
       const qpc_tensor* t = nullptr;
       for (int k = 0; k < n; ++k)
         if (io.name == inputs[k].name) t = &inputs[k];
-      const int dt = t->dtype == QPC_F32_DEVICE ? QPC_F32 : t->dtype;
+      const int dt = base_dtype(t->dtype);
       if (dt != io.dtype) throw GraphError{"input " + io.name + ": dtype differs from the plan's"};
-      if (t->dtype == QPC_F32_DEVICE)
+      if (t->dtype == QPC_F32_DEVICE || t->dtype == QPC_U8_IMAGE_DEVICE)
         QPC_CUDA_OR_THROW(cudaMemcpyAsync(io.dev, t->data, io.bytes, cudaMemcpyDeviceToDevice, p->stream));
       else if (pinned_contains(t->data, io.bytes))  // caller's pinned buffer: DMA, no staging
         QPC_CUDA_OR_THROW(cudaMemcpyAsync(io.dev, t->data, io.bytes, cudaMemcpyHostToDevice, p->stream));
@@ -2580,7 +2622,8 @@ PlanInstance* Session::launch(const qpc_tensor* inputs, int n) {
       QPC_CUDA_OR_THROW(cudaEventRecord(compute_done_, p->stream));
     }
     for (auto& io : p->outs)
-      QPC_CUDA_OR_THROW(cudaMemcpyAsync(io.host, io.dev, io.count * sizeof(float), cudaMemcpyDeviceToHost, p->stream));
+      if (!io.device_only)
+        QPC_CUDA_OR_THROW(cudaMemcpyAsync(io.host, io.dev, io.bytes, cudaMemcpyDeviceToHost, p->stream));
     QPC_CUDA_OR_THROW(cudaEventRecord(p->ev[3], p->stream));
   } catch (...) {
     release(p);

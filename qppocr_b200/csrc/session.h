@@ -75,8 +75,9 @@ struct PlanInstance {
     float* dev = nullptr;
     int64_t count = 0;
     float* host = nullptr;  // pinned
-    size_t bytes = 0;       // bytes moved per run (inputs: u8 images are 1 byte per value)
+    size_t bytes = 0;       // bytes moved per run (inputs: u8 images are 1 byte per value; outputs: D2H bytes)
     int dtype = 0;          // qpc_dtype of the run tensor
+    bool device_only = false;  // output kept in device memory (no D2H, host == nullptr)
   };
   std::vector<IO> ins, outs;
   std::atomic<bool> busy{false};
@@ -106,6 +107,9 @@ class Session {
   int role() const { return role_; }
   int math() const { return opts_.math; }
   bool argmax_exit() const { return argmax_exit_; }
+  bool det_mask_exit() const { return opts_.det_mask_exit != 0; }
+  float mask_thresh() const { return opts_.mask_thresh; }
+  bool mask_dilate() const { return opts_.mask_dilate != 0; }
   const std::vector<Node>& nodes() const { return nodes_; }
   const std::vector<std::string>& graph_inputs() const { return inputs_; }
   const std::vector<std::string>& graph_outputs() const { return outputs_; }
