@@ -211,7 +211,8 @@ def e2e_seconds(sess, feeds, steps, world, copy=False):
     warm = [sess.run_deferred(feeds), sess.run_deferred(feeds)]  # builds / warms both plan instances
     for r in warm:
         r.complete(copy=True)
-    del warm
+        r.release()  # (a run with device-resident outputs is otherwise held until dropped)
+    del warm, r
     barrier(world)
     t0 = time.perf_counter()
     pend = sess.run_deferred(feeds)

@@ -145,7 +145,9 @@ typedef struct {
   int argmax_exit;           /* rec: emit [B,T,2] (val, idx bits) instead of [B,T,C]
                                 (DeviceSession::rec_argmax_pairs, device.rs:159-163);
                                 -1 = role default (on for REC) */
-  int64_t plan_budget_bytes; /* per-shape plan cache byte budget; 0 = default (8 GiB) */
+  int64_t plan_budget_bytes; /* plan cache byte budget (idle plans evicted oldest first when a
+                                new one would exceed it); 0 = default, a quarter of the
+                                device's memory (at least 8 GiB) */
   int use_cuda_graph;        /* 1 = one captured CUDA graph per shape (default), 0 = stream launches */
   int det_mask_exit;         /* det (role DET, one [n,1,h,w] output): output 0 becomes the [n,h,w]
                                 QPC_U8 mask pred > mask_thresh, 2x2-dilated when mask_dilate

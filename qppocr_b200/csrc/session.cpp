@@ -235,7 +235,15 @@ Session::Session(int device, const qpc_graph* g, const qpc_tensor* w, int nw, in
   opts_.mask_dilate = 1;
   if (opts) opts_ = *opts;
   if (opts_.det_mask_exit && role != QPC_ROLE_DET) throw GraphError{"det_mask_exit needs the det role"};
-  if (opts_.plan_budget_bytes <= 0) opts_.plan_budget_bytes = (int64_t)8 << 30;
+  if (opts_.plan_budget_bytes <= 0) {
+    // a quarter of the device's memory: room for two in-flight instances of
+    // a large shape (a 960 x 960 det plan at batch 64 holds ~4.5 GB) plus
+    // the other shapes, without evicting the instance the next run needs
+    size_t free_b = 0, total_b = 0;
+    QPC_CUDA_OR_THROW(cudaSetDevice(device));
+    QPC_CUDA_OR_THROW(cudaMemGetInfo(&free_b, &total_b));
+    opts_.plan_budget_bytes = std::max<int64_t>((int64_t)8 << 30, (int64_t)(total_b / 4));
+  }
   argmax_exit_ = opts_.argmax_exit < 0 ? (role == QPC_ROLE_REC) : (opts_.argmax_exit != 0);
   device_state(device_);
   for (int k = 0; k < g->n_nodes; ++k) {
