@@ -155,12 +155,12 @@ def barrier(world):
 # or per line (rec), from ncu dram__bytes_read.sum + dram__bytes_write.sum
 # captures.  The roofline's `traffic` is this times the batch, for the
 # dominant family.
-DET_TRAFFIC_PER_IMAGE = {"gemm_tc": 10579557, "dwconv": 15433143, "conv_tc": 12606576, "conv_direct": 25509848,
-                         "resize": 5653212, "convt_pair": 8577152, "gap": 1383226, "det_preprocess": 3216060}
-REC_TRAFFIC_PER_LINE = {"gemm_tc": 115481, "dwconv": 276782, "head_gemm": 54870, "bmm_small": 58308,
-                        "layernorm": 19268, "softmax": 51293, "pool2d": 231737, "head_combine": 94134,
-                        "conv_direct": 209899, "binary": 23149, "copy": 19274}
-TRAFFIC_SOURCE = "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, per image (line), scaled by batch"
+DET_TRAFFIC_PER_IMAGE = {"dwpw": 13524404, "gemm_tc": 8810649, "conv_tc": 12279394, "dwconv": 13399754,
+                         "conv_direct": 23703775, "resize": 4868821, "convt_pair": 7491018, "gap": 1382703}
+REC_TRAFFIC_PER_LINE = {"gemm_tc": 90276, "dwpw": 321667, "dwconv": 236061, "pool2d": 231634, "layernorm": 19268,
+                        "head_gemm": 54868, "head_combine": 94135}
+TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum summed over the family's launches of one pass on a "
+                  "small case (det batch 24, rec batch 256), per image (line) per launch, scaled to this batch")
 
 
 def roofline(profile, hbm, tf, traffic_per_unit=None, units=1):

@@ -417,6 +417,11 @@ bool dwpw_ok(const ConvGeom& g, int n_out) {
   if (g.ph >= g.kh || g.pw >= g.kw) return false;
   // rows of the NHWC tensors stay addressable with 32-bit tile coordinates
   if ((int64_t)g.n * g.oh * g.ow >= (int64_t)1 << 31) return false;
+  // maps the 8 x 16 tiles cover poorly (the rec lines' 3-row maps: 31% of a
+  // tile's rows carry outputs) do more work fused than as two kernels
+  const double cover = (double)g.oh * g.ow /
+                       ((double)((g.oh + DW_TH - 1) / DW_TH) * DW_TH * ((g.ow + DW_TW - 1) / DW_TW) * DW_TW);
+  if (cover < 0.7) return false;
   return dwpw_plan(g.kh, g.sh, dwpw_bn(n_out), g.c, dwpw_ngrp(g.sh, dwpw_bn(n_out))).xs > 0;
 }
 

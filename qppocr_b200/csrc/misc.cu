@@ -931,59 +931,61 @@ cudaError_t launch_reduce_mean(const float* x, float* y, int64_t outer, int64_t 
   return cudaGetLastError();
 }
 
-// activation.rs:321-403 softmax_last_dim, one thread per row: 8-lane max,
-// exp1(x - max), per-lane partial sums combined by the hsum8 tree, scalar
-// tail, y = e * (1 / sum).  Bit-identical to the reference row kernel.
+// activation.rs:321-403 softmax_last_dim on one row: 8-lane max, exp1(x -
+// max), per-lane partial sums combined by the hsum8 tree, scalar tail,
+// y = e * (1 / sum).  Bit-identical to the reference row kernel.  `row` and
+// `out` may alias.
+__device__ __forceinline__ void softmax_row(const float* row, float* out, int inner) {
+  int i = 0;
+  float mx;
+  if (inner >= 8) {
+    float vmax[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) vmax[j] = row[0];
+    for (; i + 8 <= inner; i += 8)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float v = row[i + j];
+        if (v > vmax[j]) vmax[j] = v;
+      }
+    mx = vmax[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j)
+      if (vmax[j] > mx) mx = vmax[j];
+  } else {
+    i = 1;
+    mx = row[0];
+  }
+  for (; i < inner; ++i)
+    if (row[i] > mx) mx = row[i];
+  float sum = 0.f;
+  int i2 = 0;
+  if (inner >= 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (; i2 + 8 <= inner; i2 += 8)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float e = exp1(__fsub_rn(row[i2 + j], mx));
+        out[i2 + j] = e;
+        acc[j] = __fadd_rn(acc[j], e);
+      }
+    const float t0 = __fadd_rn(acc[0], acc[4]), t1 = __fadd_rn(acc[1], acc[5]);
+    const float t2 = __fadd_rn(acc[2], acc[6]), t3 = __fadd_rn(acc[3], acc[7]);
+    sum = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
+  }
+  for (; i2 < inner; ++i2) {
+    const float e = exp1(__fsub_rn(row[i2], mx));
+    out[i2] = e;
+    sum = __fadd_rn(sum, e);
+  }
+  const float inv = __fdiv_rn(1.0f, sum);
+  for (int j = 0; j < inner; ++j) out[j] = __fmul_rn(out[j], inv);
+}
+
+// One thread per row.
 __global__ void softmax_rows_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t rows,
                                     int inner) {
-  GRID_LOOP(r, rows) {
-    const float* row = x + r * inner;
-    float* out = y + r * inner;
-    int i = 0;
-    float mx;
-    if (inner >= 8) {
-      float vmax[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) vmax[j] = row[0];
-      for (; i + 8 <= inner; i += 8)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float v = row[i + j];
-          if (v > vmax[j]) vmax[j] = v;
-        }
-      mx = vmax[0];
-#pragma unroll
-      for (int j = 1; j < 8; ++j)
-        if (vmax[j] > mx) mx = vmax[j];
-    } else {
-      i = 1;
-      mx = row[0];
-    }
-    for (; i < inner; ++i)
-      if (row[i] > mx) mx = row[i];
-    float sum = 0.f;
-    int i2 = 0;
-    if (inner >= 8) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (; i2 + 8 <= inner; i2 += 8)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float e = exp1(__fsub_rn(row[i2 + j], mx));
-          out[i2 + j] = e;
-          acc[j] = __fadd_rn(acc[j], e);
-        }
-      const float t0 = __fadd_rn(acc[0], acc[4]), t1 = __fadd_rn(acc[1], acc[5]);
-      const float t2 = __fadd_rn(acc[2], acc[6]), t3 = __fadd_rn(acc[3], acc[7]);
-      sum = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
-    }
-    for (; i2 < inner; ++i2) {
-      const float e = exp1(__fsub_rn(row[i2], mx));
-      out[i2] = e;
-      sum = __fadd_rn(sum, e);
-    }
-    const float inv = __fdiv_rn(1.0f, sum);
-    for (int j = 0; j < inner; ++j) out[j] = __fmul_rn(out[j], inv);
-  }
+  GRID_LOOP(r, rows) softmax_row(x + r * inner, y + r * inner, inner);
 }
 
 cudaError_t launch_softmax_rows(const float* x, float* y, int64_t rows, int inner, cudaStream_t st) {
@@ -1162,6 +1164,125 @@ cudaError_t launch_softmax_argmax(const float* x, float* pairs, int64_t rows, in
                                   cudaStream_t st) {
   const int64_t blocks = (rows + 7) / 8;
   softmax_argmax_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, pairs, rows, cols);
+  return cudaGetLastError();
+}
+
+}  // namespace qpc
+
+namespace qpc {
+
+// softmax_row on a shared-memory row, by one warp: lanes 0-7 keep the
+// reference's eight lane accumulators (element i goes to lane i % 8, in
+// ascending order), the max and the hsum8 tree are combined from them in the
+// reference's order, the scalar tail follows sequentially, and all lanes
+// scale.  Bit-identical to softmax_row.
+__device__ __forceinline__ void softmax_row_warp(float* row, int inner, int lane) {
+  if (inner < 8) {
+    if (lane == 0) softmax_row(row, row, inner);
+    __syncwarp();
+    return;
+  }
+  const int n8 = inner & ~7;
+  const int j = lane & 7;
+  float vmax = row[0];
+  if (lane < 8)
+    for (int i = 0; i < n8; i += 8) {
+      const float v = row[i + j];
+      if (v > vmax) vmax = v;
+    }
+  float mx = __shfl_sync(0xffffffffu, vmax, 0);
+#pragma unroll
+  for (int k = 1; k < 8; ++k) {
+    const float vk = __shfl_sync(0xffffffffu, vmax, k);
+    if (vk > mx) mx = vk;
+  }
+  for (int i = n8; i < inner; ++i)
+    if (row[i] > mx) mx = row[i];
+  float acc = 0.f;
+  if (lane < 8)
+    for (int i = 0; i < n8; i += 8) {
+      const float e = exp1(__fsub_rn(row[i + j], mx));
+      row[i + j] = e;
+      acc = __fadd_rn(acc, e);
+    }
+  float a[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] = __shfl_sync(0xffffffffu, acc, k);
+  const float t0 = __fadd_rn(a[0], a[4]), t1 = __fadd_rn(a[1], a[5]);
+  const float t2 = __fadd_rn(a[2], a[6]), t3 = __fadd_rn(a[3], a[7]);
+  float sum = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
+  __syncwarp();
+  for (int i = n8; i < inner; ++i) {
+    const float e = exp1(__fsub_rn(row[i], mx));
+    sum = __fadd_rn(sum, e);
+    __syncwarp();
+    if (lane == 0) row[i] = e;
+  }
+  const float inv = __fdiv_rn(1.0f, sum);
+  __syncwarp();
+  for (int i = lane; i < inner; i += 32) row[i] = __fmul_rn(row[i], inv);
+  __syncwarp();
+}
+
+// Fused multi-head attention of the SVTR rec block, one CTA per (line,
+// head), bit-identical to the reference's separate ops: q' = q * scale
+// (Mul), s[t][u] = fma chain over d ascending of q'[t][d] k[u][d] from 0
+// (the dynamic MatMul's per-row outer product, shape.rs:669-697), the row
+// softmax (activation.rs:321-403), o[t][d] = fma chain over u ascending of
+// p[t][u] v[u][d] from 0, written at column h*D + d of the line's [T, H*D]
+// rows (the Transpose + Reshape).  q, k, v of the head are staged in shared
+// memory; each warp takes query rows t = warp, warp + 8, ...: its lanes make
+// the scores, lanes 0-7 the softmax (softmax_row_warp, in the reference's
+// order), lanes < D the output.
+__global__ void __launch_bounds__(256) attention_kernel(const float* __restrict__ qkv, float* __restrict__ out,
+                                                        int T, int H, int D, float scale) {
+  extern __shared__ float sm[];
+  const int b = blockIdx.x / H, h = blockIdx.x % H;
+  const int C = H * D, C3 = 3 * C;
+  float* qs = sm;            // [T][D], scaled
+  float* ks = qs + T * D;    // [T][D]
+  float* vs = ks + T * D;    // [T][D]
+  float* pr = vs + T * D;    // [8][T] score / probability rows, one per warp
+  const float* base = qkv + (int64_t)b * T * C3 + h * D;
+  for (int i = threadIdx.x; i < T * D; i += blockDim.x) {
+    const int t = i / D, d = i - t * D;
+    const float* r = base + (int64_t)t * C3 + d;
+    qs[i] = __fmul_rn(__ldg(r), scale);
+    ks[i] = __ldg(r + C);
+    vs[i] = __ldg(r + 2 * C);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* p = pr + warp * T;
+  for (int t = warp; t < T; t += 8) {
+    const float* q = qs + t * D;
+    for (int u = lane; u < T; u += 32) {
+      const float* k = ks + u * D;
+      float acc = 0.f;
+      for (int d = 0; d < D; ++d) acc = __fmaf_rn(q[d], k[d], acc);
+      p[u] = acc;
+    }
+    __syncwarp();
+    softmax_row_warp(p, T, lane);
+    if (lane < D) {
+      float acc = 0.f;
+      for (int u = 0; u < T; ++u) acc = __fmaf_rn(p[u], vs[u * D + lane], acc);
+      out[((int64_t)b * T + t) * C + h * D + lane] = acc;
+    }
+    __syncwarp();
+  }
+}
+
+cudaError_t launch_attention(const float* qkv, int64_t B, int T, int H, int D, float scale, float* out,
+                             cudaStream_t st) {
+  if (B < 0 || T <= 0 || H <= 0 || D <= 0 || D > 32) return cudaErrorInvalidValue;
+  if (B == 0) return cudaSuccess;
+  const int64_t blocks = B * H;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
+  const size_t smem = ((size_t)3 * T * D + 8 * (size_t)T) * sizeof(float);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  if (cudaError_t e = ensure_dyn_smem((const void*)attention_kernel, (int)smem); e != cudaSuccess) return e;
+  attention_kernel<<<(unsigned)blocks, 256, smem, st>>>(qkv, out, T, H, D, scale);
   return cudaGetLastError();
 }
 

@@ -54,6 +54,11 @@ cudaError_t launch_affine_nhwc(const float* x, const float* a, const float* b, f
 cudaError_t launch_copy_view(const float* a, float* y, const StridedDims& sd, cudaStream_t st);
 cudaError_t launch_layernorm(const float* x, const float* gamma, const float* beta, float* y,
                              int64_t rows, int c, float eps, cudaStream_t st);
+// Fused SVTR multi-head attention: qkv [B, T, 3*H*D] -> out [B, T, H*D]
+// (q scaled, softmax(q k^T) v per head), bit-identical to the reference's
+// Mul / MatMul / Softmax / MatMul ops.  D <= 32.
+cudaError_t launch_attention(const float* qkv, int64_t B, int T, int H, int D, float scale, float* out,
+                             cudaStream_t st);
 cudaError_t launch_softmax_argmax(const float* x, float* pairs, int64_t rows, int cols,
                                   cudaStream_t st);
 

@@ -219,7 +219,7 @@ static const std::set<std::string>& supported_ops() {
       "Transpose", "Reshape", "Squeeze", "Unsqueeze", "Flatten", "ReduceMean", "MatMul",
       "Identity", "Dropout", "Gather", "Shape", "Cast",
       // internal (produced by Session::fuse)
-      "QpcLinear", "QpcConvT", "QpcConvTPair", "QpcLayerNorm", "QpcCtcHead"};
+      "QpcLinear", "QpcConvT", "QpcConvTPair", "QpcLayerNorm", "QpcCtcHead", "QpcAttention"};
   return ops;
 }
 
@@ -752,6 +752,107 @@ void Session::fuse() {
     for (int k : absorbed) alive[k] = false;
     N[last] = ln;
     alive[last] = true;
+  }
+
+  // SVTR multi-head attention (the rec transformer block; the reference
+  // runs it as separate Mul / MatMul / Softmax / MatMul passes, its GPU plan
+  // as n_attn_mm + n_softmax, plan.rs:1882-1908, 2026-2055):
+  //   qkv [B,T,3*H*D] -Reshape[0,0,3,H,D]-> -Transpose[2,0,3,1,4]-> Slice j,
+  //   Squeeze -> q, k, v;  Mul(q, scale) -> MatMul(., Transpose(k)[0,1,3,2])
+  //   -> Softmax(-1) -> MatMul(., v) -> Transpose[0,2,1,3] -> Reshape[0,0,H*D]
+  // becomes QpcAttention(qkv, scale) -> [B,T,H*D] (launch_attention), when
+  // every intermediate has exactly the consumers of this pattern.
+  {
+    auto producer = [&](const std::string& t) -> int {
+      for (size_t j = 0; j < N.size(); ++j)
+        if (alive[j] && !N[j].out.empty() && N[j].out[0] == t) return (int)j;
+      return -1;
+    };
+    auto ints = [&](const Node& n, size_t k, const char* attr) -> std::vector<int64_t> {
+      if (n.has_in(k)) {
+        const HostTensor* h = weight(n.in[k]);
+        if (!h) return {};
+        if (h->dtype == QPC_I64) return h->i;
+        std::vector<int64_t> v;
+        for (float f : h->f) v.push_back((int64_t)f);
+        return v;
+      }
+      return n.getints(attr);
+    };
+    auto sole = [&](const std::string& t, int who) {
+      if (gouts.count(t)) return false;
+      auto cs = consumers(t);
+      return cs.size() == 1 && cs[0] == who;
+    };
+    // Squeeze(Slice(tq, [j], [j+1], [0]), [0]) -> (tq, j); -1 on mismatch
+    auto slice_of = [&](const std::string& t, int who, std::string* tq) -> int {
+      const int sq = producer(t);
+      if (sq < 0 || N[sq].op != "Squeeze" || !sole(t, who) || ints(N[sq], 1, "axes") != std::vector<int64_t>{0})
+        return -1;
+      const int sl = producer(N[sq].in[0]);
+      if (sl < 0 || N[sl].op != "Slice" || !sole(N[sl].out[0], sq)) return -1;
+      const auto st = ints(N[sl], 1, "starts"), en = ints(N[sl], 2, "ends"), ax = ints(N[sl], 3, "axes");
+      if (st.size() != 1 || en.size() != 1 || ax != std::vector<int64_t>{0} || en[0] != st[0] + 1) return -1;
+      if (N[sl].has_in(4) && ints(N[sl], 4, "steps") != std::vector<int64_t>{1}) return -1;
+      *tq = N[sl].in[0];
+      return (int)st[0];
+    };
+    for (size_t i = 0; i < N.size(); ++i) {
+      if (!alive[i] || N[i].op != "Softmax" || N[i].geti("axis", -1) != -1) continue;
+      const int m1 = producer(N[i].in[0]);
+      if (m1 < 0 || N[m1].op != "MatMul" || !sole(N[i].in[0], (int)i)) continue;
+      const auto cs = consumers(N[i].out[0]);
+      if (gouts.count(N[i].out[0]) || cs.size() != 1 || N[cs[0]].op != "MatMul" || N[cs[0]].in[0] != N[i].out[0])
+        continue;
+      const int m2 = cs[0];
+      const int mu = producer(N[m1].in[0]), tk = producer(N[m1].in[1]);
+      if (mu < 0 || tk < 0 || N[mu].op != "Mul" || N[tk].op != "Transpose") continue;
+      if (!sole(N[m1].in[0], m1) || !sole(N[m1].in[1], m1) || N[tk].getints("perm") != std::vector<int64_t>{0, 1, 3, 2})
+        continue;
+      const bool q_first = !is_const(N[mu].in[0]);
+      const std::string qn = q_first ? N[mu].in[0] : N[mu].in[1], sn = q_first ? N[mu].in[1] : N[mu].in[0];
+      double scale = 0;
+      if (!const_scalar(sn, &scale)) continue;
+      std::string tq0, tq1, tq2;
+      if (slice_of(qn, mu, &tq0) != 0 || slice_of(N[tk].in[0], tk, &tq1) != 1 ||
+          slice_of(N[m2].in[1], m2, &tq2) != 2 || tq0 != tq1 || tq0 != tq2)
+        continue;
+      if (gouts.count(tq0) || consumers(tq0).size() != 3) continue;
+      const int tr = producer(tq0);
+      if (tr < 0 || N[tr].op != "Transpose" || N[tr].getints("perm") != std::vector<int64_t>{2, 0, 3, 1, 4}) continue;
+      const int rs = producer(N[tr].in[0]);
+      if (rs < 0 || N[rs].op != "Reshape" || !sole(N[tr].in[0], tr)) continue;
+      const auto rshape = ints(N[rs], 1, "shape");
+      if (rshape.size() != 5 || rshape[0] != 0 || rshape[1] != 0 || rshape[2] != 3 || rshape[3] <= 0 || rshape[4] <= 0)
+        continue;
+      const int64_t H = rshape[3], D = rshape[4];
+      const auto c2 = consumers(N[m2].out[0]);
+      if (gouts.count(N[m2].out[0]) || c2.size() != 1 || N[c2[0]].op != "Transpose" ||
+          N[c2[0]].getints("perm") != std::vector<int64_t>{0, 2, 1, 3})
+        continue;
+      const int ot = c2[0];
+      const auto c3 = consumers(N[ot].out[0]);
+      if (gouts.count(N[ot].out[0]) || c3.size() != 1 || N[c3[0]].op != "Reshape") continue;
+      const int orr = c3[0];
+      if (ints(N[orr], 1, "shape") != std::vector<int64_t>{0, 0, H * D}) continue;
+      Node at;
+      at.op = "QpcAttention";
+      at.name = N[m1].name + "+attention";
+      at.in = {N[rs].in[0]};
+      at.out = N[orr].out;
+      at.seti("heads", H);
+      at.seti("head_dim", D);
+      at.setf("scale", (float)scale);
+      for (int k : {rs, tr, mu, tk, m1, (int)i, m2, ot})
+        alive[k] = false;
+      for (const std::string& t : {qn, N[tk].in[0], N[m2].in[1]}) {
+        const int sq = producer(t);
+        alive[producer(N[sq].in[0])] = false;
+        alive[sq] = false;
+      }
+      N[orr] = at;
+      alive[orr] = true;
+    }
   }
 
   // Rec CTC head: QpcLinear -> Softmax(last axis) -> graph output, with the
@@ -1329,6 +1430,7 @@ class Planner {
     if (op == "QpcLinear") return plan_linear(n, false);
     if (op == "QpcCtcHead") return plan_linear(n, true);
     if (op == "QpcLayerNorm") return plan_layernorm(n);
+    if (op == "QpcAttention") return plan_attention(n);
     if (op == "BatchNormalization") return plan_bn(n);
     if (op == "Relu" || op == "Sigmoid" || op == "HardSigmoid" || op == "FusedGelu" ||
         op == "Erf" || op == "Sqrt" || op == "Clip")
@@ -1988,6 +2090,26 @@ class Planner {
   }
 
   // ------------------------------------------------------------ LayerNorm
+  // QpcAttention: [B, T, 3*H*D] qkv (row-major) -> [B, T, H*D].
+  void plan_attention(const Node& n) {
+    const Val& x0 = get(n.in[0]);
+    const int64_t H = n.geti("heads", 0), D = n.geti("head_dim", 0);
+    if (x0.shape.size() != 3 || x0.shape[2] != 3 * H * D) throw GraphError{"attention input " + shape_str(x0.shape)};
+    const int64_t B = x0.shape[0], T = x0.shape[1];
+    Val x = as_rowmajor(x0, n.name);
+    Val y = new_val({B, T, H * D}, false);
+    const float* xp = out_ptr(x);
+    float* yp = out_ptr(y);
+    const float scale = n.getf("scale", 1.0f);
+    const double bytes = 4.0 * B * T * 4 * H * D;
+    const double flops = 4.0 * B * H * T * T * D;
+    step("attention", n.name, bytes, flops, [=](cudaStream_t st) {
+      return launch_attention(xp, B, (int)T, (int)H, (int)D, scale, yp, st);
+    });
+    unref(x);
+    define(n.out[0], y);
+  }
+
   void plan_layernorm(const Node& n) {
     const Val& x0 = get(n.in[0]);
     Val x = as_rowmajor(x0, n.name);

@@ -70,6 +70,10 @@ def test_rec_per_node(cuda_ctx, math):
     fused, errs = per_node(cuda_ctx, nets.build_rec, nets.rec_input(4), math, "rec")
     ops = [f[0] for f in fused]
     assert ops.count("QpcLayerNorm") == 5 and ops.count("QpcLinear") >= 9
+    # the fused attention (scale, QK^T, softmax, PV) is bit-exact on its own input
+    att = [o for op, _, o in fused if op == "QpcAttention"]
+    assert len(att) == 2
+    assert all(errs[o][1] == 0.0 for o in att), [errs[o] for o in att]
     worst = max(errs.items(), key=lambda kv: kv[1][1])
     assert worst[1][1] < TOL[math], worst
 
