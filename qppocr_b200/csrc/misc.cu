@@ -726,57 +726,88 @@ cudaError_t launch_pool2d_nhwc(const float* x, float* y, int n, int h, int w, in
   return cudaGetLastError();
 }
 
-// resize.rs:8-57 nearest: iy = min((int)((float)oy * H / oh), H - 1).  Writes
-// into a channel slice [c_off, c_off + C) of an output with ldc channels, so
-// the FPN concat needs no separate copy.
-// Threads take one (ox, channel quad) column of the output, its source
-// column found once; blockIdx.y takes RESIZE_ROWS consecutive output rows
-// (n * OH + oy), whose loads are all issued before their stores so several
-// are in flight per thread.  Source index (int)((float)o * in / out),
-// clamped (resize.rs:43-50), in 32-bit arithmetic.
+// resize.rs:8-57 nearest: iy = min((int)((float)oy * H / oh), H - 1), the
+// source index (int)((float)o * in / out) clamped (resize.rs:43-50), in
+// 32-bit arithmetic.  Up to RESIZE_MAX_SRC sources of one output size are
+// written in one launch, each into its channel slice [c_off, c_off + C) of an
+// output with ldc channels: the FPN's upsampled maps land in their concat
+// slices side by side, so each output pixel's slices are written together.
+// Threads take one (ox, channel quad) column of the output (quads enumerated
+// source after source), its source and source column found once; blockIdx.y
+// takes RESIZE_ROWS consecutive output rows (n * OH + oy), whose loads are all
+// issued before their stores so several are in flight per thread.
 constexpr int RESIZE_ROWS = 8;
-__global__ void __launch_bounds__(256) resize_nearest_nhwc_kernel(const float* __restrict__ x,
-                                                                  float* __restrict__ y, int N, int H, int W,
-                                                                  int C, int OH, int OW, int ldc, int c_off) {
-  const int C4 = C >> 2;
+__global__ void __launch_bounds__(256) resize_nearest_nhwc_kernel(const ResizeSrcs s, float* __restrict__ y,
+                                                                  int N, int OH, int OW, int ldc) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= OW * C4) return;
-  const int ox = i / C4, c4 = i - ox * C4;
+  if (i >= OW * s.quads) return;
+  const int ox = i / s.quads;
+  int q = i - ox * s.quads, k = 0;
+#pragma unroll
+  for (int j = 0; j < RESIZE_MAX_SRC - 1; ++j)
+    if (k + 1 < s.n && q >= s.c4[k]) {
+      q -= s.c4[k];
+      ++k;
+    }
+  const int H = s.h[k], W = s.w[k], C = 4 * s.c4[k];
+  const float* __restrict__ x = s.x[k];
   int ix = (int)__fdiv_rn(__fmul_rn((float)ox, (float)W), (float)OW);
   ix = ix < W - 1 ? ix : W - 1;
+  const int col = s.c_off[k] + 4 * q;
   const int rows = N * OH;
   for (int row0 = blockIdx.y * RESIZE_ROWS; row0 < rows; row0 += gridDim.y * RESIZE_ROWS) {
     float4 v[RESIZE_ROWS];
 #pragma unroll
-    for (int k = 0; k < RESIZE_ROWS; ++k) {
-      const int row = row0 + k;
+    for (int r = 0; r < RESIZE_ROWS; ++r) {
+      const int row = row0 + r;
       if (row < rows) {
         const int n = row / OH, oy = row - n * OH;
         int iy = (int)__fdiv_rn(__fmul_rn((float)oy, (float)H), (float)OH);
         iy = iy < H - 1 ? iy : H - 1;
-        v[k] = __ldg(reinterpret_cast<const float4*>(x + (((int64_t)n * H + iy) * W + ix) * C) + c4);
+        v[r] = __ldg(reinterpret_cast<const float4*>(x + (((int64_t)n * H + iy) * W + ix) * C) + q);
       }
     }
 #pragma unroll
-    for (int k = 0; k < RESIZE_ROWS; ++k) {
-      const int row = row0 + k;
-      if (row < rows)
-        *reinterpret_cast<float4*>(y + ((int64_t)row * OW + ox) * ldc + c_off + c4 * 4) = v[k];
+    for (int r = 0; r < RESIZE_ROWS; ++r) {
+      const int row = row0 + r;
+      if (row < rows) *reinterpret_cast<float4*>(y + ((int64_t)row * OW + ox) * ldc + col) = v[r];
     }
   }
+}
+
+cudaError_t launch_resize_nearest_multi_nhwc(const ResizeSrcs& s, float* y, int n, int oh, int ow, int ldc,
+                                             cudaStream_t st) {
+  if (s.n < 1 || s.n > RESIZE_MAX_SRC || (ldc & 3)) return cudaErrorInvalidValue;
+  int quads = 0;
+  for (int k = 0; k < s.n; ++k) {
+    if (s.c4[k] <= 0 || (s.c_off[k] & 3) || s.c_off[k] + 4 * s.c4[k] > ldc || s.h[k] <= 0 || s.w[k] <= 0)
+      return cudaErrorInvalidValue;
+    quads += s.c4[k];
+  }
+  if (quads != s.quads) return cudaErrorInvalidValue;
+  if ((int64_t)n * oh + RESIZE_ROWS >= (1LL << 31) || (int64_t)ow * quads >= (1LL << 31))
+    return cudaErrorInvalidValue;
+  if (n <= 0 || oh <= 0 || ow <= 0) return cudaSuccess;
+  const int per_row = ow * quads;
+  const int row_groups = (n * oh + RESIZE_ROWS - 1) / RESIZE_ROWS;
+  dim3 grid((per_row + 255) / 256, row_groups < 65535 ? row_groups : 65535);
+  resize_nearest_nhwc_kernel<<<grid, 256, 0, st>>>(s, y, n, oh, ow, ldc);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_resize_nearest_nhwc(const float* x, float* y, int n, int h, int w, int c, int oh,
                                        int ow, int ldc, int c_off, cudaStream_t st) {
   if ((c & 3) || (ldc & 3) || (c_off & 3)) return cudaErrorInvalidValue;
-  if ((int64_t)n * oh + RESIZE_ROWS >= (1LL << 31) || (int64_t)ow * (c / 4) >= (1LL << 31))
-    return cudaErrorInvalidValue;
   if (n <= 0 || oh <= 0 || ow <= 0 || c <= 0) return cudaSuccess;
-  const int per_row = ow * (c / 4);
-  const int row_groups = (n * oh + RESIZE_ROWS - 1) / RESIZE_ROWS;
-  dim3 grid((per_row + 255) / 256, row_groups < 65535 ? row_groups : 65535);
-  resize_nearest_nhwc_kernel<<<grid, 256, 0, st>>>(x, y, n, h, w, c, oh, ow, ldc, c_off);
-  return cudaGetLastError();
+  ResizeSrcs s{};
+  s.n = 1;
+  s.x[0] = x;
+  s.h[0] = h;
+  s.w[0] = w;
+  s.c4[0] = c / 4;
+  s.c_off[0] = c_off;
+  s.quads = c / 4;
+  return launch_resize_nearest_multi_nhwc(s, y, n, oh, ow, ldc, st);
 }
 
 // ------------------------------------------------------------ elementwise

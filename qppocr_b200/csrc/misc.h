@@ -30,6 +30,17 @@ cudaError_t launch_gap_nhwc(const float* x, float* y, int n, int hw, int c, cuda
 cudaError_t launch_pool2d_nhwc(const float* x, float* y, int n, int h, int w, int c, int oh, int ow,
                                int kh, int kw, int sh, int sw, int ph, int pw, int is_max,
                                cudaStream_t st);
+// Nearest-neighbour resize sources written by one launch (FPN concat slices).
+constexpr int RESIZE_MAX_SRC = 4;
+struct ResizeSrcs {
+  const float* x[RESIZE_MAX_SRC];  // NHWC [n, h, w, 4 * c4]
+  int h[RESIZE_MAX_SRC], w[RESIZE_MAX_SRC], c4[RESIZE_MAX_SRC];
+  int c_off[RESIZE_MAX_SRC];       // first output channel of each source's slice
+  int n;                           // sources used
+  int quads;                       // sum of c4
+};
+cudaError_t launch_resize_nearest_multi_nhwc(const ResizeSrcs& s, float* y, int n, int oh, int ow, int ldc,
+                                             cudaStream_t st);
 cudaError_t launch_resize_nearest_nhwc(const float* x, float* y, int n, int h, int w, int c, int oh,
                                        int ow, int ldc, int c_off, cudaStream_t st);
 cudaError_t launch_binary(const float* a, const float* b, float* y, const StridedDims& sd, int op,

@@ -1084,6 +1084,7 @@ class Planner {
       for (auto& o : n.out)
         if (!uses_.count(o) || uses_[o] == 0) drop(o);
     }
+    if (!pending_resize_.empty()) throw GraphError{"internal: resize into a concat that was never planned"};
     // Graph outputs: contiguous row-major, dedicated buffers.
     for (const std::string& go : S.graph_outputs()) {
       auto it = vals_.find(go);
@@ -1153,6 +1154,15 @@ class Planner {
   std::unordered_map<std::string, std::vector<int>> consumers_;
   std::unordered_map<std::string, int> producer_;
   std::unordered_map<std::string, Val> concat_bufs_;  // Concat output -> buffer allocated early
+  // Nearest resizes writing a slice of a Concat, held until the Concat is
+  // planned and then launched together (one output pixel's slices written
+  // by one kernel).  Each keeps its source alive (src) until then.
+  struct PendingResize {
+    Val src, dst;
+    int h, w, c;
+    std::string name;
+  };
+  std::unordered_map<std::string, std::vector<PendingResize>> pending_resize_;
 
   // Channel count of a 4-D tensor from its producer chain (before it exists).
   int64_t channels_of(const std::string& name, int depth = 0) {
@@ -1275,7 +1285,8 @@ class Planner {
   // If `o` (4-D, NHWC-produced) feeds only a channel Concat, return the view of
   // its slice in the Concat's buffer (allocated now, at the first part, so no
   // buffer that is live in between can alias it).
-  bool concat_slot(const std::string& o, const std::vector<int64_t>& oshape, Val* dst) {
+  bool concat_slot(const std::string& o, const std::vector<int64_t>& oshape, Val* dst,
+                   std::string* concat_out = nullptr) {
     auto cit = consumers_.find(o);
     if (cit == consumers_.end() || cit->second.size() != 1) return false;
     const Node& c = S.nodes()[cit->second[0]];
@@ -1304,7 +1315,40 @@ class Planner {
     const Val& f = it->second;
     if (f.shape[0] != oshape[0] || f.shape[2] != oshape[2] || f.shape[3] != oshape[3]) return false;
     *dst = view_of(f, oshape, f.strides, f.off + off);
+    if (concat_out) *concat_out = c.out[0];
     return true;
+  }
+
+  // Launch the resizes held for Concat `co`, up to RESIZE_MAX_SRC per kernel.
+  void flush_resizes(const std::string& co) {
+    auto it = pending_resize_.find(co);
+    if (it == pending_resize_.end()) return;
+    std::vector<PendingResize> parts = std::move(it->second);
+    pending_resize_.erase(it);
+    const Val& f = concat_bufs_.at(co);
+    float* yp = out_ptr(f);
+    const int64_t N = f.shape[0], oh = f.shape[2], ow = f.shape[3], ldc = f.strides[3];
+    for (size_t b = 0; b < parts.size(); b += RESIZE_MAX_SRC) {
+      ResizeSrcs rs{};
+      double bytes = 0;
+      std::string nm;
+      for (size_t k = b; k < parts.size() && k < b + RESIZE_MAX_SRC; ++k) {
+        const PendingResize& r = parts[k];
+        const int j = rs.n++;
+        rs.x[j] = out_ptr(r.src);
+        rs.h[j] = r.h;
+        rs.w[j] = r.w;
+        rs.c4[j] = r.c / 4;
+        rs.c_off[j] = (int)(r.dst.off - f.off);
+        rs.quads += r.c / 4;
+        bytes += 4.0 * ((double)N * r.c * r.h * r.w + (double)N * r.c * oh * ow);
+        nm += (nm.empty() ? "" : "+") + r.name;
+      }
+      step("resize", nm, bytes, 0, [=](cudaStream_t st) {
+        return launch_resize_nearest_multi_nhwc(rs, yp, (int)N, (int)oh, (int)ow, (int)ldc, st);
+      });
+    }
+    for (auto& r : parts) unref(r.src);
   }
 
   // ------------------------------------------------------------ bookkeeping
@@ -2286,13 +2330,18 @@ class Planner {
     const int64_t N = x0.shape[0], C = x0.shape[1], H = x0.shape[2], W = x0.shape[3];
     Val x = as_nhwc(x0, n.name);
     const std::vector<int64_t> oshape = {N, C, oh, ow};
+    if (C % 4) throw GraphError{"Resize: C % 4 != 0 unsupported"};
     Val y;
     int64_t ldc = C;
-    if (concat_slot(n.out[0], oshape, &y)) ldc = y.strides[3];
-    else y = new_val(oshape, true);
+    std::string co;
+    if (concat_slot(n.out[0], oshape, &y, &co)) {
+      pending_resize_[co].push_back({x, y, (int)H, (int)W, (int)C, n.name});
+      define(n.out[0], y);
+      return;
+    }
+    y = new_val(oshape, true);
     const float* xp = out_ptr(x);
     float* yp = out_ptr(y);
-    if (C % 4) throw GraphError{"Resize: C % 4 != 0 unsupported"};
     step("resize", n.name, 4.0 * (N * C * H * W + N * C * oh * ow), 0, [=](cudaStream_t s) {
       return launch_resize_nearest_nhwc(xp, yp, (int)N, (int)H, (int)W, (int)C, (int)oh, (int)ow,
                                         (int)ldc, 0, s);
@@ -2303,6 +2352,7 @@ class Planner {
 
   // ------------------------------------------------------------ Concat
   void plan_concat(const Node& n) {
+    flush_resizes(n.out[0]);
     std::vector<Val> parts;
     for (auto& nm : n.in) parts.push_back(operand(nm));
     const int64_t r = (int64_t)parts[0].shape.size();
