@@ -834,33 +834,70 @@ __global__ void __launch_bounds__(256, 1)
 }
 
 // Tap-folded row-band implicit GEMM for k x k stride-1 convs with M <= 32
-// output channels (TF32).  A 128 x N x 8 TF32 MMA costs the same for N = 32
-// as for N = 128, so the kw taps of one kernel row go into N: B rows are
-// (kx, m) pairs (NF = kw*M rounded up to 16) and one MMA over an unshifted
-// 128-pixel input row j produces, for every input pixel p, all kw tap
-// products P[p][kx][m] of kernel row ky = j - i for output row i.  Output
-// pixel t of the tile is sum_kx P[t + kx][kx][m]: the epilogue takes slice
-// kx = 0 from its own TMEM lane and slices kx >= 1 from lanes t + kx through
-// shared memory, so a tile row yields TWO = 128 - (kw - 1) outputs.  Per
-// output row: kh * cblocks * 4 MMAs instead of kh * kw * cblocks * 4.
-// Accumulator i of a tile sums ky and channels on the tensor core; the kx
-// slices are added in fp32 (slice 0, then 1, then 2) in the epilogue.
-// The filter stays in shared memory ([kh][cblocks] tiles of NF rows).
+// output channels (TF32).  A 128 x N x 8 TF32 MMA with a small N costs about
+// as much as a wide one (its issue, not its arithmetic, sets the pace), so
+// the kw taps of one kernel row go into N: B rows are (kx, m) pairs (NF =
+// kw*M rounded up to 16) and one MMA over an unshifted 128-pixel input row j
+// produces, for every input pixel p, all kw tap products P[p][kx][m] of
+// kernel row ky = j - i for output row i.  Output pixel t of the tile is
+// sum_kx P[t + kx][kx][m]: the epilogue takes slice kx = 0 from its own TMEM
+// lane and slices kx >= 1 from lanes t + kx through shared memory, so a tile
+// row yields TWO = 128 - (kw - 1) outputs.
+// The kernel rows go into N as well: the filter sits in shared memory as
+// [cblocks][kh][NF] with ky descending, and accumulator i (output row i of
+// the tile) occupies TMEM columns [i*NF, (i+1)*NF), so kernel rows hi..lo of
+// input row j - feeding output rows j-hi..j-lo - are one contiguous run of B
+// rows and one of D columns: a single MMA with N = (hi-lo+1)*NF per k-step.
+// Each accumulator element still receives its k-slices in the same order
+// (input row, channel block, k-step) as with one MMA per kernel row.
+// Accumulator i sums ky and channels on the tensor core; the kx slices are
+// added in fp32 (slice 0, then 1, then 2) in the epilogue.
 // Warps: w0 TMA, w1 MMA, w2-3 tf32 rounding of A, w4-7 epilogue.
-// MMAs of one staged input row for kernel rows LO..HI (3-row kernels), as one
-// straight-line run: a runtime loop around MMA issue, closed by a commit,
-// was measured to slow every MMA in it several-fold.
+//
+// MMAs of one staged input row j (channel block cb) for kernel rows LO..HI
+// of a 3-row kernel with 3*NF <= 256, straight-line: a runtime loop around
+// MMA issue, closed by a commit, was measured to slow every MMA in it
+// several-fold.  An output row's first contribution (ky = 0, cb = 0, k-step 0)
+// initialises its accumulator, so that k-step is split: row j alone with
+// accumulate off, rows j-HI..j-1 with it on.
 template <int LO, int HI>
-__device__ __forceinline__ void fold_issue(uint32_t d_base, int j, uint32_t nf, uint32_t a_addr, uint32_t w_addr,
-                                           int cblocks, int cb, uint32_t idesc) {
+__device__ __forceinline__ void fold_issue(uint32_t d_base, int j, uint32_t nf, uint32_t a_addr, uint32_t w_cb,
+                                           bool first_cb) {
+  const uint32_t d_lo = d_base + (uint32_t)(j - HI) * nf;      // accumulator of output row j - HI
+  const uint32_t b_lo = w_cb + (uint32_t)(2 - HI) * nf * 128u;  // B rows of kernel row HI (descending)
+  const uint32_t idesc = idesc_tf32(BM, (HI - LO + 1) * (int)nf);
 #pragma unroll
-  for (int ky = LO; ky <= HI; ++ky) {
-    const uint32_t d = d_base + (uint32_t)(j - ky) * nf;
-    const uint32_t b_addr = w_addr + (uint32_t)(ky * cblocks + cb) * nf * 128u;
-#pragma unroll
-    for (int ks = 0; ks < BK / 8; ++ks)
-      mma_tf32(d, sw128_kmajor_desc(a_addr + ks * 32), sw128_kmajor_desc(b_addr + ks * 32), idesc,
-               (ky | cb | ks) ? 1u : 0u);
+  for (int ks = 0; ks < BK / 8; ++ks) {
+    const uint64_t ad = sw128_kmajor_desc(a_addr + ks * 32);
+    if (LO == 0 && ks == 0 && first_cb) {
+      mma_tf32(d_base + (uint32_t)j * nf, ad, sw128_kmajor_desc(w_cb + 2u * nf * 128u), idesc_tf32(BM, (int)nf),
+               0u);
+      if (HI >= 1) mma_tf32(d_lo, ad, sw128_kmajor_desc(b_lo), idesc_tf32(BM, HI * (int)nf), 1u);
+    } else {
+      mma_tf32(d_lo, ad, sw128_kmajor_desc(b_lo + ks * 32), idesc, 1u);
+    }
+  }
+}
+
+// The same for any kernel height, in runs of at most 256 / NF kernel rows.
+__device__ __forceinline__ void fold_issue_rt(uint32_t d_base, int j, uint32_t nf, uint32_t a_addr, uint32_t w_cb,
+                                              int kh, int lo, int hi, bool first_cb) {
+  const int maxr = 256 / (int)nf;
+  for (int ks = 0; ks < BK / 8; ++ks) {
+    const uint64_t ad = sw128_kmajor_desc(a_addr + ks * 32);
+    int bottom = lo;
+    if (lo == 0 && ks == 0 && first_cb) {
+      mma_tf32(d_base + (uint32_t)j * nf, ad, sw128_kmajor_desc(w_cb + (uint32_t)(kh - 1) * nf * 128u),
+               idesc_tf32(BM, (int)nf), 0u);
+      bottom = 1;
+    }
+    for (int c_hi = hi; c_hi >= bottom;) {
+      const int c_lo = max(bottom, c_hi - maxr + 1);
+      mma_tf32(d_base + (uint32_t)(j - c_hi) * nf, ad,
+               sw128_kmajor_desc(w_cb + (uint32_t)(kh - 1 - c_hi) * nf * 128u + ks * 32),
+               idesc_tf32(BM, (c_hi - c_lo + 1) * (int)nf), 1u);
+      c_hi = c_lo - 1;
+    }
   }
 }
 
@@ -926,7 +963,7 @@ __global__ void __launch_bounds__(256, 1)
       mbar_arrive_expect_tx(&w_full, (uint32_t)w_bytes);
       for (int ky = 0; ky < kh; ++ky)
         for (int cb = 0; cb < cblocks; ++cb)
-          tma_load_4d(wsm + (ky * cblocks + cb) * nf * 128, &tmW, &w_full, cb * BK, 0, ky, 0);
+          tma_load_4d(wsm + (cb * kh + (kh - 1 - ky)) * nf * 128, &tmW, &w_full, cb * BK, 0, ky, 0);
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
@@ -964,29 +1001,21 @@ __global__ void __launch_bounds__(256, 1)
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
           const uint32_t a_addr = smem_u32(ring + s * A_TILE_BYTES);
-          if (kh == 3) {
-            // kernel rows ky with output row j - ky inside the tile: lo..hi
-            const int lo = max(0, j - (rows - 1)), hi = min(2, j);
+          const uint32_t w_cb = w_addr + (uint32_t)(cb * kh) * nf * 128u;  // [kh][NF] block of cb
+          // kernel rows ky with output row j - ky inside the tile: lo..hi
+          const int lo = max(0, j - (rows - 1)), hi = min(kh - 1, j);
+          if (kh == 3 && 3 * nf <= 256) {
             switch (lo * 4 + hi) {
-              case 0: fold_issue<0, 0>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
-              case 1: fold_issue<0, 1>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
-              case 2: fold_issue<0, 2>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
-              case 5: fold_issue<1, 1>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
-              case 6: fold_issue<1, 2>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
-              case 10: fold_issue<2, 2>(d_base, j, nf, a_addr, w_addr, cblocks, cb, idesc); break;
+              case 0: fold_issue<0, 0>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
+              case 1: fold_issue<0, 1>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
+              case 2: fold_issue<0, 2>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
+              case 5: fold_issue<1, 1>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
+              case 6: fold_issue<1, 2>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
+              case 10: fold_issue<2, 2>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
               default: break;  // lo > hi: no output row of this tile uses input row j
             }
-          } else
-          for (int ky = 0; ky < kh; ++ky) {
-            const int i = j - ky;  // output row of this tile fed by kernel row ky
-            if (i < 0 || i >= rows) continue;
-            const uint32_t d = d_base + i * nf;
-            const uint32_t b_addr = w_addr + (ky * cblocks + cb) * nf * 128;
-#pragma unroll
-            for (int ks = 0; ks < BK / 8; ++ks) {
-              const uint32_t acc = (ky | cb | ks) ? 1u : 0u;
-              mma_tf32(d, sw128_kmajor_desc(a_addr + ks * 32), sw128_kmajor_desc(b_addr + ks * 32), idesc, acc);
-            }
+          } else if (lo <= hi) {
+            fold_issue_rt(d_base, j, nf, a_addr, w_cb, kh, lo, hi, cb == 0);
           }
           mma_commit(&empty_bar[s]);
         }
