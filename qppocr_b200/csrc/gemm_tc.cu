@@ -860,48 +860,53 @@ __global__ void __launch_bounds__(256, 1)
 // several-fold.  An output row's first contribution (ky = 0, cb = 0, k-step 0)
 // initialises its accumulator, so that k-step is split: row j alone with
 // accumulate off, rows j-HI..j-1 with it on.
+// Descriptors are built once per kernel: a swizzled K-major descriptor of
+// address x + off is the one of x plus off / 16 (the address field holds
+// x / 16, and shared addresses stay below 256 KB), so the issue thread only
+// adds constants.  ids[n - 1]: instruction descriptor for N = n * NF.
 template <int LO, int HI>
-__device__ __forceinline__ void fold_issue(uint32_t d_base, int j, uint32_t nf, uint32_t a_addr, uint32_t w_cb,
-                                           bool first_cb) {
-  const uint32_t d_lo = d_base + (uint32_t)(j - HI) * nf;      // accumulator of output row j - HI
-  const uint32_t b_lo = w_cb + (uint32_t)(2 - HI) * nf * 128u;  // B rows of kernel row HI (descending)
-  const uint32_t idesc = idesc_tf32(BM, (HI - LO + 1) * (int)nf);
+__device__ __forceinline__ void fold_issue(uint32_t d_base, int j, uint32_t nf, uint64_t a_desc, uint64_t b_cb,
+                                           bool first_cb, const uint32_t (&ids)[3]) {
+  const uint32_t d_lo = d_base + (uint32_t)(j - HI) * nf;  // accumulator of output row j - HI
+  const uint64_t b_lo = b_cb + (uint64_t)((2 - HI) * nf * 8u);  // B rows of kernel row HI (descending)
 #pragma unroll
   for (int ks = 0; ks < BK / 8; ++ks) {
-    const uint64_t ad = sw128_kmajor_desc(a_addr + ks * 32);
+    const uint64_t ad = a_desc + (uint64_t)(ks * 2);
     if (LO == 0 && ks == 0 && first_cb) {
-      mma_tf32(d_base + (uint32_t)j * nf, ad, sw128_kmajor_desc(w_cb + 2u * nf * 128u), idesc_tf32(BM, (int)nf),
-               0u);
-      if (HI >= 1) mma_tf32(d_lo, ad, sw128_kmajor_desc(b_lo), idesc_tf32(BM, HI * (int)nf), 1u);
+      mma_tf32(d_base + (uint32_t)j * nf, ad, b_cb + (uint64_t)(2u * nf * 8u), ids[0], 0u);
+      if (HI >= 1) mma_tf32(d_lo, ad, b_lo, ids[HI >= 1 ? HI - 1 : 0], 1u);
     } else {
-      mma_tf32(d_lo, ad, sw128_kmajor_desc(b_lo + ks * 32), idesc, 1u);
+      mma_tf32(d_lo, ad, b_lo + (uint64_t)(ks * 2), ids[HI - LO], 1u);
     }
   }
 }
 
 // The same for any kernel height, in runs of at most 256 / NF kernel rows.
-__device__ __forceinline__ void fold_issue_rt(uint32_t d_base, int j, uint32_t nf, uint32_t a_addr, uint32_t w_cb,
+__device__ __forceinline__ void fold_issue_rt(uint32_t d_base, int j, uint32_t nf, uint64_t a_desc, uint64_t b_cb,
                                               int kh, int lo, int hi, bool first_cb) {
   const int maxr = 256 / (int)nf;
   for (int ks = 0; ks < BK / 8; ++ks) {
-    const uint64_t ad = sw128_kmajor_desc(a_addr + ks * 32);
+    const uint64_t ad = a_desc + (uint64_t)(ks * 2);
     int bottom = lo;
     if (lo == 0 && ks == 0 && first_cb) {
-      mma_tf32(d_base + (uint32_t)j * nf, ad, sw128_kmajor_desc(w_cb + (uint32_t)(kh - 1) * nf * 128u),
-               idesc_tf32(BM, (int)nf), 0u);
+      mma_tf32(d_base + (uint32_t)j * nf, ad, b_cb + (uint64_t)((kh - 1) * nf * 8u), idesc_tf32(BM, (int)nf), 0u);
       bottom = 1;
     }
     for (int c_hi = hi; c_hi >= bottom;) {
       const int c_lo = max(bottom, c_hi - maxr + 1);
-      mma_tf32(d_base + (uint32_t)(j - c_hi) * nf, ad,
-               sw128_kmajor_desc(w_cb + (uint32_t)(kh - 1 - c_hi) * nf * 128u + ks * 32),
+      mma_tf32(d_base + (uint32_t)(j - c_hi) * nf, ad, b_cb + (uint64_t)((kh - 1 - c_hi) * nf * 8u + ks * 2),
                idesc_tf32(BM, (c_hi - c_lo + 1) * (int)nf), 1u);
       c_hi = c_lo - 1;
     }
   }
 }
 
-template <int STAGES>
+// MT > 0: the conv has MT output channels and a kw = 3 kernel, known at
+// compile time, so the epilogue's exchange offsets are constants, its
+// shared-memory loads are issued as one batch and the bias sits in registers
+// (added after the slice sums, where the store would add it).  MT == 0: the
+// same arithmetic with runtime sizes.
+template <int STAGES, int MT>
 __global__ void __launch_bounds__(256, 1)
     conv_fold_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmOut, const GemmArgs args, int w_bytes, int nf,
@@ -984,7 +989,10 @@ __global__ void __launch_bounds__(256, 1)
       // ---------------- MMA issuer
       const uint32_t idesc = idesc_tf32(BM, nf);
       bool ok = mbar_wait(&w_full, 0, args.err);
-      const uint32_t w_addr = smem_u32(wsm);
+      const uint64_t w_desc = sw128_kmajor_desc(smem_u32(wsm));
+      const uint64_t ring_desc = sw128_kmajor_desc(smem_u32(ring));
+      const uint32_t ids[3] = {idesc_tf32(BM, nf), 2 * nf <= 256 ? idesc_tf32(BM, 2 * nf) : 0u,
+                               3 * nf <= 256 ? idesc_tf32(BM, 3 * nf) : 0u};
       uint32_t it = 0, acc_i = 0;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++acc_i) {
         const TileCoord tc = tile_coord(args, tile, 1, 32);
@@ -995,29 +1003,33 @@ __global__ void __launch_bounds__(256, 1)
           tc_fence_after();  // the epilogue's TMEM reads of this accumulator come first
         }
         const uint32_t d_base = tmem_d + buf * (uint32_t)(rb * nf);
+        int j = 0, cb = 0;  // input row of the tile, channel block
         for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
-          const int j = kb / cblocks, cb = kb % cblocks;
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
-          const uint32_t a_addr = smem_u32(ring + s * A_TILE_BYTES);
-          const uint32_t w_cb = w_addr + (uint32_t)(cb * kh) * nf * 128u;  // [kh][NF] block of cb
+          const uint64_t a_desc = ring_desc + (uint64_t)(s * (A_TILE_BYTES >> 4));
+          const uint64_t b_cb = w_desc + (uint64_t)((cb * kh) * nf * 8u);  // [kh][NF] block of cb
           // kernel rows ky with output row j - ky inside the tile: lo..hi
           const int lo = max(0, j - (rows - 1)), hi = min(kh - 1, j);
           if (kh == 3 && 3 * nf <= 256) {
             switch (lo * 4 + hi) {
-              case 0: fold_issue<0, 0>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
-              case 1: fold_issue<0, 1>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
-              case 2: fold_issue<0, 2>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
-              case 5: fold_issue<1, 1>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
-              case 6: fold_issue<1, 2>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
-              case 10: fold_issue<2, 2>(d_base, j, nf, a_addr, w_cb, cb == 0); break;
+              case 0: fold_issue<0, 0>(d_base, j, nf, a_desc, b_cb, cb == 0, ids); break;
+              case 1: fold_issue<0, 1>(d_base, j, nf, a_desc, b_cb, cb == 0, ids); break;
+              case 2: fold_issue<0, 2>(d_base, j, nf, a_desc, b_cb, cb == 0, ids); break;
+              case 5: fold_issue<1, 1>(d_base, j, nf, a_desc, b_cb, cb == 0, ids); break;
+              case 6: fold_issue<1, 2>(d_base, j, nf, a_desc, b_cb, cb == 0, ids); break;
+              case 10: fold_issue<2, 2>(d_base, j, nf, a_desc, b_cb, cb == 0, ids); break;
               default: break;  // lo > hi: no output row of this tile uses input row j
             }
           } else if (lo <= hi) {
-            fold_issue_rt(d_base, j, nf, a_addr, w_cb, kh, lo, hi, cb == 0);
+            fold_issue_rt(d_base, j, nf, a_desc, b_cb, kh, lo, hi, cb == 0);
           }
           mma_commit(&empty_bar[s]);
+          if (++cb == cblocks) {
+            cb = 0;
+            ++j;
+          }
         }
         if (!ok) break;
         mma_commit(&acc_full[buf]);
@@ -1052,6 +1064,10 @@ __global__ void __launch_bounds__(256, 1)
     const uint32_t lane_base = tmem_d + ((uint32_t)(q * 32) << 16);
     const int r1 = min(r + 1, BM - 1), r2 = min(r + 2, BM - 1);  // rows >= TWO are not stored
     uint32_t acc_i = 0, chunk_ctr = 0;
+    const bool has_bias = args.epi.bias != nullptr;
+    float bias_r[MT > 0 ? MT : 1];
+#pragma unroll
+    for (int m = 0; m < (MT > 0 ? MT : 1); ++m) bias_r[m] = (MT > 0 && has_bias) ? __ldg(args.epi.bias + m) : 0.f;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++acc_i) {
       const TileCoord tc = tile_coord(args, tile, 1, 32);
       const int rows = min(rb, args.oh - tc.oy0);
@@ -1074,20 +1090,45 @@ __global__ void __launch_bounds__(256, 1)
           if (c >= M && c < kw * M) exch[r * xst + (c - M)] = row[c];
         named_bar_sync(2, 128);
         auto fetch = [&](int cc, float (&v)[32]) {
+          if constexpr (MT > 0) {
+            constexpr int XST = 2 * MT + 1;
+            const float* e1 = exch + r1 * XST;
+            const float* e2 = exch + r2 * XST + MT;
+            float s1[MT], s2[MT];
 #pragma unroll
-          for (int m = 0; m < 32; ++m) {
-            float o = 0.f;
-            if (m < M) {
-              o = row[m];
-              if (kw > 1) o = __fadd_rn(o, exch[r1 * xst + m]);
-              if (kw > 2) o = __fadd_rn(o, exch[r2 * xst + M + m]);
+            for (int m = 0; m < MT; ++m) {
+              s1[m] = e1[m];
+              s2[m] = e2[m];
             }
-            v[m] = o;
+#pragma unroll
+            for (int m = 0; m < 32; ++m) {
+              float o = 0.f;
+              if (m < MT) {
+                o = __fadd_rn(__fadd_rn(row[m], s1[m]), s2[m]);
+                if (has_bias && args.tma_store) o = __fadd_rn(o, bias_r[m]);  // else epilogue_store adds it
+              }
+              v[m] = o;
+            }
+          } else {
+#pragma unroll
+            for (int m = 0; m < 32; ++m) {
+              float o = 0.f;
+              if (m < M) {
+                o = row[m];
+                if (kw > 1) o = __fadd_rn(o, exch[r1 * xst + m]);
+                if (kw > 2) o = __fadd_rn(o, exch[r2 * xst + M + m]);
+              }
+              v[m] = o;
+            }
           }
         };
         if (args.tma_store) {
-          store_tile<32, 1>(args, &tmOut, out_stage, s_rrow, 1, chunk_ctr, 0, 0, tc.img, tc.oy0 + i, tc.ox0,
-                            r, gt, fetch);
+          if constexpr (MT > 0)
+            store_tile<32, 1, true, false>(args, &tmOut, out_stage, s_rrow, 1, chunk_ctr, 0, 0, tc.img, tc.oy0 + i,
+                                           tc.ox0, r, gt, fetch);
+          else
+            store_tile<32, 1>(args, &tmOut, out_stage, s_rrow, 1, chunk_ctr, 0, 0, tc.img, tc.oy0 + i, tc.ox0,
+                              r, gt, fetch);
         } else {
           const RowMap m = row_map<1>(args, 0, tc.img, tc.oy0 + i, tc.ox0, r);
           float v[32];
@@ -1463,7 +1504,7 @@ cudaError_t launch_conv_tc(const float* x, const ConvGeom& g, const float* wk, c
       const uint32_t box[4] = {32, (uint32_t)two, 1, 1};
       args.tma_store = make_map(&mo, obase, 4, dims, strides, box) ? 1 : 0;
     }
-    auto kern = conv_fold_kernel<FOLD_STAGES>;
+    auto kern = (g.m == 24 && g.kw == 3) ? conv_fold_kernel<FOLD_STAGES, 24> : conv_fold_kernel<FOLD_STAGES, 0>;
     if (cudaError_t e = ensure_dyn_smem((const void*)kern, smem); e != cudaSuccess) return e;
     const int grid = args.m_tiles < sm_count() ? args.m_tiles : sm_count();
     kern<<<grid, 256, smem, st>>>(ma, mw, mo, args, w_bytes, nf, rb);

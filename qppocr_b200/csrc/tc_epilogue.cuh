@@ -115,7 +115,8 @@ __device__ __forceinline__ void load_residual(const GemmArgs& args, int64_t rrow
 }
 
 // RES = false: the caller never passes a residual (saves its registers).
-template <int BN, int A_MODE, bool RES = true, class Fetch>
+// BIAS = false: `fetch` has already added the bias.
+template <int BN, int A_MODE, bool RES = true, bool BIAS = true, class Fetch>
 __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorMap* tm_out,
                                            uint8_t* stage, int64_t* s_rrow, int bar_id,
                                            uint32_t& chunk_ctr, int m_blk, int n0, int img, int oy0,
@@ -136,7 +137,7 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
     }
     float v[32];
     fetch(cc, v);
-    if (e.bias) {
+    if (BIAS && e.bias) {
       // columns past N are clipped by the TMA store; keep their reads in bounds
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
