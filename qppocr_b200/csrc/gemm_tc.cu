@@ -930,6 +930,7 @@ __global__ void __launch_bounds__(256, 1)
   const int kw = args.kw, kh = args.taps / args.kw, cblocks = args.cblocks, M = args.N;
   const int nkb = (rb + kh - 1) * cblocks;
   const int xst = (kw - 1) * M + 1;                       // exchange row stride (odd)
+  const bool a_pre = args.epi.a_rounded != 0;
   uint8_t* wsm = smem;                                    // [kh][cblocks] x NF x 128 B
   uint8_t* ring = smem + w_bytes;                         // STAGES x 16 KB
   float* exch = reinterpret_cast<float*>(ring + STAGES * A_TILE_BYTES);  // 128 x xst
@@ -1007,7 +1008,8 @@ __global__ void __launch_bounds__(256, 1)
         for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
-          if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
+          // A rounded by its producer: straight from the TMA barrier
+          if (!mbar_wait(a_pre ? &full_bar[s] : &conv_bar[s], ph, args.err)) { ok = false; break; }
           const uint64_t a_desc = ring_desc + (uint64_t)(s * (A_TILE_BYTES >> 4));
           const uint64_t b_cb = w_desc + (uint64_t)((cb * kh) * nf * 8u);  // [kh][NF] block of cb
           // kernel rows ky with output row j - ky inside the tile: lo..hi
@@ -1036,10 +1038,11 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
   } else if (warp < 4) {
-    // ---------------- converters: round the input row to tf32 (nearest) in place
+    // ---------------- converters: round the input row to tf32 (nearest) in
+    // place; idle when the producer stored A rounded
     const int t = threadIdx.x - 64;
     uint32_t it = 0;
-    bool ok = true;
+    bool ok = !a_pre;
     for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % STAGES;

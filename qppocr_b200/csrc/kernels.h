@@ -69,8 +69,13 @@ struct GemmEpilogue {
   // partials[n_tile * M + row] (float4); nothing is written to `out`.
   float4* partials = nullptr;
   // A already rounded to tf32 by its producer (a depthwise conv with
-  // ActParams::round_tf32): TF32 rows-mode GEMMs skip the rounding pass.
+  // ActParams::round_tf32, or an epilogue / resize storing rounded values):
+  // TF32 rows-mode GEMMs and the tap-folded conv skip their rounding pass.
   int a_rounded = 0;
+  // Store the outputs rounded to tf32 (nearest), after bias, activation and
+  // residual: set when every consumer reads them only as a TF32 A operand,
+  // which would round them to the same values.
+  int round_out = 0;
   // ConvT pair epilogue (two 2x2 stride-2 ConvTranspose layers, the second
   // to one channel; launch_convt_pair): set by that launcher only.
   int pair_h = 0, pair_w = 0;  // input map of the first ConvT

@@ -767,6 +767,10 @@ __global__ void __launch_bounds__(256) resize_nearest_nhwc_kernel(const ResizeSr
         v[r] = __ldg(reinterpret_cast<const float4*>(x + (((int64_t)n * H + iy) * W + ix) * C) + q);
       }
     }
+    if (s.round_tf32)
+#pragma unroll
+      for (int r = 0; r < RESIZE_ROWS; ++r)
+        v[r] = make_float4(tf32_rna(v[r].x), tf32_rna(v[r].y), tf32_rna(v[r].z), tf32_rna(v[r].w));
 #pragma unroll
     for (int r = 0; r < RESIZE_ROWS; ++r) {
       const int row = row0 + r;

@@ -38,6 +38,7 @@ struct ResizeSrcs {
   int c_off[RESIZE_MAX_SRC];       // first output channel of each source's slice
   int n;                           // sources used
   int quads;                       // sum of c4
+  int round_tf32;                  // store tf32-rounded (nearest) values
 };
 cudaError_t launch_resize_nearest_multi_nhwc(const ResizeSrcs& s, float* y, int n, int oh, int ow, int ldc,
                                              cudaStream_t st);

@@ -1010,6 +1010,23 @@ bool takes_pointwise_gemm(const Node& n, const HostTensor& w, int64_t H, int64_t
          pew == 0 && (cg % 4) == 0;
 }
 
+// The tap-folded tensor-core path of plan_conv (TF32 only): a k x k,
+// stride-1, ungrouped conv over a C % 4 == 0 input of N x C x H x W that
+// conv_fold_ok accepts (the geometry launch_conv_tc checks).
+bool takes_fold_conv(const Node& n, const HostTensor& w, int64_t N, int64_t C, int64_t H, int64_t W) {
+  if (w.shape.size() != 4 || takes_pointwise_gemm(n, w, H, W)) return false;
+  const int64_t M = w.shape[0], cg = w.shape[1], kh = w.shape[2], kw = w.shape[3];
+  auto st = n.getints("strides");
+  const int64_t sh = st.size() == 2 ? st[0] : 1, sw = st.size() == 2 ? st[1] : 1;
+  if (n.geti("group", 1) != 1 || cg != C || sh != 1 || sw != 1 || (C % 4) != 0 || kh * kw <= 1) return false;
+  int64_t ph, pw, peh, pew;
+  resolve_pads(n, H, W, kh, kw, sh, sw, &ph, &pw, &peh, &pew);
+  const int64_t oh = H + ph + peh - kh + 1, ow = W + pw + pew - kw + 1;
+  if (oh <= 0 || ow <= 0) return false;
+  ConvGeom g{(int)N, (int)H, (int)W, (int)C, (int)oh, (int)ow, (int)M, (int)kh, (int)kw, 1, 1, (int)ph, (int)pw};
+  return conv_fold_ok(g);
+}
+
 }  // namespace
 
 class Planner {
@@ -1160,6 +1177,7 @@ class Planner {
   struct PendingResize {
     Val src, dst;
     int h, w, c;
+    bool round;  // store tf32-rounded
     std::string name;
   };
   std::unordered_map<std::string, std::vector<PendingResize>> pending_resize_;
@@ -1259,25 +1277,41 @@ class Planner {
     define(n.out[0], y);
   }
 
-  // Whether every consumer of `o` (an NCHW-shaped value of spatial size H x W)
-  // is a TF32 conv that takes the pointwise GEMM path (the same predicate
-  // plan_conv uses) and reads `o` as its A operand (input 0 only), so `o` may
-  // be stored tf32-rounded: the GEMM would round it to the same values.
-  // plan_conv checks, when it plans each such consumer, that it took that path.
+  // Whether every consumer of `o` (an N x C x H x W value) reads it only as
+  // the A operand (input 0) of a TF32 conv on a tensor-core path that rounds
+  // A to tf32 (nearest) - the pointwise GEMM or the tap-folded k x k conv,
+  // the predicates plan_conv routes by - possibly through a channel Concat
+  // whose output does the same.  Then `o` may be stored tf32-rounded: each
+  // consumer would round it to the same values.  plan_conv checks, when it
+  // plans each such consumer, that it took one of those paths.
   std::set<std::string> tf32_rounded_;
-  bool feeds_only_tf32_pointwise(const std::string& o, int64_t H, int64_t W) {
-    if (S.math() != QPC_MATH_TF32) return false;
+  bool feeds_only_tf32_a(const std::string& o, int64_t N, int64_t C, int64_t H, int64_t W, int depth = 0) {
+    if (S.math() != QPC_MATH_TF32 || depth > 4) return false;
     for (auto& go : S.graph_outputs())
       if (go == o) return false;
     auto cit = consumers_.find(o);
     if (cit == consumers_.end() || cit->second.empty()) return false;
     for (int ci : cit->second) {
       const Node& c = S.nodes()[ci];
+      if (c.op == "Concat") {
+        int64_t axis = c.geti("axis", 0);
+        if (axis < 0) axis += 4;
+        if (axis != 1 || cit->second.size() != 1) return false;
+        int64_t total = 0, seen = 0;
+        for (auto& x : c.in) {
+          const int64_t ch = channels_of(x);
+          if (ch < 0) return false;
+          total += ch;
+          seen += x == o;
+        }
+        if (seen != 1 || !feeds_only_tf32_a(c.out[0], N, total, H, W, depth + 1)) return false;
+        continue;
+      }
       if (c.op != "Conv" || c.in.size() < 2 || c.in[0] != o) return false;
       for (size_t k = 1; k < c.in.size(); ++k)
         if (c.in[k] == o) return false;
       const HostTensor* w = S.weight(c.in[1]);
-      if (!w || !takes_pointwise_gemm(c, *w, H, W)) return false;
+      if (!w || !(takes_pointwise_gemm(c, *w, H, W) || takes_fold_conv(c, *w, N, C, H, W))) return false;
     }
     return true;
   }
@@ -1330,10 +1364,12 @@ class Planner {
     const int64_t N = f.shape[0], oh = f.shape[2], ow = f.shape[3], ldc = f.strides[3];
     for (size_t b = 0; b < parts.size(); b += RESIZE_MAX_SRC) {
       ResizeSrcs rs{};
+      rs.round_tf32 = parts[b].round ? 1 : 0;
       double bytes = 0;
       std::string nm;
       for (size_t k = b; k < parts.size() && k < b + RESIZE_MAX_SRC; ++k) {
         const PendingResize& r = parts[k];
+        if (r.round != parts[b].round) throw GraphError{"internal: concat resizes disagree on rounding"};
         const int j = rs.n++;
         rs.x[j] = out_ptr(r.src);
         rs.h[j] = r.h;
@@ -1570,10 +1606,11 @@ class Planner {
                (int)sh, (int)sw, (int)ph, (int)pw};
     const bool dw = group > 1 && cg == 1 && M == C;
     const bool pw1 = takes_pointwise_gemm(n, *w, H, W);
-    if (tf32_rounded_.count(n.in[0]) && !pw1)
-      throw GraphError{"internal: " + n.name + " reads a tf32-rounded value but is not a pointwise GEMM"};
     const bool kxk_tc = group == 1 && sh == 1 && sw == 1 && (C % 4) == 0 && !pw1 && kh * kw > 1;
     const int math = S.math();
+    const bool fold = kxk_tc && math == QPC_MATH_TF32 && takes_fold_conv(n, *w, N, C, H, W);
+    if (tf32_rounded_.count(n.in[0]) && !pw1 && !fold)
+      throw GraphError{"internal: " + n.name + " reads a tf32-rounded value but is not a TF32 tensor-core conv"};
     const double flops = 2.0 * N * oh * ow * M * cg * kh * kw;
     const double out_bytes = 4.0 * N * oh * ow * M;
     if (dw && !n.has_in(3) && dw_fusable(n, g)) {
@@ -1641,7 +1678,7 @@ class Planner {
       const float* wt = S.dweight(n.in[1], "dw");
       const double bytes = 4.0 * N * H * W * C + out_bytes + (has_res ? out_bytes : 0);
       ActParams dact = act;
-      if (feeds_only_tf32_pointwise(n.out[0], oh, ow)) {
+      if (feeds_only_tf32_a(n.out[0], N, M, oh, ow)) {
         dact.round_tf32 = 1;
         tf32_rounded_.insert(n.out[0]);
       }
@@ -1674,6 +1711,10 @@ class Planner {
         e.a_gate_rows = (int)(H * W);
       } else if (tf32_rounded_.count(n.in[0])) {
         e.a_rounded = 1;
+      }
+      if (feeds_only_tf32_a(n.out[0], N, M, oh, ow)) {
+        e.round_out = 1;
+        tf32_rounded_.insert(n.out[0]);
       }
       const int64_t rows = N * H * W;
       const double bytes = 4.0 * rows * C + out_bytes + 4.0 * M * C + res_bytes;
@@ -1721,6 +1762,11 @@ class Planner {
       e.ldo = (int)ldo;
       e.ldr = (int)M;
       e.act = act;
+      e.a_rounded = (fold && tf32_rounded_.count(n.in[0])) ? 1 : 0;
+      if (feeds_only_tf32_a(n.out[0], N, M, oh, ow)) {
+        e.round_out = 1;
+        tf32_rounded_.insert(n.out[0]);
+      }
       if (res_h > 0) {
         e.rh = res_h;
         e.rw = res_w;
@@ -2335,7 +2381,9 @@ class Planner {
     int64_t ldc = C;
     std::string co;
     if (concat_slot(n.out[0], oshape, &y, &co)) {
-      pending_resize_[co].push_back({x, y, (int)H, (int)W, (int)C, n.name});
+      const bool rnd = feeds_only_tf32_a(n.out[0], N, C, oh, ow);
+      if (rnd) tf32_rounded_.insert(n.out[0]);
+      pending_resize_[co].push_back({x, y, (int)H, (int)W, (int)C, rnd, n.name});
       define(n.out[0], y);
       return;
     }
@@ -2400,6 +2448,9 @@ class Planner {
       }
       off += p.shape[axis];
     }
+    bool all_rounded = true;
+    for (auto& nm : n.in) all_rounded = all_rounded && tf32_rounded_.count(nm) > 0;
+    if (all_rounded) tf32_rounded_.insert(n.out[0]);
     define(n.out[0], y);
   }
 

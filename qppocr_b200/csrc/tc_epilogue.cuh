@@ -42,6 +42,9 @@ __device__ __forceinline__ void epilogue_store(const GemmArgs& args, const float
 #pragma unroll
     for (int j = 0; j < 16; ++j)
       if (col0 + j < args.N) o[j] = __fadd_rn(o[j], __ldg(e.residual + rrow * e.ldr + col0 + j));
+  if (e.round_out)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j] = tf32_rna(o[j]);
   float* dst = e.out + orow * e.ldo + e.col_off + col0;
   const bool vec_ok = ((e.ldo | e.col_off) & 3) == 0 && col0 + 16 <= args.N;
   if (vec_ok) {
@@ -165,6 +168,9 @@ __device__ __forceinline__ void store_tile(const GemmArgs& args, const CUtensorM
     if (t == 0) bulk_wait_group_read<1>();
     named_bar_sync(bar_id, 128);  // staging buffer free
     float* myrow = sb + r * 32;
+    if (e.round_out)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = tf32_rna(v[j]);
 #pragma unroll
     for (int c4 = 0; c4 < 8; ++c4)
       *reinterpret_cast<float4*>(myrow + ((c4 ^ (r & 7)) << 2)) =
