@@ -155,8 +155,8 @@ def barrier(world):
 # or per line (rec), from ncu dram__bytes_read.sum + dram__bytes_write.sum
 # captures.  The roofline's `traffic` is this times the batch, for the
 # dominant family.
-DET_TRAFFIC_PER_IMAGE = {"dwpw": 13524404, "gemm_tc": 8810649, "conv_tc": 12279394, "dwconv": 13399754,
-                         "conv_direct": 23703775, "resize": 4868821, "convt_pair": 7491018, "gap": 1382703}
+DET_TRAFFIC_PER_IMAGE = {"dwpw": 13515751, "gemm_tc": 8826127, "conv_tc": 12302626, "dwconv": 13393150,
+                         "conv_direct": 23704267, "resize": 18179488, "convt_pair": 7496064, "gap": 1382699}
 REC_TRAFFIC_PER_LINE = {"gemm_tc": 90276, "dwpw": 321667, "dwconv": 236061, "pool2d": 231634, "layernorm": 19268,
                         "head_gemm": 54868, "head_combine": 94135}
 TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum summed over the family's launches of one pass on a "
