@@ -4,7 +4,8 @@
 //  * box_score_fast (crates/qppocr-core/src/pipeline/geometry.rs:221-269):
 //    mean DB probability inside a quadrilateral by scan-line even-odd fill.
 //    The sum is f64 in the reference's order (rows ascending, spans left to
-//    right), so one thread scores one box sequentially.
+//    right), so one warp scores one box: the lanes load each 32-pixel piece
+//    of a span (coalesced) into shared memory and lane 0 adds them in order.
 //  * crop_text_box (crates/qppocr-core/src/pipeline/crop.rs:8-127): the
 //    perspective crop of a box.  Thread 0 of the box's block solves the 8 x 9
 //    homography system in f64 exactly as the reference does (Gauss-Jordan,
@@ -31,7 +32,10 @@ namespace {
 __device__ __forceinline__ int to_i32(double v) { return __double2int_rz(v); }
 __device__ __forceinline__ int to_i32f(float v) { return __float2int_rz(v); }
 
-__device__ float box_score_one(const float* __restrict__ pred, int hh, int ww, const float* __restrict__ bp) {
+// One warp per box; every lane follows the scan (uniform control flow) and
+// lane 0 holds the sum.
+__device__ float box_score_warp(const float* __restrict__ pred, int hh, int ww, const float* __restrict__ bp,
+                                int lane, float* __restrict__ stage) {
   float fxmin = 3.40282347e38f, fxmax = -3.40282347e38f, fymin = 3.40282347e38f, fymax = -3.40282347e38f;
   float px[4], py[4];
 #pragma unroll
@@ -75,9 +79,16 @@ __device__ float box_score_one(const float* __restrict__ pred, int hh, int ww, c
       const int xa = max(to_i32f(ceilf(__fsub_rn(xs[i], 0.5f))), xmin);
       const int xb = min(to_i32f(floorf(__fsub_rn(xs[i + 1], 0.5f))), xmax);
       const float* row = pred + (int64_t)y * ww;
-      for (int x = xa; x <= xb; ++x) {
-        sum = __dadd_rn(sum, (double)__ldg(row + x));
-        ++count;
+      for (int x0 = xa; x0 <= xb; x0 += 32) {
+        const int cnt = min(32, xb - x0 + 1);
+        stage[lane] = lane < cnt ? __ldg(row + x0 + lane) : 0.0f;
+        __syncwarp();
+        if (lane == 0) {
+#pragma unroll 8
+          for (int j = 0; j < cnt; ++j) sum = __dadd_rn(sum, (double)stage[j]);
+        }
+        __syncwarp();  // lane 0 has read the piece before it is overwritten
+        count += cnt;
       }
     }
   }
@@ -85,20 +96,34 @@ __device__ float box_score_one(const float* __restrict__ pred, int hh, int ww, c
   return __double2float_rn(__ddiv_rn(sum, (double)count));
 }
 
-__global__ void box_score_kernel(const float* __restrict__ pred, int hh, int ww, const float* __restrict__ boxes,
-                                 const int* __restrict__ img, int n, float* __restrict__ out) {
-  const int k = blockIdx.x * blockDim.x + threadIdx.x;
-  if (k >= n) return;
-  out[k] = box_score_one(pred + (int64_t)img[k] * hh * ww, hh, ww, boxes + 8 * (int64_t)k);
+__global__ void __launch_bounds__(256) box_score_kernel(const float* __restrict__ pred, int hh, int ww,
+                                                        const float* __restrict__ boxes,
+                                                        const int* __restrict__ img, int n,
+                                                        float* __restrict__ out) {
+  __shared__ float stage[8][32];  // one 32-value piece per warp
+  const int k = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (k >= n) return;  // whole warps
+  const float r = box_score_warp(pred + (int64_t)img[k] * hh * ww, hh, ww, boxes + 8 * (int64_t)k, lane,
+                                 stage[threadIdx.x >> 5]);
+  if (lane == 0) out[k] = r;
 }
 
-// One block per box: thread 0 solves the homography into shared memory.
+// Pixels of one crop per block: 4 per thread, so the homography (thread 0's
+// serial f64 solve) is repeated once per 1024 pixels.
+constexpr int CROP_PIX_PER_BLOCK = 1024;
+
+// Blocks (x, k): crop k, pixels [x * 1024, (x + 1) * 1024); thread 0 of each
+// active block solves the homography into shared memory.
 __global__ void __launch_bounds__(256) crop_boxes_kernel(const uint8_t* __restrict__ imgs, int h, int w,
                                                          const float* __restrict__ pts, const int* __restrict__ img,
                                                          const int* __restrict__ cws, const int* __restrict__ chs,
                                                          const int64_t* __restrict__ off, uint8_t* __restrict__ out) {
   const int k = blockIdx.y;
   const int cw = cws[k], ch = chs[k];
+  // blocks past this crop's pixels (the grid is sized for the largest crop)
+  // leave before solving
+  if ((int64_t)blockIdx.x * CROP_PIX_PER_BLOCK >= (int64_t)cw * ch) return;
   __shared__ double hm[9];
   if (threadIdx.x == 0) {
     const float* p = pts + 8 * (int64_t)k;
@@ -153,7 +178,8 @@ __global__ void __launch_bounds__(256) crop_boxes_kernel(const uint8_t* __restri
   const bool rot = __fdiv_rn((float)ch, (float)cw) >= 1.5f;
   const uint8_t* src = imgs + (int64_t)img[k] * h * w * 3;
   uint8_t* dst = out + off[k];
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cw * ch; i += gridDim.x * blockDim.x) {
+  const int i_end = min(cw * ch, (int)((blockIdx.x + 1) * CROP_PIX_PER_BLOCK));
+  for (int i = blockIdx.x * CROP_PIX_PER_BLOCK + threadIdx.x; i < i_end; i += blockDim.x) {
     const int y = i / cw, x = i - y * cw;
     const double xf = (double)x, yf = (double)y;
     const double den = __dadd_rn(__dadd_rn(__dmul_rn(hm[6], xf), __dmul_rn(hm[7], yf)), hm[8]);
@@ -261,7 +287,7 @@ cudaError_t launch_box_score(const float* pred, int h, int w, const float* boxes
                              float* out, cudaStream_t st) {
   if (n < 0 || h <= 0 || w <= 0) return cudaErrorInvalidValue;
   if (n == 0) return cudaSuccess;
-  box_score_kernel<<<(n + 63) / 64, 64, 0, st>>>(pred, h, w, boxes, img, n, out);
+  box_score_kernel<<<(unsigned)((n + 7) / 8), 256, 0, st>>>(pred, h, w, boxes, img, n, out);  // a warp per box
   return cudaGetLastError();
 }
 
@@ -270,8 +296,9 @@ cudaError_t launch_crop_boxes(const uint8_t* imgs, int h, int w, const float* pt
                               cudaStream_t st) {
   if (n < 0 || h <= 0 || w <= 0 || n > 65535 || max_pixels <= 0) return cudaErrorInvalidValue;
   if (n == 0) return cudaSuccess;
-  const int bx = (max_pixels + 255) / 256;
-  dim3 grid(bx < 64 ? bx : 64, n);
+  const int bx = (max_pixels + CROP_PIX_PER_BLOCK - 1) / CROP_PIX_PER_BLOCK;
+  if (bx > 65535) return cudaErrorInvalidValue;
+  dim3 grid(bx, n);
   crop_boxes_kernel<<<grid, 256, 0, st>>>(imgs, h, w, pts, img, cw, ch, off, out);
   return cudaGetLastError();
 }

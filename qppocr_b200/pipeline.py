@@ -23,7 +23,7 @@ step on the device:
      session's argmax exit, decoded on the host (rec.rs:82-120).
 """
 import time
-from typing import Dict, Optional
+from typing import Dict, Iterable, Iterator, Optional
 
 import numpy as np
 
@@ -87,19 +87,68 @@ class OcrPipeline:
         boxes: [n, k, 4, 2] f32 corners in image coordinates.  Returns the
         mask, box scores, cls probabilities and flips, and per line the
         decoded (indices, confidence); keep=True adds the device
-        intermediates (crops, packed cls and rec batches) for checking."""
+        intermediates (crops, packed cls and rec batches) for checking.
+        `timings` holds the wall-clock ms of each stage, as the reference
+        bench reports det / crop / cls / rec (crates/qppocr-cli/src/main.rs:
+        860-880): det (to the mask on the host), boxes + crops, cls, rec
+        (packing, runs and CTC decode)."""
+        import torch
+
+        t0 = time.perf_counter()
+        torch.cuda.current_stream(torch.device("cuda", self.device)).synchronize()  # images in place
+        # 1. det with the mask exit; the probability map stays on the device
+        mask, pred = self.det.run({"x": images})
+        return self._after_det(images, boxes, mask, pred, keep, t0)
+
+    def run_many(self, batches: Iterable, keep: bool = False) -> Iterator[Dict]:
+        """run() over an iterable of (images, boxes) or (images, boxes,
+        ready) batches, yielding one result per batch, with det one batch
+        ahead: as soon as a batch's det finishes, the next batch's det is
+        submitted (run_deferred, a second plan instance) and runs on the GPU
+        while this batch's boxes, crops, cls and rec are done - the overlap
+        the reference engine gets from keeping two batches in flight
+        (engine.rs:1409-1450).  `ready`, when given, is a torch.cuda.Event
+        recorded after the batch's images were copied to the device (on any
+        stream); without it the current stream is synchronised.  Results are
+        those of run() batch by batch; `timings["det_ms"]` is then the wait for
+        that batch's det after the previous batch was done."""
+        import torch
+
+        dev = torch.device("cuda", self.device)
+
+        def submit(b):
+            if len(b) > 2 and b[2] is not None:
+                b[2].synchronize()
+            else:
+                torch.cuda.current_stream(dev).synchronize()
+            return self.det.run_deferred({"x": b[0]})
+
+        it = iter(batches)
+        cur = next(it, None)
+        if cur is None:
+            return
+        pend = submit(cur)
+        nxt = next(it, None)  # the caller may start its upload now
+        while cur is not None:
+            t0 = time.perf_counter()
+            mask, pred = pend.complete()
+            pend = submit(nxt) if nxt is not None else None
+            after = next(it, None) if nxt is not None else None
+            res = self._after_det(cur[0], cur[1], mask, pred, keep, t0)
+            mask = pred = None
+            yield res
+            cur, nxt = nxt, after
+
+    def _after_det(self, images, boxes, mask, pred, keep, t0) -> Dict:
+        """Steps 2-5 of run() for one batch whose det outputs are at hand."""
         import torch
 
         dev = torch.device("cuda", self.device)
         n, h, w, _ = images.shape
         k = boxes.shape[1]
-        t0 = time.perf_counter()
-        torch.cuda.current_stream(dev).synchronize()  # the images are in place before the det session copies them
-        out: Dict = {}
-        # 1. det with the mask exit; the probability map stays on the device
-        mask, pred = self.det.run({"x": images})
         assert isinstance(pred, DeviceOutput)
-        out["mask"] = mask
+        out: Dict = {"mask": mask}
+        t_det = time.perf_counter()
         # 2. boxes scored on the kept map
         pts = np.ascontiguousarray(boxes, np.float32).reshape(n * k, 4, 2)
         img = np.repeat(np.arange(n, dtype=np.int32), k)
@@ -116,6 +165,7 @@ class OcrPipeline:
         probs = np.empty((lines, 2), np.float32)
         cls_in = []
         torch.cuda.current_stream(dev).synchronize()  # crops complete before the sessions read them
+        t_crop = time.perf_counter()
         for b in range(0, lines, self.cls_batch):
             e = min(b + self.cls_batch, lines)
             xb = op_line_pack(crops, off[b:e], cw_[b:e], x0[b:e], ch_[b:e], vw[b:e], crw[b:e],
@@ -125,6 +175,7 @@ class OcrPipeline:
             if keep:
                 cls_in.append(xb.cpu().numpy())
         flips = ((probs[:, 1] > probs[:, 0]) & (probs[:, 1] >= self.cls_thresh)).astype(np.int32)
+        t_cls = time.perf_counter()
         # 5. rec, one batch packed and submitted while the previous one runs
         rrw = packed_width(ch_, cw_, self.rec_h, self.rec_w)
         zeros = np.zeros(lines, np.int32)
@@ -144,12 +195,15 @@ class OcrPipeline:
             pending = (d, b, e)
         if pending is not None:
             rec_pairs.append(self._finish(*pending, results))
+        t_rec = time.perf_counter()
         out["scores"] = sc.cpu().numpy()
         if keep:
             out["pred"] = pmap.cpu().numpy()
         del pmap, pred
         out.update(probs=probs, flips=flips.astype(bool), results=results, lines=lines,
-                   seconds=time.perf_counter() - t0)
+                   seconds=time.perf_counter() - t0,
+                   timings={"det_ms": 1e3 * (t_det - t0), "crop_ms": 1e3 * (t_crop - t_det),
+                            "cls_ms": 1e3 * (t_cls - t_crop), "rec_ms": 1e3 * (t_rec - t_cls)})
         if keep:
             out.update(crops=crops.cpu().numpy(), off=off, crop_h=ch_, crop_w=cw_, cls_in=np.concatenate(cls_in),
                        rec_in=np.concatenate(rec_in), rec_pairs=np.concatenate(rec_pairs))

@@ -76,3 +76,47 @@ def test_pipeline_matches_oracle(cuda_ctx):
     assert len(out["results"]) == N * K and all(r is not None for r in out["results"])
     for s in (det, cls, rec):
         s.close()
+
+
+def test_run_many_equals_run(cuda_ctx):
+    """run_many (det one batch ahead, two det plan instances in flight) gives
+    run()'s results batch by batch, bit for bit, including batches of
+    different sizes and uploads signalled by events from a side stream."""
+    import torch
+    gd, wd = nets.build_det()
+    gd = q.optimize(gd, wd)
+    gc, wc = nets.build_cls()
+    gc = q.optimize(gc, wc)
+    gr, wr = nets.build_rec()
+    gr = q.optimize(gr, wr)
+    det = cuda_ctx.create_session(gd, wd, role="det", math="tf32", det_mask_exit=True)
+    cls = cuda_ctx.create_session(gc, wc, role="cls", math="tf32")
+    rec = cuda_ctx.create_session(gr, wr, role="rec", math="tf32")
+    pipe = OcrPipeline(det, cls, rec, cls_batch=64, rec_batch=64)
+    rng = np.random.Generator(np.random.PCG64(61))
+    sizes = [4, 4, 3, 4]
+    host = [rng.integers(0, 256, (n, H, W, 3), dtype=np.uint8) for n in sizes]
+    boxes = [synthetic_boxes(n, K, H, W, seed=90 + i) for i, n in enumerate(sizes)]
+    ref = [pipe.run(torch.from_numpy(h).cuda(), b) for h, b in zip(host, boxes)]
+    up = torch.cuda.Stream()
+
+    def batches():
+        for h, b in zip(host, boxes):
+            with torch.cuda.stream(up):
+                t = torch.from_numpy(h).pin_memory().cuda(non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(up)
+            yield t, b, ev
+
+    got = list(pipe.run_many(batches()))
+    assert len(got) == len(ref)
+    for g, r in zip(got, ref):
+        assert np.array_equal(g["mask"], r["mask"])
+        assert np.array_equal(g["scores"].view(np.uint32), r["scores"].view(np.uint32))
+        assert np.array_equal(g["probs"].view(np.uint32), r["probs"].view(np.uint32))
+        assert np.array_equal(g["flips"], r["flips"])
+        assert [list(x[0]) for x in g["results"]] == [list(x[0]) for x in r["results"]]
+        assert np.array_equal(np.array([x[1] for x in g["results"]], np.float32).view(np.uint32),
+                              np.array([x[1] for x in r["results"]], np.float32).view(np.uint32))
+    for s_ in (det, cls, rec):
+        s_.close()
