@@ -1269,8 +1269,13 @@ __device__ __forceinline__ void softmax_row_warp(float* row, int inner, int lane
 // memory; each warp takes query rows t = warp, warp + 8, ...: its lanes make
 // the scores, lanes 0-7 the softmax (softmax_row_warp, in the reference's
 // order), lanes < D the output.
+// TT, DD > 0: T and D known at compile time (the rec net's 40 x 15), so the
+// dot-product and P V loops unroll and their shared-memory loads are issued
+// ahead of the FMA chains, whose order is unchanged; 0: runtime sizes.
+template <int TT, int DD>
 __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict__ qkv, float* __restrict__ out,
-                                                        int T, int H, int D, float scale) {
+                                                        int T_rt, int H, int D_rt, float scale) {
+  const int T = TT > 0 ? TT : T_rt, D = DD > 0 ? DD : D_rt;
   extern __shared__ float sm[];
   const int b = blockIdx.x / H, h = blockIdx.x % H;
   const int C = H * D, C3 = 3 * C;
@@ -1294,6 +1299,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
     for (int u = lane; u < T; u += 32) {
       const float* k = ks + u * D;
       float acc = 0.f;
+#pragma unroll
       for (int d = 0; d < D; ++d) acc = __fmaf_rn(q[d], k[d], acc);
       p[u] = acc;
     }
@@ -1301,6 +1307,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
     softmax_row_warp(p, T, lane);
     if (lane < D) {
       float acc = 0.f;
+#pragma unroll
       for (int u = 0; u < T; ++u) acc = __fmaf_rn(p[u], vs[u * D + lane], acc);
       out[((int64_t)b * T + t) * C + h * D + lane] = acc;
     }
@@ -1316,8 +1323,9 @@ cudaError_t launch_attention(const float* qkv, int64_t B, int T, int H, int D, f
   if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
   const size_t smem = ((size_t)3 * T * D + 8 * (size_t)T) * sizeof(float);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  if (cudaError_t e = ensure_dyn_smem((const void*)attention_kernel, (int)smem); e != cudaSuccess) return e;
-  attention_kernel<<<(unsigned)blocks, 256, smem, st>>>(qkv, out, T, H, D, scale);
+  auto kern = (T == 40 && D == 15) ? attention_kernel<40, 15> : attention_kernel<0, 0>;
+  if (cudaError_t e = ensure_dyn_smem((const void*)kern, (int)smem); e != cudaSuccess) return e;
+  kern<<<(unsigned)blocks, 256, smem, st>>>(qkv, out, T, H, D, scale);
   return cudaGetLastError();
 }
 
