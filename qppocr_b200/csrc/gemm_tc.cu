@@ -101,18 +101,31 @@ __device__ __forceinline__ void argmax_tile(const GemmArgs& args, int64_t orow, 
         v[4 * j + 3] = __fadd_rn(v[4 * j + 3], b.w);
       }
     }
+    if (valid < 32)  // the head's last chunk
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j >= valid) v[j] = -INFINITY;
-    // chunk max and its first column (ascending scan keeps the lowest on ties)
-    float cm = v[0];
-    int cj = 0;
+      for (int j = 0; j < 32; ++j)
+        if (j >= valid) v[j] = -INFINITY;
+    // chunk max and its first column: a pairwise tree (depth 5 instead of a
+    // 31-step chain); on equal values the lower column wins, as in an
+    // ascending scan with a strict compare
+    float tv[16];
+    int ti[16];
 #pragma unroll
-    for (int j = 1; j < 32; ++j) {
-      const bool gt = v[j] > cm;
-      cm = gt ? v[j] : cm;
-      cj = gt ? j : cj;
+    for (int j = 0; j < 16; ++j) {
+      const bool gt = v[2 * j + 1] > v[2 * j];
+      tv[j] = gt ? v[2 * j + 1] : v[2 * j];
+      ti[j] = gt ? 2 * j + 1 : 2 * j;
     }
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+      for (int j = 0; j < w; ++j) {
+        const bool gt = tv[j + w] > tv[j] || (tv[j + w] == tv[j] && ti[j + w] < ti[j]);
+        tv[j] = gt ? tv[j + w] : tv[j];
+        ti[j] = gt ? ti[j + w] : ti[j];
+      }
+    const float cm = tv[0];
+    const int cj = ti[0];
     float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
