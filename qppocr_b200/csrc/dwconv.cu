@@ -315,8 +315,11 @@ cudaError_t launch_dwconv_nhwc(const float* x, const float* wt, const float* bia
       e = c32 ? run_dw_tile<3, 2, 32, 16, 8, 1>(x, wt, bias, residual, y, g, act, err, st)
               : run_dw_tile<3, 2, 16, 16, 8, 1>(x, wt, bias, residual, y, g, act, err, st);
     else if (g.kh == 5 && g.sh == 1 && c32)
-      e = g.ow <= 32 ? run_dw_tile<5, 1, 32, 10, 16, 2>(x, wt, bias, residual, y, g, act, err, st)
-                     : run_dw_tile<5, 1, 32, 20, 8, 2>(x, wt, bias, residual, y, g, act, err, st);
+      // maps at most 4 rows tall (the rec lines' 3 x 40): a 40 x 4 tile, so
+      // an 8-row tile does not compute 5 rows of nothing
+      e = g.oh <= 4   ? run_dw_tile<5, 1, 32, 40, 4, 2>(x, wt, bias, residual, y, g, act, err, st)
+          : g.ow <= 32 ? run_dw_tile<5, 1, 32, 10, 16, 2>(x, wt, bias, residual, y, g, act, err, st)
+                       : run_dw_tile<5, 1, 32, 20, 8, 2>(x, wt, bias, residual, y, g, act, err, st);
     else if (g.kh == 5 && g.sh == 1)
       e = run_dw_tile<5, 1, 16, 32, 8, 1>(x, wt, bias, residual, y, g, act, err, st);
     else if (g.kh == 5 && g.sh == 2)

@@ -718,9 +718,61 @@ __global__ void pool2d_nhwc_kernel(const float* __restrict__ x, float* __restric
   }
 }
 
+// C % 4 == 0 and fewer than 2^31 input elements: a thread makes 4 adjacent
+// channels of one output pixel (float4 loads and stores, 32-bit index math),
+// each channel with the generic kernel's operations in its order.
+__global__ void __launch_bounds__(256) pool2d_nhwc4_kernel(const float4* __restrict__ x, float4* __restrict__ y,
+                                                           int N, int H, int W, int C4, int OH, int OW, int KH,
+                                                           int KW, int SH, int SW, int PH, int PW, int is_max) {
+  const int total = N * OH * OW * C4;
+  const float inv_n = (float)(KH * KW);
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+    const int c4 = t % C4;
+    int r = t / C4;
+    const int ox = r % OW;
+    r /= OW;
+    const int oy = r % OH;
+    const int n = r / OH;
+    float4 acc = is_max ? make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int ky = 0; ky < KH; ++ky) {
+      const int iy = oy * SH - PH + ky;
+      if (iy < 0 || iy >= H) continue;
+      for (int kx = 0; kx < KW; ++kx) {
+        const int ix = ox * SW - PW + kx;
+        if (ix < 0 || ix >= W) continue;
+        const float4 v = __ldg(x + ((n * H + iy) * W + ix) * C4 + c4);
+        if (is_max) {
+          acc.x = v.x > acc.x ? v.x : acc.x;
+          acc.y = v.y > acc.y ? v.y : acc.y;
+          acc.z = v.z > acc.z ? v.z : acc.z;
+          acc.w = v.w > acc.w ? v.w : acc.w;
+        } else {
+          acc.x = __fadd_rn(acc.x, v.x);
+          acc.y = __fadd_rn(acc.y, v.y);
+          acc.z = __fadd_rn(acc.z, v.z);
+          acc.w = __fadd_rn(acc.w, v.w);
+        }
+      }
+    }
+    if (!is_max)
+      acc = make_float4(__fdiv_rn(acc.x, inv_n), __fdiv_rn(acc.y, inv_n), __fdiv_rn(acc.z, inv_n),
+                        __fdiv_rn(acc.w, inv_n));
+    y[t] = acc;
+  }
+}
+
 cudaError_t launch_pool2d_nhwc(const float* x, float* y, int n, int h, int w, int c, int oh, int ow,
                                int kh, int kw, int sh, int sw, int ph, int pw, int is_max,
                                cudaStream_t st) {
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  if ((c & 3) == 0 && aligned && (int64_t)n * h * w * c < ((int64_t)1 << 31) &&
+      (int64_t)n * oh * ow * c < ((int64_t)1 << 31)) {
+    const int64_t total = (int64_t)n * oh * ow * (c / 4);
+    pool2d_nhwc4_kernel<<<grid_for(total), 256, 0, st>>>(reinterpret_cast<const float4*>(x),
+                                                         reinterpret_cast<float4*>(y), n, h, w, c / 4, oh, ow, kh,
+                                                         kw, sh, sw, ph, pw, is_max);
+    return cudaGetLastError();
+  }
   pool2d_nhwc_kernel<<<grid_for((int64_t)n * oh * ow * c), 256, 0, st>>>(x, y, n, h, w, c, oh, ow, kh,
                                                                         kw, sh, sw, ph, pw, is_max);
   return cudaGetLastError();
