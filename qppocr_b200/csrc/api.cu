@@ -422,7 +422,7 @@ int qpc_op_ctc_head(const float* x, int64_t rows, int k, const float* w, const f
     e.ldo = n;
     unsigned int* err = device_state(current_device()).err_word;
     cudaError_t le = launch_gemm_tc(x, rows, k, k, w, w_lo, n, e, math, err, st);
-    if (le == cudaSuccess) le = launch_argmax_combine(static_cast<float4*>(part), ntiles, rows, pairs, st);
+    if (le == cudaSuccess) le = launch_argmax_combine(static_cast<float4*>(part), ntiles, rows, math, pairs, st);
     cudaFreeAsync(part, st);
     QPC_CUDA_OR_THROW(le);
     return (int)OK;

@@ -65,85 +65,126 @@ struct Smem {
   static constexpr int STAGE = A_BYTES + B_BYTES + (SPLIT ? (A_BYTES + B_BYTES) : 0);
 };
 
-// Row-argmax epilogue for one tile (CTC head): per row, the first strict
-// maximum of logits + bias over this tile's columns, its column, and the sum
-// of exp(l - max) over the tile, in one online pass over 32-column chunks
-// (fast exp; the combine step rescales across tiles).
+// CTC head (A_MODE 6).  Tile schedule: worker w = CTA * NGRP + group owns
+// the contiguous tiles [head_lo(w), head_lo(w + 1)) of the row-major tile
+// order, so it meets each row block's column tiles in ascending order and
+// keeps one running (max, argmax, sum exp) per row across them.  The CTA
+// issues its workers' tiles round-robin: slot k is worker k % NGRP's
+// (k / NGRP)-th tile, so epilogue group g still receives slots g, g + NGRP,
+// ... (worker tile counts differ by at most one, so only the last round has
+// empty slots).
+__device__ __forceinline__ int head_lo(int w, int T, int W) { return (int)((int64_t)w * T / W); }
+
+// Tile of slot k: >= 0; -1 for an empty slot of the last round; -2 past it.
+template <bool HEAD, int NGRP>
+__device__ __forceinline__ int cta_tile(int k, int T) {
+  if constexpr (HEAD) {
+    const int W = (int)gridDim.x * NGRP;
+    const int r = k / NGRP;
+    if (r >= (T + W - 1) / W) return -2;
+    const int w = (int)blockIdx.x * NGRP + k % NGRP;
+    const int t = head_lo(w, T, W) + r;
+    return t < head_lo(w + 1, T, W) ? t : -1;
+  } else {
+    const int64_t t = (int64_t)blockIdx.x + (int64_t)k * gridDim.x;
+    return t < T ? (int)t : -2;
+  }
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// 2^x (MUFU; subnormal results flush to zero).  exp(x) is taken as
+// 2^(x log2 e): the head only sums these terms for the softmax denominator.
+__device__ __forceinline__ float exp2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
+// One row's running softmax state over the columns merged so far.
+struct HeadRun {
+  float m;  // first strict maximum of logit + bias
+  float s;  // sum of exp(l - m)
+  int mi;   // its column
+};
+
+// Merges one tile's columns into `hr`, in 32-column chunks.  Per chunk: bias
+// (loaded before the TMEM read so the two latencies overlap), padding
+// columns -> -inf, the chunk max (three-input max tree), its first column (a
+// descending select scan: the lowest column holding the max, as an ascending
+// scan with a strict compare keeps), then sum exp(l - max).  Chunks and
+// tiles arrive in ascending column order, so `cm > hr.m` keeps the first
+// maximum across them too.
 template <int BN, class Fetch>
-__device__ __forceinline__ void argmax_tile(const GemmArgs& args, int64_t orow, int n0, int n_blk,
-                                            Fetch&& fetch) {
-  const GemmEpilogue& e = args.epi;
-  float m = -INFINITY, s = 0.f;
-  int mi = n0;
+__device__ __forceinline__ void head_tile(const GemmArgs& args, int n0, HeadRun& hr, Fetch&& fetch) {
+  const float* bias = args.epi.bias;
 #pragma unroll 1
   for (int cc = 0; cc < BN; cc += 32) {
     const int c0 = n0 + cc;
     if (c0 >= args.N) break;
-    float v[32];
-    fetch(cc, v);
     const int valid = args.N - c0;  // columns >= valid are padding
-    if (e.bias) {
-      const float4* b4 = reinterpret_cast<const float4*>(e.bias + c0);
+    float4 b[8];
+    if (bias) {
+      const float4* b4 = reinterpret_cast<const float4*>(bias + c0);
+      if (valid >= 32) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float4 b;
-        if (4 * j + 3 < valid) {
-          b = __ldg(b4 + j);
-        } else {  // partial trailing quad: stay inside the bias array
-          b.x = 4 * j < valid ? __ldg(e.bias + c0 + 4 * j) : 0.f;
-          b.y = 4 * j + 1 < valid ? __ldg(e.bias + c0 + 4 * j + 1) : 0.f;
-          b.z = 4 * j + 2 < valid ? __ldg(e.bias + c0 + 4 * j + 2) : 0.f;
-          b.w = 0.f;
+        for (int j = 0; j < 8; ++j) b[j] = __ldg(b4 + j);
+      } else {  // the head's last chunk: stay inside the bias array
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          b[j].x = 4 * j < valid ? __ldg(bias + c0 + 4 * j) : 0.f;
+          b[j].y = 4 * j + 1 < valid ? __ldg(bias + c0 + 4 * j + 1) : 0.f;
+          b[j].z = 4 * j + 2 < valid ? __ldg(bias + c0 + 4 * j + 2) : 0.f;
+          b[j].w = 4 * j + 3 < valid ? __ldg(bias + c0 + 4 * j + 3) : 0.f;
         }
-        v[4 * j] = __fadd_rn(v[4 * j], b.x);
-        v[4 * j + 1] = __fadd_rn(v[4 * j + 1], b.y);
-        v[4 * j + 2] = __fadd_rn(v[4 * j + 2], b.z);
-        v[4 * j + 3] = __fadd_rn(v[4 * j + 3], b.w);
       }
     }
-    if (valid < 32)  // the head's last chunk
+    float v[32];
+    fetch(cc, v);
+    if (bias) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[4 * j] = __fadd_rn(v[4 * j], b[j].x);
+        v[4 * j + 1] = __fadd_rn(v[4 * j + 1], b[j].y);
+        v[4 * j + 2] = __fadd_rn(v[4 * j + 2], b[j].z);
+        v[4 * j + 3] = __fadd_rn(v[4 * j + 3], b[j].w);
+      }
+    }
+    if (valid < 32)
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         if (j >= valid) v[j] = -INFINITY;
-    // chunk max and its first column: a pairwise tree (depth 5 instead of a
-    // 31-step chain); on equal values the lower column wins, as in an
-    // ascending scan with a strict compare
-    float tv[16];
-    int ti[16];
+    float t[11];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const bool gt = v[2 * j + 1] > v[2 * j];
-      tv[j] = gt ? v[2 * j + 1] : v[2 * j];
-      ti[j] = gt ? 2 * j + 1 : 2 * j;
-    }
+    for (int j = 0; j < 10; ++j) t[j] = max3f(v[3 * j], v[3 * j + 1], v[3 * j + 2]);
+    t[10] = fmaxf(v[30], v[31]);
+    const float cm = max3f(max3f(t[0], t[1], t[2]), max3f(t[3], t[4], t[5]),
+                           max3f(t[6], t[7], fmaxf(t[8], fmaxf(t[9], t[10]))));
+    int cj = 31;
 #pragma unroll
-    for (int w = 8; w >= 1; w >>= 1)
-#pragma unroll
-      for (int j = 0; j < w; ++j) {
-        const bool gt = tv[j + w] > tv[j] || (tv[j + w] == tv[j] && ti[j + w] < ti[j]);
-        tv[j] = gt ? tv[j + w] : tv[j];
-        ti[j] = gt ? ti[j + w] : ti[j];
-      }
-    const float cm = tv[0];
-    const int cj = ti[0];
+    for (int j = 30; j >= 0; --j) cj = v[j] == cm ? j : cj;
+    const float cmL = cm * kLog2e;
     float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
-      p0 += __expf(v[j] - cm);
-      p1 += __expf(v[j + 1] - cm);
-      p2 += __expf(v[j + 2] - cm);
-      p3 += __expf(v[j + 3] - cm);
+      p0 += exp2_ftz(fmaf(v[j], kLog2e, -cmL));
+      p1 += exp2_ftz(fmaf(v[j + 1], kLog2e, -cmL));
+      p2 += exp2_ftz(fmaf(v[j + 2], kLog2e, -cmL));
+      p3 += exp2_ftz(fmaf(v[j + 3], kLog2e, -cmL));
     }
     const float cs = (p0 + p1) + (p2 + p3);
-    if (cm > m) {
-      s = s * __expf(m - cm) + cs;
-      m = cm;
-      mi = c0 + cj;
+    if (cm > hr.m) {
+      hr.s = hr.s * exp2_ftz((hr.m - cm) * kLog2e) + cs;
+      hr.m = cm;
+      hr.mi = c0 + cj;
     } else {
-      s += cs * __expf(cm - m);
+      hr.s += cs * exp2_ftz((cm - hr.m) * kLog2e);
     }
   }
-  if (orow >= 0) e.partials[(int64_t)n_blk * args.M + orow] = make_float4(m, __uint_as_float((unsigned)mi), s, 0.f);
 }
 
 // ConvT pair epilogue for one tile (A_MODE 4: up to 32 channels between the
@@ -205,11 +246,14 @@ __device__ __forceinline__ void pair_tile(const GemmArgs& args, int64_t orow, co
 // where a tile carries little work and the chain's latency sets the pace, and
 // 2 otherwise; 3xTF32 keeps one group, whose registers hold the promoted
 // accumulator.
-// The ConvT pair mode (A_MODE 4) runs 4 groups: its epilogue is arithmetic
-// (a second layer per row), and it stages no output in shared memory.
+// The ConvT pair mode (A_MODE 4/5) runs 4 groups: its epilogue is arithmetic
+// (a second layer per row), and it stages no output in shared memory.  The
+// CTC head (A_MODE 6) stages nothing either; it runs HEAD_GROUPS groups.
+constexpr int HEAD_GROUPS = 2;
 template <int BN, bool SPLIT, int A_MODE = 0>
 struct Roles {
-  static constexpr int EPI_GROUPS = SPLIT ? 1 : ((BN <= 32 || A_MODE >= 4) ? 4 : 2);
+  static constexpr int EPI_GROUPS =
+      SPLIT ? 1 : (A_MODE == 6 ? HEAD_GROUPS : ((BN <= 32 || A_MODE >= 4) ? 4 : 2));
   static constexpr int THREADS = 128 + 128 * EPI_GROUPS;
   static constexpr int STAGING = A_MODE >= 4 ? 0 : EPI_GROUPS * 2 * OUT_STAGE_BYTES;
 };
@@ -255,13 +299,20 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
                    const GemmArgs args, const __grid_constant__ typename ModeConsts<A_MODE>::type mc) {
   using SM = Smem<BN, SPLIT, A_MODE>;
   // A_MODE 3: rows mode (0) with the per-image channel gate applied to A;
-  // A_MODE 4: rows mode with the ConvT pair epilogue (pair_tile)
+  // A_MODE 4/5: rows mode with the ConvT pair epilogue (pair_tile);
+  // A_MODE 6: rows mode with the CTC head epilogue (head_tile)
   constexpr int AM = (A_MODE == 3 || A_MODE >= 4) ? 0 : A_MODE;
   constexpr bool GATED = A_MODE == 3;
-  constexpr bool PAIR = A_MODE >= 4;
+  constexpr bool PAIR = A_MODE == 4 || A_MODE == 5;
+  constexpr bool HEAD = A_MODE == 6;
   constexpr int PAIR_M = A_MODE == 5 ? 24 : 32;
   constexpr int NBUF = Accs<BN, SPLIT>::NBUF;
   constexpr int NGRP = Roles<BN, SPLIT, A_MODE>::EPI_GROUPS;
+  static_assert(NBUF % NGRP == 0, "each accumulator must belong to one epilogue group");
+  // A stored tf32-rounded by its producer (rows mode, no gate or split): the
+  // converters have nothing to do, and the MMA thread takes each stage from
+  // the TMA barrier directly.
+  const bool conv_skip = AM == 0 && !GATED && !SPLIT && !PAIR && args.epi.a_rounded != 0;
   constexpr uint32_t TMEM_COLS = (NBUF * BN < 32) ? 32 : NBUF * BN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -315,7 +366,10 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
       const uint32_t bytes = SPLIT ? (a_bytes + 2 * b_bytes) : (a_bytes + b_bytes);
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      for (int k = 0; ok; ++k) {
+        const int tile = cta_tile<HEAD, NGRP>(k, total_tiles);
+        if (tile == -2) break;
+        if (tile < 0) continue;
         const TileCoord tc = tile_coord(args, tile, n_tiles, BN);
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int s = it % STAGES;
@@ -351,7 +405,13 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
       constexpr uint32_t idesc = idesc_tf32(BM, BN);
       uint32_t it = 0, acc_i = 0;  // acc_i: accumulator fills (tiles, or chunks in 3xTF32)
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+      for (int k = 0; ok; ++k) {
+        const int tile = cta_tile<HEAD, NGRP>(k, total_tiles);
+        if (tile == -2) break;
+        if (tile < 0) continue;
+        // one accumulator per slot: an empty slot (head schedule, last round)
+        // leaves its buffer unused, and the later slots keep theirs
+        if constexpr (!SPLIT) acc_i = (uint32_t)k;
         for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
           const bool first = SPLIT ? (kb % CH) == 0 : kb == 0;
           const uint32_t buf = acc_i % NBUF;
@@ -367,7 +427,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
           // Operand stages need no tcgen05 fence: the mbarrier wait orders the
           // TMA writes and the converters' (proxy-fenced) writes before the MMAs,
           // and a fence per stage would stall this thread on the MMAs in flight.
-          if (!mbar_wait(&conv_bar[s], ph, args.err)) { ok = false; break; }
+          if (!mbar_wait(conv_skip ? &full_bar[s] : &conv_bar[s], ph, args.err)) { ok = false; break; }
           const uint32_t d_tmem = tmem_d + buf * BN;
           const uint32_t a_addr = smem_u32(smem + s * SM::STAGE);
           const uint32_t b_addr = a_addr + SM::A_BYTES;
@@ -413,7 +473,10 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
     const float* gate = GATED ? args.epi.a_gate : nullptr;
     const int ghw = GATED ? args.epi.a_gate_rows : 1;
     const int64_t img_last = GATED ? (args.M - 1) / ghw : 0;
-    for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x) {
+    for (int k = 0; ok && !conv_skip; ++k) {
+      const int tile = cta_tile<HEAD, NGRP>(k, total_tiles);
+      if (tile == -2) break;
+      if (tile < 0) continue;
       // image of this tile's first row and that row's place in it (rows are
       // consecutive pixels, so a row's image is img0 + the number of image
       // boundaries crossed, at most one when an image has >= 128 rows)
@@ -447,10 +510,8 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
         if (!mbar_wait(&full_bar[s], ph, args.err)) { ok = false; break; }
         float4* a = reinterpret_cast<float4*>(smem + s * SM::STAGE);
         float4* lo = reinterpret_cast<float4*>(smem + s * SM::STAGE + SM::A_BYTES + SM::B_BYTES);
-        // (A rounded by its producer: nothing to do but hand the stage on)
-        const int n4 = (AM == 0 && !GATED && !SPLIT && args.epi.a_rounded)
-                           ? 0
-                           : (AM == 2 ? (BM + args.kw - 1) * (BK / 4) : A_TILE_BYTES / 16);
+        // (A rounded by its producer in rows mode: conv_skip, no converters)
+        const int n4 = AM == 2 ? (BM + args.kw - 1) * (BK / 4) : A_TILE_BYTES / 16;
         if (GATED && ghw >= BM) {
           // rows past M and channels past K hold TMA zero fill (or, past a
           // 24-wide k-block, bytes no MMA reads): no bounds checks needed
@@ -529,11 +590,38 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
     bool ok = true;
     float accr[SPLIT ? BN : 1];
     bool first_tile = true;
-    for (int tile = blockIdx.x + grp * gridDim.x; tile < total_tiles && ok; tile += NGRP * gridDim.x) {
+    // Head: this group's worker range, and the running state of row r of the
+    // row block in hand (written to partials[slot][row] when the row block
+    // changes and at the end; slot = the segment's first column tile)
+    int t_first = blockIdx.x + grp * gridDim.x, t_end = total_tiles, t_step = NGRP * gridDim.x;
+    HeadRun hr{-INFINITY, 0.f, 0};
+    int head_mblk = -1, head_slot = 0;
+    auto head_flush = [&]() {
+      const int64_t row = (int64_t)head_mblk * BM + r;
+      if (row < args.M)
+        e.partials[(int64_t)head_slot * args.M + row] = make_float4(hr.m, __uint_as_float((unsigned)hr.mi), hr.s, 0.f);
+    };
+    if constexpr (HEAD) {
+      const int W = (int)gridDim.x * NGRP, w = (int)blockIdx.x * NGRP + grp;
+      t_first = head_lo(w, total_tiles, W);
+      t_end = head_lo(w + 1, total_tiles, W);
+      t_step = 1;
+    }
+    for (int tile = t_first; tile < t_end && ok; tile += t_step) {
       const TileCoord tc = tile_coord(args, tile, n_tiles, BN);
       const RowMap rm = row_map<AM>(args, tc.m_blk, tc.img, tc.oy0, tc.ox0, r);
       const int64_t orow = rm.orow, rrow = rm.orow >= 0 ? rm.rrow : -1;
-      if (!SPLIT && NGRP <= 2 && e.residual) {
+      if constexpr (HEAD) {
+        if (tc.m_blk != head_mblk) {
+          if (head_mblk >= 0) head_flush();
+          head_mblk = tc.m_blk;
+          head_slot = tc.n0 / BN;
+          hr = HeadRun{-INFINITY, 0.f, 0};
+        }
+        // this tile's bias lines into L1 while its MMAs finish
+        if (e.bias && lane < BN / 32 && tc.n0 + 32 * lane < args.N) prefetch_l1(e.bias + tc.n0 + 32 * lane);
+      }
+      if (!HEAD && !SPLIT && NGRP <= 2 && e.residual) {
         // Residual lines of this group's next tile (and, first, of this one)
         // into L2 while the MMAs run, so the per-chunk loads hit L2.
         auto prefetch = [&](const TileCoord& pc, int64_t prow) {
@@ -569,8 +657,8 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
         };
         if constexpr (PAIR) {
           pair_tile<PAIR_M>(args, orow, mc, fetch);
-        } else if (e.partials) {
-          argmax_tile<BN>(args, orow, tc.n0, tc.n0 / BN, fetch);
+        } else if constexpr (HEAD) {
+          head_tile<BN>(args, tc.n0, hr, fetch);
         } else if (args.tma_store) {
           store_tile<BN, AM>(args, &tmOut, my_stage, s_rrow[grp], 1 + grp, chunk_ctr, tc.m_blk, tc.n0, tc.img,
                              tc.oy0, tc.ox0, r, gt, fetch);
@@ -619,8 +707,8 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
         };
         if constexpr (PAIR) {
           pair_tile<PAIR_M>(args, orow, mc, fetch);
-        } else if (e.partials) {
-          argmax_tile<BN>(args, orow, tc.n0, tc.n0 / BN, fetch);
+        } else if constexpr (HEAD) {
+          head_tile<BN>(args, tc.n0, hr, fetch);
         } else if (args.tma_store) {
           store_tile<BN, AM>(args, &tmOut, my_stage, s_rrow[grp], 1 + grp, chunk_ctr, tc.m_blk, tc.n0, tc.img,
                              tc.oy0, tc.ox0, r, gt, fetch);
@@ -636,6 +724,9 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
           }
         }
       }
+    }
+    if constexpr (HEAD) {
+      if (ok && head_mblk >= 0) head_flush();
     }
   }
   if (args.tma_store && threadIdx.x >= 128 && ((threadIdx.x - 128) & 127) == 0)
@@ -1331,26 +1422,37 @@ int gemm_tc_col_tiles(int N, int math) {
 }
 
 namespace {
-__global__ void argmax_combine_kernel(const float4* __restrict__ partials, int n_tiles, int64_t M,
+// Largest worker w with head_lo(w) <= t: the worker holding tile t.
+__device__ __forceinline__ int head_worker_of(int t, int T, int W) {
+  return (int)((((int64_t)t + 1) * W + T - 1) / T) - 1;
+}
+
+// Per row: the workers that covered its row block, in ascending column
+// order; each left one partial at slot = its first column tile there.
+__global__ void argmax_combine_kernel(const float4* __restrict__ partials, int n_tiles, int64_t M, int W,
                                       float* __restrict__ pairs) {
+  const int T = (int)((M + BM - 1) / BM) * n_tiles;
   for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < M;
        r += (int64_t)gridDim.x * blockDim.x) {
+    const int t0 = (int)(r / BM) * n_tiles, t1 = t0 + n_tiles;
+    const int w0 = head_worker_of(t0, T, W), w1 = head_worker_of(t1 - 1, T, W);
     float best = -INFINITY;
     unsigned idx = 0;
-    // (unrolled: eight tiles' loads in flight before their compares)
-#pragma unroll 8
-    for (int t = 0; t < n_tiles; ++t) {  // tiles ascend in column: strict > keeps the lowest
-      const float4 p = partials[(int64_t)t * M + r];
+    for (int w = w0; w <= w1; ++w) {  // strict >: the lowest column keeps a tie
+      const int lo = max(head_lo(w, T, W), t0);
+      if (lo >= head_lo(w + 1, T, W)) continue;  // a worker without tiles
+      const float4 p = partials[(int64_t)(lo - t0) * M + r];
       if (p.x > best) {
         best = p.x;
         idx = __float_as_uint(p.y);
       }
     }
     float s = 0.f;
-#pragma unroll 8
-    for (int t = 0; t < n_tiles; ++t) {
-      const float4 p = partials[(int64_t)t * M + r];
-      s += p.z * __expf(p.x - best);
+    for (int w = w0; w <= w1; ++w) {
+      const int lo = max(head_lo(w, T, W), t0);
+      if (lo >= head_lo(w + 1, T, W)) continue;
+      const float4 p = partials[(int64_t)(lo - t0) * M + r];
+      s += p.z * exp2_ftz((p.x - best) * kLog2e);
     }
     pairs[2 * r] = 1.0f / s;
     pairs[2 * r + 1] = __uint_as_float(idx);
@@ -1358,11 +1460,18 @@ __global__ void argmax_combine_kernel(const float4* __restrict__ partials, int n
 }
 }  // namespace
 
-cudaError_t launch_argmax_combine(const float4* partials, int n_tiles, int64_t M, float* pairs,
+int head_workers(int64_t M, int n_tiles, int math) {
+  const int64_t T = ((M + BM - 1) / BM) * n_tiles;
+  const int grid = T < sm_count() ? (int)T : sm_count();  // run_kernel's grid
+  return grid * (math == MATH_3XTF32 ? 1 : HEAD_GROUPS);
+}
+
+cudaError_t launch_argmax_combine(const float4* partials, int n_tiles, int64_t M, int math, float* pairs,
                                   cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  const int W = head_workers(M, n_tiles, math);
   int64_t blocks = (M + 63) / 64;  // 64-row blocks: a rec batch's 10,240 rows cover every SM
-  if (blocks < 1) blocks = 1;
-  argmax_combine_kernel<<<(unsigned)blocks, 64, 0, st>>>(partials, n_tiles, M, pairs);
+  argmax_combine_kernel<<<(unsigned)blocks, 64, 0, st>>>(partials, n_tiles, M, W, pairs);
   return cudaGetLastError();
 }
 
@@ -1410,6 +1519,10 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
     args.tma_store = make_map(&mo, obase, 2, dims, strides, box) ? 1 : 0;
   }
   const int grid_m = (int)((M + BM - 1) / BM);
+  if (epi.partials) {  // CTC head: no gate, nothing stored
+    if (epi.a_gate) return cudaErrorInvalidValue;
+    return dispatch<6>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
+  }
   if (epi.a_gate) return dispatch<3>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
   return dispatch<0>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
 }

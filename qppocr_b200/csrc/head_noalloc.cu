@@ -114,15 +114,15 @@ extern "C" int qpc_op_ctc_head_noalloc(const float* x, int64_t rows, int k, cons
   if (!device_ptrs(dev, &p)) return QPC_ERR_DEVICE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // The call's own fault word must start at zero (its kernels stop early
-  // while it is set); the partials are fully rewritten by the GEMM before the
-  // combine reads them.  The fold afterwards keeps any fault for the host.
+  // while it is set); every partial the combine reads is rewritten by the
+  // GEMM first.  The fold afterwards keeps any fault for the host.
   e = cudaMemsetAsync(p.err, 0, sizeof(unsigned int), st);
   qpc::GemmEpilogue epi;
   epi.bias = bias;
   epi.partials = p.partials;
   epi.ldo = n;
   if (e == cudaSuccess) e = qpc::launch_gemm_tc(x, rows, k, k, w, w_lo, n, epi, math, p.err, st);
-  if (e == cudaSuccess) e = qpc::launch_argmax_combine(p.partials, ntiles, rows, pairs, st);
+  if (e == cudaSuccess) e = qpc::launch_argmax_combine(p.partials, ntiles, rows, math, pairs, st);
   if (e == cudaSuccess) {
     keep_fault_kernel<<<1, 1, 0, st>>>(p.err);
     e = cudaGetLastError();

@@ -64,9 +64,12 @@ struct GemmEpilogue {
   // is rounded on chip, so x * g is never written.  Rows-mode GEMM only.
   const float* a_gate = nullptr;
   int a_gate_rows = 0;
-  // Row-argmax epilogue (CTC head): instead of storing D, each output tile
-  // writes per row (max, argmax bits, sum exp(l - max)) of its columns to
-  // partials[n_tile * M + row] (float4); nothing is written to `out`.
+  // Row-argmax epilogue (CTC head): instead of storing D, each epilogue
+  // worker (a contiguous run of tiles) writes per row of each row block it
+  // covers (max, argmax bits, sum exp(l - max)) over its columns there to
+  // partials[slot * M + row] (float4), slot = its first column tile in that
+  // block; nothing is written to `out`.  Buffer: n_tiles * M float4, of
+  // which launch_argmax_combine reads only the slots written.
   float4* partials = nullptr;
   // A already rounded to tf32 by its producer (a depthwise conv with
   // ActParams::round_tf32, or an epilogue / resize storing rounded values):
@@ -100,9 +103,14 @@ int gemm_tc_col_tiles(int N, int math);
 
 // Combines row-argmax partials into (value, index-bits) pairs: the first
 // strict maximum over all columns (ties -> lowest column) and its softmax
-// probability 1 / sum_j exp(l_j - max).
-cudaError_t launch_argmax_combine(const float4* partials, int n_tiles, int64_t M, float* pairs,
+// probability 1 / sum_j exp(l_j - max).  `math` must be the head GEMM's
+// (it fixes the number of epilogue workers, hence the slots written).
+cudaError_t launch_argmax_combine(const float4* partials, int n_tiles, int64_t M, int math, float* pairs,
                                   cudaStream_t st);
+// Epilogue workers of the CTC head GEMM over M rows and n_tiles column tiles
+// on the current device (each leaves one partial per row of every row block
+// it touches: at most M / 128 + workers row blocks' worth in all).
+int head_workers(int64_t M, int n_tiles, int math);
 
 // kxk stride-1 dense conv as implicit GEMM on tcgen05: A tiles are 4-D TMA
 // boxes of the NHWC input shifted per tap (out-of-bounds rows/cols read as

@@ -1180,36 +1180,103 @@ cudaError_t launch_copy_view(const float* a, float* y, const StridedDims& sd, cu
 // LayerNorm over the last axis, fused from the reference's decomposed chain
 // (executor ReduceMean -> Sub -> Pow 2 -> ReduceMean -> Add eps -> Sqrt ->
 // Div -> Mul gamma -> Add beta; shape.rs:510-566 f64 means, elementwise.rs
-// single roundings).  One thread per row, sequential f64 sums in index order,
-// so every intermediate equals the reference's.
+// single roundings).  Per row, the two sums are sequential f64 sums in index
+// order, so every intermediate equals the reference's.  `round` stores the
+// result tf32-rounded (nearest, ties away), for a value read only as a TF32
+// A operand.
+__device__ __forceinline__ float layernorm_elem(float x, float mean, float sd, const float* __restrict__ gamma,
+                                                const float* __restrict__ beta, int i, int round) {
+  float v = __fdiv_rn(__fsub_rn(x, mean), sd);
+  if (gamma) v = __fmul_rn(v, __ldg(gamma + i));
+  if (beta) v = __fadd_rn(v, __ldg(beta + i));
+  return round ? tf32_rna(v) : v;
+}
+__device__ __forceinline__ void layernorm_stats(const float* p, int C, float eps, float* mean_out, float* sd_out) {
+  double s = 0.0;
+  for (int i = 0; i < C; ++i) s += (double)p[i];
+  const float mean = (float)(s / (double)C);
+  double s2 = 0.0;
+  for (int i = 0; i < C; ++i) {
+    const float d = __fsub_rn(p[i], mean);
+    s2 += (double)__fmul_rn(d, d);
+  }
+  const float var = (float)(s2 / (double)C);
+  *mean_out = mean;
+  *sd_out = __fsqrt_rn(__fadd_rn(var, eps));
+}
+
+// One thread per row (rows wider than the staged kernel takes).
 __global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                  const float* __restrict__ beta, float* __restrict__ y,
-                                 int64_t rows, int C, float eps) {
+                                 int64_t rows, int C, float eps, int round) {
   GRID_LOOP(r, rows) {
     const float* p = x + r * C;
-    float* o = y + r * C;
-    double s = 0.0;
-    for (int i = 0; i < C; ++i) s += (double)p[i];
-    const float mean = (float)(s / (double)C);
-    double s2 = 0.0;
-    for (int i = 0; i < C; ++i) {
-      const float d = __fsub_rn(p[i], mean);
-      s2 += (double)__fmul_rn(d, d);
-    }
-    const float var = (float)(s2 / (double)C);
-    const float sd = __fsqrt_rn(__fadd_rn(var, eps));
-    for (int i = 0; i < C; ++i) {
-      float v = __fdiv_rn(__fsub_rn(p[i], mean), sd);
-      if (gamma) v = __fmul_rn(v, __ldg(gamma + i));
-      if (beta) v = __fadd_rn(v, __ldg(beta + i));
-      o[i] = v;
-    }
+    float mean, sd;
+    layernorm_stats(p, C, eps, &mean, &sd);
+    for (int i = 0; i < C; ++i) y[r * C + i] = layernorm_elem(p[i], mean, sd, gamma, beta, i, round);
+  }
+}
+
+// Rows of at most LN_STAGED_MAX_C channels, C % 4 == 0: each warp takes 8
+// consecutive rows (one contiguous block of 8 C floats), copies them into
+// shared memory with 16-byte coalesced loads, lane 4 r computes row r's
+// mean and sd (the sequential sums), then the row's 4 lanes normalise its
+// columns sub, sub + 4, ... in place, and the block leaves with 16-byte
+// coalesced stores.  Row pitch = 4 (mod 32) floats: the 8 summing lanes read
+// 8 distinct banks, and the 32 lanes of the elementwise pass 32.  (One
+// thread per row over global memory touched 32 lines per warp access and
+// left the elementwise pass to one lane per row.)
+constexpr int LN_STAGED_MAX_C = 352;  // 4 warps x 8 rows x pitch floats within 48 KB
+constexpr int LN_WARPS = 4;
+__host__ __device__ __forceinline__ int ln_pitch(int C) { return C + ((4 - C) % 32 + 32) % 32; }
+__global__ void __launch_bounds__(32 * LN_WARPS) layernorm_staged_kernel(
+    const float* __restrict__ x, const float* __restrict__ gamma, const float* __restrict__ beta,
+    float* __restrict__ y, int64_t rows, int C, float eps, int round) {
+  extern __shared__ __align__(16) float ln_rows[];
+  const int pitch = ln_pitch(C);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int64_t r0 = ((int64_t)blockIdx.x * LN_WARPS + wid) * 8;
+  if (r0 >= rows) return;
+  const int nr = rows - r0 < 8 ? (int)(rows - r0) : 8;
+  float* buf = ln_rows + wid * 8 * pitch;
+  const int n4 = nr * C / 4;
+  const float4* s4 = reinterpret_cast<const float4*>(x + r0 * C);
+  float4* d4 = reinterpret_cast<float4*>(y + r0 * C);
+  const int c4 = C / 4;
+#pragma unroll 4
+  for (int q = lane; q < n4; q += 32) {
+    const int row = q / c4;
+    *reinterpret_cast<float4*>(buf + row * pitch + 4 * (q - row * c4)) = __ldg(s4 + q);
+  }
+  __syncwarp();
+  const int rr = lane >> 2, sub = lane & 3;
+  float mean = 0.f, sd = 1.f;
+  if (sub == 0 && rr < nr) layernorm_stats(buf + rr * pitch, C, eps, &mean, &sd);
+  mean = __shfl_sync(0xffffffffu, mean, lane & ~3);
+  sd = __shfl_sync(0xffffffffu, sd, lane & ~3);
+  if (rr < nr) {
+    float* p = buf + rr * pitch;
+    for (int i = sub; i < C; i += 4) p[i] = layernorm_elem(p[i], mean, sd, gamma, beta, i, round);
+  }
+  __syncwarp();
+#pragma unroll 4
+  for (int q = lane; q < n4; q += 32) {
+    const int row = q / c4;
+    d4[q] = *reinterpret_cast<const float4*>(buf + row * pitch + 4 * (q - row * c4));
   }
 }
 
 cudaError_t launch_layernorm(const float* x, const float* gamma, const float* beta, float* y,
-                             int64_t rows, int c, float eps, cudaStream_t st) {
-  layernorm_kernel<<<grid_for(rows, 128), 128, 0, st>>>(x, gamma, beta, y, rows, c, eps);
+                             int64_t rows, int c, float eps, int round, cudaStream_t st) {
+  if (rows <= 0 || c <= 0) return cudaSuccess;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  if (c <= LN_STAGED_MAX_C && (c & 3) == 0 && aligned) {
+    const int64_t blocks = (rows + 8 * LN_WARPS - 1) / (8 * LN_WARPS);
+    const size_t smem = (size_t)LN_WARPS * 8 * ln_pitch(c) * sizeof(float);
+    layernorm_staged_kernel<<<(unsigned)blocks, 32 * LN_WARPS, smem, st>>>(x, gamma, beta, y, rows, c, eps, round);
+  } else {
+    layernorm_kernel<<<grid_for(rows, 128), 128, 0, st>>>(x, gamma, beta, y, rows, c, eps, round);
+  }
   return cudaGetLastError();
 }
 

@@ -64,8 +64,10 @@ cudaError_t launch_affine_nhwc(const float* x, const float* a, const float* b, f
                                int64_t total, int c, const ActParams& act, cudaStream_t st);
 
 cudaError_t launch_copy_view(const float* a, float* y, const StridedDims& sd, cudaStream_t st);
+// round: store tf32-rounded (nearest, ties away) outputs, for a value that
+// is read only as a TF32 A operand.
 cudaError_t launch_layernorm(const float* x, const float* gamma, const float* beta, float* y,
-                             int64_t rows, int c, float eps, cudaStream_t st);
+                             int64_t rows, int c, float eps, int round, cudaStream_t st);
 // Fused SVTR multi-head attention: qkv [B, T, 3*H*D] -> out [B, T, H*D]
 // (q scaled, softmax(q k^T) v per head), bit-identical to the reference's
 // Mul / MatMul / Softmax / MatMul ops.  D <= 32.

@@ -1281,9 +1281,10 @@ class Planner {
   // the A operand (input 0) of a TF32 conv on a tensor-core path that rounds
   // A to tf32 (nearest) - the pointwise GEMM or the tap-folded k x k conv,
   // the predicates plan_conv routes by - possibly through a channel Concat
-  // whose output does the same.  Then `o` may be stored tf32-rounded: each
-  // consumer would round it to the same values.  plan_conv checks, when it
-  // plans each such consumer, that it took one of those paths.
+  // whose output does the same, or of a linear / CTC head (plan_linear: the
+  // rows-mode GEMM, which always rounds A).  Then `o` may be stored
+  // tf32-rounded: each consumer would round it to the same values.  plan_conv
+  // checks, when it plans each such consumer, that it took one of those paths.
   std::set<std::string> tf32_rounded_;
   bool feeds_only_tf32_a(const std::string& o, int64_t N, int64_t C, int64_t H, int64_t W, int depth = 0) {
     if (S.math() != QPC_MATH_TF32 || depth > 4) return false;
@@ -1305,6 +1306,12 @@ class Planner {
           seen += x == o;
         }
         if (seen != 1 || !feeds_only_tf32_a(c.out[0], N, total, H, W, depth + 1)) return false;
+        continue;
+      }
+      if (c.op == "QpcLinear" || c.op == "QpcCtcHead") {
+        if (c.in.empty() || c.in[0] != o) return false;
+        for (size_t k = 1; k < c.in.size(); ++k)
+          if (c.in[k] == o) return false;
         continue;
       }
       if (c.op != "Conv" || c.in.size() < 2 || c.in[0] != o) return false;
@@ -2211,8 +2218,10 @@ class Planner {
     const float* gp = n.has_in(1) ? S.dweight(n.in[1], "raw") : nullptr;
     const float* bp = n.has_in(2) ? S.dweight(n.in[2], "raw") : nullptr;
     const float eps = n.getf("qpc_eps", 1e-5f);
+    const int rnd = feeds_only_tf32_a(n.out[0], 0, C, 0, 0) ? 1 : 0;
+    if (rnd) tf32_rounded_.insert(n.out[0]);
     step("layernorm", n.name, 8.0 * x.numel(), 8.0 * x.numel(),
-         [=](cudaStream_t s) { return launch_layernorm(xp, gp, bp, yp, rows, (int)C, eps, s); });
+         [=](cudaStream_t s) { return launch_layernorm(xp, gp, bp, yp, rows, (int)C, eps, rnd, s); });
     unref(x);
     define(n.out[0], y);
   }
@@ -2244,6 +2253,8 @@ class Planner {
     unsigned int* err = device_state(S.device()).err_word;
     const double flops = 2.0 * rows * K * Nn;
     const float* xp = out_ptr(x);
+    // A stored tf32-rounded by its producer (the GEMM skips its rounding pass)
+    const int a_rounded = (!split && tf32_rounded_.count(n.in[0])) ? 1 : 0;
     if (!head) {
       Val y = new_val(oshape, false);
       GemmEpilogue e;
@@ -2253,6 +2264,11 @@ class Planner {
       e.ldo = (int)Nn;
       e.ldr = (int)Nn;
       e.act = act_of(n);
+      e.a_rounded = a_rounded;
+      if (feeds_only_tf32_a(n.out[0], 0, Nn, 0, 0)) {
+        e.round_out = 1;
+        tf32_rounded_.insert(n.out[0]);
+      }
       step("gemm_tc", n.name, 4.0 * (rows * K + rows * Nn + K * Nn), flops, [=](cudaStream_t s) {
         return launch_gemm_tc(xp, rows, (int)K, (int)K, wb, wl, (int)Nn, e, math, err, s);
       });
@@ -2267,6 +2283,10 @@ class Planner {
     if (has_res) throw GraphError{"CTC head with a residual"};
     const int ntiles = gemm_tc_col_tiles((int)Nn, math);
     Val part = new_val({(int64_t)ntiles * rows * 4}, false);
+    // partials written and read: one per (worker, row block) it touches
+    const int64_t mblk = (rows + 127) / 128;
+    const double part_bytes =
+        16.0 * 128 * (double)std::min<int64_t>(mblk * ntiles, mblk + head_workers(rows, ntiles, math));
     float4* pp4 = reinterpret_cast<float4*>(out_ptr(part));
     GemmEpilogue e;
     e.bias = bias;
@@ -2274,15 +2294,16 @@ class Planner {
     e.out = nullptr;
     e.ldo = (int)Nn;
     e.act = act_of(n);
-    step("head_gemm", n.name, 4.0 * (rows * K + K * Nn) + 16.0 * ntiles * rows, flops,
+    e.a_rounded = a_rounded;
+    step("head_gemm", n.name, 4.0 * (rows * K + K * Nn) + part_bytes, flops,
          [=](cudaStream_t s) { return launch_gemm_tc(xp, rows, (int)K, (int)K, wb, wl, (int)Nn, e, math, err, s); });
     unref(x);
     std::vector<int64_t> pshape = oshape;
     pshape.back() = 2;
     Val pr = new_val(pshape, false);
     float* prp = out_ptr(pr);
-    step("head_combine", n.name, 16.0 * ntiles * rows + 8.0 * rows, 0,
-         [=](cudaStream_t s) { return launch_argmax_combine(pp4, ntiles, rows, prp, s); });
+    step("head_combine", n.name, part_bytes + 8.0 * rows, 0,
+         [=](cudaStream_t s) { return launch_argmax_combine(pp4, ntiles, rows, math, prp, s); });
     unref(part);
     define(n.out[0], pr);
   }

@@ -83,3 +83,25 @@ def test_cls_per_node(cuda_ctx, math):
     fused, errs = per_node(cuda_ctx, nets.build_cls, nets.cls_input(8), math, "cls")
     worst = max(errs.items(), key=lambda kv: kv[1][1])
     assert worst[1][1] < TOL[math], worst
+
+
+@pytest.mark.parametrize("rows,c", [(77, 120), (8, 120), (1, 12), (300, 36), (45, 30), (19, 400)])
+def test_layernorm_bit_exact(cuda_ctx, rows, c):
+    """The fused LayerNorm (sequential f64 sums per row in index order,
+    shape.rs:510-566) equals the oracle's decomposed chain bit for bit, for
+    ragged row counts and both kernel paths: rows of <= 352 channels with
+    C % 4 == 0 take the shared-memory kernel (8 rows per warp), the others
+    one thread per row.  The output is a graph output, so it is stored
+    unrounded; a linear consumer would get it tf32-rounded."""
+    b = nets.Builder(5, "ln")
+    y = b.layernorm("x", c)
+    g, w = b.graph(["x"], [y], [[1, 0, c]])
+    g = q.optimize(g, w)
+    rng = np.random.Generator(np.random.PCG64(rows * 1000 + c))
+    x = (rng.standard_normal((1, rows, c)) * 3 + 0.5).astype(np.float32)
+    ref = orc.run_graph(g, w, {"x": x})[0]
+    s = cuda_ctx.create_session(g, w, role="other", math="tf32")
+    assert [f[0] for f in s.fused_nodes()] == ["QpcLayerNorm"]
+    got = s.run({"x": x})[0]
+    assert got.shape == ref.shape == (1, rows, c)
+    assert np.array_equal(got, ref), rel(got, ref)
