@@ -157,8 +157,8 @@ def barrier(world):
 # dominant family.
 DET_TRAFFIC_PER_IMAGE = {"dwpw": 13515751, "gemm_tc": 8826127, "conv_tc": 12302626, "dwconv": 13393150,
                          "conv_direct": 23704267, "resize": 18179488, "convt_pair": 7496064, "gap": 1382699}
-REC_TRAFFIC_PER_LINE = {"gemm_tc": 90276, "dwpw": 321667, "dwconv": 236061, "pool2d": 231634, "layernorm": 19268,
-                        "head_gemm": 54868, "head_combine": 94135}
+REC_TRAFFIC_PER_LINE = {"gemm_tc": 92693, "dwpw": 384948, "dwconv": 211184, "pool2d": 230540, "layernorm": 19287,
+                        "attention": 57700, "conv_direct": 219519, "head_gemm": 54705, "head_combine": 3660}
 TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum summed over the family's launches of one pass on a "
                   "small case (det batch 24, rec batch 256), per image (line) per launch, scaled to this batch")
 

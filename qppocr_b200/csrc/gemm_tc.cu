@@ -57,37 +57,36 @@ constexpr int HALO_ROWS = 136;
 constexpr int HALO_BYTES = HALO_ROWS * BK * 4;
 static_assert(BM + MAX_KW_HALO - 1 <= HALO_ROWS, "halo row does not fit its buffer");
 
+// A_MODE 7 (CTC head, A resident): the stages hold B only; the row block's
+// A, up to HEAD_RES_KB k-blocks, sits in RES bytes after them.
+constexpr int HEAD_RES_KB = 5;
 template <int BN, bool SPLIT, int A_MODE>
 struct Smem {
-  static constexpr int A_BYTES = A_MODE == 2 ? HALO_BYTES : A_TILE_BYTES;
+  static constexpr int A_BYTES = A_MODE == 7 ? 0 : (A_MODE == 2 ? HALO_BYTES : A_TILE_BYTES);
   static constexpr int B_TILE = BN * BK * 4;
   static constexpr int B_BYTES = (A_MODE == 2 ? MAX_KW_HALO : 1) * B_TILE;
   static constexpr int STAGE = A_BYTES + B_BYTES + (SPLIT ? (A_BYTES + B_BYTES) : 0);
+  static constexpr int RES = A_MODE == 7 ? HEAD_RES_KB * A_TILE_BYTES : 0;
 };
 
-// CTC head (A_MODE 6).  Tile schedule: worker w = CTA * NGRP + group owns
-// the contiguous tiles [head_lo(w), head_lo(w + 1)) of the row-major tile
-// order, so it meets each row block's column tiles in ascending order and
-// keeps one running (max, argmax, sum exp) per row across them.  The CTA
-// issues its workers' tiles round-robin: slot k is worker k % NGRP's
-// (k / NGRP)-th tile, so epilogue group g still receives slots g, g + NGRP,
-// ... (worker tile counts differ by at most one, so only the last round has
-// empty slots).
-__device__ __forceinline__ int head_lo(int w, int T, int W) { return (int)((int64_t)w * T / W); }
+// CTC head (A_MODE 6, 7).  Tile schedule: CTA b owns the contiguous tiles
+// [head_lo(b), head_lo(b + 1)) of the row-major tile order (so a row block's
+// column tiles reach it in ascending order, one row block after the other),
+// and its epilogue group g takes the CTA's tiles g, g + NGRP, ... as in the
+// strided schedule.  Each group keeps one running (max, argmax, sum exp) per
+// row over its tiles of a row block and leaves it in the partials slot of
+// its first tile there.
+__device__ __forceinline__ int head_lo(int b, int T, int W) { return (int)((int64_t)b * T / W); }
 
-// Tile of slot k: >= 0; -1 for an empty slot of the last round; -2 past it.
-template <bool HEAD, int NGRP>
+// Tile of slot k of this CTA, or -1 past its last tile.
+template <bool HEAD>
 __device__ __forceinline__ int cta_tile(int k, int T) {
   if constexpr (HEAD) {
-    const int W = (int)gridDim.x * NGRP;
-    const int r = k / NGRP;
-    if (r >= (T + W - 1) / W) return -2;
-    const int w = (int)blockIdx.x * NGRP + k % NGRP;
-    const int t = head_lo(w, T, W) + r;
-    return t < head_lo(w + 1, T, W) ? t : -1;
+    const int t = head_lo((int)blockIdx.x, T, (int)gridDim.x) + k;
+    return t < head_lo((int)blockIdx.x + 1, T, (int)gridDim.x) ? t : -1;
   } else {
     const int64_t t = (int64_t)blockIdx.x + (int64_t)k * gridDim.x;
-    return t < T ? (int)t : -2;
+    return t < T ? (int)t : -1;
   }
 }
 
@@ -248,12 +247,12 @@ __device__ __forceinline__ void pair_tile(const GemmArgs& args, int64_t orow, co
 // accumulator.
 // The ConvT pair mode (A_MODE 4/5) runs 4 groups: its epilogue is arithmetic
 // (a second layer per row), and it stages no output in shared memory.  The
-// CTC head (A_MODE 6) stages nothing either; it runs HEAD_GROUPS groups.
+// CTC head (A_MODE 6, 7) stages nothing either; it runs HEAD_GROUPS groups.
 constexpr int HEAD_GROUPS = 2;
 template <int BN, bool SPLIT, int A_MODE = 0>
 struct Roles {
   static constexpr int EPI_GROUPS =
-      SPLIT ? 1 : (A_MODE == 6 ? HEAD_GROUPS : ((BN <= 32 || A_MODE >= 4) ? 4 : 2));
+      SPLIT ? 1 : ((A_MODE == 6 || A_MODE == 7) ? HEAD_GROUPS : ((BN <= 32 || A_MODE >= 4) ? 4 : 2));
   static constexpr int THREADS = 128 + 128 * EPI_GROUPS;
   static constexpr int STAGING = A_MODE >= 4 ? 0 : EPI_GROUPS * 2 * OUT_STAGE_BYTES;
 };
@@ -300,11 +299,14 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
   using SM = Smem<BN, SPLIT, A_MODE>;
   // A_MODE 3: rows mode (0) with the per-image channel gate applied to A;
   // A_MODE 4/5: rows mode with the ConvT pair epilogue (pair_tile);
-  // A_MODE 6: rows mode with the CTC head epilogue (head_tile)
+  // A_MODE 6: rows mode with the CTC head epilogue (head_tile);
+  // A_MODE 7: the same with the row block's A resident in shared memory
+  // (tf32-rounded by its producer; loaded once per row block, B streams)
   constexpr int AM = (A_MODE == 3 || A_MODE >= 4) ? 0 : A_MODE;
   constexpr bool GATED = A_MODE == 3;
   constexpr bool PAIR = A_MODE == 4 || A_MODE == 5;
-  constexpr bool HEAD = A_MODE == 6;
+  constexpr bool HEAD = A_MODE == 6 || A_MODE == 7;
+  constexpr bool ARES = A_MODE == 7;
   constexpr int PAIR_M = A_MODE == 5 ? 24 : 32;
   constexpr int NBUF = Accs<BN, SPLIT>::NBUF;
   constexpr int NGRP = Roles<BN, SPLIT, A_MODE>::EPI_GROUPS;
@@ -312,7 +314,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
   // A stored tf32-rounded by its producer (rows mode, no gate or split): the
   // converters have nothing to do, and the MMA thread takes each stage from
   // the TMA barrier directly.
-  const bool conv_skip = AM == 0 && !GATED && !SPLIT && !PAIR && args.epi.a_rounded != 0;
+  const bool conv_skip = ARES || (AM == 0 && !GATED && !SPLIT && !PAIR && args.epi.a_rounded != 0);
   constexpr uint32_t TMEM_COLS = (NBUF * BN < 32) ? 32 : NBUF * BN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -322,6 +324,8 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
   __shared__ __align__(8) uint64_t conv_bar[STAGES];
   __shared__ __align__(8) uint64_t acc_full[NBUF];
   __shared__ __align__(8) uint64_t acc_empty[NBUF];
+  __shared__ __align__(8) uint64_t a_full;   // ARES: the row block's A landed
+  __shared__ __align__(8) uint64_t a_empty;  // ARES: the MMAs on the previous A completed
   __shared__ uint32_t tmem_base_slot;
   __shared__ int64_t s_rrow[NGRP][BM];
 
@@ -341,6 +345,8 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 128);
     }
+    mbar_init(&a_full, 1);
+    mbar_init(&a_empty, 1);
     fence_barrier_init();
     prefetch_tensormap(&tmA);
     prefetch_tensormap(&tmB);
@@ -348,6 +354,7 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
     if (args.tma_store) prefetch_tensormap(&tmOut);
   }
   uint8_t* out_stage = smem + STAGES * SM::STAGE;  // 2 x 16 KB, 1024-aligned
+  uint8_t* a_res = out_stage + Roles<BN, SPLIT, A_MODE>::STAGING;  // ARES: SM::RES bytes
   if (warp == 0) {
     tmem_alloc(&tmem_base_slot, TMEM_COLS);
     tmem_relinquish();
@@ -363,21 +370,33 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
       const uint32_t a_bytes = AM == 2 ? (uint32_t)(BM + args.kw - 1) * BK * 4
                                        : (AM == 0 ? (uint32_t)(BM * args.bkw * 4) : A_TILE_BYTES);
       const uint32_t b_bytes = AM == 2 ? args.kw * SM::B_TILE : (AM == 0 ? (uint32_t)(BN * args.bkw * 4) : SM::B_TILE);
-      const uint32_t bytes = SPLIT ? (a_bytes + 2 * b_bytes) : (a_bytes + b_bytes);
-      uint32_t it = 0;
+      const uint32_t bytes = ARES ? b_bytes : (SPLIT ? (a_bytes + 2 * b_bytes) : (a_bytes + b_bytes));
+      uint32_t it = 0, a_loads = 0;
+      int a_mblk = -1;
       bool ok = true;
       for (int k = 0; ok; ++k) {
-        const int tile = cta_tile<HEAD, NGRP>(k, total_tiles);
-        if (tile == -2) break;
-        if (tile < 0) continue;
+        const int tile = cta_tile<HEAD>(k, total_tiles);
+        if (tile < 0) break;
         const TileCoord tc = tile_coord(args, tile, n_tiles, BN);
+        if constexpr (ARES) {
+          if (tc.m_blk != a_mblk) {  // the row block's A, once the MMAs on the last one are done
+            if (a_loads > 0 && !mbar_wait(&a_empty, (a_loads - 1) & 1u, args.err)) { ok = false; break; }
+            mbar_arrive_expect_tx(&a_full, (uint32_t)nkb * a_bytes);
+            for (int kb = 0; kb < nkb; ++kb)
+              tma_load_2d(a_res + kb * A_TILE_BYTES, &tmA, &a_full, kb * args.bkw, tc.m_blk * BM);
+            ++a_loads;
+            a_mblk = tc.m_blk;
+          }
+        }
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.err)) { ok = false; break; }
           uint8_t* st = smem + s * SM::STAGE;
           mbar_arrive_expect_tx(&full_bar[s], bytes);
-          if (AM == 0) {
+          if (ARES) {
+            tma_load_2d(st, &tmB, &full_bar[s], kb * args.bkw, tc.n0);
+          } else if (AM == 0) {
             tma_load_2d(st, &tmA, &full_bar[s], kb * args.bkw, tc.m_blk * BM);
             tma_load_2d(st + SM::A_BYTES, &tmB, &full_bar[s], kb * args.bkw, tc.n0);
             if (SPLIT) tma_load_2d(st + 2 * SM::A_BYTES + SM::B_BYTES, &tmBlo, &full_bar[s], kb * args.bkw, tc.n0);
@@ -404,14 +423,23 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
       // ---------------- MMA issuer
       constexpr uint32_t idesc = idesc_tf32(BM, BN);
       uint32_t it = 0, acc_i = 0;  // acc_i: accumulator fills (tiles, or chunks in 3xTF32)
+      uint32_t a_uses = 0;
+      int a_mblk = -1;
       bool ok = true;
       for (int k = 0; ok; ++k) {
-        const int tile = cta_tile<HEAD, NGRP>(k, total_tiles);
-        if (tile == -2) break;
-        if (tile < 0) continue;
-        // one accumulator per slot: an empty slot (head schedule, last round)
-        // leaves its buffer unused, and the later slots keep theirs
-        if constexpr (!SPLIT) acc_i = (uint32_t)k;
+        const int tile = cta_tile<HEAD>(k, total_tiles);
+        if (tile < 0) break;
+        if constexpr (ARES) {
+          const int m_blk = tile / n_tiles;
+          if (m_blk != a_mblk) {
+            // a_empty completes once every MMA issued so far (those reading
+            // the previous A) has; then wait for this row block's A
+            if (a_uses > 0) mma_commit(&a_empty);
+            if (!mbar_wait(&a_full, a_uses & 1u, args.err)) { ok = false; break; }
+            ++a_uses;
+            a_mblk = m_blk;
+          }
+        }
         for (int kb = 0; kb < nkb && ok; ++kb, ++it) {
           const bool first = SPLIT ? (kb % CH) == 0 : kb == 0;
           const uint32_t buf = acc_i % NBUF;
@@ -429,8 +457,8 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
           // and a fence per stage would stall this thread on the MMAs in flight.
           if (!mbar_wait(conv_skip ? &full_bar[s] : &conv_bar[s], ph, args.err)) { ok = false; break; }
           const uint32_t d_tmem = tmem_d + buf * BN;
-          const uint32_t a_addr = smem_u32(smem + s * SM::STAGE);
-          const uint32_t b_addr = a_addr + SM::A_BYTES;
+          const uint32_t a_addr = ARES ? smem_u32(a_res + kb * A_TILE_BYTES) : smem_u32(smem + s * SM::STAGE);
+          const uint32_t b_addr = ARES ? smem_u32(smem + s * SM::STAGE) : a_addr + SM::A_BYTES;
           const uint32_t alo_addr = b_addr + SM::B_BYTES;
           const uint32_t blo_addr = alo_addr + SM::A_BYTES;
           // AM 2: tap kx of this kernel row is the halo shifted by kx rows
@@ -474,9 +502,8 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
     const int ghw = GATED ? args.epi.a_gate_rows : 1;
     const int64_t img_last = GATED ? (args.M - 1) / ghw : 0;
     for (int k = 0; ok && !conv_skip; ++k) {
-      const int tile = cta_tile<HEAD, NGRP>(k, total_tiles);
-      if (tile == -2) break;
-      if (tile < 0) continue;
+      const int tile = cta_tile<HEAD>(k, total_tiles);
+      if (tile < 0) break;
       // image of this tile's first row and that row's place in it (rows are
       // consecutive pixels, so a row's image is img0 + the number of image
       // boundaries crossed, at most one when an image has >= 128 rows)
@@ -590,9 +617,10 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
     bool ok = true;
     float accr[SPLIT ? BN : 1];
     bool first_tile = true;
-    // Head: this group's worker range, and the running state of row r of the
-    // row block in hand (written to partials[slot][row] when the row block
-    // changes and at the end; slot = the segment's first column tile)
+    // Head: this group's tiles of the CTA's range, and the running state of
+    // row r of the row block in hand (written to partials[slot][row] when the
+    // row block changes and at the end; slot = the group's first column tile
+    // in that row block)
     int t_first = blockIdx.x + grp * gridDim.x, t_end = total_tiles, t_step = NGRP * gridDim.x;
     HeadRun hr{-INFINITY, 0.f, 0};
     int head_mblk = -1, head_slot = 0;
@@ -602,10 +630,9 @@ __global__ void __launch_bounds__(Roles<BN, SPLIT, A_MODE>::THREADS, 1)
         e.partials[(int64_t)head_slot * args.M + row] = make_float4(hr.m, __uint_as_float((unsigned)hr.mi), hr.s, 0.f);
     };
     if constexpr (HEAD) {
-      const int W = (int)gridDim.x * NGRP, w = (int)blockIdx.x * NGRP + grp;
-      t_first = head_lo(w, total_tiles, W);
-      t_end = head_lo(w + 1, total_tiles, W);
-      t_step = 1;
+      t_first = head_lo((int)blockIdx.x, total_tiles, (int)gridDim.x) + grp;
+      t_end = head_lo((int)blockIdx.x + 1, total_tiles, (int)gridDim.x);
+      t_step = NGRP;
     }
     for (int tile = t_first; tile < t_end && ok; tile += t_step) {
       const TileCoord tc = tile_coord(args, tile, n_tiles, BN);
@@ -1317,7 +1344,8 @@ int sm_count() { return current_sm_count(); }
 // most 8.  An instantiation with room for fewer than 2 stages is not built.
 template <int BN, bool SPLIT, int A_MODE>
 constexpr int stages_raw() {
-  return (224 * 1024 - Roles<BN, SPLIT, A_MODE>::STAGING - 1024) / Smem<BN, SPLIT, A_MODE>::STAGE;
+  return (224 * 1024 - Roles<BN, SPLIT, A_MODE>::STAGING - Smem<BN, SPLIT, A_MODE>::RES - 1024) /
+         Smem<BN, SPLIT, A_MODE>::STAGE;
 }
 template <int BN, bool SPLIT, int A_MODE>
 constexpr int stages_for() {
@@ -1333,7 +1361,8 @@ cudaError_t run_kernel(const CUtensorMap& a, const CUtensorMap& b, const CUtenso
   } else {
   constexpr int STAGES = stages_for<BN, SPLIT, A_MODE>();
   auto kern = gemm_tc_kernel<BN, STAGES, SPLIT, A_MODE>;
-  const int smem = STAGES * Smem<BN, SPLIT, A_MODE>::STAGE + Roles<BN, SPLIT, A_MODE>::STAGING + 1024;
+  const int smem = STAGES * Smem<BN, SPLIT, A_MODE>::STAGE + Roles<BN, SPLIT, A_MODE>::STAGING +
+                   Smem<BN, SPLIT, A_MODE>::RES + 1024;
   if (cudaError_t e = ensure_dyn_smem((const void*)kern, smem); e != cudaSuccess) return e;
   const int grid = tiles < sm_count() ? tiles : sm_count();
   kern<<<grid, Roles<BN, SPLIT, A_MODE>::THREADS, smem, st>>>(a, b, blo, out, args, mc);
@@ -1409,6 +1438,12 @@ int pick_bn(int n, bool split) {
   return c256 <= c128 ? 256 : 128;
 }
 
+// CTC head tile width: 256 columns whenever N allows in TF32.  A head k-block
+// (24 or 32 floats) carries only 3-4 MMAs, and each pipeline stage costs a
+// fixed few hundred cycles of barrier round trip whatever its size, so the
+// wider tile doubles the math per stage.  3xTF32 keeps its 128-column limit.
+int head_bn(int n, bool split) { return (!split && n > 128) ? 256 : pick_bn(n, split); }
+
 }  // namespace
 
 bool conv_fold_ok(const ConvGeom& g) {
@@ -1417,42 +1452,63 @@ bool conv_fold_ok(const ConvGeom& g) {
 }
 
 int gemm_tc_col_tiles(int N, int math) {
-  const int bn = pick_bn(N, math == MATH_3XTF32);
+  const int bn = head_bn(N, math == MATH_3XTF32);
   return (N + bn - 1) / bn;
 }
 
 namespace {
-// Largest worker w with head_lo(w) <= t: the worker holding tile t.
-__device__ __forceinline__ int head_worker_of(int t, int T, int W) {
+// Largest CTA b with head_lo(b) <= t: the CTA holding tile t.
+__device__ __forceinline__ int head_cta_of(int t, int T, int W) {
   return (int)((((int64_t)t + 1) * W + T - 1) / T) - 1;
 }
 
-// Per row: the workers that covered its row block, in ascending column
-// order; each left one partial at slot = its first column tile there.
+// Per row: the partials of the (CTA, epilogue group) pairs that covered its
+// row block.  A pair's partial is the first maximum over its columns there,
+// and the pairs' columns interleave, so the merge keeps the larger value and,
+// on equal values, the lower column: the first maximum over all columns.
+template <int NGRP>
 __global__ void argmax_combine_kernel(const float4* __restrict__ partials, int n_tiles, int64_t M, int W,
                                       float* __restrict__ pairs) {
   const int T = (int)((M + BM - 1) / BM) * n_tiles;
   for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < M;
        r += (int64_t)gridDim.x * blockDim.x) {
     const int t0 = (int)(r / BM) * n_tiles, t1 = t0 + n_tiles;
-    const int w0 = head_worker_of(t0, T, W), w1 = head_worker_of(t1 - 1, T, W);
+    const int b0 = head_cta_of(t0, T, W), b1 = head_cta_of(t1 - 1, T, W);
     float best = -INFINITY;
-    unsigned idx = 0;
-    for (int w = w0; w <= w1; ++w) {  // strict >: the lowest column keeps a tie
-      const int lo = max(head_lo(w, T, W), t0);
-      if (lo >= head_lo(w + 1, T, W)) continue;  // a worker without tiles
-      const float4 p = partials[(int64_t)(lo - t0) * M + r];
-      if (p.x > best) {
-        best = p.x;
-        idx = __float_as_uint(p.y);
+    unsigned idx = 0xffffffffu;
+    float4 p[8];  // this row's partials (at most 8 per CTA span, re-read beyond)
+    int np = 0;
+    for (int b = b0; b <= b1; ++b) {
+      const int lo = head_lo(b, T, W);
+      const int s0 = max(lo, t0), s1 = min(head_lo(b + 1, T, W), t1);
+#pragma unroll
+      for (int g = 0; g < NGRP; ++g) {
+        const int first = s0 + ((g - (s0 - lo)) % NGRP + NGRP) % NGRP;
+        if (first >= s1) continue;
+        const float4 q = partials[(int64_t)(first - t0) * M + r];
+        const unsigned qi = __float_as_uint(q.y);
+        if (q.x > best || (q.x == best && qi < idx)) {
+          best = q.x;
+          idx = qi;
+        }
+        if (np < 8) p[np] = q;
+        ++np;
       }
     }
     float s = 0.f;
-    for (int w = w0; w <= w1; ++w) {
-      const int lo = max(head_lo(w, T, W), t0);
-      if (lo >= head_lo(w + 1, T, W)) continue;
-      const float4 p = partials[(int64_t)(lo - t0) * M + r];
-      s += p.z * exp2_ftz((p.x - best) * kLog2e);
+    if (np <= 8) {
+      for (int i = 0; i < np; ++i) s += p[i].z * exp2_ftz((p[i].x - best) * kLog2e);
+    } else {
+      for (int b = b0; b <= b1; ++b) {
+        const int lo = head_lo(b, T, W);
+        const int s0 = max(lo, t0), s1 = min(head_lo(b + 1, T, W), t1);
+        for (int g = 0; g < NGRP; ++g) {
+          const int first = s0 + ((g - (s0 - lo)) % NGRP + NGRP) % NGRP;
+          if (first >= s1) continue;
+          const float4 q = partials[(int64_t)(first - t0) * M + r];
+          s += q.z * exp2_ftz((q.x - best) * kLog2e);
+        }
+      }
     }
     pairs[2 * r] = 1.0f / s;
     pairs[2 * r + 1] = __uint_as_float(idx);
@@ -1461,9 +1517,9 @@ __global__ void argmax_combine_kernel(const float4* __restrict__ partials, int n
 }  // namespace
 
 int head_workers(int64_t M, int n_tiles, int math) {
+  (void)math;
   const int64_t T = ((M + BM - 1) / BM) * n_tiles;
-  const int grid = T < sm_count() ? (int)T : sm_count();  // run_kernel's grid
-  return grid * (math == MATH_3XTF32 ? 1 : HEAD_GROUPS);
+  return T < sm_count() ? (int)T : sm_count();  // run_kernel's grid: one tile range per CTA
 }
 
 cudaError_t launch_argmax_combine(const float4* partials, int n_tiles, int64_t M, int math, float* pairs,
@@ -1471,7 +1527,10 @@ cudaError_t launch_argmax_combine(const float4* partials, int n_tiles, int64_t M
   if (M <= 0) return cudaSuccess;
   const int W = head_workers(M, n_tiles, math);
   int64_t blocks = (M + 63) / 64;  // 64-row blocks: a rec batch's 10,240 rows cover every SM
-  argmax_combine_kernel<<<(unsigned)blocks, 64, 0, st>>>(partials, n_tiles, M, W, pairs);
+  if (math == MATH_3XTF32)
+    argmax_combine_kernel<1><<<(unsigned)blocks, 64, 0, st>>>(partials, n_tiles, M, W, pairs);
+  else
+    argmax_combine_kernel<HEAD_GROUPS><<<(unsigned)blocks, 64, 0, st>>>(partials, n_tiles, M, W, pairs);
   return cudaGetLastError();
 }
 
@@ -1484,7 +1543,7 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
     return cudaErrorInvalidValue;
   const bool split = math == MATH_3XTF32;
   if (split && !b_lo) return cudaErrorInvalidValue;
-  const int bn = pick_bn(N, split);
+  const int bn = epi.partials ? head_bn(N, split) : pick_bn(N, split);
   const int bkw = k_block_width(K);
   CUtensorMap ma, mb, mblo;
   {
@@ -1521,6 +1580,17 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
   const int grid_m = (int)((M + BM - 1) / BM);
   if (epi.partials) {  // CTC head: no gate, nothing stored
     if (epi.a_gate) return cudaErrorInvalidValue;
+    if (!split && epi.a_rounded && args.nkb <= HEAD_RES_KB) {
+      // A rounded by its producer and small enough to stay resident per row block
+      args.m_tiles = grid_m;
+      const int tiles = grid_m * ((N + bn - 1) / bn);
+      switch (bn) {
+        case 32: return run_kernel<32, false, 7>(ma, mb, mblo, mo, args, tiles, st);
+        case 64: return run_kernel<64, false, 7>(ma, mb, mblo, mo, args, tiles, st);
+        case 128: return run_kernel<128, false, 7>(ma, mb, mblo, mo, args, tiles, st);
+        default: return run_kernel<256, false, 7>(ma, mb, mblo, mo, args, tiles, st);
+      }
+    }
     return dispatch<6>(bn, split, ma, mb, mblo, mo, args, grid_m, st);
   }
   if (epi.a_gate) return dispatch<3>(bn, split, ma, mb, mblo, mo, args, grid_m, st);

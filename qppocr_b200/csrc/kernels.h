@@ -64,12 +64,13 @@ struct GemmEpilogue {
   // is rounded on chip, so x * g is never written.  Rows-mode GEMM only.
   const float* a_gate = nullptr;
   int a_gate_rows = 0;
-  // Row-argmax epilogue (CTC head): instead of storing D, each epilogue
-  // worker (a contiguous run of tiles) writes per row of each row block it
-  // covers (max, argmax bits, sum exp(l - max)) over its columns there to
-  // partials[slot * M + row] (float4), slot = its first column tile in that
-  // block; nothing is written to `out`.  Buffer: n_tiles * M float4, of
-  // which launch_argmax_combine reads only the slots written.
+  // Row-argmax epilogue (CTC head): instead of storing D, each CTA (a
+  // contiguous run of tiles) has each epilogue group write, per row of each
+  // row block it covers, (max, argmax bits, sum exp(l - max)) over the
+  // group's columns there to partials[slot * M + row] (float4), slot = the
+  // group's first column tile in that block; nothing is written to `out`.
+  // Buffer: n_tiles * M float4, of which launch_argmax_combine reads only the
+  // slots written.
   float4* partials = nullptr;
   // A already rounded to tf32 by its producer (a depthwise conv with
   // ActParams::round_tf32, or an epilogue / resize storing rounded values):
@@ -97,8 +98,8 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
                            const float* b_lo, int N, const GemmEpilogue& epi, int math,
                            unsigned int* err, cudaStream_t st);
 
-// Number of output-column tiles launch_gemm_tc uses for N (sizes the
-// row-argmax partials buffer: n_tiles * M float4).
+// Number of output-column tiles launch_gemm_tc uses for N with the
+// row-argmax epilogue (sizes the partials buffer: n_tiles * M float4).
 int gemm_tc_col_tiles(int N, int math);
 
 // Combines row-argmax partials into (value, index-bits) pairs: the first
@@ -107,9 +108,9 @@ int gemm_tc_col_tiles(int N, int math);
 // (it fixes the number of epilogue workers, hence the slots written).
 cudaError_t launch_argmax_combine(const float4* partials, int n_tiles, int64_t M, int math, float* pairs,
                                   cudaStream_t st);
-// Epilogue workers of the CTC head GEMM over M rows and n_tiles column tiles
-// on the current device (each leaves one partial per row of every row block
-// it touches: at most M / 128 + workers row blocks' worth in all).
+// CTAs of the CTC head GEMM over M rows and n_tiles column tiles on the
+// current device; each owns a contiguous tile range, and each of its epilogue
+// groups leaves one partial per row of every row block it touches.
 int head_workers(int64_t M, int n_tiles, int math);
 
 // kxk stride-1 dense conv as implicit GEMM on tcgen05: A tiles are 4-D TMA

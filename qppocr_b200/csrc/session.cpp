@@ -2283,10 +2283,10 @@ class Planner {
     if (has_res) throw GraphError{"CTC head with a residual"};
     const int ntiles = gemm_tc_col_tiles((int)Nn, math);
     Val part = new_val({(int64_t)ntiles * rows * 4}, false);
-    // partials written and read: one per (worker, row block) it touches
+    // partials written and read: one per (CTA, epilogue group, row block)
     const int64_t mblk = (rows + 127) / 128;
     const double part_bytes =
-        16.0 * 128 * (double)std::min<int64_t>(mblk * ntiles, mblk + head_workers(rows, ntiles, math));
+        16.0 * 128 * (double)std::min<int64_t>(mblk * ntiles, 2 * (mblk + head_workers(rows, ntiles, math)));
     float4* pp4 = reinterpret_cast<float4*>(out_ptr(part));
     GemmEpilogue e;
     e.bias = bias;

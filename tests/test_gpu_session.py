@@ -157,3 +157,25 @@ def test_unsupported_op_is_named(cuda_ctx):
     g = q.Graph([q.Node("Einsum", "e0", ["x"], ["y"], {})], ["x"], ["y"])
     with pytest.raises(q.GraphError, match="Einsum"):
         cuda_ctx.create_session(g, {})
+
+
+@pytest.mark.parametrize("batch", [7, 64])
+def test_rec_head_rounded_input_is_invisible(cuda_ctx, batch):
+    """In TF32 the final LayerNorm feeds only the CTC head, so it stores its
+    output tf32-rounded and the head GEMM keeps each row block's A resident
+    in shared memory, streaming only the weights.  Exposing the LayerNorm
+    output as a graph output as well makes it unrounded, and the head then
+    streams A and rounds it on chip.  The (value, index) pairs must be
+    identical bit for bit (ragged and multi-block row counts)."""
+    import copy
+    g, w = load(nets.build_rec)
+    x = nets.rec_input(batch, seed=3)
+    s = cuda_ctx.create_session(g, w, role="rec", math="tf32")
+    lns = [o for op, _, o in s.fused_nodes() if op == "QpcLayerNorm"]
+    pairs = s.run({"x": x})[0]
+    g2 = copy.deepcopy(g)
+    g2.outputs = list(g.outputs) + [lns[-1]]
+    s2 = cuda_ctx.create_session(g2, w, role="rec", math="tf32")
+    out2 = s2.run({"x": x})
+    assert np.array_equal(pairs, out2[0])
+    assert out2[1].shape[-1] == 120

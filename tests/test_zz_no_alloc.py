@@ -94,6 +94,7 @@ def test_noalloc_rejects_oversize_before_touching_the_device():
     assert rc == q.QPC_ERR_INVALID
     msg = L.qpc_last_error()
     assert b"exceeds" in msg and b"column tiles" in msg
-    # 2^21 rows of one column tile is exactly the limit; 2^20 rows of 3 tiles is over
-    rc = L.qpc_op_ctc_head_noalloc(dummy, 1 << 20, 8, dummy, None, 300, None, 0, dummy, None)
+    # 2^21 rows of one column tile is exactly the limit; 2^20 rows of 3 tiles
+    # (n = 600: TF32 heads use 256-column tiles) is over
+    rc = L.qpc_op_ctc_head_noalloc(dummy, 1 << 20, 8, dummy, None, 600, None, 0, dummy, None)
     assert rc == q.QPC_ERR_INVALID
