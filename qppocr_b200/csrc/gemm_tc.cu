@@ -1543,7 +1543,14 @@ cudaError_t launch_gemm_tc(const float* a, int64_t M, int K, int lda, const floa
     return cudaErrorInvalidValue;
   const bool split = math == MATH_3XTF32;
   if (split && !b_lo) return cudaErrorInvalidValue;
-  const int bn = epi.partials ? head_bn(N, split) : pick_bn(N, split);
+  int bn = epi.partials ? head_bn(N, split) : pick_bn(N, split);
+  // A grid with fewer tiles than SMs (the rec linears: 80 row blocks) leaves
+  // SMs idle while each CTA runs its one long tile alone: halve the tile width
+  // (down to 64 columns) until every SM has work and both epilogue groups of
+  // a CTA can run at once.  The column split changes no output element's
+  // arithmetic.
+  if (!epi.partials)
+    while (bn > 64 && ((M + BM - 1) / BM) * ((N + bn - 1) / bn) < sm_count()) bn /= 2;
   const int bkw = k_block_width(K);
   CUtensorMap ma, mb, mblo;
   {

@@ -138,3 +138,26 @@ def test_ctc_head_parity(cuda_ctx, rows, n, math):
     assert not ((gi != ri) & (gap >= tol * probs.max())).any()
     assert rel(got[:, 0], ref[:, 0]) < 10 * tol
     assert q.kernel_error(0) == 0
+
+
+@pytest.mark.parametrize("n", [240, 120])
+@pytest.mark.parametrize("math", ["tf32", "3xtf32"])
+def test_gemm_column_split_is_bit_identical(cuda_ctx, math, n):
+    """A GEMM whose grid would leave SMs idle runs narrower column tiles
+    (60 row blocks here: N = 240 as 128-column tiles instead of 256, N = 120
+    as 64 instead of 128, against 160 row blocks for the same rows inside a
+    larger M).  The tile width changes no output element's arithmetic: the
+    shared rows must match bit for bit."""
+    import torch
+    rng = np.random.Generator(np.random.PCG64(17))
+    k, small, large = 120, 128 * 60, 128 * 160
+    x = rng.uniform(-1, 1, (large, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) * np.sqrt(2.0 / k)).astype(np.float32)
+    b = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    hi, lo = q.op_split_tf32(dev(w))
+    lo = lo if math == "3xtf32" else None
+    y_large = q.op_gemm(dev(x), hi, bias=dev(b), act="hswish", math=math, w_lo=lo)
+    y_small = q.op_gemm(dev(x[:small]), hi, bias=dev(b), act="hswish", math=math, w_lo=lo)
+    torch.cuda.synchronize()
+    assert np.array_equal(y_small.cpu().numpy(), y_large.cpu().numpy()[:small])
+    assert q.kernel_error(0) == 0
