@@ -105,3 +105,30 @@ def test_layernorm_bit_exact(cuda_ctx, rows, c):
     got = s.run({"x": x})[0]
     assert got.shape == ref.shape == (1, rows, c)
     assert np.array_equal(got, ref), rel(got, ref)
+
+
+def test_layernorm_edge_rows(cuda_ctx):
+    """Rows whose f64 sums are sensitive to order or sign: constant (all
+    deviations zero), zeros of both signs, a 1e-30 .. 1e3 range, small
+    perturbations of 1 (tiny squared deviations), near-underflow terms, and
+    ordinary ones; the fused LayerNorm must equal the oracle's sequential
+    f64 sums bit for bit."""
+    c, rows = 120, 37
+    b = nets.Builder(6, "lnx")
+    y = b.layernorm("x", c)
+    g, w = b.graph(["x"], [y], [[1, 0, c]])
+    g = q.optimize(g, w)
+    rng = np.random.Generator(np.random.PCG64(99))
+    x = (rng.standard_normal((1, rows, c)) * 2).astype(np.float32)
+    x[0, 0] = 0.75
+    x[0, 1] = 0.0
+    x[0, 1, ::3] = -0.0
+    x[0, 2] = rng.standard_normal(c) * 1e3
+    x[0, 2, ::7] = 1e-30
+    x[0, 3] = 1.0 + rng.standard_normal(c) * 1e-6
+    x[0, 4, ::5] = 3e-38
+    x = x.astype(np.float32)
+    ref = orc.run_graph(g, w, {"x": x})[0]
+    s = cuda_ctx.create_session(g, w, role="other", math="tf32")
+    got = s.run({"x": x})[0]
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)) or np.array_equal(got, ref), rel(got, ref)
