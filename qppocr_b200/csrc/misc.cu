@@ -1378,6 +1378,58 @@ __device__ __forceinline__ void softmax_row_warp(float* row, int inner, int lane
   __syncwarp();
 }
 
+// softmax_row_warp's computation for one row by one 8-lane group of the warp
+// (lanes 8 g .. 8 g + 7; j = lane & 7): the same 8 strided accumulators, the
+// same max and hsum8 order, bit-identical.  Every lane of the warp calls it
+// (the groups' shuffles are warp-wide); `valid` = false marks a group without
+// a row (its scratch row is processed and nothing reads it).
+__device__ __forceinline__ void softmax_row_group8(float* row, int inner, int j, bool valid) {
+  const unsigned full = 0xffffffffu;
+  const int base = (threadIdx.x & 31) & ~7;
+  if (inner < 8) {
+    if (j == 0 && valid) softmax_row(row, row, inner);
+    __syncwarp();
+    return;
+  }
+  const int n8 = inner & ~7;
+  float vmax = row[0];
+  for (int i = 0; i < n8; i += 8) {
+    const float v = row[i + j];
+    if (v > vmax) vmax = v;
+  }
+  float mx = __shfl_sync(full, vmax, base);
+#pragma unroll
+  for (int k = 1; k < 8; ++k) {
+    const float vk = __shfl_sync(full, vmax, base + k);
+    if (vk > mx) mx = vk;
+  }
+  for (int i = n8; i < inner; ++i)
+    if (row[i] > mx) mx = row[i];
+  float acc = 0.f;
+  for (int i = 0; i < n8; i += 8) {
+    const float e = exp1(__fsub_rn(row[i + j], mx));
+    row[i + j] = e;
+    acc = __fadd_rn(acc, e);
+  }
+  float a[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) a[k] = __shfl_sync(full, acc, base + k);
+  const float t0 = __fadd_rn(a[0], a[4]), t1 = __fadd_rn(a[1], a[5]);
+  const float t2 = __fadd_rn(a[2], a[6]), t3 = __fadd_rn(a[3], a[7]);
+  float sum = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
+  __syncwarp();
+  for (int i = n8; i < inner; ++i) {
+    const float e = exp1(__fsub_rn(row[i], mx));
+    sum = __fadd_rn(sum, e);
+    __syncwarp();
+    if (j == 0) row[i] = e;
+  }
+  const float inv = __fdiv_rn(1.0f, sum);
+  __syncwarp();
+  for (int i = j; i < inner; i += 8) row[i] = __fmul_rn(row[i], inv);
+  __syncwarp();
+}
+
 // Fused multi-head attention of the SVTR rec block, one CTA per (line,
 // head), bit-identical to the reference's separate ops: q' = q * scale
 // (Mul), s[t][u] = fma chain over d ascending of q'[t][d] k[u][d] from 0
@@ -1385,15 +1437,19 @@ __device__ __forceinline__ void softmax_row_warp(float* row, int inner, int lane
 // softmax (activation.rs:321-403), o[t][d] = fma chain over u ascending of
 // p[t][u] v[u][d] from 0, written at column h*D + d of the line's [T, H*D]
 // rows (the Transpose + Reshape).  q, k, v of the head are staged in shared
-// memory; each warp takes query rows t = warp, warp + 8, ...: its lanes make
-// the scores, lanes 0-7 the softmax (softmax_row_warp, in the reference's
-// order), lanes < D the output.
+// memory; each warp takes 4 query rows at a time (the rec net's 40 rows: one
+// quad per warp): all 32 lanes make the 4 x T scores, each 8-lane group one
+// row's softmax (softmax_row_group8, in the reference's order), and all lanes
+// the 4 x D outputs.  (One row per warp at a time left 24 lanes idle in the
+// softmax and 17 in P V.)
 // TT, DD > 0: T and D known at compile time (the rec net's 40 x 15), so the
 // dot-product and P V loops unroll and their shared-memory loads are issued
 // ahead of the FMA chains, whose order is unchanged; 0: runtime sizes.
+constexpr int ATT_WARPS = 10;
 template <int TT, int DD>
-__global__ void __launch_bounds__(256) attention_kernel(const float* __restrict__ qkv, float* __restrict__ out,
-                                                        int T_rt, int H, int D_rt, float scale) {
+__global__ void __launch_bounds__(32 * ATT_WARPS) attention_kernel(const float* __restrict__ qkv,
+                                                                  float* __restrict__ out, int T_rt, int H,
+                                                                  int D_rt, float scale) {
   const int T = TT > 0 ? TT : T_rt, D = DD > 0 ? DD : D_rt;
   extern __shared__ float sm[];
   const int b = blockIdx.x / H, h = blockIdx.x % H;
@@ -1401,7 +1457,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
   float* qs = sm;            // [T][D], scaled
   float* ks = qs + T * D;    // [T][D]
   float* vs = ks + T * D;    // [T][D]
-  float* pr = vs + T * D;    // [8][T] score / probability rows, one per warp
+  float* pr = vs + T * D;    // [ATT_WARPS][4][T] score / probability rows
   const float* base = qkv + (int64_t)b * T * C3 + h * D;
   for (int i = threadIdx.x; i < T * D; i += blockDim.x) {
     const int t = i / D, d = i - t * D;
@@ -1412,23 +1468,30 @@ __global__ void __launch_bounds__(256) attention_kernel(const float* __restrict_
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* p = pr + warp * T;
-  for (int t = warp; t < T; t += 8) {
-    const float* q = qs + t * D;
-    for (int u = lane; u < T; u += 32) {
+  const int g = lane >> 3, j = lane & 7;  // 8-lane group g: query row 4 quad + g
+  float* p4 = pr + warp * 4 * T;
+  for (int t0 = 4 * warp; t0 < T; t0 += 4 * ATT_WARPS) {
+    const int nq = min(4, T - t0);
+    // scores: (row, key) pairs over all lanes, each a D-long fma chain
+    for (int idx = lane; idx < nq * T; idx += 32) {
+      const int r = idx / T, u = idx - r * T;
+      const float* q = qs + (t0 + r) * D;
       const float* k = ks + u * D;
       float acc = 0.f;
 #pragma unroll
       for (int d = 0; d < D; ++d) acc = __fmaf_rn(q[d], k[d], acc);
-      p[u] = acc;
+      p4[r * T + u] = acc;
     }
     __syncwarp();
-    softmax_row_warp(p, T, lane);
-    if (lane < D) {
+    softmax_row_group8(p4 + g * T, T, j, g < nq);
+    // P V: (row, dim) pairs over all lanes, each a T-long fma chain
+    for (int idx = lane; idx < nq * D; idx += 32) {
+      const int r = idx / D, d = idx - r * D;
+      const float* pp = p4 + r * T;
       float acc = 0.f;
 #pragma unroll
-      for (int u = 0; u < T; ++u) acc = __fmaf_rn(p[u], vs[u * D + lane], acc);
-      out[((int64_t)b * T + t) * C + h * D + lane] = acc;
+      for (int u = 0; u < T; ++u) acc = __fmaf_rn(pp[u], vs[u * D + d], acc);
+      out[((int64_t)b * T + t0 + r) * C + h * D + d] = acc;
     }
     __syncwarp();
   }
@@ -1440,11 +1503,11 @@ cudaError_t launch_attention(const float* qkv, int64_t B, int T, int H, int D, f
   if (B == 0) return cudaSuccess;
   const int64_t blocks = B * H;
   if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
-  const size_t smem = ((size_t)3 * T * D + 8 * (size_t)T) * sizeof(float);
+  const size_t smem = ((size_t)3 * T * D + (size_t)ATT_WARPS * 4 * T) * sizeof(float);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   auto kern = (T == 40 && D == 15) ? attention_kernel<40, 15> : attention_kernel<0, 0>;
   if (cudaError_t e = ensure_dyn_smem((const void*)kern, (int)smem); e != cudaSuccess) return e;
-  kern<<<(unsigned)blocks, 256, smem, st>>>(qkv, out, T, H, D, scale);
+  kern<<<(unsigned)blocks, 32 * ATT_WARPS, smem, st>>>(qkv, out, T, H, D, scale);
   return cudaGetLastError();
 }
 

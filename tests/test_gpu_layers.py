@@ -132,3 +132,15 @@ def test_layernorm_edge_rows(cuda_ctx):
     s = cuda_ctx.create_session(g, w, role="other", math="tf32")
     got = s.run({"x": x})[0]
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)) or np.array_equal(got, ref), rel(got, ref)
+
+
+@pytest.mark.parametrize("width", [200, 56])
+def test_rec_attention_runtime_sizes(cuda_ctx, width):
+    """The fused attention at token counts other than the compile-time 40
+    (width / 8: T = 25, a partial group of 4 query rows, and T = 7, a row
+    shorter than the softmax's 8 accumulators) stays bit-exact on its own
+    input."""
+    fused, errs = per_node(cuda_ctx, nets.build_rec, nets.rec_input(2, w=width), "tf32", "rec")
+    att = [o for op, _, o in fused if op == "QpcAttention"]
+    assert len(att) == 2
+    assert all(errs[o][1] == 0.0 for o in att), [errs[o] for o in att]
