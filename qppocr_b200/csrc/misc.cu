@@ -1325,62 +1325,12 @@ cudaError_t launch_softmax_argmax(const float* x, float* pairs, int64_t rows, in
 
 namespace qpc {
 
-// softmax_row on a shared-memory row, by one warp: lanes 0-7 keep the
+// softmax_row on a shared-memory row, by one 8-lane group of the warp
+// (lanes 8 g .. 8 g + 7; j = lane & 7): the group's lanes keep the
 // reference's eight lane accumulators (element i goes to lane i % 8, in
 // ascending order), the max and the hsum8 tree are combined from them in the
-// reference's order, the scalar tail follows sequentially, and all lanes
-// scale.  Bit-identical to softmax_row.
-__device__ __forceinline__ void softmax_row_warp(float* row, int inner, int lane) {
-  if (inner < 8) {
-    if (lane == 0) softmax_row(row, row, inner);
-    __syncwarp();
-    return;
-  }
-  const int n8 = inner & ~7;
-  const int j = lane & 7;
-  float vmax = row[0];
-  if (lane < 8)
-    for (int i = 0; i < n8; i += 8) {
-      const float v = row[i + j];
-      if (v > vmax) vmax = v;
-    }
-  float mx = __shfl_sync(0xffffffffu, vmax, 0);
-#pragma unroll
-  for (int k = 1; k < 8; ++k) {
-    const float vk = __shfl_sync(0xffffffffu, vmax, k);
-    if (vk > mx) mx = vk;
-  }
-  for (int i = n8; i < inner; ++i)
-    if (row[i] > mx) mx = row[i];
-  float acc = 0.f;
-  if (lane < 8)
-    for (int i = 0; i < n8; i += 8) {
-      const float e = exp1(__fsub_rn(row[i + j], mx));
-      row[i + j] = e;
-      acc = __fadd_rn(acc, e);
-    }
-  float a[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) a[k] = __shfl_sync(0xffffffffu, acc, k);
-  const float t0 = __fadd_rn(a[0], a[4]), t1 = __fadd_rn(a[1], a[5]);
-  const float t2 = __fadd_rn(a[2], a[6]), t3 = __fadd_rn(a[3], a[7]);
-  float sum = __fadd_rn(__fadd_rn(t0, t1), __fadd_rn(t2, t3));
-  __syncwarp();
-  for (int i = n8; i < inner; ++i) {
-    const float e = exp1(__fsub_rn(row[i], mx));
-    sum = __fadd_rn(sum, e);
-    __syncwarp();
-    if (lane == 0) row[i] = e;
-  }
-  const float inv = __fdiv_rn(1.0f, sum);
-  __syncwarp();
-  for (int i = lane; i < inner; i += 32) row[i] = __fmul_rn(row[i], inv);
-  __syncwarp();
-}
-
-// softmax_row_warp's computation for one row by one 8-lane group of the warp
-// (lanes 8 g .. 8 g + 7; j = lane & 7): the same 8 strided accumulators, the
-// same max and hsum8 order, bit-identical.  Every lane of the warp calls it
+// reference's order, the scalar tail follows sequentially, and the group
+// scales.  Bit-identical to softmax_row.  Every lane of the warp calls it
 // (the groups' shuffles are warp-wide); `valid` = false marks a group without
 // a row (its scratch row is processed and nothing reads it).
 __device__ __forceinline__ void softmax_row_group8(float* row, int inner, int j, bool valid) {
