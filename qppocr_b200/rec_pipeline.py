@@ -178,24 +178,37 @@ class RecStage:
         shapes = [(int(c.shape[0]), int(c.shape[1])) for c in crops]
         batches = self.plan(shapes)
         dev = torch.device("cuda", self.device)
-        # all crops uploaded once, back to back
+        # all crops uploaded once, back to back: concatenated straight into
+        # pinned memory (one copy), then one DMA
         sizes = [c.size for c in crops]
         offs = np.zeros(len(crops), np.int64)
         if len(crops) > 1:
             offs[1:] = np.cumsum(sizes)[:-1]
-        host = np.empty(max(int(sum(sizes)), 1), np.uint8)
-        for i, c in enumerate(crops):
-            host[offs[i]:offs[i] + sizes[i]] = np.ascontiguousarray(c, np.uint8).reshape(-1)
-        blob = torch.from_numpy(host).pin_memory().to(dev, non_blocking=True)
+        total = int(sum(sizes))
+        pinned = torch.empty(max(total, 1), dtype=torch.uint8, pin_memory=True)
+        if total:
+            np.concatenate([np.ascontiguousarray(c, np.uint8).reshape(-1) for c in crops], out=pinned.numpy()[:total])
+        blob = pinned.to(dev, non_blocking=True)
+        # every batch's line table (offset, h, w, resized width, pad flag), in
+        # batch order, also uploaded once; each batch takes its columns
+        n_lines = sum(len(ids) for ids, _ in batches)
+        table = torch.empty((5, max(n_lines, 1)), dtype=torch.int64, pin_memory=True)
+        tab = table.numpy()
+        spans, col = [], 0
+        for ids, img_w in batches:
+            for i in ids:
+                h, w = shapes[i]
+                p = crop_pads(h, self.img_h, self.pad_min_h)
+                tab[:, col] = (offs[i], h, w, min(w, img_w) if p else resized_width(h, w, self.img_h, img_w), int(p))
+                col += 1
+            spans.append((col - len(ids), col))
+        dtab = table.to(dev, non_blocking=True)
         results: List = [None] * len(crops)
 
-        def submit(ids, img_w):
-            pads = [crop_pads(shapes[i][0], self.img_h, self.pad_min_h) for i in ids]
-            rws = [min(shapes[i][1], img_w) if p else resized_width(shapes[i][0], shapes[i][1], self.img_h, img_w)
-                   for i, p in zip(ids, pads)]
-            meta = np.array([[shapes[i][0], shapes[i][1], rw, int(p)] for i, rw, p in zip(ids, rws, pads)], np.int32)
-            m = torch.from_numpy(np.ascontiguousarray(meta.T)).to(dev)
-            o = torch.from_numpy(offs[list(ids)]).to(dev)
+        def submit(ids, img_w, span):
+            a, b = span
+            o = dtab[0, a:b].contiguous()
+            m = dtab[1:, a:b].to(torch.int32)
             x = op_rec_pack(blob, o, m[0].contiguous(), m[1].contiguous(), m[2].contiguous(), m[3].contiguous(),
                             self.img_h, img_w)
             torch.cuda.current_stream(dev).synchronize()  # packed before the session's stream copies it
@@ -203,8 +216,8 @@ class RecStage:
             return self.s.run_deferred({"x": x})
 
         pending = None
-        for ids, img_w in batches:
-            d = submit(ids, img_w)
+        for (ids, img_w), span in zip(batches, spans):
+            d = submit(ids, img_w, span)
             if pending is not None:
                 self._finish(*pending, results)
             pending = (d, ids)
