@@ -123,11 +123,15 @@ def ctc_decode_pairs_batch(pairs, charset: Optional[Sequence[str]] = None):
     cnt = emit.sum(axis=1)
     sums = np.cumsum(np.where(emit, vals, 0.0), axis=1)[:, -1] if t else np.zeros(b)
     keep = emit if charset is None else emit & (idx < len(charset))
-    out = []
+    with np.errstate(divide="ignore", invalid="ignore"):
+        conf = np.where(cnt > 0, sums / np.maximum(cnt, 1), 0.0).astype(np.float32)
+    flat = idx[keep].tolist()  # row-major: line k's kept indices are consecutive
+    lens = keep.sum(axis=1).tolist()
+    out, pos = [], 0
     for k in range(b):
-        conf = np.float32(sums[k] / cnt[k]) if cnt[k] else np.float32(0.0)
-        ids = idx[k][keep[k]].tolist()
-        out.append(("".join(charset[i] for i in ids) if charset is not None else ids, conf))
+        ids = flat[pos:pos + lens[k]]
+        pos += lens[k]
+        out.append(("".join(map(charset.__getitem__, ids)) if charset is not None else ids, conf[k]))
     return out
 
 
@@ -139,6 +143,53 @@ def ctc_decode_probs(probs, charset: Optional[Sequence[str]] = None):
     pairs[:, 0] = probs[np.arange(probs.shape[0]), best]
     pairs[:, 1] = best.astype(np.uint32).view(np.float32)
     return ctc_decode_pairs(pairs, charset)
+
+
+def plan_lines(shapes: Sequence[Tuple[int, int]], img_h: int, pad_min_h: float, min_width: int, grain: int,
+               per_batch: int):
+    """The engine's line plan (batch_ratio, a stable sort, group_lines,
+    batch_width) with array operations: the same float32 arithmetic per line,
+    the same stable order; the raw widths are non-decreasing along the sorted
+    ratios, so each group's end is one binary search.  Returns [(ids, img_w)]."""
+    hw = np.asarray(shapes, np.int64).reshape(-1, 2)
+    h, w = hw[:, 0], hw[:, 1]
+    pads = (pad_min_h > 0.0) & (h > 0) & (h <= img_h) & (h >= pad_min_h * img_h)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        ratio = np.where(pads, w.astype(F32) / F32(img_h), w.astype(F32) / h.astype(F32)).astype(F32)
+    ratio[h <= 0] = F32(1.0)
+    order = np.argsort(ratio, kind="stable")
+    rs = ratio[order]
+    raw = (F32(img_h) * rs).astype(np.int64)
+    m0 = F32(min_width) / F32(img_h)
+    out, beg, n = [], 0, len(rs)
+    while beg < n:
+        if grain > 1:
+            lim = int(np.searchsorted(raw, raw[beg] + grain, side="right"))
+            end = max(beg + 1, min(beg + per_batch, lim))
+        else:
+            end = max(beg + 1, min(beg + per_batch, n))
+        wb = int(F32(img_h) * max(m0, rs[beg:end].max()))
+        if grain > 1:
+            wb = (wb + grain - 1) // grain * grain
+        out.append((order[beg:end].tolist(), wb))
+        beg = end
+    return out
+
+
+def line_table(shapes: Sequence[Tuple[int, int]], batches, offs, img_h: int, pad_min_h: float) -> np.ndarray:
+    """[5, lines] int64 in batch order: crop offset, h, w, resized width
+    (ceil(img_h * w / h) clamped to [1, img_w], or min(w, img_w) for a padded
+    crop, as resized_width / crop_pads), pad flag."""
+    ids = np.asarray([i for b, _ in batches for i in b], np.int64)
+    img_w = np.asarray([wb for b, wb in batches for _ in b], np.int64)
+    hw = np.asarray(shapes, np.int64).reshape(-1, 2)[ids] if len(ids) else np.zeros((0, 2), np.int64)
+    h, w = hw[:, 0], hw[:, 1]
+    if (h <= 0).any():
+        raise ValueError("crop of height 0")
+    pads = (pad_min_h > 0.0) & (h <= img_h) & (h >= pad_min_h * img_h)
+    rw = np.ceil(F32(img_h) * (w.astype(F32) / h.astype(F32))).astype(np.int64)
+    rw = np.where(pads, np.minimum(w, img_w), np.maximum(np.minimum(rw, img_w), 1))
+    return np.stack([np.asarray(offs, np.int64)[ids], h, w, rw, pads.astype(np.int64)])
 
 
 class RecStage:
@@ -162,15 +213,7 @@ class RecStage:
 
     def plan(self, shapes: Sequence[Tuple[int, int]]):
         """Order, batches and per-line widths for crops of these (h, w)."""
-        ratios = [batch_ratio(h, w, self.img_h, self.pad_min_h) for h, w in shapes]
-        order = sorted(range(len(shapes)), key=lambda i: ratios[i])  # stable, as sort_by
-        groups = group_lines([ratios[i] for i in order], self.img_h, self.grain, self.per_batch)
-        out = []
-        for beg, end in groups:
-            ids = order[beg:end]
-            img_w = batch_width([ratios[i] for i in ids], self.img_h, self.min_width, self.grain)
-            out.append((ids, img_w))
-        return out
+        return plan_lines(shapes, self.img_h, self.pad_min_h, self.min_width, self.grain, self.per_batch)
 
     def run(self, crops: Sequence[np.ndarray]):
         import torch
@@ -193,15 +236,12 @@ class RecStage:
         # batch order, also uploaded once; each batch takes its columns
         n_lines = sum(len(ids) for ids, _ in batches)
         table = torch.empty((5, max(n_lines, 1)), dtype=torch.int64, pin_memory=True)
-        tab = table.numpy()
+        if n_lines:
+            table.numpy()[:, :n_lines] = line_table(shapes, batches, offs, self.img_h, self.pad_min_h)
         spans, col = [], 0
-        for ids, img_w in batches:
-            for i in ids:
-                h, w = shapes[i]
-                p = crop_pads(h, self.img_h, self.pad_min_h)
-                tab[:, col] = (offs[i], h, w, min(w, img_w) if p else resized_width(h, w, self.img_h, img_w), int(p))
-                col += 1
-            spans.append((col - len(ids), col))
+        for ids, _ in batches:
+            spans.append((col, col + len(ids)))
+            col += len(ids)
         dtab = table.to(dev, non_blocking=True)
         results: List = [None] * len(crops)
 

@@ -1,6 +1,7 @@
 """Host logic of the recognition stage (engine.rs:1160-1500, crop.rs:129-185,
 rec.rs:34-120) on hand-worked cases and against the oracle's CTC decoder."""
 import numpy as np
+import pytest
 
 import oracle as orc
 from qppocr_b200 import rec_pipeline as rp
@@ -97,3 +98,44 @@ def test_batch_decode_matches_per_line():
         for k in range(b):
             ref = ctc_decode_pairs(pairs[k], cs)
             assert got[k][0] == ref[0] and got[k][1] == ref[1] and type(got[k][1]) == type(ref[1])
+
+
+def _plan_scalar(shapes, img_h, pad_min_h, min_width, grain, per_batch):
+    """The plan line by line with the scalar restatements (batch_ratio,
+    sorted, group_lines, batch_width)."""
+    ratios = [rp.batch_ratio(h, w, img_h, pad_min_h) for h, w in shapes]
+    order = sorted(range(len(shapes)), key=lambda i: ratios[i])
+    groups = rp.group_lines([ratios[i] for i in order], img_h, grain, per_batch)
+    return [(order[b:e], rp.batch_width([ratios[i] for i in order[b:e]], img_h, min_width, grain)) for b, e in groups]
+
+
+@pytest.mark.parametrize("pad_min_h", [0.0, 0.8])
+@pytest.mark.parametrize("grain,per_batch", [(1, 6), (16, 8), (64, 256), (32, 1)])
+def test_vectorised_plan_and_line_table_match_the_scalar_rules(pad_min_h, grain, per_batch):
+    """RecStage's array-form plan and per-line table equal the line-by-line
+    restatements exactly: same order, groups, batch widths, resized widths and
+    pad flags (ties in ratio included)."""
+    rng = np.random.Generator(np.random.PCG64(int(pad_min_h * 10) + grain * 7 + per_batch))
+    for n in (0, 1, 7, 300, 1024):
+        hs = rng.integers(1, 80, n)
+        ws = rng.integers(1, 900, n)
+        if n > 20:
+            hs[:10], ws[:10] = 32, 96  # equal ratios: the stable order decides
+        shapes = [(int(h), int(w)) for h, w in zip(hs, ws)]
+        got = rp.plan_lines(shapes, 48, pad_min_h, 16, grain, per_batch)
+        ref = _plan_scalar(shapes, 48, pad_min_h, 16, grain, per_batch)
+        assert got == ref
+        offs = np.cumsum([0] + [h * w * 3 for h, w in shapes])[:-1]
+        tab = rp.line_table(shapes, got, offs, 48, pad_min_h)
+        col = 0
+        for ids, img_w in got:
+            for i in ids:
+                h, w = shapes[i]
+                p = rp.crop_pads(h, 48, pad_min_h)
+                rw = min(w, img_w) if p else rp.resized_width(h, w, 48, img_w)
+                assert tuple(tab[:, col]) == (offs[i], h, w, rw, int(p)), (i, tab[:, col])
+                col += 1
+        assert tab.shape == (5, n)
+    # zero-height crops keep ratio 1 in the plan
+    shapes = [(0, 50), (10, 40), (0, 5), (20, 20)]
+    assert rp.plan_lines(shapes, 48, 0.0, 16, 16, 8) == _plan_scalar(shapes, 48, 0.0, 16, 16, 8)
