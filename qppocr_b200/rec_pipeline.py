@@ -243,14 +243,13 @@ class RecStage:
             spans.append((col, col + len(ids)))
             col += len(ids)
         dtab = table.to(dev, non_blocking=True)
+        d32 = dtab[1:].to(torch.int32)  # h, w, resized width, pad flag: one conversion for all lines
         results: List = [None] * len(crops)
 
         def submit(ids, img_w, span):
-            a, b = span
-            o = dtab[0, a:b].contiguous()
-            m = dtab[1:, a:b].to(torch.int32)
-            x = op_rec_pack(blob, o, m[0].contiguous(), m[1].contiguous(), m[2].contiguous(), m[3].contiguous(),
-                            self.img_h, img_w)
+            a, b = span  # this batch's columns: contiguous slices of each table row
+            x = op_rec_pack(blob, dtab[0, a:b], d32[0, a:b], d32[1, a:b], d32[2, a:b], d32[3, a:b], self.img_h,
+                            img_w)
             torch.cuda.current_stream(dev).synchronize()  # packed before the session's stream copies it
             self.batches += 1
             return self.s.run_deferred({"x": x})
